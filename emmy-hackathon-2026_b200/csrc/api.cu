@@ -1,0 +1,135 @@
+// Context management and memory helpers of the C ABI (include/b200k.h).
+#include <new>
+
+#include "common.cuh"
+
+namespace b2k {
+
+int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream) {
+  if (bytes <= ctx->workspace_bytes) return B2K_OK;
+  // Scratch is reused by every call on this context's stream order; wait for
+  // in-flight users before releasing the old arena.
+  cudaError_t err = cudaStreamSynchronize(stream);
+  if (err != cudaSuccess) return cuda_fail(ctx, err, "workspace: stream sync");
+  if (ctx->workspace) {
+    err = cudaFree(ctx->workspace);
+    ctx->workspace = nullptr;
+    ctx->workspace_bytes = 0;
+    if (err != cudaSuccess) return cuda_fail(ctx, err, "workspace: cudaFree");
+  }
+  const size_t rounded = (bytes + (size_t(1) << 21) - 1) & ~((size_t(1) << 21) - 1);
+  err = cudaMalloc(&ctx->workspace, rounded);
+  if (err != cudaSuccess) {
+    ctx->workspace = nullptr;
+    return cuda_fail(ctx, err, "workspace: cudaMalloc");
+  }
+  ctx->workspace_bytes = rounded;
+  return B2K_OK;
+}
+
+}  // namespace b2k
+
+extern "C" {
+
+int b2k_version(void) { return 100; }
+
+int b2k_init(int device_ordinal, b2k_ctx **out) {
+  if (!out) return B2K_EINVAL;
+  *out = nullptr;
+  int count = 0;
+  cudaError_t err = cudaGetDeviceCount(&count);
+  if (err != cudaSuccess) return B2K_ECUDA;
+  if (device_ordinal < 0 || device_ordinal >= count) return B2K_EINVAL;
+  b2k_ctx *ctx = new (std::nothrow) b2k_ctx;
+  if (!ctx) return B2K_ECUDA;
+  ctx->device = device_ordinal;
+  if ((err = cudaSetDevice(device_ordinal)) != cudaSuccess ||
+      (err = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device_ordinal)) !=
+          cudaSuccess ||
+      (err = cudaDeviceGetAttribute(&ctx->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                                    device_ordinal)) != cudaSuccess) {
+    delete ctx;
+    return B2K_ECUDA;
+  }
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device_ordinal);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device_ordinal);
+  if (major != 10 || minor != 0) {
+    // The fatbin holds sm_100a code only; any other device cannot run it.
+    delete ctx;
+    return B2K_EUNSUPPORTED;
+  }
+  err = cudaMalloc(&ctx->error_flag, sizeof(unsigned int) * 4);
+  if (err == cudaSuccess) err = cudaMemset(ctx->error_flag, 0, sizeof(unsigned int) * 4);
+  if (err != cudaSuccess) {
+    delete ctx;
+    return B2K_ECUDA;
+  }
+  *out = ctx;
+  return B2K_OK;
+}
+
+int b2k_destroy(b2k_ctx *ctx) {
+  if (!ctx) return B2K_EINVAL;
+  cudaSetDevice(ctx->device);
+  if (ctx->workspace) cudaFree(ctx->workspace);
+  if (ctx->error_flag) cudaFree(ctx->error_flag);
+  delete ctx;
+  return B2K_OK;
+}
+
+const char *b2k_last_error(const b2k_ctx *ctx) { return ctx ? ctx->error.c_str() : "null context"; }
+
+int b2k_sm_count(const b2k_ctx *ctx) { return ctx ? ctx->sm_count : 0; }
+
+int b2k_malloc(b2k_ctx *ctx, void **ptr, size_t bytes) {
+  B2K_CHECK_CTX(ctx);
+  if (!ptr) return b2k::fail(ctx, B2K_EINVAL, "b2k_malloc: null output pointer");
+  cudaError_t err = cudaMalloc(ptr, bytes ? bytes : 1);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaMalloc");
+  return B2K_OK;
+}
+
+int b2k_free(b2k_ctx *ctx, void *ptr) {
+  B2K_CHECK_CTX(ctx);
+  cudaError_t err = cudaFree(ptr);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaFree");
+  return B2K_OK;
+}
+
+int b2k_memcpy_htod(b2k_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream) {
+  B2K_CHECK_CTX(ctx);
+  cudaError_t err = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaMemcpyAsync(HtoD)");
+  return B2K_OK;
+}
+
+int b2k_memcpy_dtoh(b2k_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream) {
+  B2K_CHECK_CTX(ctx);
+  cudaError_t err = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaMemcpyAsync(DtoH)");
+  return B2K_OK;
+}
+
+int b2k_memset(b2k_ctx *ctx, void *dst, int value, size_t bytes, void *stream) {
+  B2K_CHECK_CTX(ctx);
+  cudaError_t err = cudaMemsetAsync(dst, value, bytes, (cudaStream_t)stream);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaMemsetAsync");
+  return B2K_OK;
+}
+
+int b2k_stream_sync(b2k_ctx *ctx, void *stream) {
+  B2K_CHECK_CTX(ctx);
+  cudaError_t err = cudaStreamSynchronize((cudaStream_t)stream);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaStreamSynchronize");
+  unsigned int flag = 0;
+  err = cudaMemcpy(&flag, ctx->error_flag, sizeof flag, cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "error flag readback");
+  if (flag) {
+    cudaMemset(ctx->error_flag, 0, sizeof(unsigned int) * 4);
+    return b2k::fail(ctx, B2K_ETIMEOUT, "a kernel's bounded wait expired (code 0x%x)", flag);
+  }
+  return B2K_OK;
+}
+
+}  // extern "C"

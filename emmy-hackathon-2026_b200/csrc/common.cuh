@@ -1,0 +1,116 @@
+// Shared definitions of the B200 backend: the context object, error plumbing
+// and device helpers used by more than one kernel file.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "b200k.h"
+
+struct b2k_ctx {
+  int device = 0;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  std::string error;
+  // Context-owned scratch arena (grown on demand, never shrunk).
+  void *workspace = nullptr;
+  size_t workspace_bytes = 0;
+  // Device-side error word written by kernels whose bounded waits expire.
+  unsigned int *error_flag = nullptr;
+};
+
+namespace b2k {
+
+// Record a formatted reason on the context and return `code`.
+inline int fail(b2k_ctx *ctx, int code, const char *fmt, ...) {
+  char buffer[512];
+  va_list args;
+  va_start(args, fmt);
+  vsnprintf(buffer, sizeof buffer, fmt, args);
+  va_end(args);
+  if (ctx) ctx->error = buffer;
+  return code;
+}
+
+inline int cuda_fail(b2k_ctx *ctx, cudaError_t err, const char *what) {
+  return fail(ctx, B2K_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
+}
+
+// Check the launch that was just enqueued (configuration errors only; the
+// kernel itself runs asynchronously).
+inline int check_launch(b2k_ctx *ctx, const char *what) {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_fail(ctx, err, what);
+  ctx->error.clear();
+  return B2K_OK;
+}
+
+inline int make_current(b2k_ctx *ctx) {
+  cudaError_t err = cudaSetDevice(ctx->device);
+  if (err != cudaSuccess) return cuda_fail(ctx, err, "cudaSetDevice");
+  return B2K_OK;
+}
+
+// Grow the context's scratch arena to at least `bytes`.
+int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream);
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace b2k
+
+#define B2K_CHECK_CTX(ctx)                                   \
+  do {                                                       \
+    if (!(ctx)) return B2K_EINVAL;                           \
+    int b2k_status_ = b2k::make_current(ctx);                \
+    if (b2k_status_ != B2K_OK) return b2k_status_;           \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// Device helpers
+// ---------------------------------------------------------------------------
+
+// Selective subnormal-preserving exponential (the reference's method,
+// compile.py:2953-2965): t = x*log2(e) in FP32; arguments with t < -125 are
+// shifted by +126 into the normal range of the flush-to-zero ex2, and the
+// result is scaled back by an exact 2^-126 multiply that is NOT flushed, so
+// results in the subnormal range survive.  Relies on this library being
+// compiled without -ftz / --use_fast_math.
+__device__ __forceinline__ float b2k_exp(float x) {
+  float t = __fmul_rn(x, 1.44269502162933349609375f);  // f32(log2(e))
+  const bool tiny = t < -125.0f;
+  if (tiny) t = __fadd_rn(t, 126.0f);
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(t));
+  if (tiny) r = __fmul_rn(r, 1.17549435082228750797e-38f);  // exact 2^-126
+  return r;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int offset = 16; offset > 0; offset >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int offset = 16; offset > 0; offset >>= 1) v += __shfl_xor_sync(0xffffffffu, v, offset);
+  return v;
+}
+
+__device__ __forceinline__ float4 ld_stream(const float4 *p) {
+  float4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_stream(float4 *p, float4 v) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}

@@ -1,0 +1,173 @@
+"""ctypes binding of ``libb200k.so`` (include/b200k.h).
+
+This is the thin C-ABI shim the front end dispatches through: no PyTorch, no
+CPU fallback.  If the library is missing the import of :func:`library` fails
+loudly -- a recognised kernel never silently runs anywhere but the GPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "libb200k.so"
+
+B2K_OK, B2K_EINVAL, B2K_EUNSUPPORTED, B2K_ECUDA, B2K_ETIMEOUT = 0, 1, 2, -1, -2
+STATUS_NAMES = {B2K_EINVAL: "EINVAL", B2K_EUNSUPPORTED: "EUNSUPPORTED", B2K_ECUDA: "ECUDA",
+                B2K_ETIMEOUT: "ETIMEOUT"}
+
+PW_MAX_INPUTS, PW_MAX_INSNS = 8, 48
+
+OPCODES = {
+    "const": 0, "copy": 1, "add": 2, "subtract": 3, "multiply": 4, "divide": 5, "maximum": 6,
+    "minimum": 7, "negative": 8, "reciprocal": 9, "sqrt": 10, "rsqrt": 11, "exp": 12, "relu": 13,
+    "abs": 14, "fma": 15, "greater": 16, "greater_equal": 17, "less": 18, "less_equal": 19,
+    "where": 20, "log": 21,
+}
+
+
+class B2KError(RuntimeError):
+    """A non-OK status from the C ABI, with the library's reason string."""
+
+    def __init__(self, status: int, reason: str, call: str):
+        self.status = status
+        super().__init__(f"{call}: {STATUS_NAMES.get(status, status)}: {reason}")
+
+
+class PwInsn(C.Structure):
+    _fields_ = [("op", C.c_int32), ("a", C.c_int32), ("b", C.c_int32), ("c", C.c_int32), ("imm", C.c_float)]
+
+
+class PwProgram(C.Structure):
+    _fields_ = [("n_inputs", C.c_int32), ("n_insns", C.c_int32), ("result", C.c_int32),
+                ("broadcast", C.c_int32 * PW_MAX_INPUTS), ("insns", PwInsn * PW_MAX_INSNS)]
+
+
+_P, _I32, _I64, _SZ, _F = C.c_void_p, C.c_int32, C.c_int64, C.c_size_t, C.c_float
+
+# name -> (argtypes without the leading context pointer, or None for no ctx)
+SIGNATURES: dict[str, tuple] = {
+    "b2k_version": ([], C.c_int),
+    "b2k_init": ([C.c_int, C.POINTER(_P)], C.c_int),
+    "b2k_destroy": ([_P], C.c_int),
+    "b2k_last_error": ([_P], C.c_char_p),
+    "b2k_sm_count": ([_P], C.c_int),
+    "b2k_malloc": ([_P, C.POINTER(_P), _SZ], C.c_int),
+    "b2k_free": ([_P, _P], C.c_int),
+    "b2k_memcpy_htod": ([_P, _P, _P, _SZ, _P], C.c_int),
+    "b2k_memcpy_dtoh": ([_P, _P, _P, _SZ, _P], C.c_int),
+    "b2k_memset": ([_P, _P, C.c_int, _SZ, _P], C.c_int),
+    "b2k_stream_sync": ([_P, _P], C.c_int),
+    "b2k_pointwise_f32": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _P], C.c_int),
+    "b2k_row_softmax_f32": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
+    "b2k_selective_exp_f32": ([_P, _P, _P, _I64, _P], C.c_int),
+}
+
+_lock = threading.Lock()
+_lib: C.CDLL | None = None
+
+
+def library() -> C.CDLL:
+    """Load ``libb200k.so`` once; raise if it has not been built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIBRARY_PATH.exists():
+                raise ImportError(f"{LIBRARY_PATH} is missing: build it with __graft_entry__.build() "
+                                  "(the backend has no CPU fallback)")
+            lib = C.CDLL(str(LIBRARY_PATH))
+            for name, (argtypes, restype) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes, fn.restype = argtypes, restype
+            _lib = lib
+        return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+def make_program(n_inputs: int, insns: list[tuple], result: int, broadcast=()) -> PwProgram:
+    """Build a :class:`PwProgram`; ``insns`` are ``(opname, a, b, c, imm)`` tuples."""
+    if n_inputs > PW_MAX_INPUTS or len(insns) > PW_MAX_INSNS:
+        raise ValueError("pointwise program exceeds the kernel's register budget")
+    prog = PwProgram()
+    prog.n_inputs, prog.n_insns, prog.result = n_inputs, len(insns), result
+    for i in range(PW_MAX_INPUTS):
+        prog.broadcast[i] = 1 if i in tuple(broadcast) else 0
+    for i, (op, a, b, c, imm) in enumerate(insns):
+        prog.insns[i] = PwInsn(OPCODES[op] if isinstance(op, str) else int(op), a, b, c, float(imm))
+    return prog
+
+
+class Context:
+    """One ``b2k_ctx`` on one CUDA device (not thread-safe, like the C object)."""
+
+    def __init__(self, device: int = 0):
+        self.lib = library()
+        handle = _P()
+        status = self.lib.b2k_init(device, C.byref(handle))
+        if status != B2K_OK:
+            raise B2KError(status, "context creation failed (no sm_100 device?)", "b2k_init")
+        self.handle, self.device = handle, device
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.b2k_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self) -> "Context":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, status: int, call: str) -> None:
+        if status != B2K_OK:
+            reason = self.lib.b2k_last_error(self.handle) or b""
+            raise B2KError(status, reason.decode(errors="replace"), call)
+
+    @property
+    def sm_count(self) -> int:
+        return self.lib.b2k_sm_count(self.handle)
+
+    # --- kernels (pointers are plain integers: device addresses) ----------
+    def pointwise(self, program: PwProgram, inputs: list[int], out: int, n: int, stream: int = 0) -> None:
+        arr = (_P * max(1, len(inputs)))(*inputs)
+        self.check(self.lib.b2k_pointwise_f32(self.handle, C.byref(program), arr, out, n, stream),
+                   "b2k_pointwise_f32")
+
+    def row_softmax(self, x: int, y: int, rows: int, cols: int, ld_x: int | None = None,
+                    ld_y: int | None = None, stream: int = 0) -> None:
+        self.check(self.lib.b2k_row_softmax_f32(self.handle, x, y, rows, cols, ld_x or cols, ld_y or cols, stream),
+                   "b2k_row_softmax_f32")
+
+    def selective_exp(self, x: int, y: int, n: int, stream: int = 0) -> None:
+        self.check(self.lib.b2k_selective_exp_f32(self.handle, x, y, n, stream), "b2k_selective_exp_f32")
+
+    def sync(self, stream: int = 0) -> None:
+        self.check(self.lib.b2k_stream_sync(self.handle, stream), "b2k_stream_sync")
+
+    # --- memory helpers (used by callers without PyTorch) -------------------
+    def malloc(self, nbytes: int) -> int:
+        ptr = _P()
+        self.check(self.lib.b2k_malloc(self.handle, C.byref(ptr), nbytes), "b2k_malloc")
+        return ptr.value or 0
+
+    def free(self, ptr: int) -> None:
+        self.check(self.lib.b2k_free(self.handle, ptr), "b2k_free")
+
+    def htod(self, dst: int, src: int, nbytes: int, stream: int = 0) -> None:
+        self.check(self.lib.b2k_memcpy_htod(self.handle, dst, src, nbytes, stream), "b2k_memcpy_htod")
+
+    def dtoh(self, dst: int, src: int, nbytes: int, stream: int = 0) -> None:
+        self.check(self.lib.b2k_memcpy_dtoh(self.handle, dst, src, nbytes, stream), "b2k_memcpy_dtoh")
+
+    def memset(self, dst: int, value: int, nbytes: int, stream: int = 0) -> None:
+        self.check(self.lib.b2k_memset(self.handle, dst, value, nbytes, stream), "b2k_memset")

@@ -1,0 +1,138 @@
+/*
+ * b200k.h -- C ABI of the B200 (sm_100a) kernel backend for Emmy Kernel IR.
+ *
+ * The reference compiler turns each recognised Kernel-IR kernel into PTX text
+ * (compile.py:9628-9724 compile_path) which a runner assembles and launches
+ * with cuLaunchKernel, passing positional arguments in meta.json's arg_order
+ * (tools/local_runner.py:246-342, launch at :309-324).  This library replaces
+ * that emitted PTX: a front end recognises the kernel and calls one of the
+ * entry points below with the same device buffers.
+ *
+ * Conventions shared by every entry point:
+ *   - Plain C types only: device pointers, 64-bit extents, a cudaStream_t
+ *     passed as void* (NULL = the legacy default stream).
+ *   - The caller owns every buffer; the library only reads inputs and writes
+ *     outputs.  Scratch memory (the GEMM's TF32 operand split) belongs to the
+ *     context and is reused across calls.
+ *   - Return value: B2K_OK, a positive validation code (nothing was
+ *     launched), or a negative device-side code.  b2k_last_error() gives a
+ *     human-readable reason.
+ *   - A context is not thread-safe: use one per (host thread, device).
+ */
+#ifndef B200K_H
+#define B200K_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2K_OK 0
+#define B2K_EINVAL 1       /* invalid argument; nothing launched */
+#define B2K_EUNSUPPORTED 2 /* valid request outside this build's kernels */
+#define B2K_ECUDA (-1)     /* CUDA runtime/driver error */
+#define B2K_ETIMEOUT (-2)  /* a device-side bounded wait expired (kernel error flag) */
+
+typedef struct b2k_ctx b2k_ctx;
+
+/* ABI version of this header (major*100 + minor). */
+int b2k_version(void);
+
+/* Create a context on CUDA device `device_ordinal` (makes it current on this
+ * thread).  Replaces the runner's per-worker context set-up
+ * (tools/local_runner.py:258-280). */
+int b2k_init(int device_ordinal, b2k_ctx **out);
+int b2k_destroy(b2k_ctx *ctx);
+/* Reason for the last non-OK return on this context ("" if none). */
+const char *b2k_last_error(const b2k_ctx *ctx);
+/* Streaming multiprocessor count of the context's device. */
+int b2k_sm_count(const b2k_ctx *ctx);
+
+/* --- device memory helpers for callers without their own allocator ------
+ * (the runner's cuMemAlloc / cuMemcpyHtoD / cuMemcpyDtoH / cuMemsetD8 calls,
+ * tools/local_runner.py:287-300, 320-322, 333-338). */
+int b2k_malloc(b2k_ctx *ctx, void **ptr, size_t bytes);
+int b2k_free(b2k_ctx *ctx, void *ptr);
+int b2k_memcpy_htod(b2k_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream);
+int b2k_memcpy_dtoh(b2k_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream);
+int b2k_memset(b2k_ctx *ctx, void *dst, int value, size_t bytes, void *stream);
+int b2k_stream_sync(b2k_ctx *ctx, void *stream);
+
+/* --- pointwise programs ---------------------------------------------------
+ * Replaces the SIMT Emitter's pointwise lowering: Tile decode
+ * (compile.py:8473-8585), 16-byte vector load/store groups
+ * (compile.py:1425-1600, 5865-5942, 8586-8661) and scalar arithmetic
+ * (compile.py:2645-2965).  A program is a straight-line list of FP32
+ * operations over up to B2K_PW_MAX_INPUTS input streams; register r < n_inputs
+ * holds input r's element, later registers hold instruction results. */
+#define B2K_PW_MAX_INPUTS 8
+#define B2K_PW_MAX_INSNS 48
+#define B2K_PW_MAX_REGS (B2K_PW_MAX_INPUTS + B2K_PW_MAX_INSNS)
+
+enum b2k_pw_opcode {
+  B2K_OP_CONST = 0,      /* dst = imm */
+  B2K_OP_COPY = 1,       /* dst = a */
+  B2K_OP_ADD = 2,        /* dst = a + b (round to nearest) */
+  B2K_OP_SUB = 3,
+  B2K_OP_MUL = 4,
+  B2K_OP_DIV = 5,        /* IEEE division, round to nearest */
+  B2K_OP_MAX = 6,
+  B2K_OP_MIN = 7,
+  B2K_OP_NEG = 8,
+  B2K_OP_RCP = 9,        /* 1/a, round to nearest */
+  B2K_OP_SQRT = 10,      /* round to nearest */
+  B2K_OP_RSQRT = 11,     /* 1/sqrt(a) */
+  B2K_OP_EXP = 12,       /* selective subnormal-preserving exp (compile.py:2953-2965) */
+  B2K_OP_RELU = 13,      /* max(a, 0) */
+  B2K_OP_ABS = 14,
+  B2K_OP_FMA = 15,       /* dst = a * b + c, single rounding */
+  B2K_OP_GT = 16,        /* dst = (a > b) ? 1 : 0 */
+  B2K_OP_GE = 17,
+  B2K_OP_LT = 18,
+  B2K_OP_LE = 19,
+  B2K_OP_WHERE = 20,     /* dst = (a != 0) ? b : c */
+  B2K_OP_LOG = 21,       /* natural log via lg2.approx * ln2 (compile.py:2938-2942) */
+  B2K_OP_COUNT = 22
+};
+
+typedef struct b2k_pw_insn {
+  int32_t op;       /* enum b2k_pw_opcode */
+  int32_t a, b, c;  /* source registers (unused ones ignored) */
+  float imm;        /* B2K_OP_CONST value */
+} b2k_pw_insn;
+
+typedef struct b2k_pw_program {
+  int32_t n_inputs;                        /* input streams, registers 0..n_inputs-1 */
+  int32_t n_insns;                         /* instructions; insn i writes register n_inputs+i */
+  int32_t result;                          /* register stored to the output */
+  int32_t broadcast[B2K_PW_MAX_INPUTS];    /* 1: input is a scalar buffer read at element 0 */
+  b2k_pw_insn insns[B2K_PW_MAX_INSNS];
+} b2k_pw_program;
+
+/* out[i] = program(inputs[0][i], inputs[1][i], ...) for i in [0, n).
+ * Non-broadcast inputs and out must hold n FP32 elements; 16-byte vector
+ * accesses are used when every stream is 16-byte aligned. */
+int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, const float *const *inputs,
+                      float *out, int64_t n, void *stream);
+
+/* --- row softmax ----------------------------------------------------------
+ * Replaces the Emitter's row-reduction softmax passes: online/two-pass
+ * max+sum (compile.py:1656-1711, 6492-6644), warp-shuffle and shared-tree
+ * combine (compile.py:8958-9035, 9175-9268), selective exp
+ * (compile.py:2953-2965) and the reciprocal-multiply normalisation.
+ * y[r, :] = exp(x[r, :] - max_r) / sum_r for a row-major rows x cols matrix
+ * with leading dimensions ld_x / ld_y (elements). */
+int b2k_row_softmax_f32(b2k_ctx *ctx, const float *x, float *y, int64_t rows, int64_t cols,
+                        int64_t ld_x, int64_t ld_y, void *stream);
+
+/* Elementwise selective exponential (compile.py:2953-2965); exposed for the
+ * subnormal-range accuracy tests. */
+int b2k_selective_exp_f32(b2k_ctx *ctx, const float *x, float *y, int64_t n, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200K_H */

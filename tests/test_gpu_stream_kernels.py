@@ -1,0 +1,114 @@
+"""GPU parity of the bandwidth-bound kernels (pointwise programs, row softmax,
+selective exp) through the C ABI, against the float64 oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import pkg
+from oracle import refs, sexp
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(torch, array):
+    return torch.from_numpy(np.ascontiguousarray(array)).cuda()
+
+
+def run_program(ctx, torch, program, arrays, n):
+    inputs = [dev(torch, a) for a in arrays]
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
+    ctx.pointwise(program, [t.data_ptr() for t in inputs], out.data_ptr(), n)
+    ctx.sync()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("n", [1, 3, 4, 127, 128, 1024, 4099, 65537, 1 << 20])
+def test_add_bit_exact(ctx, torch_cuda, n):
+    runtime = pkg("runtime")
+    rng = np.random.default_rng(n)
+    a, b = rng.standard_normal(n).astype(np.float32), rng.standard_normal(n).astype(np.float32)
+    prog = runtime.make_program(2, [("add", 0, 1, 0, 0.0)], 2)
+    got = run_program(ctx, torch_cuda, prog, [a, b], n)
+    np.testing.assert_array_equal(got, refs.pointwise("add", a, b))
+
+
+def test_add_baseline_size_bit_exact(ctx, torch_cuda):
+    runtime, workloads = pkg("runtime"), pkg("workloads")
+    a, b = workloads.add_inputs()
+    prog = runtime.make_program(2, [("add", 0, 1, 0, 0.0)], 2)
+    got = run_program(ctx, torch_cuda, prog, [a, b], a.size)
+    np.testing.assert_array_equal(got, (a + b).astype(np.float32))
+
+
+def test_add_unaligned_views(ctx, torch_cuda):
+    """Offsets that break 16-byte alignment take the scalar path and stay exact."""
+    runtime = pkg("runtime")
+    torch = torch_cuda
+    n = 1001
+    a = torch.randn(n + 3, device="cuda")
+    b = torch.randn(n + 3, device="cuda")
+    out = torch.empty(n + 3, device="cuda")
+    prog = runtime.make_program(2, [("add", 0, 1, 0, 0.0)], 2)
+    ctx.pointwise(prog, [a[1:].data_ptr(), b[2:].data_ptr()], out[3:].data_ptr(), n)
+    ctx.sync()
+    expect = (a[1:1 + n].cpu().numpy() + b[2:2 + n].cpu().numpy()).astype(np.float32)
+    np.testing.assert_array_equal(out[3:3 + n].cpu().numpy(), expect)
+
+
+def test_programs_scale_shift_and_relu_mul(ctx, torch_cuda):
+    runtime = pkg("runtime")
+    rng = np.random.default_rng(7)
+    n = 4096
+    x, y = rng.standard_normal(n).astype(np.float32), rng.standard_normal(n).astype(np.float32)
+    # p02 shape: add(add_c1, multiply(mul_c1, x)) with two broadcast scalars
+    prog = runtime.make_program(3, [("multiply", 0, 2, 0, 0.0), ("add", 1, 3, 0, 0.0)], 4, broadcast=(0, 1))
+    got = run_program(ctx, torch_cuda, prog, [np.array([2.0], np.float32), np.array([1.0], np.float32), x], n)
+    ok, bad, err = refs.allclose_report(got, refs.pointwise("scale_shift", x, np.array([2.0]), np.array([1.0])),
+                                        1e-6, 1e-6)
+    assert ok, (bad, err)
+    # p03 shape: multiply(y, relu(x)), rtol = atol = 0
+    prog = runtime.make_program(2, [("relu", 0, 0, 0, 0.0), ("multiply", 1, 2, 0, 0.0)], 3)
+    got = run_program(ctx, torch_cuda, prog, [x, y], n)
+    np.testing.assert_array_equal(got, refs.pointwise("relu_mul", x, y))
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 256), (5, 257), (3, 127), (32, 31), (16, 8192), (2, 20000), (7, 4096)])
+def test_row_softmax_matches_float64(ctx, torch_cuda, rows, cols):
+    rng = np.random.default_rng(rows * 100003 + cols)
+    x = (rng.standard_normal((rows, cols)) * 4).astype(np.float32)
+    xd = dev(torch_cuda, x)
+    y = torch_cuda.empty_like(xd)
+    ctx.row_softmax(xd.data_ptr(), y.data_ptr(), rows, cols)
+    ctx.sync()
+    ok, bad, err = refs.allclose_report(y.cpu().numpy(), refs.softmax(x), 1e-3, 1e-5)
+    assert ok, (bad, err)
+
+
+def test_row_softmax_baseline_config(ctx, torch_cuda):
+    """4096 x 8192, N(0, 16) with 1 % of entries at -100 (checked on every row)."""
+    workloads = pkg("workloads")
+    x = workloads.softmax_input()
+    xd = dev(torch_cuda, x)
+    y = torch_cuda.empty_like(xd)
+    ctx.row_softmax(xd.data_ptr(), y.data_ptr(), *x.shape)
+    ctx.sync()
+    got = y.cpu().numpy()
+    ok, bad, err = refs.allclose_report(got, refs.softmax(x), 1e-3, 1e-5)
+    assert ok, (bad, err)
+    # size-independent property: every row sums to one
+    np.testing.assert_allclose(got.astype(np.float64).sum(axis=1), 1.0, rtol=1e-5)
+
+
+def test_selective_exp_subnormal_range(ctx, torch_cuda):
+    """exp over [-104, -86] keeps subnormal results within the method's bound."""
+    x = np.linspace(-110.0, 5.0, 1 << 16, dtype=np.float32)
+    xd = dev(torch_cuda, x)
+    y = torch_cuda.empty_like(xd)
+    ctx.selective_exp(xd.data_ptr(), y.data_ptr(), x.size)
+    ctx.sync()
+    got = y.cpu().numpy()
+    report = sexp.check_against_exp(x, got)
+    assert report["ok"], report
+    sub = (x > -103.0) & (x < -88.0)
+    assert np.all(got[sub] > 0.0), "subnormal results were flushed"
