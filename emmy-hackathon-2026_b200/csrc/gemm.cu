@@ -1,0 +1,433 @@
+// 3xTF32 FP32 GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// C[M,N] = epilogue(A[M,K] * B[K,N]), every product computed as the three-term
+// TF32 expansion hi*hi + hi*lo + lo*hi with FP32 accumulation -- the
+// arithmetic contract of the reference's tensor-core emitter
+// (tf32_emitter.py:22-96 model, :291-710 production_ptx, three mma.sync per
+// K step and a hh+hl+lh epilogue at :675-684).
+//
+// Pipeline (per CTA, one 128 x BN output tile):
+//   split pre-pass   A -> A_hi, A_lo ; B -> B_hi, B_lo (K-major, K padded to 32),
+//                    once per GEMM instead of once per element per K step
+//   warp 0           TMA producer: four swizzled tiles (A/B hi/lo) per stage
+//   warp 1           TMEM allocator + single-thread tcgen05.mma issuer:
+//                    per 8-wide K step, lo*hi, hi*lo and hi*hi into one
+//                    FP32 TMEM accumulator (128 lanes x BN columns) per
+//                    256-wide K chunk, double-buffered
+//   warps 2..9       epilogue: fold each chunk into FP32 registers, then
+//                    bias -> ReLU -> global stores
+// All mbarrier waits are bounded (see sm100.cuh).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int KPAD = 32;  // K is zero-padded to a multiple of this in the split operands
+
+// --- split pre-pass --------------------------------------------------------
+// hi = rna(x) with the TF32 bit rule of tf32_emitter.py:22-29; lo = rna(x - hi).
+// Deviation from the reference model, on purpose: when rounding a finite x
+// overflows to infinity (|x| near FLT_MAX) hi falls back to truncation, so
+// max-finite * 0 stays 0 instead of inf * 0 = NaN (the bundled
+// maxfinite-times-zero witness expects 0).  Non-finite x gives hi = x, lo = 0.
+__device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
+  const uint32_t bits = __float_as_uint(x);
+  if (!isfinite(x)) {
+    hi = x;
+    lo = 0.0f;
+    return;
+  }
+  float h = __uint_as_float((bits + 0x1000u) & 0xFFFFE000u);
+  if (!isfinite(h)) h = __uint_as_float(bits & 0xFFFFE000u);
+  const float r = __fsub_rn(x, h);
+  hi = h;
+  lo = __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
+}
+
+// Row-major [rows, K] (leading dimension ld) -> hi/lo [rows, Kp], zero padded.
+__global__ void __launch_bounds__(256) split_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t K,
+                                                         int64_t ld, int64_t Kp, float *__restrict__ hi,
+                                                         float *__restrict__ lo, int vec_src) {
+  const int64_t kp4 = Kp >> 2;
+  const int64_t total = rows * kp4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / kp4;
+    const int64_t k = (i - r * kp4) << 2;
+    float v[4];
+    if (vec_src && k + 3 < K) {
+      const float4 t = *reinterpret_cast<const float4 *>(src + r * ld + k);
+      v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? src[r * ld + k + j] : 0.0f;
+    }
+    float4 h, l;
+    split_tf32(v[0], h.x, l.x);
+    split_tf32(v[1], h.y, l.y);
+    split_tf32(v[2], h.z, l.z);
+    split_tf32(v[3], h.w, l.w);
+    *reinterpret_cast<float4 *>(hi + r * Kp + k) = h;
+    *reinterpret_cast<float4 *>(lo + r * Kp + k) = l;
+  }
+}
+
+// Row-major B [K, N] (ld) -> transposed hi/lo [N, Kp] (K-major), zero padded.
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float *__restrict__ src, int64_t K, int64_t N,
+                                                              int64_t ld, int64_t Kp, float *__restrict__ hi,
+                                                              float *__restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int64_t k = k0 + ty + i, n = n0 + tx;
+    tile[ty + i][tx] = (k < K && n < N) ? src[k * ld + n] : 0.0f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int64_t n = n0 + ty + i, k = k0 + tx;
+    if (n < N && k < Kp) {
+      float h, l;
+      split_tf32(tile[tx][ty + i], h, l);
+      hi[n * Kp + k] = h;
+      lo[n * Kp + k] = l;
+    }
+  }
+}
+
+// --- main kernel -----------------------------------------------------------
+// The tensor core's in-instruction accumulation is not round-to-nearest: its
+// error grows linearly with the number of MMAs folded into one accumulator
+// (measured ~1.1e-8 relative per MMA on B200, 2.8e-6 at K = 256).  So K is
+// cut into chunks of kChunkK: each chunk accumulates into a fresh TMEM
+// buffer (two buffers, double-buffered), and the epilogue warps fold every
+// finished chunk into FP32 registers with round-to-nearest adds while the
+// tensor core fills the other buffer.
+constexpr int kChunkK = 256;
+constexpr int kEpilogueWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpilogueWarps;  // producer, MMA, epilogue
+
+struct GemmArgs {
+  float *c;
+  const float *bias;
+  int64_t m, n, ldc;
+  int num_kb;
+  int relu;
+  unsigned *err;
+};
+
+template <int BN, int SW, int STAGES>
+struct GemmShape {
+  static constexpr int BK = SW / 4;                       // FP32 elements per K block
+  static constexpr int kTileA = BM * SW;                  // bytes of one A tile
+  static constexpr int kTileB = BN * SW;
+  static constexpr int kStage = 2 * kTileA + 2 * kTileB;  // hi + lo of A and B
+  static constexpr int kSmem = STAGES * kStage + 1024;
+  static constexpr int kChunkBlocks = kChunkK / BK;
+  static constexpr int kColsPerThread = BN / 2;           // two epilogue warps per TMEM lane quarter
+  static_assert(BN == 128 || BN == 256, "BN");
+  static_assert(kSmem <= 227 * 1024, "stage ring exceeds shared memory");
+};
+
+template <int BN, int SW, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+                       const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
+                       const GemmArgs args) {
+  using Shape = GemmShape<BN, SW, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tmem_full[2];
+  __shared__ __align__(8) uint64_t tmem_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_word;
+
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t n0 = (int64_t)blockIdx.x * BN;
+  const int64_t m0 = (int64_t)blockIdx.y * BM;
+  const int num_kb = args.num_kb;
+  const int num_chunks = (num_kb + Shape::kChunkBlocks - 1) / Shape::kChunkBlocks;
+  volatile int *abort = &abort_word;
+
+  auto a_hi = [&](int s) { return smem + s * Shape::kStage; };
+  auto a_lo = [&](int s) { return smem + s * Shape::kStage + Shape::kTileA; };
+  auto b_hi = [&](int s) { return smem + s * Shape::kStage + 2 * Shape::kTileA; };
+  auto b_lo = [&](int s) { return smem + s * Shape::kStage + 2 * Shape::kTileA + Shape::kTileB; };
+
+  if (threadIdx.x == 0) {
+    abort_word = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full_bar[s], 1);
+      sm100::mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&tmem_full[b], 1);
+      sm100::mbar_init(&tmem_empty[b], kEpilogueWarps);
+    }
+    sm100::mbar_init(&drain_bar, 1);
+    sm100::fence_barrier_init();
+    sm100::prefetch_tensormap(&map_ahi);
+    sm100::prefetch_tensormap(&map_alo);
+    sm100::prefetch_tensormap(&map_bhi);
+    sm100::prefetch_tensormap(&map_blo);
+  }
+  if (warp == 1) sm100::tmem_alloc(&tmem_slot, 2 * BN);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  if (warp == 0) {
+    if (sm100::elect_lane0()) {
+      // TMA producer.
+      int issued = 0;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t round = kb / STAGES;
+        if (kb >= STAGES &&
+            !sm100::mbar_wait(&empty_bar[s], (round & 1) ^ 1, args.err, sm100::kSiteProducerEmpty, abort))
+          break;
+        sm100::mbar_arrive_expect_tx(&full_bar[s], Shape::kStage);
+        const int kx = kb * Shape::BK;
+        sm100::tma_load_2d(a_hi(s), &map_ahi, &full_bar[s], kx, (int)m0);
+        sm100::tma_load_2d(a_lo(s), &map_alo, &full_bar[s], kx, (int)m0);
+        sm100::tma_load_2d(b_hi(s), &map_bhi, &full_bar[s], kx, (int)n0);
+        sm100::tma_load_2d(b_lo(s), &map_blo, &full_bar[s], kx, (int)n0);
+        issued = kb + 1;
+      }
+      // Drain: every issued load must land before the CTA may exit.  These
+      // waits ignore the abort word (budget only): the data is in flight.
+      int never = 0;
+      for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; ++kb)
+        sm100::mbar_wait(&full_bar[kb % STAGES], (kb / STAGES) & 1, args.err, sm100::kSiteDrain, &never);
+    }
+  } else if (warp == 1) {
+    if (sm100::elect_lane0()) {
+      // MMA issuer: chunk c accumulates into TMEM buffer c & 1.
+      constexpr uint32_t idesc = sm100::idesc_tf32(BM, BN);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int chunk = kb / Shape::kChunkBlocks;
+        const int buf = chunk & 1;
+        const bool first = (kb % Shape::kChunkBlocks) == 0;
+        const bool last = ((kb + 1) % Shape::kChunkBlocks) == 0 || kb + 1 == num_kb;
+        if (first && chunk >= 2 &&
+            !sm100::mbar_wait(&tmem_empty[buf], ((chunk >> 1) & 1) ^ 1, args.err, sm100::kSiteMmaFull, abort))
+          break;
+        const int s = kb % STAGES;
+        if (!sm100::mbar_wait(&full_bar[s], (kb / STAGES) & 1, args.err, sm100::kSiteMmaFull, abort)) break;
+        sm100::tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+        const uint32_t ahi = sm100::smem_addr(a_hi(s)), alo = sm100::smem_addr(a_lo(s));
+        const uint32_t bhi = sm100::smem_addr(b_hi(s)), blo = sm100::smem_addr(b_lo(s));
+#pragma unroll
+        for (int k = 0; k < Shape::BK / 8; ++k) {
+          const uint32_t off = k * 32;  // 8 TF32 elements = 32 bytes along the swizzled row
+          const uint64_t dah = sm100::desc_kmajor<SW>(ahi + off), dal = sm100::desc_kmajor<SW>(alo + off);
+          const uint64_t dbh = sm100::desc_kmajor<SW>(bhi + off), dbl = sm100::desc_kmajor<SW>(blo + off);
+          sm100::mma_tf32(d, dal, dbh, idesc, (first && k == 0) ? 0u : 1u);
+          sm100::mma_tf32(d, dah, dbl, idesc, 1u);
+          sm100::mma_tf32(d, dah, dbh, idesc, 1u);
+        }
+        sm100::mma_commit(&empty_bar[s]);
+        if (last) sm100::mma_commit(&tmem_full[buf]);
+      }
+      // Every MMA issued so far must finish before TMEM is released.
+      sm100::mma_commit(&drain_bar);
+      int never = 0;
+      sm100::mbar_wait(&drain_bar, 0, args.err, sm100::kSiteDrain, &never);
+    }
+  } else {
+    // Epilogue warps 2..9: warp w reads TMEM lanes 32*(w%4)..+31 (its lane
+    // quarter) and half (w-2)/4 of the BN columns.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int CPT = Shape::kColsPerThread;
+    float acc[CPT];
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) acc[j] = 0.0f;
+    bool ok = true;
+    for (int chunk = 0; chunk < num_chunks; ++chunk) {
+      const int buf = chunk & 1;
+      ok = sm100::mbar_wait(&tmem_full[buf], (chunk >> 1) & 1, args.err, sm100::kSiteEpilogueAccum, abort,
+                            3 * sm100::kWaitCycles);
+      if (!ok) break;
+      sm100::tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + half * CPT);
+#pragma unroll
+      for (int j = 0; j < CPT; j += 32) {
+        uint32_t r[32];
+        sm100::tmem_ld_32x32b_x32(taddr + j, r);
+        sm100::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&tmem_empty[buf]);
+    }
+    const int64_t row = m0 + quarter * 32 + lane;
+    const int64_t col0 = n0 + half * CPT;
+    if (ok && row < args.m && col0 < args.n) {
+      float *crow = args.c + row * args.ldc + col0;
+      const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 15) == 0) &&
+                       col0 + CPT <= args.n;
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        float x = acc[j];
+        if (args.bias) x = __fadd_rn(x, (col0 + j < args.n) ? __ldg(args.bias + col0 + j) : 0.0f);
+        if (args.relu) x = x > 0.0f ? x : 0.0f;
+        acc[j] = x;
+      }
+      if (vec) {
+#pragma unroll
+        for (int j = 0; j < CPT; j += 4)
+          *reinterpret_cast<float4 *>(crow + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < CPT; ++j)
+          if (col0 + j < args.n) crow[j] = acc[j];
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// --- host side -------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// K-major FP32 operand [rows, Kp]: box [box_rows, SW/4] with the SW-byte swizzle.
+int make_operand_map(b2k_ctx *ctx, CUtensorMap *map, const float *base, int64_t rows, int64_t Kp, int box_rows,
+                     int sw) {
+  auto encode = encode_fn();
+  if (!encode) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
+  cuuint32_t box[2] = {(cuuint32_t)(sw / 4), (cuuint32_t)box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  const CUtensorMapSwizzle swizzle = sw == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)res);
+  return B2K_OK;
+}
+
+template <int BN, int SW, int STAGES>
+int launch_main(b2k_ctx *ctx, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
+                int64_t Kp, GemmArgs args, cudaStream_t s) {
+  using Shape = GemmShape<BN, SW, STAGES>;
+  CUtensorMap maps[4];
+  int status;
+  if ((status = make_operand_map(ctx, &maps[0], a_hi, args.m, Kp, BM, SW)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[1], a_lo, args.m, Kp, BM, SW)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[2], b_hi, args.n, Kp, BN, SW)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[3], b_lo, args.n, Kp, BN, SW)) != B2K_OK) return status;
+  args.num_kb = (int)(Kp / Shape::BK);
+  auto kernel = gemm_tf32x3_kernel<BN, SW, STAGES>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: set smem");
+  dim3 grid((unsigned)((args.n + BN - 1) / BN), (unsigned)((args.m + BM - 1) / BM));
+  kernel<<<grid, kThreads, Shape::kSmem, s>>>(maps[0], maps[1], maps[2], maps[3], args);
+  return b2k::check_launch(ctx, "gemm launch");
+}
+
+}  // namespace
+
+// Kernel variant selector (tile width, swizzle, stage count); settable for
+// tuning through b2k_gemm_set_variant.
+static int g_gemm_variant = 0;
+
+// Shared by the public entry point and the attention path: split both
+// operands into `ws` (A_hi, A_lo: m x Kp; B_hi, B_lo: n x Kp) and run the
+// tensor-core kernel.  `b_kmajor`: B is stored [n, K] (else [K, n]).
+int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                         int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu,
+                         float *ws, cudaStream_t s) {
+  const int64_t Kp = (k + KPAD - 1) / KPAD * KPAD;
+  float *a_hi = ws, *a_lo = ws + m * Kp, *b_hi = ws + 2 * m * Kp, *b_lo = ws + 2 * m * Kp + n * Kp;
+  const int grid_split = ctx->sm_count * 8;
+  split_rows_kernel<<<grid_split, 256, 0, s>>>(a, m, k, lda, Kp, a_hi, a_lo,
+                                               (lda % 4 == 0) && b2k::aligned16(a));
+  if (b_kmajor) {
+    split_rows_kernel<<<grid_split, 256, 0, s>>>(b, n, k, ldb, Kp, b_hi, b_lo,
+                                                 (ldb % 4 == 0) && b2k::aligned16(b));
+  } else {
+    dim3 grid((unsigned)((n + 31) / 32), (unsigned)((Kp + 31) / 32));
+    split_transpose_kernel<<<grid, 256, 0, s>>>(b, k, n, ldb, Kp, b_hi, b_lo);
+  }
+  int status = b2k::check_launch(ctx, "gemm split launch");
+  if (status != B2K_OK) return status;
+  GemmArgs args{c, bias, m, n, ldc, 0, relu, ctx->error_flag};
+  switch (g_gemm_variant) {
+    case 1: return launch_main<256, 64, 4>(ctx, a_hi, a_lo, b_hi, b_lo, Kp, args, s);
+    case 2: return launch_main<128, 128, 3>(ctx, a_hi, a_lo, b_hi, b_lo, Kp, args, s);
+    default: return launch_main<256, 128, 2>(ctx, a_hi, a_lo, b_hi, b_lo, Kp, args, s);
+  }
+}
+
+extern "C" int b2k_gemm_set_variant(int variant) {
+  if (variant < 0 || variant > 2) return B2K_EINVAL;
+  g_gemm_variant = variant;
+  return B2K_OK;
+}
+
+size_t b2k_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  const int64_t Kp = (k + KPAD - 1) / KPAD * KPAD;
+  return (size_t)(2 * (m + n) * Kp) * sizeof(float);
+}
+
+extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n,
+                               int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout,
+                               const float *bias, int32_t relu, void *stream) {
+  B2K_CHECK_CTX(ctx);
+  if (m < 0 || n < 0 || k < 0) return b2k::fail(ctx, B2K_EINVAL, "gemm: negative extent");
+  if (b_layout != B2K_B_KN && b_layout != B2K_B_NK) return b2k::fail(ctx, B2K_EINVAL, "gemm: bad b_layout");
+  if (m == 0 || n == 0) return B2K_OK;
+  if (!a || !b || !c) return b2k::fail(ctx, B2K_EINVAL, "gemm: null buffer");
+  if (lda < k || ldc < n || ldb < (b_layout == B2K_B_NK ? k : n))
+    return b2k::fail(ctx, B2K_EINVAL, "gemm: leading dimension too small");
+  if (m > INT32_MAX - 256 || n > INT32_MAX - 256 || k > INT32_MAX - 64)
+    return b2k::fail(ctx, B2K_EINVAL, "gemm: extent exceeds 32-bit TMA coordinates");
+  if (k == 0) {
+    // Empty contraction: C = epilogue(0).
+    cudaStream_t s = (cudaStream_t)stream;
+    for (int64_t r = 0; r < m; ++r) {
+      cudaError_t err = cudaMemsetAsync(c + r * ldc, 0, (size_t)n * 4, s);
+      if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: zero fill");
+    }
+    if (!bias) return B2K_OK;
+    return b2k::fail(ctx, B2K_EUNSUPPORTED, "gemm: bias with K = 0");
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  int status = b2k::reserve_workspace(ctx, b2k_gemm_workspace_bytes(m, n, k), s);
+  if (status != B2K_OK) return status;
+  return b2k_gemm_tf32x3_impl(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu,
+                              static_cast<float *>(ctx->workspace), s);
+}

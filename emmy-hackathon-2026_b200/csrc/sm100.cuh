@@ -1,0 +1,182 @@
+// Thin inline-PTX wrappers for the Blackwell (sm_100a) features used by the
+// tensor-core kernels: mbarriers with bounded waits, TMA tile loads,
+// tcgen05 TMEM allocation, UMMA descriptors, tcgen05.mma / commit / ld.
+//
+// Every wait here is bounded: a wait that exceeds its cycle budget records a
+// code in the context's device error word and returns false, so a kernel can
+// drain and exit instead of hanging the GPU.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+namespace sm100 {
+
+// ~2 s at the B200's maximum SM clock.
+constexpr long long kWaitCycles = 4000000000ll;
+
+enum WaitSite : unsigned {
+  kSiteProducerEmpty = 0x1,
+  kSiteMmaFull = 0x2,
+  kSiteEpilogueAccum = 0x4,
+  kSiteDrain = 0x8,
+  kSiteAttention = 0x10,
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait until the barrier phase with `parity` has completed.  Returns false
+// when the cycle budget runs out (after recording `site` in *err and raising
+// the CTA's shared abort word) or when another role of the CTA has already
+// aborted, so every role leaves its loop promptly once one wait fails.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned *err, unsigned site,
+                                          volatile int *abort, long long budget = kWaitCycles) {
+  const uint32_t addr = smem_addr(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(addr, parity)) {
+    if (*abort) return false;
+    if (clock64() - start > budget) {
+      atomicOr(err, site);
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// 2-D TMA tile load into shared memory, completing on `bar` (tx bytes).
+// Coordinates: x = innermost (elements), y = rows.  x * elem_size must be a
+// multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// --- TMEM ----------------------------------------------------------------
+// Executed by one full warp.  The allocated base address is written to *slot.
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// --- UMMA descriptors ----------------------------------------------------
+// Shared-memory matrix descriptor for a K-major operand tile whose rows are
+// SW bytes (SW = 128 or 64) stored with the matching TMA swizzle, in 8-row
+// swizzle atoms of 8*SW bytes:
+//   bits  0-13 start address >> 4
+//   bits 16-29 leading-dimension byte offset >> 4 (unused for swizzled K-major; 1)
+//   bits 32-45 stride byte offset >> 4 (8*SW bytes between 8-row groups)
+//   bits 46-47 descriptor version (1 on sm_100)
+//   bits 61-63 layout: 2 = SWIZZLE_128B, 4 = SWIZZLE_64B
+// The tile base must be aligned to its swizzle atom; the start address may
+// then advance along K in 32-byte steps (one 8-element TF32 MMA slice).
+template <int SW>
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
+  static_assert(SW == 128 || SW == 64, "supported swizzles: 128B, 64B");
+  constexpr uint64_t layout = SW == 128 ? 2u : 4u;
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>((8u * SW) >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= layout << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::tf32, FP32 accumulate, both operands K-major.
+//   bits 4-5 D format (1 = F32), 7-9 A format (2 = TF32), 10-12 B format,
+//   15/16 A/B major (0 = K), 17-22 N >> 3, 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread completes.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread t of the warp receives its
+// TMEM lane's 32 columns starting at `taddr`.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; }
+
+}  // namespace sm100

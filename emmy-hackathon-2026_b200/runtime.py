@@ -17,6 +17,7 @@ STATUS_NAMES = {B2K_EINVAL: "EINVAL", B2K_EUNSUPPORTED: "EUNSUPPORTED", B2K_ECUD
                 B2K_ETIMEOUT: "ETIMEOUT"}
 
 PW_MAX_INPUTS, PW_MAX_INSNS = 8, 48
+B_KN, B_NK = 0, 1
 
 OPCODES = {
     "const": 0, "copy": 1, "add": 2, "subtract": 3, "multiply": 4, "divide": 5, "maximum": 6,
@@ -61,6 +62,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_pointwise_f32": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _P], C.c_int),
     "b2k_row_softmax_f32": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_selective_exp_f32": ([_P, _P, _P, _I64, _P], C.c_int),
+    "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
+    "b2k_gemm_set_variant": ([C.c_int], C.c_int),
 }
 
 _lock = threading.Lock()
@@ -150,6 +153,15 @@ class Context:
 
     def selective_exp(self, x: int, y: int, n: int, stream: int = 0) -> None:
         self.check(self.lib.b2k_selective_exp_f32(self.handle, x, y, n, stream), "b2k_selective_exp_f32")
+
+    def gemm(self, a: int, b: int, c: int, m: int, n: int, k: int, *, b_layout: int = B_KN,
+             lda: int | None = None, ldb: int | None = None, ldc: int | None = None,
+             bias: int = 0, relu: bool = False, stream: int = 0) -> None:
+        lda = k if lda is None else lda
+        ldb = (n if b_layout == B_KN else k) if ldb is None else ldb
+        ldc = n if ldc is None else ldc
+        self.check(self.lib.b2k_gemm_tf32x3(self.handle, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias or None,
+                                            int(relu), stream), "b2k_gemm_tf32x3")
 
     def sync(self, stream: int = 0) -> None:
         self.check(self.lib.b2k_stream_sync(self.handle, stream), "b2k_stream_sync")

@@ -131,6 +131,33 @@ int b2k_row_softmax_f32(b2k_ctx *ctx, const float *x, float *y, int64_t rows, in
  * subnormal-range accuracy tests. */
 int b2k_selective_exp_f32(b2k_ctx *ctx, const float *x, float *y, int64_t n, void *stream);
 
+/* --- 3xTF32 GEMM -----------------------------------------------------------
+ * Replaces the reference's dense-contraction back ends: the 3xTF32
+ * mma.sync emitter tf32_emitter.production_ptx (tf32_emitter.py:291-710,
+ * arithmetic model :22-96) and the exact-FP32 SIMT plan emitter
+ * compile.plan_simt_ptx (compile.py:9326-9611) selected for proven plans
+ * (compile.py:9614-9625, tensor_core.py MatmulPlan :232-330).
+ *
+ * C[m, n] = relu?(A[m, k] * B + bias[n]) with every product expanded as
+ * hi*hi + hi*lo + lo*hi of TF32 halves and FP32 accumulation.
+ * A is row-major with leading dimension lda.  b_layout B2K_B_KN: B is
+ * row-major [k, n] (ldb >= n); B2K_B_NK: B is stored transposed, row-major
+ * [n, k] (ldb >= k).  bias may be NULL; relu is 0 or 1.  C is row-major
+ * (ldc >= n).  Uses 2 * (m + n) * round_up(k, 32) * 4 bytes of context
+ * scratch for the split operands. */
+#define B2K_B_KN 0
+#define B2K_B_NK 1
+int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                    int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
+                    void *stream);
+
+/* Select the GEMM kernel variant for subsequent calls (process-wide; for
+ * tuning and benchmarking): 0 = 128x256 tile, 128-byte swizzle, 2 stages
+ * (default); 1 = 128x256, 64-byte swizzle, 4 stages; 2 = 128x128,
+ * 128-byte swizzle, 3 stages.  No counterpart in the reference, whose plan
+ * geometry comes from the IR. */
+int b2k_gemm_set_variant(int variant);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,94 @@
+"""GPU parity of the tcgen05 3xTF32 GEMM through the C ABI.
+
+Tolerances: the matmul family's metadata tolerance (rtol = atol = 1e-3,
+tools/research_cases.py:30-35) elementwise against the float64 reference, and
+the north-star bound for 3xTF32 evaluated normwise:
+max|C - C64| / max|C64| <= 1e-5.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import pkg
+from oracle import refs, tf32
+
+pytestmark = pytest.mark.gpu
+
+NORMWISE = 1e-5
+
+
+def dev(torch, array):
+    return torch.from_numpy(np.ascontiguousarray(array)).cuda()
+
+
+def run_gemm(ctx, torch, a, b, *, b_layout=0, bias=None, relu=False):
+    m, k = a.shape
+    n = b.shape[1] if b_layout == 0 else b.shape[0]
+    da, db = dev(torch, a), dev(torch, b)
+    dc = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    dbias = dev(torch, bias) if bias is not None else None
+    ctx.gemm(da.data_ptr(), db.data_ptr(), dc.data_ptr(), m, n, k, b_layout=b_layout,
+             bias=dbias.data_ptr() if dbias is not None else 0, relu=relu)
+    ctx.sync()
+    return dc.cpu().numpy()
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 32), (128, 256, 64), (256, 512, 128), (512, 512, 512),
+                                   (64, 65, 32), (3, 16, 31), (130, 300, 200), (1000, 257, 96)])
+def test_gemm_kn_matches_float64(ctx, torch_cuda, m, n, k):
+    rng = np.random.default_rng(m * 7 + n * 13 + k)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    got = run_gemm(ctx, torch_cuda, a, b)
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    assert tf32.normwise_error(got, exact) <= NORMWISE
+    ok, bad, err = refs.allclose_report(got, refs.matmul(a, b), 1e-3, 1e-3)
+    assert ok, (bad, err)
+
+
+def test_gemm_matches_3xtf32_model(ctx, torch_cuda):
+    """Against the oracle's 3xTF32 contract (hh + hl + lh, lo*lo dropped)."""
+    rng = np.random.default_rng(3)
+    a = (rng.standard_normal((256, 384)) * 8).astype(np.float32)
+    b = (rng.standard_normal((384, 256)) * 8).astype(np.float32)
+    got = run_gemm(ctx, torch_cuda, a, b)
+    model = tf32.gemm_3xtf32(a, b)
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    assert tf32.normwise_error(got, model) <= 2e-6
+    assert tf32.normwise_error(got, exact) <= NORMWISE
+
+
+def test_gemm_nk_bias_relu_ragged(ctx, torch_cuda):
+    """The ragged configuration: M=4097, N=1000, K=777, B stored N x K, bias + ReLU."""
+    workloads = pkg("workloads")
+    a, bt, bias = workloads.ragged_inputs()
+    got = run_gemm(ctx, torch_cuda, a, bt, b_layout=1, bias=bias, relu=True)
+    expect = refs.matmul_bias_relu(a, bt, bias)
+    ok, bad, err = refs.allclose_report(got, expect, 1e-3, 1e-3)
+    assert ok, (bad, err)
+    exact = np.maximum(a.astype(np.float64) @ bt.astype(np.float64).T + bias, 0.0)
+    assert tf32.normwise_error(got, exact) <= NORMWISE
+
+
+def test_gemm_maxfinite_times_zero(ctx, torch_cuda):
+    """The bundled TF32 range witness: lhs max-finite, rhs zeros, expected 0."""
+    a = np.full((16, 8), np.finfo(np.float32).max, dtype=np.float32)
+    b = np.zeros((8, 8), dtype=np.float32)
+    got = run_gemm(ctx, torch_cuda, a, b)
+    np.testing.assert_array_equal(got, np.zeros((16, 8), np.float32))
+
+
+def test_gemm_4096_cubed(ctx, torch_cuda):
+    """The benchmark configuration, checked on sampled rows against float64."""
+    workloads = pkg("workloads")
+    a, b = workloads.gemm_inputs()
+    got = run_gemm(ctx, torch_cuda, a, b)
+    rows = np.random.default_rng(11).choice(a.shape[0], 64, replace=False)
+    exact = a[rows].astype(np.float64) @ b.astype(np.float64)
+    assert tf32.normwise_error(got[rows], exact) <= NORMWISE
+    ok, bad, err = refs.allclose_report(got[rows], exact.astype(np.float32), 1e-3, 1e-3)
+    assert ok, (bad, err)
+    # size-independent checksum: column sums of C equal (1^T A) B
+    colsum = (a.astype(np.float64).sum(axis=0) @ b.astype(np.float64))
+    np.testing.assert_allclose(got.astype(np.float64).sum(axis=0), colsum, rtol=1e-4, atol=1e-2)
