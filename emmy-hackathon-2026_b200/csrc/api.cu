@@ -27,9 +27,72 @@ int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream) {
   return B2K_OK;
 }
 
+static cudaEvent_t take_event(b2k_ctx *ctx) {
+  if (!ctx->event_pool.empty()) {
+    cudaEvent_t e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+PhaseTimer::PhaseTimer(b2k_ctx *ctx, int phase, cudaStream_t stream) : ctx_(ctx), phase_(phase), stream_(stream) {
+  if (!ctx_->timing) return;
+  start_ = take_event(ctx_);
+  if (start_) cudaEventRecord(start_, stream_);
+}
+
+PhaseTimer::~PhaseTimer() {
+  if (!start_) return;
+  cudaEvent_t stop = take_event(ctx_);
+  if (!stop) {
+    ctx_->event_pool.push_back(start_);
+    return;
+  }
+  cudaEventRecord(stop, stream_);
+  ctx_->phase_events[phase_].emplace_back(start_, stop);
+}
+
 }  // namespace b2k
 
 extern "C" {
+
+int b2k_timing_enable(b2k_ctx *ctx, int on) {
+  if (!ctx) return B2K_EINVAL;
+  ctx->timing = on != 0;
+  return B2K_OK;
+}
+
+int b2k_timing_read(b2k_ctx *ctx, int phase, double *total_ms, int64_t *launches) {
+  if (!ctx || phase < 0 || phase >= B2K_PHASE_COUNT || !total_ms || !launches) return B2K_EINVAL;
+  double sum = 0.0;
+  for (auto &pair : ctx->phase_events[phase]) {
+    cudaError_t err = cudaEventSynchronize(pair.second);
+    if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "timing: event sync");
+    float ms = 0.0f;
+    err = cudaEventElapsedTime(&ms, pair.first, pair.second);
+    if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "timing: elapsed");
+    sum += ms;
+  }
+  *total_ms = sum;
+  *launches = (int64_t)ctx->phase_events[phase].size();
+  return B2K_OK;
+}
+
+int b2k_timing_reset(b2k_ctx *ctx) {
+  if (!ctx) return B2K_EINVAL;
+  for (auto &list : ctx->phase_events) {
+    for (auto &pair : list) {
+      cudaEventSynchronize(pair.second);
+      ctx->event_pool.push_back(pair.first);
+      ctx->event_pool.push_back(pair.second);
+    }
+    list.clear();
+  }
+  return B2K_OK;
+}
 
 int b2k_version(void) { return 100; }
 
@@ -72,6 +135,8 @@ int b2k_init(int device_ordinal, b2k_ctx **out) {
 int b2k_destroy(b2k_ctx *ctx) {
   if (!ctx) return B2K_EINVAL;
   cudaSetDevice(ctx->device);
+  b2k_timing_reset(ctx);
+  for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->error_flag) cudaFree(ctx->error_flag);
   delete ctx;
@@ -94,6 +159,21 @@ int b2k_free(b2k_ctx *ctx, void *ptr) {
   B2K_CHECK_CTX(ctx);
   cudaError_t err = cudaFree(ptr);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaFree");
+  return B2K_OK;
+}
+
+int b2k_host_alloc(b2k_ctx *ctx, void **ptr, size_t bytes) {
+  B2K_CHECK_CTX(ctx);
+  if (!ptr) return b2k::fail(ctx, B2K_EINVAL, "b2k_host_alloc: null output pointer");
+  cudaError_t err = cudaMallocHost(ptr, bytes ? bytes : 1);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaMallocHost");
+  return B2K_OK;
+}
+
+int b2k_host_free(b2k_ctx *ctx, void *ptr) {
+  B2K_CHECK_CTX(ctx);
+  cudaError_t err = cudaFreeHost(ptr);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "cudaFreeHost");
   return B2K_OK;
 }
 

@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <vector>
 
 #include "b200k.h"
 
@@ -21,6 +22,10 @@ struct b2k_ctx {
   size_t workspace_bytes = 0;
   // Device-side error word written by kernels whose bounded waits expire.
   unsigned int *error_flag = nullptr;
+  // Optional per-phase CUDA-event timing (b2k_timing_*).
+  bool timing = false;
+  std::vector<cudaEvent_t> event_pool;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> phase_events[B2K_PHASE_COUNT];
 };
 
 namespace b2k {
@@ -59,6 +64,20 @@ inline int make_current(b2k_ctx *ctx) {
 int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Brackets the kernels of one phase with CUDA events on `stream` when the
+// context's timing is enabled; a no-op otherwise.
+class PhaseTimer {
+ public:
+  PhaseTimer(b2k_ctx *ctx, int phase, cudaStream_t stream);
+  ~PhaseTimer();
+
+ private:
+  b2k_ctx *ctx_;
+  int phase_;
+  cudaStream_t stream_;
+  cudaEvent_t start_ = nullptr;
+};
 
 }  // namespace b2k
 

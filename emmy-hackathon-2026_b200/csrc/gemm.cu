@@ -373,18 +373,22 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
   const int64_t Kp = (k + KPAD - 1) / KPAD * KPAD;
   float *a_hi = ws, *a_lo = ws + m * Kp, *b_hi = ws + 2 * m * Kp, *b_lo = ws + 2 * m * Kp + n * Kp;
   const int grid_split = ctx->sm_count * 8;
-  split_rows_kernel<<<grid_split, 256, 0, s>>>(a, m, k, lda, Kp, a_hi, a_lo,
-                                               (lda % 4 == 0) && b2k::aligned16(a));
-  if (b_kmajor) {
-    split_rows_kernel<<<grid_split, 256, 0, s>>>(b, n, k, ldb, Kp, b_hi, b_lo,
-                                                 (ldb % 4 == 0) && b2k::aligned16(b));
-  } else {
-    dim3 grid((unsigned)((n + 31) / 32), (unsigned)((Kp + 31) / 32));
-    split_transpose_kernel<<<grid, 256, 0, s>>>(b, k, n, ldb, Kp, b_hi, b_lo);
+  {
+    b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
+    split_rows_kernel<<<grid_split, 256, 0, s>>>(a, m, k, lda, Kp, a_hi, a_lo,
+                                                 (lda % 4 == 0) && b2k::aligned16(a));
+    if (b_kmajor) {
+      split_rows_kernel<<<grid_split, 256, 0, s>>>(b, n, k, ldb, Kp, b_hi, b_lo,
+                                                   (ldb % 4 == 0) && b2k::aligned16(b));
+    } else {
+      dim3 grid((unsigned)((n + 31) / 32), (unsigned)((Kp + 31) / 32));
+      split_transpose_kernel<<<grid, 256, 0, s>>>(b, k, n, ldb, Kp, b_hi, b_lo);
+    }
   }
   int status = b2k::check_launch(ctx, "gemm split launch");
   if (status != B2K_OK) return status;
   GemmArgs args{c, bias, m, n, ldc, 0, relu, ctx->error_flag};
+  b2k::PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
   switch (g_gemm_variant) {
     case 1: return launch_main<256, 64, 4>(ctx, a_hi, a_lo, b_hi, b_lo, Kp, args, s);
     case 2: return launch_main<128, 128, 3>(ctx, a_hi, a_lo, b_hi, b_lo, Kp, args, s);

@@ -206,6 +206,7 @@ extern "C" int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, co
     if (!program->broadcast[i]) vector_ok = vector_ok && b2k::aligned16(inputs[i]);
   }
   cudaStream_t s = (cudaStream_t)stream;
+  b2k::PhaseTimer timer(ctx, B2K_PHASE_POINTWISE, s);
   int64_t done = 0;
   if (vector_ok && n >= 4) {
     const int64_t n4 = n >> 2;

@@ -124,6 +124,7 @@ extern "C" int b2k_row_softmax_f32(b2k_ctx *ctx, const float *x, float *y, int64
   const bool vec = (cols % 4 == 0) && (ld_x % 4 == 0) && (ld_y % 4 == 0) && b2k::aligned16(x) && b2k::aligned16(y);
   const int64_t cols4 = cols / 4;
   const int grid = (int)rows;
+  b2k::PhaseTimer timer(ctx, B2K_PHASE_SOFTMAX, s);
   if (vec && cols4 <= kThreads * 1) softmax_rows_vec<1><<<grid, kThreads, 0, s>>>(x, y, cols4, ld_x, ld_y);
   else if (vec && cols4 <= kThreads * 2) softmax_rows_vec<2><<<grid, kThreads, 0, s>>>(x, y, cols4, ld_x, ld_y);
   else if (vec && cols4 <= kThreads * 4) softmax_rows_vec<4><<<grid, kThreads, 0, s>>>(x, y, cols4, ld_x, ld_y);

@@ -58,13 +58,20 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_memcpy_htod": ([_P, _P, _P, _SZ, _P], C.c_int),
     "b2k_memcpy_dtoh": ([_P, _P, _P, _SZ, _P], C.c_int),
     "b2k_memset": ([_P, _P, C.c_int, _SZ, _P], C.c_int),
+    "b2k_host_alloc": ([_P, C.POINTER(_P), _SZ], C.c_int),
+    "b2k_host_free": ([_P, _P], C.c_int),
     "b2k_stream_sync": ([_P, _P], C.c_int),
     "b2k_pointwise_f32": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _P], C.c_int),
     "b2k_row_softmax_f32": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_selective_exp_f32": ([_P, _P, _P, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
+    "b2k_timing_enable": ([_P, C.c_int], C.c_int),
+    "b2k_timing_read": ([_P, C.c_int, C.POINTER(C.c_double), C.POINTER(_I64)], C.c_int),
+    "b2k_timing_reset": ([_P], C.c_int),
 }
+
+PHASES = {"split": 0, "mma": 1, "pointwise": 2, "softmax": 3, "attention": 4}
 
 _lock = threading.Lock()
 _lib: C.CDLL | None = None
@@ -163,6 +170,22 @@ class Context:
         self.check(self.lib.b2k_gemm_tf32x3(self.handle, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias or None,
                                             int(relu), stream), "b2k_gemm_tf32x3")
 
+    def timing(self, on: bool) -> None:
+        self.check(self.lib.b2k_timing_enable(self.handle, int(on)), "b2k_timing_enable")
+
+    def timing_read(self, phase: str) -> tuple[float, int]:
+        """(total milliseconds, launches) recorded for one phase since the last reset."""
+        ms, count = C.c_double(), _I64()
+        self.check(self.lib.b2k_timing_read(self.handle, PHASES[phase], C.byref(ms), C.byref(count)),
+                   "b2k_timing_read")
+        return ms.value, count.value
+
+    def timing_reset(self) -> None:
+        self.check(self.lib.b2k_timing_reset(self.handle), "b2k_timing_reset")
+
+    def set_gemm_variant(self, variant: int) -> None:
+        self.check(self.lib.b2k_gemm_set_variant(variant), "b2k_gemm_set_variant")
+
     def sync(self, stream: int = 0) -> None:
         self.check(self.lib.b2k_stream_sync(self.handle, stream), "b2k_stream_sync")
 
@@ -171,6 +194,14 @@ class Context:
         ptr = _P()
         self.check(self.lib.b2k_malloc(self.handle, C.byref(ptr), nbytes), "b2k_malloc")
         return ptr.value or 0
+
+    def host_alloc(self, nbytes: int) -> int:
+        ptr = _P()
+        self.check(self.lib.b2k_host_alloc(self.handle, C.byref(ptr), nbytes), "b2k_host_alloc")
+        return ptr.value or 0
+
+    def host_free(self, ptr: int) -> None:
+        self.check(self.lib.b2k_host_free(self.handle, ptr), "b2k_host_free")
 
     def free(self, ptr: int) -> None:
         self.check(self.lib.b2k_free(self.handle, ptr), "b2k_free")

@@ -58,7 +58,27 @@ int b2k_free(b2k_ctx *ctx, void *ptr);
 int b2k_memcpy_htod(b2k_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream);
 int b2k_memcpy_dtoh(b2k_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream);
 int b2k_memset(b2k_ctx *ctx, void *dst, int value, size_t bytes, void *stream);
+/* Page-locked host memory, so host<->device copies run asynchronously at
+ * full PCIe/C2C bandwidth. */
+int b2k_host_alloc(b2k_ctx *ctx, void **ptr, size_t bytes);
+int b2k_host_free(b2k_ctx *ctx, void *ptr);
 int b2k_stream_sync(b2k_ctx *ctx, void *stream);
+
+/* --- per-phase timing -------------------------------------------------------
+ * When enabled, every entry point brackets the kernels of each of its phases
+ * with CUDA events recorded on the caller's stream (the runner's event
+ * timing, tools/local_runner.py:318-332, per kernel instead of per launch
+ * request).  b2k_timing_read synchronises and sums the recorded intervals of
+ * one phase; b2k_timing_reset forgets them. */
+#define B2K_PHASE_SPLIT 0     /* 3xTF32 operand split pre-pass */
+#define B2K_PHASE_MMA 1       /* tcgen05 GEMM main kernel */
+#define B2K_PHASE_POINTWISE 2 /* pointwise programs */
+#define B2K_PHASE_SOFTMAX 3   /* row softmax */
+#define B2K_PHASE_ATTENTION 4 /* fused attention */
+#define B2K_PHASE_COUNT 5
+int b2k_timing_enable(b2k_ctx *ctx, int on);
+int b2k_timing_read(b2k_ctx *ctx, int phase, double *total_ms, int64_t *launches);
+int b2k_timing_reset(b2k_ctx *ctx);
 
 /* --- pointwise programs ---------------------------------------------------
  * Replaces the SIMT Emitter's pointwise lowering: Tile decode
