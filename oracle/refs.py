@@ -73,16 +73,24 @@ def attention_batched(q, k, v, scale: float | None = None) -> np.ndarray:
     return np.einsum("hst,htd->hsd", stable_softmax(scores), v).astype(np.float32)
 
 
-def rmsnorm(x, w, eps: float = 1e-5) -> np.ndarray:
-    """suite.py:222-225."""
+def rmsnorm(x, w=None, eps: float = 1e-5) -> np.ndarray:
+    """suite.py:222-225 (with weight) / research_cases.py:99-100 (without)."""
     x = _f64(x)
-    return (x / np.sqrt(np.mean(x ** 2, axis=-1, keepdims=True) + eps) * _f64(w)).astype(np.float32)
+    value = x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
+    if w is not None:
+        value = value * _f64(w)
+    return value.astype(np.float32)
 
 
-def l2norm(x) -> np.ndarray:
-    """suite.py:226-229."""
+def l2norm(x, eps: float = 0.0) -> np.ndarray:
+    """suite.py:226-229 (eps 0) / research_cases.py:101-102."""
     x = _f64(x)
-    return (x / np.sqrt(np.sum(x ** 2, axis=-1, keepdims=True))).astype(np.float32)
+    return (x / np.sqrt(np.sum(x * x, axis=-1, keepdims=True) + eps)).astype(np.float32)
+
+
+def mean(x) -> np.ndarray:
+    """r03_mean: the float64 mean of all elements."""
+    return np.asarray([_f64(x).mean()], dtype=np.float32)
 
 
 def array_sum(x) -> np.ndarray:
