@@ -12,9 +12,10 @@ from pathlib import Path
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "libb200k.so"
 
-B2K_OK, B2K_EINVAL, B2K_EUNSUPPORTED, B2K_ECUDA, B2K_ETIMEOUT = 0, 1, 2, -1, -2
+B2K_OK, B2K_EINVAL, B2K_EUNSUPPORTED, B2K_ECUDA, B2K_ETIMEOUT, B2K_ESCRATCH = 0, 1, 2, -1, -2, 3
+NOALLOC_SCRATCH_BYTES = 32 << 20
 STATUS_NAMES = {B2K_EINVAL: "EINVAL", B2K_EUNSUPPORTED: "EUNSUPPORTED", B2K_ECUDA: "ECUDA",
-                B2K_ETIMEOUT: "ETIMEOUT"}
+                B2K_ETIMEOUT: "ETIMEOUT", B2K_ESCRATCH: "ESCRATCH"}
 
 PW_MAX_INPUTS, PW_MAX_INSNS = 8, 48
 B_KN, B_NK = 0, 1
@@ -66,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_selective_exp_f32": ([_P, _P, _P, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
+    "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_timing_enable": ([_P, C.c_int], C.c_int),
     "b2k_timing_read": ([_P, C.c_int, C.POINTER(C.c_double), C.POINTER(_I64)], C.c_int),
     "b2k_timing_reset": ([_P], C.c_int),

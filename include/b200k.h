@@ -34,6 +34,7 @@ extern "C" {
 #define B2K_EUNSUPPORTED 2 /* valid request outside this build's kernels */
 #define B2K_ECUDA (-1)     /* CUDA runtime/driver error */
 #define B2K_ETIMEOUT (-2)  /* a device-side bounded wait expired (kernel error flag) */
+#define B2K_ESCRATCH 3     /* problem needs more than the fixed no-alloc scratch array */
 
 typedef struct b2k_ctx b2k_ctx;
 
@@ -170,6 +171,27 @@ int b2k_selective_exp_f32(b2k_ctx *ctx, const float *x, float *y, int64_t n, voi
 int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                     int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
                     void *stream);
+
+/* The same GEMM for callers that cannot allocate device memory (code running
+ * under CUDA-graph capture or a fixed memory plan, or memory owned by another
+ * allocator).  No counterpart in the reference.  It takes no context and
+ * allocates nothing: the operand split goes to a fixed scratch array inside
+ * the library image (B2K_NOALLOC_SCRATCH_BYTES per device that loads the
+ * library, kept until exit).  Problems with 2 * (m + n) * round_up(k, 32) * 4
+ * bytes of split operands above that size return B2K_ESCRATCH and launch
+ * nothing; K = 0 returns B2K_EUNSUPPORTED.  Runs on the calling thread's
+ * current device and the given stream.  The first call on a device looks up
+ * the scratch array's device address (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  Every call on a device shares the one
+ * array, so calls that overlap on the GPU (different streams, no ordering)
+ * race and corrupt each other's results; calls on one stream are safe.  Each
+ * call rewrites all the scratch it reads, so nothing needs clearing.  A
+ * device-side bounded-wait expiry is not reported by this entry point.
+ * Other return codes as b2k_gemm_tf32x3 (B2K_EINVAL, B2K_ECUDA). */
+#define B2K_NOALLOC_SCRATCH_BYTES (32u << 20)
+int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                            int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias,
+                            int32_t relu, void *stream);
 
 /* Select the GEMM kernel variant for subsequent calls (process-wide; for
  * tuning and benchmarking): 0 = 128x256 tile, 128-byte swizzle, 2 stages
