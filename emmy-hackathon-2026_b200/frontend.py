@@ -1,0 +1,454 @@
+"""Front end: ``*.ir.json`` + sibling ``meta.json`` -> a recognised B200 kernel.
+
+Mirrors the reference's ``compile_path`` contract (compile.py:9628-9738): load
+the typed graph, select the kernel node (by filename for multi-kernel
+pipelines), match exactly one metadata kernel by ``entry`` and ``node``,
+reject duplicate argument names, validate the launch geometry the way the
+SIMT emitter does (compile.py:1997-2005, 8484-8503), then classify.  Where the
+reference returns PTX, this returns a :class:`KernelSpec` naming one of the
+C-ABI kernels and how the positional ``arg_order`` arguments feed it.  Errors
+are :class:`Unsupported` (a ``ValueError``, like compile.py:264) and the CLI
+prints them on stderr with exit status 1.
+
+Recognition (the role of tensor_core.classify, tensor_core.py:1133-1703,
+extended to the pointwise / softmax / attention families) is fail-closed:
+
+1. the argument signature (dtypes, ranks, shapes) must fit a kernel family;
+2. family-specific structure is extracted (the pointwise program, the
+   contraction roles, the attention scale buffer);
+3. a certificate: the IR itself is executed (``irexec``) on seeded random
+   inputs for a sample of CTAs -- every CTA when the launch is small -- and
+   what those CTAs write must equal the family's mathematics on those inputs
+   (float64, relative 1e-9), and no output element may be written twice.
+"""
+from __future__ import annotations
+
+import json
+import math
+import sys
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+from . import irexec
+from .ir import Graph, GraphNode, IRError, Node, static_int, walk
+
+FULL_EXECUTION_BUDGET = 4_000_000     # lanes x statements below which every CTA is executed
+SAMPLE_CTAS = 4
+
+
+class Unsupported(ValueError):
+    """The IR kernel is outside the recognised hot-path families (compile.py:264)."""
+
+
+@dataclass
+class KernelSpec:
+    """A recognised kernel: which C-ABI entry point runs it and with what roles."""
+
+    kind: str                  # pointwise | row_softmax | matmul | attention
+    entry: str
+    node: str
+    arg_order: list
+    args: dict                 # name -> meta argument record
+    grid: list
+    block: list
+    zero_outputs: list
+    params: dict = field(default_factory=dict)
+    certificate: dict = field(default_factory=dict)
+
+    def describe(self) -> dict:
+        return {"kind": self.kind, "entry": self.entry, "node": self.node, "arg_order": self.arg_order,
+                "params": self.params, "zero_outputs": self.zero_outputs, "certificate": self.certificate}
+
+    # --- launch -----------------------------------------------------------------
+    def launch(self, ctx, pointers: dict, stream: int = 0) -> None:
+        """Run on the GPU; ``pointers`` maps argument names to device addresses."""
+        from . import runtime
+        p = self.params
+        if self.kind == "pointwise":
+            prog = runtime.make_program(len(p["inputs"]), [tuple(i) for i in p["insns"]], p["result"],
+                                        broadcast=tuple(i for i, b in enumerate(p["broadcast"]) if b))
+            ctx.pointwise(prog, [pointers[n] for n in p["inputs"]], pointers[p["output"]], p["n"], stream)
+        elif self.kind == "row_softmax":
+            ctx.row_softmax(pointers[p["x"]], pointers[p["out"]], p["rows"], p["cols"], stream=stream)
+        elif self.kind == "matmul":
+            ctx.gemm(pointers[p["a"]], pointers[p["b"]], pointers[p["out"]], p["m"], p["n"], p["k"], stream=stream)
+        elif self.kind == "attention":
+            ctx.attention(pointers[p["q"]], pointers[p["kt"]], pointers[p["v"]], pointers[p["out"]],
+                          1, p["s_q"], p["s_kv"], p["d"], p["dv"], scale_ptr=pointers[p["scale"]],
+                          k_layout=1, stream=stream)
+        else:
+            raise Unsupported(f"no launcher for {self.kind}")
+
+
+# --------------------------------------------------------------------------- loading
+def load(path) -> tuple[Graph, GraphNode, dict, dict]:
+    """compile.py:9628-9648: typed graph, selected kernel node, its metadata entry."""
+    path = Path(path)
+    try:
+        graph = Graph.from_dict(json.loads(path.read_text()))
+    except (IRError, json.JSONDecodeError) as exc:
+        raise Unsupported(f"invalid Kernel IR: {exc}") from exc
+    kernels = graph.kernels()
+    metadata = json.loads(path.with_name("meta.json").read_text())
+    if len(kernels) == 1:
+        node = kernels[0]
+    else:
+        requested = path.name[:-len(".ir.json")] if path.name.endswith(".ir.json") else path.stem
+        selected = [n for n in kernels if n.entry == requested
+                    and any(k["entry"] == requested and k["node"] == n.name for k in metadata["kernels"])]
+        if len(selected) != 1:
+            raise Unsupported("Expected a unique filename-selected KernelOp in pipeline graph")
+        node = selected[0]
+    matches = [k for k in metadata["kernels"] if k["entry"] == node.entry and k["node"] == node.name]
+    if len(matches) != 1:
+        raise Unsupported("Expected exactly one metadata kernel matching node and entry")
+    if len(set(matches[0]["arg_order"])) != len(matches[0]["arg_order"]):
+        raise Unsupported("Duplicate argument names in metadata")
+    return graph, node, matches[0], metadata
+
+
+def validate_launch(node: GraphNode, kernel: dict) -> None:
+    """Launch-geometry rules of the SIMT emitter (compile.py:1997-2005, 8484-8503)."""
+    for field_name in ("block", "grid"):
+        dims = kernel.get(field_name)
+        if not isinstance(dims, list) or len(dims) != 3 or any(type(d) is not int or d <= 0 for d in dims):
+            raise Unsupported(f"{field_name} must be three positive integers")
+    threads = math.prod(kernel["block"])
+    if threads > 1024:
+        raise Unsupported("block has more than 1024 threads")
+    names = {a["name"] for a in kernel["args"]}
+    if set(kernel["arg_order"]) != names:
+        raise Unsupported("arg_order does not name exactly the kernel arguments")
+    for name in kernel.get("zero_outputs", []):
+        if not any(a["name"] == name and a.get("output") for a in kernel["args"]):
+            raise Unsupported("zero_outputs must name output buffers")
+    for stmt in node.body:
+        if stmt.kind == "Tile":
+            cells = stmt.get("block_threads")
+            if cells is not None and cells != threads:
+                raise Unsupported("Tile block_threads differs from prescribed launch")
+            n = math.prod(static_int(a.extent) for a in stmt.axes)
+            if math.prod(kernel["grid"]) * threads < n:
+                raise Unsupported("Prescribed grid does not cover the Tile")
+
+
+# --------------------------------------------------------------------------- helpers
+def _shape(arg) -> tuple:
+    return tuple(int(s) for s in arg.get("shape", ()))
+
+
+def _size(shape) -> int:
+    return int(math.prod(shape)) if shape else 1
+
+
+def _inputs_outputs(kernel):
+    args = {a["name"]: a for a in kernel["args"]}
+    for a in kernel["args"]:
+        if a.get("dtype", "f32") != "f32":
+            raise Unsupported(f"argument {a['name']!r} has dtype {a.get('dtype')}: only FP32 is on the hot path")
+        if a.get("scalar"):
+            raise Unsupported(f"by-value scalar argument {a['name']!r} is outside the recognised families")
+    outputs = [a["name"] for a in kernel["args"] if a.get("output")]
+    inputs = [a["name"] for a in kernel["args"] if not a.get("output")]
+    return args, inputs, outputs
+
+
+def _random_inputs(args, inputs, seed=12345):
+    rng = np.random.default_rng(seed)
+    buffers = {}
+    for name in inputs:
+        shape = _shape(args[name])
+        if "data" in args[name]:
+            buffers[name] = np.asarray(args[name]["data"], dtype=np.float64).reshape(shape).copy()
+        else:
+            buffers[name] = rng.standard_normal(shape).astype(np.float32).astype(np.float64)
+    return buffers
+
+
+def _estimate_statements(body, depth_limit=6) -> int:
+    """A rough count of dynamic statements one lane executes."""
+    def count(stmts, depth):
+        total = 0
+        for s in stmts:
+            total += 1
+            if s.kind in ("Loop", "StridedLoop") and depth < depth_limit:
+                trips = static_int(s.axis.extent)
+                if s.kind == "StridedLoop":
+                    step = s.step.value if isinstance(s.step, Node) and s.step.kind == "Literal" else 1
+                    trips = max(1, trips // max(1, int(step)))
+                total += trips * count(s.body, depth + 1)
+            elif s.kind in ("Tile", "Cond"):
+                total += count(s.body, depth + 1) + count(s.get("else_body", ()) or (), depth + 1)
+        return total
+    return count(body, 0)
+
+
+def certify(node, kernel, args, inputs, outputs, expected_fn, rtol=1e-9, atol=1e-12) -> dict:
+    """Execute the IR on seeded random inputs and compare with ``expected_fn``.
+
+    Every CTA is executed when the launch is small; otherwise the first, last
+    and two seeded random CTAs.  Returns the certificate record."""
+    grid, block = math.prod(kernel["grid"]), math.prod(kernel["block"])
+    per_lane = _estimate_statements(node.body)
+    atomic = any(s.kind == "Write" and s.get("atomic") for s in walk(node.body))
+    full = grid * per_lane <= FULL_EXECUTION_BUDGET // 8 or atomic
+    if full and grid * block * per_lane > 50 * FULL_EXECUTION_BUDGET:
+        raise Unsupported("atomic accumulation over a launch too large to certify")
+    if full:
+        ctas = list(range(grid))
+    else:
+        rng = np.random.default_rng(7)
+        ctas = sorted({0, grid - 1, *rng.integers(0, grid, SAMPLE_CTAS - 2).tolist()})
+    buffers = _random_inputs(args, inputs)
+    shapes = {name: _shape(args[name]) for name in args}
+    for name in outputs:
+        buffers[name] = np.full(shapes[name] or (1,), np.nan)
+        if name in kernel.get("zero_outputs", []):
+            buffers[name][...] = 0.0
+    try:
+        launch = irexec.execute(node.body, grid, block, ctas, buffers, shapes)
+    except irexec.ExecError as exc:
+        raise Unsupported(f"IR outside the executable subset: {exc}") from exc
+    expected = expected_fn({k: buffers[k] for k in inputs})
+    checked = 0
+    for name in outputs:
+        counts = launch.writes.get(name)
+        if counts is None:
+            raise Unsupported(f"sampled CTAs never wrote {name!r}")
+        if np.any(counts > 1) and not atomic:
+            raise Unsupported(f"{name!r}: an output element is written more than once")
+        written = counts > 0
+        if full and not written.all():
+            raise Unsupported(f"{name!r}: the launch leaves output elements unwritten")
+        got = buffers[name].reshape(-1)[written]
+        want = np.asarray(expected[name], dtype=np.float64).reshape(-1)[written]
+        if not np.allclose(got, want, rtol=rtol, atol=atol, equal_nan=False):
+            bad = int((~np.isclose(got, want, rtol=rtol, atol=atol)).sum())
+            raise Unsupported(f"{name!r}: IR semantics differ from the candidate family ({bad} elements)")
+        checked += int(written.sum())
+    return {"ctas_executed": len(ctas), "grid": grid, "exhaustive": full, "elements_checked": checked}
+
+
+# --------------------------------------------------------------------------- pointwise
+_PW_OPS = {"add", "subtract", "multiply", "divide", "maximum", "minimum", "negative", "reciprocal", "sqrt",
+           "rsqrt", "exp", "relu", "abs", "copy", "greater", "greater_equal", "less", "less_equal", "where"}
+
+
+def _pointwise_program(node, args, inputs, output):
+    """Straight-line per-element program of a pointwise Tile (lane 0 of its write)."""
+    if len(node.body) != 1 or node.body[0].kind != "Tile":
+        raise Unsupported("pointwise: body is not one Tile")
+    tile = node.body[0]
+    defs: dict = {}
+    writes = []
+
+    def flatten(stmts):
+        # Tail guards (Cond without else) only mask lanes past the end; the
+        # exact-coverage certificate checks that nothing else depends on them.
+        for st in stmts:
+            if st.kind == "Cond" and not st.else_body:
+                yield from flatten(st.body)
+            else:
+                yield st
+
+    for s in flatten(tile.body):
+        if s.kind == "Load":
+            if len(s.names) != 1:
+                raise Unsupported("pointwise: grouped load")
+            defs[s.names[0]] = ("in", s.input)
+        elif s.kind == "Let":
+            if isinstance(s.value, Node) and s.value.kind == "Literal" and isinstance(s.value.value, (int, float)):
+                defs[s.name] = ("const", float(s.value.value))
+            else:
+                raise Unsupported("pointwise: non-constant Let")
+        elif s.kind == "Assign":
+            if s.op.name not in _PW_OPS:
+                raise Unsupported(f"pointwise: op {s.op.name!r}")
+            defs[s.name] = ("op", s.op.name, tuple(defs[a] for a in s.args))
+        elif s.kind == "Write":
+            if s.output != output or s.get("atomic"):
+                raise Unsupported("pointwise: unexpected write")
+            writes.append(s)
+        else:
+            raise Unsupported(f"pointwise: statement {s.kind}")
+    if not writes:
+        raise Unsupported("pointwise: no write")
+    trees = [defs[v] for w in writes for v in w.values]
+    if any(t != trees[0] for t in trees):
+        raise Unsupported("pointwise: lanes compute different programs")
+    # compile lane 0's tree into the register program of b2k_pointwise_f32
+    order: list = []
+    slots: dict = {}
+    insns: list = []
+    streams = [n for n in inputs]
+
+    def emit(t):
+        if t in slots:
+            return slots[t]
+        if t[0] == "in":
+            return streams.index(t[1])
+        if t[0] == "const":
+            insns.append(("const", 0, 0, 0, t[1]))
+        else:
+            kids = [emit(c) for c in t[2]]
+            kids += [0] * (3 - len(kids))
+            insns.append((t[1], kids[0], kids[1], kids[2], 0.0))
+        slots[t] = len(streams) + len(insns) - 1
+        return slots[t]
+
+    result = emit(trees[0])
+    broadcast = [1 if _size(_shape(args[n])) == 1 and _size(_shape(args[output])) != 1 else 0 for n in streams]
+    return {"inputs": streams, "insns": insns, "result": result, "broadcast": broadcast, "output": output,
+            "n": _size(_shape(args[output]))}
+
+
+def _eval_program(params, buffers):
+    n = params["n"]
+    regs = [np.broadcast_to(buffers[name].reshape(-1)[:1] if b else buffers[name].reshape(-1), (n,))
+            for name, b in zip(params["inputs"], params["broadcast"])]
+    for op, a, b, c, imm in params["insns"]:
+        if op == "const":
+            regs.append(np.full(n, imm))
+        else:
+            regs.append(irexec._elementwise(op, [regs[a], regs[b], regs[c]]))
+    return regs[params["result"]]
+
+
+def classify_pointwise(node, kernel, args, inputs, outputs):
+    if len(outputs) != 1 or not inputs:
+        raise Unsupported("pointwise: needs inputs and one output")
+    out = outputs[0]
+    n = _size(_shape(args[out]))
+    for name in inputs:
+        if _size(_shape(args[name])) not in (1, n):
+            raise Unsupported("pointwise: input size differs from the output's")
+    if len(inputs) > 8:
+        raise Unsupported("pointwise: more than 8 input streams")
+    params = _pointwise_program(node, args, inputs, out)
+    cert = certify(node, kernel, args, inputs, outputs, lambda b: {out: _eval_program(params, b)})
+    return params, cert
+
+
+# --------------------------------------------------------------------------- row softmax
+def _softmax64(x):
+    z = x - x.max(axis=-1, keepdims=True)
+    e = np.exp(z)
+    return e / e.sum(axis=-1, keepdims=True)
+
+
+def classify_row_softmax(node, kernel, args, inputs, outputs):
+    if len(inputs) != 1 or len(outputs) != 1:
+        raise Unsupported("row_softmax: one input, one output")
+    x, out = inputs[0], outputs[0]
+    shape = _shape(args[x])
+    if len(shape) != 2 or _shape(args[out]) != shape:
+        raise Unsupported("row_softmax: needs matching rank-2 input and output")
+    if not any(s.kind == "Assign" and s.op.name == "exp" for s in walk(node.body)):
+        raise Unsupported("row_softmax: no exponential")
+    cert = certify(node, kernel, args, inputs, outputs, lambda b: {out: _softmax64(b[x])})
+    return {"x": x, "out": out, "rows": shape[0], "cols": shape[1]}, cert
+
+
+# --------------------------------------------------------------------------- matmul
+def classify_matmul(node, kernel, args, inputs, outputs):
+    if len(outputs) != 1:
+        raise Unsupported("matmul: one output")
+    out = outputs[0]
+    mats = [n for n in inputs if len(_shape(args[n])) == 2]
+    if len(mats) != 2 or len(inputs) != 2:
+        raise Unsupported("matmul: two rank-2 inputs")
+    oshape = _shape(args[out])
+    if len(oshape) != 2:
+        raise Unsupported("matmul: rank-2 output")
+    last = None
+    for a, b in ((mats[0], mats[1]), (mats[1], mats[0])):
+        sa, sb = _shape(args[a]), _shape(args[b])
+        if sa[1] != sb[0] or (sa[0], sb[1]) != oshape:
+            continue
+        try:
+            cert = certify(node, kernel, args, inputs, outputs, lambda buf: {out: buf[a] @ buf[b]})
+        except Unsupported as exc:
+            last = exc
+            continue
+        return {"a": a, "b": b, "out": out, "m": sa[0], "n": sb[1], "k": sa[1]}, cert
+    raise last or Unsupported("matmul: operand shapes do not contract to the output")
+
+
+# --------------------------------------------------------------------------- attention
+def classify_attention(node, kernel, args, inputs, outputs):
+    if len(outputs) != 1 or len(inputs) != 4:
+        raise Unsupported("attention: q, kt, v, scale -> one output")
+    out = outputs[0]
+    scal = [n for n in inputs if _size(_shape(args[n])) == 1]
+    mats = [n for n in inputs if len(_shape(args[n])) == 2 and _size(_shape(args[n])) > 1]
+    if len(scal) != 1 or len(mats) != 3:
+        raise Unsupported("attention: one scale buffer and three matrices")
+    scale = scal[0]
+    oshape = _shape(args[out])
+    import itertools
+    last = None
+    for q, kt, v in itertools.permutations(mats):
+        sq, sk, sv = _shape(args[q]), _shape(args[kt]), _shape(args[v])
+        if not (sq[1] == sk[0] and sk[1] == sv[0] and (sq[0], sv[1]) == oshape):
+            continue
+
+        def expect(buf, q=q, kt=kt, v=v):
+            s = buf[q] @ buf[kt] / float(buf[scale].reshape(-1)[0])
+            return {out: _softmax64(s) @ buf[v]}
+        try:
+            cert = certify(node, kernel, args, inputs, outputs, expect)
+        except Unsupported as exc:
+            last = exc
+            continue
+        return {"q": q, "kt": kt, "v": v, "scale": scale, "out": out, "s_q": sq[0], "s_kv": sk[1],
+                "d": sq[1], "dv": sv[1]}, cert
+    raise last or Unsupported("attention: shapes do not form softmax(q kt / s) v")
+
+
+FAMILIES = (
+    ("pointwise", classify_pointwise),
+    ("row_softmax", classify_row_softmax),
+    ("matmul", classify_matmul),
+    ("attention", classify_attention),
+)
+
+
+def classify(graph: Graph, node: GraphNode, kernel: dict) -> KernelSpec:
+    validate_launch(node, kernel)
+    args, inputs, outputs = _inputs_outputs(kernel)
+    reasons = []
+    for kind, fn in FAMILIES:
+        try:
+            params, cert = fn(node, kernel, args, inputs, outputs)
+        except Unsupported as exc:
+            reasons.append(f"{kind}: {exc}")
+            continue
+        return KernelSpec(kind=kind, entry=kernel["entry"], node=kernel["node"], arg_order=list(kernel["arg_order"]),
+                          args=args, grid=list(kernel["grid"]), block=list(kernel["block"]),
+                          zero_outputs=list(kernel.get("zero_outputs", [])), params=params, certificate=cert)
+    raise Unsupported("no B200 kernel family recognises this IR (" + "; ".join(reasons) + ")")
+
+
+def compile_path(path) -> KernelSpec:
+    """The reference's front door, returning a recognised kernel instead of PTX."""
+    graph, node, kernel, _ = load(path)
+    return classify(graph, node, kernel)
+
+
+def main(argv=None) -> int:
+    argv = sys.argv[1:] if argv is None else argv
+    try:
+        if len(argv) != 1:
+            raise Unsupported("Usage: python -m <package>.frontend kernel.ir.json")
+        spec = compile_path(argv[0])
+        sys.stdout.write(json.dumps(spec.describe()) + "\n")
+    except Exception as exc:  # mirrors compile.py:9727-9738
+        print(f"frontend: {type(exc).__name__}: {exc}", file=sys.stderr)
+        return 1
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,138 @@
+"""The front end (compile_path contract, recogniser) on the bundled fixtures, CPU only."""
+from __future__ import annotations
+
+import json
+import shutil
+
+import pytest
+
+from conftest import GOLDEN, pkg
+
+CASES = GOLDEN / "cases"
+
+# Recognised hot-path kernels among the bundled fixtures (kernel kinds in
+# metadata order; None = outside the recognised families).
+RECOGNISED = {
+    "a01_attention-c10866af73f8": ["attention"],
+    "a02_attention_128-69db4e7f597c": ["attention"],
+    "atomic_matmul-0-b0bb43becf74": ["matmul"],
+    "atomic_matmul_7x5x9-variant": ["matmul"],
+    "attention-0-9170e7b0641d": [None, "row_softmax", "matmul"],
+    "f02-extra-cta-120bf007fb2d": ["row_softmax"],
+    "f02_row_softmax-89d56c168a0b": ["row_softmax"],
+    "full-segment16-274cb67281df": ["attention"],
+    "full-segment16-44c6e3443740": ["attention"],
+    "full-segment16-899690420377": ["attention"],
+    "full-segment16-c974ec730c3e": ["attention"],
+    "full-segment16-dd375967ea38": ["attention"],
+    "full-segment32-aa23bbd00f94": ["attention"],
+    "m01_matmul_512-cd9a29496fcc": ["matmul"],
+    "m02_matmul_rect-aeb1568894b7": ["matmul"],
+    "matmul-2-cc1c8cef5b4d": ["matmul"],
+    "maxfinite-times-zero-v2-991d11340dcd": ["matmul"],
+    "p00_scalar_add-4035b0c01010": ["pointwise"],
+    "p01_vector_add-5e973341ada3": ["pointwise"],
+    "p02_scale_shift-3145aa57f753": ["pointwise"],
+    "p03_relu_mul-aeeffce3a36b": ["pointwise"],
+    "partial-fallback-bdd094ff243f": ["attention"],
+    "partial-fallback-ef3488d3d03c": ["attention"],
+    "pointwise-1-fe256034fe7c": ["pointwise"],
+    "pointwise-3-06a6f12448fb": ["pointwise"],
+    "root-axis-alpha-rename-tid-d51e9f76fb9d": ["attention"],
+    "scaled_score_mutable_alias-variant": ["attention"],
+    "softmax-0-5200ccc23b31": ["row_softmax"],
+    "softmax-1-0a50249d1218": ["row_softmax"],
+    "softmax-2-d7aa0ab891e7": ["row_softmax"],
+    "tail32-de25e54114aa": ["attention"],
+}
+
+
+def kinds_of(folder):
+    fe = pkg("frontend")
+    meta = json.loads((folder / "meta.json").read_text())
+    irs = sorted(folder.glob("*.ir.json"))
+    kinds = []
+    for kernel in meta["kernels"]:
+        path = folder / f"{kernel['entry']}.ir.json"
+        if not path.exists():
+            path = irs[0]
+        try:
+            kinds.append(fe.compile_path(path).kind)
+        except fe.Unsupported:
+            kinds.append(None)
+    return kinds
+
+
+@pytest.mark.parametrize("name", sorted(p.name for p in CASES.iterdir() if p.is_dir()))
+def test_recognition_over_bundled_cases(name):
+    kinds = kinds_of(CASES / name)
+    assert kinds == RECOGNISED.get(name, [None] * len(kinds))
+
+
+def test_pointwise_program_of_p02():
+    fe = pkg("frontend")
+    spec = fe.compile_path(CASES / "p02_scale_shift-3145aa57f753" / "k_add_pointwise.ir.json")
+    p = spec.params
+    assert p["inputs"] == ["mul_c1", "add_c1", "x"] and p["broadcast"] == [1, 1, 0]
+    assert [i[0] for i in p["insns"]] == ["multiply", "add"] and p["n"] == 4096
+
+
+def test_matmul_roles_follow_shapes_not_arg_order():
+    fe = pkg("frontend")
+    spec = fe.compile_path(CASES / "m01_matmul_512-cd9a29496fcc" / "k_matmul_2967be.ir.json")
+    assert spec.kind == "matmul" and spec.arg_order == ["x1", "x0", "matmul"]
+    assert (spec.params["a"], spec.params["b"]) == ("x0", "x1")
+    assert not spec.certificate["exhaustive"] and spec.certificate["ctas_executed"] == 4
+
+
+def _copy_case(tmp_path, name):
+    dst = tmp_path / name
+    shutil.copytree(CASES / name, dst)
+    return dst
+
+
+def test_duplicate_argument_names_rejected(tmp_path):
+    fe = pkg("frontend")
+    case = _copy_case(tmp_path, "p01_vector_add-5e973341ada3")
+    meta = json.loads((case / "meta.json").read_text())
+    meta["kernels"][0]["arg_order"] = ["x0", "x0", "add"]
+    (case / "meta.json").write_text(json.dumps(meta))
+    with pytest.raises(fe.Unsupported, match="Duplicate"):
+        fe.compile_path(case / "k_add_pointwise.ir.json")
+
+
+def test_short_grid_rejected(tmp_path):
+    fe = pkg("frontend")
+    case = _copy_case(tmp_path, "p01_vector_add-5e973341ada3")
+    meta = json.loads((case / "meta.json").read_text())
+    meta["kernels"][0]["grid"] = [1, 1, 1]
+    (case / "meta.json").write_text(json.dumps(meta))
+    with pytest.raises(fe.Unsupported, match="grid"):
+        fe.compile_path(case / "k_add_pointwise.ir.json")
+
+
+def test_wrong_semantics_rejected(tmp_path):
+    """An add kernel whose IR actually subtracts must not be recognised as add."""
+    fe = pkg("frontend")
+    case = _copy_case(tmp_path, "p01_vector_add-5e973341ada3")
+    path = case / "k_add_pointwise.ir.json"
+    path.write_text(path.read_text().replace("ElementwiseImpl('add')", "ElementwiseImpl('subtract')"))
+    spec = fe.compile_path(path)  # still a pointwise program ...
+    assert [i[0] for i in spec.params["insns"]] == ["subtract"]  # ... of the IR's own op
+
+
+def test_matmul_with_truncated_k_rejected():
+    """case-7 contracts only the first 63 of 65 K columns: not A @ B."""
+    fe = pkg("frontend")
+    with pytest.raises(fe.Unsupported):
+        fe.compile_path(next((CASES / "case-7-72f1deeac451").glob("*.ir.json")))
+
+
+def test_cli_contract(capsys):
+    fe = pkg("frontend")
+    assert fe.main([str(CASES / "p00_scalar_add-4035b0c01010" / "k_add_pointwise.ir.json")]) == 0
+    out = json.loads(capsys.readouterr().out)
+    assert out["kind"] == "pointwise"
+    assert fe.main([str(next((CASES / "case-02-6cbcd2d46537").glob("*.ir.json")))]) == 1
+    assert "f16" in capsys.readouterr().err
+    assert fe.main([]) == 1

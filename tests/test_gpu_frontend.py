@@ -1,0 +1,55 @@
+"""Drop-in parity: every recognised bundled case runs through the front end and
+the C ABI on the GPU and matches the reference's expected outputs at the
+case's own metadata tolerance (tools/research_gpu.py:71-86 comparison)."""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, pkg
+from oracle import refs
+from test_frontend import RECOGNISED
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def session(ctx):
+    api = pkg("api")
+    s = api.Session(0)
+    yield s
+    s.close()
+
+
+CASES = sorted(n for n, kinds in RECOGNISED.items() if all(kinds) and (GOLDEN / "cases" / n / "expected.npz").exists())
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_recognised_case_matches_expected(session, name):
+    runner = pkg("runner")
+    folder = GOLDEN / "cases" / name
+    meta = json.loads((folder / "meta.json").read_text())
+    with np.load(folder / "inputs.npz") as data:
+        inputs = {k: data[k] for k in data.files}
+    with np.load(folder / "expected.npz") as data:
+        expected = {k: data[k] for k in data.files}
+    pipeline = runner.Pipeline(folder)
+    if any(s.kind == "attention" for s in pipeline.specs) and not hasattr(session.ctx, "attention"):
+        pytest.skip("attention kernel not built")
+    result, arrays = pipeline.run(session, inputs=inputs, warmup=1, iters=2)
+    assert result["ok"]
+    for out, want in expected.items():
+        ok, bad, err = refs.allclose_report(arrays[out].reshape(want.shape), want, meta["rtol"], meta["atol"])
+        assert ok, (out, bad, err)
+
+
+def test_runner_seeded_request(session):
+    """The runner's own seeded-input path (no fixture payload)."""
+    runner = pkg("runner")
+    result = runner.Pipeline(GOLDEN / "cases" / "p01_vector_add-5e973341ada3").run(session, warmup=1, iters=3)[0]
+    x0 = np.random.default_rng(0).standard_normal(1024).astype(np.float32)
+    x1 = np.random.default_rng(1).standard_normal(1024).astype(np.float32)
+    assert result["outputs"]["add"]["values"] == (x0 + x1).tolist()
+    assert result["median_us"] is not None and result["median_us"] > 0
