@@ -10,7 +10,9 @@ A step is one pass of the hot path over one batch of synthetic input:
   pre-pass + tensor-core kernel), TFLOP/s of useful 2*M*N*K work;
 * ``softmax`` -- row softmax of 4096 x 8192 FP32, GB/s of one read + one write;
 * ``add`` -- c = a + b over 2^24 FP32, GB/s of two reads + one write;
-* ``ragged`` -- relu(A B^T + bias), 4097 x 1000 x 777, TFLOP/s.
+* ``ragged`` -- relu(A B^T + bias), 4097 x 1000 x 777, TFLOP/s;
+* ``attention`` -- softmax(Q K^T / sqrt(128)) V over 4 x 16 heads, S 2048,
+  D 128, both contractions 3xTF32, TFLOP/s of useful 4*BH*S*S*D work.
 
 With N > 1 (torchrun, one rank per GPU) every rank processes its own batch of
 the same size (rows of A / rows of the matrix / ranges of the vector: the
@@ -287,7 +289,70 @@ class Add(Workload):
                 "parallelism": f"dp{self.world} (contiguous ranges per GPU)"}
 
 
+class Attention(Workload):
+    name, unit, bound, phase, launches_per_step = "attention", "TFLOP/s", "tensor", "mma", 7
+    profile = "attention_tf32x3_64x2048x128"
+
+    def __init__(self, rank, world, bh=64, seq=2048, d=128):
+        super().__init__(rank, world)
+        self.bh, self.seq, self.d = bh, seq, d
+
+    def work(self):
+        return 4.0 * self.bh * self.seq * self.seq * self.d
+
+    def dominant_work(self):
+        # two contractions per step, each 2*BH*S*S*D useful, three TF32 products each
+        return 3.0 * self.work() / 2
+
+    def setup(self, ctx, torch):
+        q, k, v = pkg("workloads").attention_inputs(self.bh, self.seq, self.d)
+        if self.rank:
+            q = np.random.default_rng(3001 + 7919 * self.rank).standard_normal(q.shape).astype(np.float32)
+        self.host = (q, k, v)
+        self.dq, self.dk, self.dv = (torch.from_numpy(t).cuda() for t in (q, k, v))
+        self.do = torch.empty_like(self.dq)
+        self.ctx = ctx
+
+    def step(self):
+        self.ctx.attention(self.dq.data_ptr(), self.dk.data_ptr(), self.dv.data_ptr(), self.do.data_ptr(),
+                           self.bh, self.seq, self.seq, self.d, self.d)
+
+    def e2e_setup(self, session):
+        self.session = session
+        self.pin = [session.pinned(t.shape) for t in self.host]
+        for p, t in zip(self.pin, self.host):
+            p[...] = t
+        self.pout = session.pinned(self.host[0].shape)
+        self.bufs = [session.empty(t.shape) for t in self.host] + [session.empty(self.host[0].shape)]
+        self.e2e_bytes = (sum(t.nbytes for t in self.host), self.pout.nbytes)
+
+    def e2e_step(self):
+        for p, b in zip(self.pin, self.bufs):
+            self.session.upload(p, b)
+        bq, bk, bv, bo = self.bufs
+        self.session.ctx.attention(bq.ptr, bk.ptr, bv.ptr, bo.ptr, self.bh, self.seq, self.seq, self.d, self.d,
+                                   stream=self.session.stream)
+        self.session.download(bo, self.pout)
+
+    def cpu_once(self, rows):
+        refs = importlib.import_module("oracle.refs")
+        q, k, v = self.host
+        heads = max(1, rows)
+        refs.attention_batched(q[:heads], k[:heads], v[:heads])
+        return 4.0 * heads * self.seq * self.seq * self.d, f"float64 NumPy attention of {heads} head(s) (S {self.seq}, D {self.d})"
+
+    default_rows = 2
+    reference_rows = 1
+
+    def config(self):
+        return {"workload": "attention_3xtf32", "batch_heads": self.bh * self.world, "batch_heads_per_gpu": self.bh,
+                "seq": self.seq, "head_dim": self.d, "scale": "1/sqrt(128)", "inputs": "Q,K,V ~ N(0,1) seeded",
+                "l2": "inputs larger than L2", "parallelism": f"dp{self.world} (batch*heads per GPU)"}
+
+
 def make_workload(name, rank, world):
+    if name == "attention":
+        return Attention(rank, world)
     if name == "gemm":
         return Gemm(rank, world)
     if name == "ragged":
@@ -482,6 +547,8 @@ def run_reference(args) -> dict | None:
     # host inputs only (no device)
     if isinstance(w, Gemm):
         w.host = w.inputs()
+    elif isinstance(w, Attention):
+        w.host = pkg("workloads").attention_inputs(w.bh, w.seq, w.d)
     elif isinstance(w, Softmax):
         w.host = pkg("workloads").softmax_input(w.rows, w.cols)
     else:
@@ -512,12 +579,12 @@ def main():
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=None)
     parser.add_argument("--warmup", type=int, default=5)
-    parser.add_argument("--workload", default="gemm", choices=["gemm", "softmax", "add", "ragged"])
+    parser.add_argument("--workload", default="gemm", choices=["gemm", "softmax", "add", "ragged", "attention"])
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     args = parser.parse_args()
     if args.steps is None:
-        args.steps = {"gemm": 1500, "ragged": 20000, "softmax": 20000, "add": 20000}[args.workload]
+        args.steps = {"gemm": 1500, "ragged": 20000, "softmax": 20000, "add": 20000, "attention": 500}[args.workload]
         if args.impl == "reference":
             args.steps = 20
     args.warmup = max(3, args.warmup) if args.impl == "ours" else args.warmup

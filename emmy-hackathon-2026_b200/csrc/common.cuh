@@ -63,6 +63,33 @@ inline int make_current(b2k_ctx *ctx) {
 // Grow the context's scratch arena to at least `bytes`.
 int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream);
 
+// --- 3xTF32 operand split and tensor-core GEMM (gemm.cu) ---------------------
+// K is zero-padded to a multiple of 32 in the split operands.
+inline int64_t gemm_kpad(int64_t k) { return (k + 31) / 32 * 32; }
+
+// Split operands of a (batched) GEMM: A_hi/A_lo [batch][m][kp] and
+// B_hi/B_lo [batch][n][kp], all K-major.
+struct SplitOperands {
+  float *a_hi, *a_lo, *b_hi, *b_lo;
+  int64_t kp;
+};
+
+// Row-major [batch][rows, k] -> hi/lo [batch][rows][kp].
+int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t ld, int64_t bs, int64_t batch,
+               int64_t kp, float *hi, float *lo, cudaStream_t s);
+// Row-major [batch][k, n] -> transposed hi/lo [batch][n][kp].
+int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_t ld, int64_t bs, int64_t batch,
+                    int64_t kp, float *hi, float *lo, cudaStream_t s);
+// C[z] = epilogue(A[z] * B[z]^T) for z < batch on pre-split operands; the
+// epilogue divides by *div_ptr (or div_value), adds bias[n], applies ReLU.
+// Row softmax of x [rows, cols] written as TF32 hi/lo halves [rows][kp] (softmax.cu).
+int softmax_split_rows(b2k_ctx *ctx, const float *x, int64_t rows, int64_t cols, int64_t ld_x, float *hi,
+                       float *lo, int64_t kp, cudaStream_t s);
+
+int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
+              int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
+              cudaStream_t s);
+
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Brackets the kernels of one phase with CUDA events on `stream` when the
@@ -106,6 +133,27 @@ __device__ __forceinline__ float b2k_exp(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(t));
   if (tiny) r = __fmul_rn(r, 1.17549435082228750797e-38f);  // exact 2^-126
   return r;
+}
+
+// TF32 split of one FP32 value: hi = rna(x) with the bit rule of
+// tf32_emitter.py:22-29 ((bits + 0x1000) & 0xFFFFE000), lo = rna(x - hi), so
+// hi + lo carries x to about 2^-22 and both halves are exact TF32 values.
+// Deviation from the reference model, on purpose: when rounding a finite x
+// overflows to infinity (|x| near FLT_MAX) hi falls back to truncation, so
+// max-finite * 0 stays 0 instead of inf * 0 = NaN (the bundled
+// maxfinite-times-zero witness expects 0).  Non-finite x gives hi = x, lo = 0.
+__device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
+  const uint32_t bits = __float_as_uint(x);
+  if (!isfinite(x)) {
+    hi = x;
+    lo = 0.0f;
+    return;
+  }
+  float h = __uint_as_float((bits + 0x1000u) & 0xFFFFE000u);
+  if (!isfinite(h)) h = __uint_as_float(bits & 0xFFFFE000u);
+  const float r = __fsub_rn(x, h);
+  hi = h;
+  lo = __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
 }
 
 __device__ __forceinline__ float warp_max(float v) {

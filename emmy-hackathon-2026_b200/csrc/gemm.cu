@@ -30,63 +30,56 @@ constexpr int BM = 128;
 constexpr int KPAD = 32;  // K is zero-padded to a multiple of this in the split operands
 
 // --- split pre-pass --------------------------------------------------------
-// hi = rna(x) with the TF32 bit rule of tf32_emitter.py:22-29; lo = rna(x - hi).
-// Deviation from the reference model, on purpose: when rounding a finite x
-// overflows to infinity (|x| near FLT_MAX) hi falls back to truncation, so
-// max-finite * 0 stays 0 instead of inf * 0 = NaN (the bundled
-// maxfinite-times-zero witness expects 0).  Non-finite x gives hi = x, lo = 0.
-__device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
-  const uint32_t bits = __float_as_uint(x);
-  if (!isfinite(x)) {
-    hi = x;
-    lo = 0.0f;
-    return;
-  }
-  float h = __uint_as_float((bits + 0x1000u) & 0xFFFFE000u);
-  if (!isfinite(h)) h = __uint_as_float(bits & 0xFFFFE000u);
-  const float r = __fsub_rn(x, h);
-  hi = h;
-  lo = __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
-}
+// (the split rule split_tf32 lives in common.cuh)
 
-// Row-major [rows, K] (leading dimension ld) -> hi/lo [rows, Kp], zero padded.
+// Row-major [batch][rows, K] (row stride ld, batch stride bs) -> hi/lo
+// [batch][rows][Kp], zero padded along K.
 __global__ void __launch_bounds__(256) split_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t K,
-                                                         int64_t ld, int64_t Kp, float *__restrict__ hi,
-                                                         float *__restrict__ lo, int vec_src) {
+                                                         int64_t ld, int64_t bs, int64_t batch, int64_t Kp,
+                                                         float *__restrict__ hi, float *__restrict__ lo,
+                                                         int vec_src) {
   const int64_t kp4 = Kp >> 2;
-  const int64_t total = rows * kp4;
+  const int64_t per_batch = rows * kp4;
+  const int64_t total = batch * per_batch;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / kp4;
-    const int64_t k = (i - r * kp4) << 2;
+    const int64_t b = i / per_batch;
+    const int64_t rem = i - b * per_batch;
+    const int64_t r = rem / kp4;
+    const int64_t k = (rem - r * kp4) << 2;
+    const float *row = src + b * bs + r * ld;
     float v[4];
     if (vec_src && k + 3 < K) {
-      const float4 t = *reinterpret_cast<const float4 *>(src + r * ld + k);
+      const float4 t = *reinterpret_cast<const float4 *>(row + k);
       v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
     } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? src[r * ld + k + j] : 0.0f;
+      for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? row[k + j] : 0.0f;
     }
     float4 h, l;
     split_tf32(v[0], h.x, l.x);
     split_tf32(v[1], h.y, l.y);
     split_tf32(v[2], h.z, l.z);
     split_tf32(v[3], h.w, l.w);
-    *reinterpret_cast<float4 *>(hi + r * Kp + k) = h;
-    *reinterpret_cast<float4 *>(lo + r * Kp + k) = l;
+    const int64_t o = (b * rows + r) * Kp + k;
+    *reinterpret_cast<float4 *>(hi + o) = h;
+    *reinterpret_cast<float4 *>(lo + o) = l;
   }
 }
 
-// Row-major B [K, N] (ld) -> transposed hi/lo [N, Kp] (K-major), zero padded.
+// Row-major B [batch][K, N] (row stride ld, batch stride bs) -> transposed
+// hi/lo [batch][N][Kp] (K-major), zero padded.  blockIdx.z is the batch.
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float *__restrict__ src, int64_t K, int64_t N,
-                                                              int64_t ld, int64_t Kp, float *__restrict__ hi,
-                                                              float *__restrict__ lo) {
+                                                              int64_t ld, int64_t bs, int64_t Kp,
+                                                              float *__restrict__ hi, float *__restrict__ lo) {
   __shared__ float tile[32][33];
   const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
+  const float *base = src + (int64_t)blockIdx.z * bs;
+  float *hb = hi + (int64_t)blockIdx.z * N * Kp, *lb = lo + (int64_t)blockIdx.z * N * Kp;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
 #pragma unroll
   for (int i = 0; i < 32; i += 8) {
     const int64_t k = k0 + ty + i, n = n0 + tx;
-    tile[ty + i][tx] = (k < K && n < N) ? src[k * ld + n] : 0.0f;
+    tile[ty + i][tx] = (k < K && n < N) ? base[k * ld + n] : 0.0f;
   }
   __syncthreads();
 #pragma unroll
@@ -95,8 +88,8 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float *__res
     if (n < N && k < Kp) {
       float h, l;
       split_tf32(tile[tx][ty + i], h, l);
-      hi[n * Kp + k] = h;
-      lo[n * Kp + k] = l;
+      hb[n * Kp + k] = h;
+      lb[n * Kp + k] = l;
     }
   }
 }
@@ -116,7 +109,9 @@ constexpr int kThreads = 64 + 32 * kEpilogueWarps;  // producer, MMA, epilogue
 struct GemmArgs {
   float *c;
   const float *bias;
-  int64_t m, n, ldc;
+  const float *div_ptr;  // epilogue divisor read from device memory (or null)
+  float div_value;       // epilogue divisor when div_ptr is null (1 = none)
+  int64_t m, n, ldc, batch_stride_c;
   int num_kb;
   int relu;
   unsigned *err;
@@ -199,10 +194,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         sm100::mbar_arrive_expect_tx(&full_bar[s], Shape::kStage);
         const int kx = kb * Shape::BK;
-        sm100::tma_load_2d(a_hi(s), &map_ahi, &full_bar[s], kx, (int)m0);
-        sm100::tma_load_2d(a_lo(s), &map_alo, &full_bar[s], kx, (int)m0);
-        sm100::tma_load_2d(b_hi(s), &map_bhi, &full_bar[s], kx, (int)n0);
-        sm100::tma_load_2d(b_lo(s), &map_blo, &full_bar[s], kx, (int)n0);
+        const int z = (int)blockIdx.z;
+        sm100::tma_load_3d(a_hi(s), &map_ahi, &full_bar[s], kx, (int)m0, z);
+        sm100::tma_load_3d(a_lo(s), &map_alo, &full_bar[s], kx, (int)m0, z);
+        sm100::tma_load_3d(b_hi(s), &map_bhi, &full_bar[s], kx, (int)n0, z);
+        sm100::tma_load_3d(b_lo(s), &map_blo, &full_bar[s], kx, (int)n0, z);
         issued = kb + 1;
       }
       // Drain: every issued load must land before the CTA may exit.  These
@@ -278,12 +274,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t row = m0 + quarter * 32 + lane;
     const int64_t col0 = n0 + half * CPT;
     if (ok && row < args.m && col0 < args.n) {
-      float *crow = args.c + row * args.ldc + col0;
-      const bool vec = ((args.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.c) & 15) == 0) &&
-                       col0 + CPT <= args.n;
+      float *crow = args.c + (int64_t)blockIdx.z * args.batch_stride_c + row * args.ldc + col0;
+      const float divisor = args.div_ptr ? __ldg(args.div_ptr) : args.div_value;
+      const bool divide = args.div_ptr != nullptr || args.div_value != 1.0f;
+      const bool vec = ((args.ldc & 3) == 0) && ((args.batch_stride_c & 3) == 0) &&
+                       ((reinterpret_cast<uintptr_t>(args.c) & 15) == 0) && col0 + CPT <= args.n;
 #pragma unroll
       for (int j = 0; j < CPT; ++j) {
         float x = acc[j];
+        if (divide) x = __fdiv_rn(x, divisor);
         if (args.bias) x = __fadd_rn(x, (col0 + j < args.n) ? __ldg(args.bias + col0 + j) : 0.0f);
         if (args.relu) x = x > 0.0f ? x : 0.0f;
         acc[j] = x;
@@ -322,17 +321,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// K-major FP32 operand [rows, Kp]: box [box_rows, SW/4] with the SW-byte swizzle.
-int make_operand_map(b2k_ctx *ctx, CUtensorMap *map, const float *base, int64_t rows, int64_t Kp, int box_rows,
-                     int sw) {
+// K-major FP32 operand [batch][rows][Kp]: box [1, box_rows, SW/4] with the
+// SW-byte swizzle.
+int make_operand_map(b2k_ctx *ctx, CUtensorMap *map, const float *base, int64_t rows, int64_t Kp, int64_t batch,
+                     int box_rows, int sw) {
   auto encode = encode_fn();
   if (!encode) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
-  cuuint32_t box[2] = {(cuuint32_t)(sw / 4), (cuuint32_t)box_rows};
-  cuuint32_t elem[2] = {1, 1};
+  cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)Kp * 4, (cuuint64_t)(rows * Kp * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)(sw / 4), (cuuint32_t)box_rows, 1};
+  cuuint32_t elem[3] = {1, 1, 1};
   const CUtensorMapSwizzle swizzle = sw == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, elem,
+  CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, elem,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (res != CUDA_SUCCESS) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)res);
@@ -340,20 +340,19 @@ int make_operand_map(b2k_ctx *ctx, CUtensorMap *map, const float *base, int64_t 
 }
 
 template <int BN, int SW, int STAGES>
-int launch_main(b2k_ctx *ctx, const float *a_hi, const float *a_lo, const float *b_hi, const float *b_lo,
-                int64_t Kp, GemmArgs args, cudaStream_t s) {
+int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, GemmArgs args, cudaStream_t s) {
   using Shape = GemmShape<BN, SW, STAGES>;
   CUtensorMap maps[4];
   int status;
-  if ((status = make_operand_map(ctx, &maps[0], a_hi, args.m, Kp, BM, SW)) != B2K_OK) return status;
-  if ((status = make_operand_map(ctx, &maps[1], a_lo, args.m, Kp, BM, SW)) != B2K_OK) return status;
-  if ((status = make_operand_map(ctx, &maps[2], b_hi, args.n, Kp, BN, SW)) != B2K_OK) return status;
-  if ((status = make_operand_map(ctx, &maps[3], b_lo, args.n, Kp, BN, SW)) != B2K_OK) return status;
-  args.num_kb = (int)(Kp / Shape::BK);
+  if ((status = make_operand_map(ctx, &maps[0], ops.a_hi, args.m, ops.kp, batch, BM, SW)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[1], ops.a_lo, args.m, ops.kp, batch, BM, SW)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[2], ops.b_hi, args.n, ops.kp, batch, BN, SW)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[3], ops.b_lo, args.n, ops.kp, batch, BN, SW)) != B2K_OK) return status;
+  args.num_kb = (int)(ops.kp / Shape::BK);
   auto kernel = gemm_tf32x3_kernel<BN, SW, STAGES>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: set smem");
-  dim3 grid((unsigned)((args.n + BN - 1) / BN), (unsigned)((args.m + BM - 1) / BM));
+  dim3 grid((unsigned)((args.n + BN - 1) / BN), (unsigned)((args.m + BM - 1) / BM), (unsigned)batch);
   kernel<<<grid, kThreads, Shape::kSmem, s>>>(maps[0], maps[1], maps[2], maps[3], args);
   return b2k::check_launch(ctx, "gemm launch");
 }
@@ -361,39 +360,62 @@ int launch_main(b2k_ctx *ctx, const float *a_hi, const float *a_lo, const float 
 }  // namespace
 
 // Kernel variant selector (tile width, swizzle, stage count); settable for
-// tuning through b2k_gemm_set_variant.
-static int g_gemm_variant = 0;
+// tuning through b2k_gemm_set_variant.  Outputs at most 128 wide always use
+// the 128-wide tile.
+static int g_gemm_variant = 1;
 
-// Shared by the public entry point and the attention path: split both
-// operands into `ws` (A_hi, A_lo: m x Kp; B_hi, B_lo: n x Kp) and run the
-// tensor-core kernel.  `b_kmajor`: B is stored [n, K] (else [K, n]).
+namespace b2k {
+
+int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t ld, int64_t bs, int64_t batch,
+               int64_t kp, float *hi, float *lo, cudaStream_t s) {
+  const bool vec = (ld % 4 == 0) && (bs % 4 == 0) && aligned16(src);
+  split_rows_kernel<<<ctx->sm_count * 8, 256, 0, s>>>(src, rows, k, ld, bs, batch, kp, hi, lo, vec);
+  return check_launch(ctx, "split_rows launch");
+}
+
+int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_t ld, int64_t bs, int64_t batch,
+                    int64_t kp, float *hi, float *lo, cudaStream_t s) {
+  if (batch > 65535) return fail(ctx, B2K_EINVAL, "split_transpose: batch exceeds 65535");
+  dim3 grid((unsigned)((n + 31) / 32), (unsigned)((kp + 31) / 32), (unsigned)batch);
+  split_transpose_kernel<<<grid, 256, 0, s>>>(src, k, n, ld, bs, kp, hi, lo);
+  return check_launch(ctx, "split_transpose launch");
+}
+
+int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
+              int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
+              cudaStream_t s) {
+  if (batch > 65535) return fail(ctx, B2K_EINVAL, "gemm: batch exceeds 65535");
+  GemmArgs args{c, bias, div_ptr, div_value, m, n, ldc, batch_stride_c, 0, relu, ctx->error_flag};
+  PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
+  if (n <= 128) return launch_main<128, 128, 3>(ctx, ops, batch, args, s);
+  switch (g_gemm_variant) {
+    case 0: return launch_main<256, 128, 2>(ctx, ops, batch, args, s);
+    case 2: return launch_main<128, 128, 3>(ctx, ops, batch, args, s);
+    default: return launch_main<256, 64, 4>(ctx, ops, batch, args, s);
+  }
+}
+
+}  // namespace b2k
+
+// Shared by the public entry points: split both operands into `ws` (A_hi,
+// A_lo: m x Kp; B_hi, B_lo: n x Kp) and run the tensor-core kernel.
+// `b_kmajor`: B is stored [n, K] (else [K, n]).
 int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                          int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu,
                          float *ws, cudaStream_t s) {
-  const int64_t Kp = (k + KPAD - 1) / KPAD * KPAD;
-  float *a_hi = ws, *a_lo = ws + m * Kp, *b_hi = ws + 2 * m * Kp, *b_lo = ws + 2 * m * Kp + n * Kp;
-  const int grid_split = ctx->sm_count * 8;
+  const int64_t kp = b2k::gemm_kpad(k);
+  b2k::SplitOperands ops{ws, ws + m * kp, ws + 2 * m * kp, ws + 2 * m * kp + n * kp, kp};
+  int status;
   {
     b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
-    split_rows_kernel<<<grid_split, 256, 0, s>>>(a, m, k, lda, Kp, a_hi, a_lo,
-                                                 (lda % 4 == 0) && b2k::aligned16(a));
-    if (b_kmajor) {
-      split_rows_kernel<<<grid_split, 256, 0, s>>>(b, n, k, ldb, Kp, b_hi, b_lo,
-                                                   (ldb % 4 == 0) && b2k::aligned16(b));
-    } else {
-      dim3 grid((unsigned)((n + 31) / 32), (unsigned)((Kp + 31) / 32));
-      split_transpose_kernel<<<grid, 256, 0, s>>>(b, k, n, ldb, Kp, b_hi, b_lo);
+    status = b2k::split_rows(ctx, a, m, k, lda, m * lda, 1, kp, ops.a_hi, ops.a_lo, s);
+    if (status == B2K_OK) {
+      status = b_kmajor ? b2k::split_rows(ctx, b, n, k, ldb, n * ldb, 1, kp, ops.b_hi, ops.b_lo, s)
+                        : b2k::split_transpose(ctx, b, k, n, ldb, k * ldb, 1, kp, ops.b_hi, ops.b_lo, s);
     }
   }
-  int status = b2k::check_launch(ctx, "gemm split launch");
   if (status != B2K_OK) return status;
-  GemmArgs args{c, bias, m, n, ldc, 0, relu, ctx->error_flag};
-  b2k::PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
-  switch (g_gemm_variant) {
-    case 1: return launch_main<256, 64, 4>(ctx, a_hi, a_lo, b_hi, b_lo, Kp, args, s);
-    case 2: return launch_main<128, 128, 3>(ctx, a_hi, a_lo, b_hi, b_lo, Kp, args, s);
-    default: return launch_main<256, 128, 2>(ctx, a_hi, a_lo, b_hi, b_lo, Kp, args, s);
-  }
+  return b2k::gemm_main(ctx, ops, m, n, 1, c, ldc, m * ldc, bias, relu, nullptr, 1.0f, s);
 }
 
 extern "C" int b2k_gemm_set_variant(int variant) {
@@ -403,8 +425,7 @@ extern "C" int b2k_gemm_set_variant(int variant) {
 }
 
 size_t b2k_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
-  const int64_t Kp = (k + KPAD - 1) / KPAD * KPAD;
-  return (size_t)(2 * (m + n) * Kp) * sizeof(float);
+  return (size_t)(2 * (m + n) * b2k::gemm_kpad(k)) * sizeof(float);
 }
 
 extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n,
@@ -419,17 +440,14 @@ extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, flo
     return b2k::fail(ctx, B2K_EINVAL, "gemm: leading dimension too small");
   if (m > INT32_MAX - 256 || n > INT32_MAX - 256 || k > INT32_MAX - 64)
     return b2k::fail(ctx, B2K_EINVAL, "gemm: extent exceeds 32-bit TMA coordinates");
+  cudaStream_t s = (cudaStream_t)stream;
   if (k == 0) {
     // Empty contraction: C = epilogue(0).
-    cudaStream_t s = (cudaStream_t)stream;
-    for (int64_t r = 0; r < m; ++r) {
-      cudaError_t err = cudaMemsetAsync(c + r * ldc, 0, (size_t)n * 4, s);
-      if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: zero fill");
-    }
-    if (!bias) return B2K_OK;
-    return b2k::fail(ctx, B2K_EUNSUPPORTED, "gemm: bias with K = 0");
+    if (bias) return b2k::fail(ctx, B2K_EUNSUPPORTED, "gemm: bias with K = 0");
+    cudaError_t err = cudaMemset2DAsync(c, (size_t)ldc * 4, 0, (size_t)n * 4, (size_t)m, s);
+    if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: zero fill");
+    return B2K_OK;
   }
-  cudaStream_t s = (cudaStream_t)stream;
   int status = b2k::reserve_workspace(ctx, b2k_gemm_workspace_bytes(m, n, k), s);
   if (status != B2K_OK) return status;
   return b2k_gemm_tf32x3_impl(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu,

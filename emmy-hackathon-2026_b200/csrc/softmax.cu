@@ -36,16 +36,55 @@ __device__ __forceinline__ float block_sum(float v, float *scratch) {
   return r;
 }
 
+// Where a normalised row goes: a plain FP32 row, or (for the attention path)
+// the TF32 hi/lo halves of the row, zero padded to `pad4` float4 chunks, in
+// the K-major layout the 3xTF32 GEMM reads as its A operand.
+struct PlainSink {
+  float *y;
+  int64_t ldy;
+  __device__ __forceinline__ void put4(int64_t row, int64_t c4, float4 o) const {
+    st_stream(reinterpret_cast<float4 *>(y + row * ldy) + c4, o);
+  }
+  __device__ __forceinline__ void put(int64_t row, int64_t c, float o) const { y[row * ldy + c] = o; }
+  __device__ __forceinline__ void finish_row(int64_t, int64_t) const {}
+};
+
+struct SplitSink {
+  float *hi, *lo;
+  int64_t kp;  // padded row length (multiple of 32)
+  __device__ __forceinline__ void put4(int64_t row, int64_t c4, float4 o) const {
+    float4 h, l;
+    split_tf32(o.x, h.x, l.x);
+    split_tf32(o.y, h.y, l.y);
+    split_tf32(o.z, h.z, l.z);
+    split_tf32(o.w, h.w, l.w);
+    st_stream(reinterpret_cast<float4 *>(hi + row * kp) + c4, h);
+    st_stream(reinterpret_cast<float4 *>(lo + row * kp) + c4, l);
+  }
+  __device__ __forceinline__ void put(int64_t row, int64_t c, float o) const {
+    float h, l;
+    split_tf32(o, h, l);
+    hi[row * kp + c] = h;
+    lo[row * kp + c] = l;
+  }
+  // zero the padding columns [cols, kp) of the row
+  __device__ __forceinline__ void finish_row(int64_t row, int64_t cols) const {
+    for (int64_t c = cols + threadIdx.x; c < kp; c += blockDim.x) {
+      hi[row * kp + c] = 0.0f;
+      lo[row * kp + c] = 0.0f;
+    }
+  }
+};
+
 // VPT float4 chunks per thread; the row (cols4 = cols/4 chunks) must satisfy
 // cols4 <= kThreads * VPT.  Rows are 16-byte aligned.
-template <int VPT>
-__global__ void __launch_bounds__(kThreads) softmax_rows_vec(const float *__restrict__ x, float *__restrict__ y,
-                                                             int64_t cols4, int64_t ldx, int64_t ldy) {
+template <int VPT, class Sink>
+__global__ void __launch_bounds__(kThreads) softmax_rows_vec(const float *__restrict__ x, const Sink sink,
+                                                             int64_t cols4, int64_t ldx) {
   __shared__ float red_max[kWarps];
   __shared__ float red_sum[kWarps];
   const int64_t row = blockIdx.x;
   const float4 *xr = reinterpret_cast<const float4 *>(x + row * ldx);
-  float4 *yr = reinterpret_cast<float4 *>(y + row * ldy);
   float4 v[VPT];
   float m = -INFINITY;
 #pragma unroll
@@ -80,21 +119,22 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_vec(const float *__rest
       o.y = __fmul_rn(v[k].y, r);
       o.z = __fmul_rn(v[k].z, r);
       o.w = __fmul_rn(v[k].w, r);
-      st_stream(yr + c, o);
+      sink.put4(row, c, o);
     }
   }
+  sink.finish_row(row, cols4 * 4);
 }
 
 // Any row length / alignment: three passes over the row (max, exp-sum,
 // normalise) with scalar coalesced accesses; later passes hit L2 for rows
 // that fit there.
-__global__ void __launch_bounds__(kThreads) softmax_rows_generic(const float *__restrict__ x, float *__restrict__ y,
-                                                                 int64_t cols, int64_t ldx, int64_t ldy) {
+template <class Sink>
+__global__ void __launch_bounds__(kThreads) softmax_rows_generic(const float *__restrict__ x, const Sink sink,
+                                                                 int64_t cols, int64_t ldx) {
   __shared__ float red_max[kWarps];
   __shared__ float red_sum[kWarps];
   const int64_t row = blockIdx.x;
   const float *xr = x + row * ldx;
-  float *yr = y + row * ldy;
   float m = -INFINITY;
   for (int64_t c = threadIdx.x; c < cols; c += kThreads) m = fmaxf(m, __ldg(xr + c));
   m = block_max(m, red_max);
@@ -102,7 +142,21 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_generic(const float *__
   for (int64_t c = threadIdx.x; c < cols; c += kThreads) s += b2k_exp(__fsub_rn(__ldg(xr + c), m));
   s = block_sum(s, red_sum);
   const float r = __frcp_rn(s);
-  for (int64_t c = threadIdx.x; c < cols; c += kThreads) yr[c] = __fmul_rn(b2k_exp(__fsub_rn(__ldg(xr + c), m)), r);
+  for (int64_t c = threadIdx.x; c < cols; c += kThreads) sink.put(row, c, __fmul_rn(b2k_exp(__fsub_rn(__ldg(xr + c), m)), r));
+  sink.finish_row(row, cols);
+}
+
+template <class Sink>
+void launch_rows(const float *x, const Sink &sink, int64_t rows, int64_t cols, int64_t ld_x, bool vec,
+                 cudaStream_t s) {
+  const int64_t cols4 = cols / 4;
+  const int grid = (int)rows;
+  if (vec && cols4 <= kThreads * 1) softmax_rows_vec<1><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
+  else if (vec && cols4 <= kThreads * 2) softmax_rows_vec<2><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
+  else if (vec && cols4 <= kThreads * 4) softmax_rows_vec<4><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
+  else if (vec && cols4 <= kThreads * 8) softmax_rows_vec<8><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
+  else if (vec && cols4 <= kThreads * 16) softmax_rows_vec<16><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
+  else softmax_rows_generic<<<grid, kThreads, 0, s>>>(x, sink, cols, ld_x);
 }
 
 __global__ void selective_exp_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t n) {
@@ -122,17 +176,24 @@ extern "C" int b2k_row_softmax_f32(b2k_ctx *ctx, const float *x, float *y, int64
   if (rows > INT32_MAX) return b2k::fail(ctx, B2K_EINVAL, "row_softmax: too many rows");
   cudaStream_t s = (cudaStream_t)stream;
   const bool vec = (cols % 4 == 0) && (ld_x % 4 == 0) && (ld_y % 4 == 0) && b2k::aligned16(x) && b2k::aligned16(y);
-  const int64_t cols4 = cols / 4;
-  const int grid = (int)rows;
   b2k::PhaseTimer timer(ctx, B2K_PHASE_SOFTMAX, s);
-  if (vec && cols4 <= kThreads * 1) softmax_rows_vec<1><<<grid, kThreads, 0, s>>>(x, y, cols4, ld_x, ld_y);
-  else if (vec && cols4 <= kThreads * 2) softmax_rows_vec<2><<<grid, kThreads, 0, s>>>(x, y, cols4, ld_x, ld_y);
-  else if (vec && cols4 <= kThreads * 4) softmax_rows_vec<4><<<grid, kThreads, 0, s>>>(x, y, cols4, ld_x, ld_y);
-  else if (vec && cols4 <= kThreads * 8) softmax_rows_vec<8><<<grid, kThreads, 0, s>>>(x, y, cols4, ld_x, ld_y);
-  else if (vec && cols4 <= kThreads * 16) softmax_rows_vec<16><<<grid, kThreads, 0, s>>>(x, y, cols4, ld_x, ld_y);
-  else softmax_rows_generic<<<grid, kThreads, 0, s>>>(x, y, cols, ld_x, ld_y);
+  launch_rows(x, PlainSink{y, ld_y}, rows, cols, ld_x, vec, s);
   return b2k::check_launch(ctx, "row_softmax launch");
 }
+
+namespace b2k {
+
+// Row softmax whose output is written as the TF32 hi/lo split [rows][kp]
+// (zero padded), ready to be the A operand of the 3xTF32 GEMM.
+int softmax_split_rows(b2k_ctx *ctx, const float *x, int64_t rows, int64_t cols, int64_t ld_x, float *hi,
+                       float *lo, int64_t kp, cudaStream_t s) {
+  if (rows > INT32_MAX) return fail(ctx, B2K_EINVAL, "softmax_split: too many rows");
+  const bool vec = (cols % 4 == 0) && (ld_x % 4 == 0) && aligned16(x) && aligned16(hi) && aligned16(lo);
+  launch_rows(x, SplitSink{hi, lo, kp}, rows, cols, ld_x, vec, s);
+  return check_launch(ctx, "softmax_split launch");
+}
+
+}  // namespace b2k
 
 extern "C" int b2k_selective_exp_f32(b2k_ctx *ctx, const float *x, float *y, int64_t n, void *stream) {
   B2K_CHECK_CTX(ctx);

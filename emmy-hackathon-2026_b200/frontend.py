@@ -77,7 +77,7 @@ class KernelSpec:
         elif self.kind == "attention":
             ctx.attention(pointers[p["q"]], pointers[p["kt"]], pointers[p["v"]], pointers[p["out"]],
                           1, p["s_q"], p["s_kv"], p["d"], p["dv"], scale_ptr=pointers[p["scale"]],
-                          k_layout=1, stream=stream)
+                          k_layout=runtime.K_DS, stream=stream)
         else:
             raise Unsupported(f"no launcher for {self.kind}")
 

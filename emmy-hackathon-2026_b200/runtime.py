@@ -19,6 +19,7 @@ STATUS_NAMES = {B2K_EINVAL: "EINVAL", B2K_EUNSUPPORTED: "EUNSUPPORTED", B2K_ECUD
 
 PW_MAX_INPUTS, PW_MAX_INSNS = 8, 48
 B_KN, B_NK = 0, 1
+K_SD, K_DS = 0, 1
 
 OPCODES = {
     "const": 0, "copy": 1, "add": 2, "subtract": 3, "multiply": 4, "divide": 5, "maximum": 6,
@@ -67,6 +68,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_selective_exp_f32": ([_P, _P, _P, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
+    "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_timing_enable": ([_P, C.c_int], C.c_int),
     "b2k_timing_read": ([_P, C.c_int, C.POINTER(C.c_double), C.POINTER(_I64)], C.c_int),
@@ -171,6 +173,13 @@ class Context:
         ldc = n if ldc is None else ldc
         self.check(self.lib.b2k_gemm_tf32x3(self.handle, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias or None,
                                             int(relu), stream), "b2k_gemm_tf32x3")
+
+    def attention(self, q: int, k: int, v: int, o: int, bh: int, s_q: int, s_kv: int, d: int, dv: int, *,
+                  scale: float | None = None, scale_ptr: int = 0, k_layout: int = K_SD, stream: int = 0) -> None:
+        """O = softmax(Q K^T / scale) V per head; scale defaults to sqrt(d)."""
+        div = float(d) ** 0.5 if scale is None else float(scale)
+        self.check(self.lib.b2k_attention_tf32x3(self.handle, q, k, v, o, bh, s_q, s_kv, d, dv, div,
+                                                 scale_ptr or None, k_layout, stream), "b2k_attention_tf32x3")
 
     def timing(self, on: bool) -> None:
         self.check(self.lib.b2k_timing_enable(self.handle, int(on)), "b2k_timing_enable")

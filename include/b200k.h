@@ -172,6 +172,22 @@ int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int6
                     int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
                     void *stream);
 
+/* --- attention ----------------------------------------------------------------
+ * Replaces the reference's fused SIMT attention lowering (compile.py:7009-7966:
+ * hoisted score rows, selective-exp softmax, P.V fold) for every head of a
+ * batch: O[h] = softmax(Q[h] K[h]^T / scale) V[h] for h < bh, both contractions
+ * as 3xTF32 on the tensor cores.  Q is [bh][s_q][d], V is [bh][s_kv][dv], O
+ * is [bh][s_q][dv] (all row-major, contiguous).  k_layout B2K_K_SD: K is
+ * [bh][s_kv][d]; B2K_K_DS: K is given transposed as [bh][d][s_kv] (the IR's
+ * `kt`).  The divisor is *scale_div_ptr when that device pointer is non-NULL
+ * (the IR's one-element `div_c1` buffer), else scale_div.  Uses context
+ * scratch for the split operands, S and P. */
+#define B2K_K_SD 0
+#define B2K_K_DS 1
+int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k, const float *v, float *o, int64_t bh,
+                         int64_t s_q, int64_t s_kv, int64_t d, int64_t dv, float scale_div,
+                         const float *scale_div_ptr, int32_t k_layout, void *stream);
+
 /* The same GEMM for callers that cannot allocate device memory (code running
  * under CUDA-graph capture or a fixed memory plan, or memory owned by another
  * allocator).  No counterpart in the reference.  It takes no context and
@@ -194,9 +210,9 @@ int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c, int64_t m,
                             int32_t relu, void *stream);
 
 /* Select the GEMM kernel variant for subsequent calls (process-wide; for
- * tuning and benchmarking): 0 = 128x256 tile, 128-byte swizzle, 2 stages
- * (default); 1 = 128x256, 64-byte swizzle, 4 stages; 2 = 128x128,
- * 128-byte swizzle, 3 stages.  No counterpart in the reference, whose plan
+ * tuning and benchmarking): 0 = 128x256 tile, 128-byte swizzle, 2 stages;
+ * 1 = 128x256, 64-byte swizzle, 4 stages (default); 2 = 128x128, 128-byte
+ * swizzle, 3 stages.  Outputs at most 128 columns wide always use 2.  No counterpart in the reference, whose plan
  * geometry comes from the IR. */
 int b2k_gemm_set_variant(int variant);
 

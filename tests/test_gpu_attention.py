@@ -1,0 +1,65 @@
+"""GPU parity of the batched 3xTF32 attention through the C ABI against the
+float64 reference (attention family tolerance: rtol 1e-3, atol 1e-4,
+tools/research_cases.py:30-35)."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from conftest import pkg
+from oracle import refs
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-3, 1e-4
+
+
+def run(ctx, torch, q, k, v, *, k_layout=0, scale=None, scale_buf=None):
+    bh, s_q, d = q.shape
+    s_kv, dv = v.shape[1], v.shape[2]
+    dq, dk, dvv = (torch.from_numpy(np.ascontiguousarray(t)).cuda() for t in (q, k, v))
+    do = torch.full((bh, s_q, dv), float("nan"), device="cuda")
+    sb = torch.from_numpy(np.asarray([scale_buf], np.float32)).cuda() if scale_buf is not None else None
+    ctx.attention(dq.data_ptr(), dk.data_ptr(), dvv.data_ptr(), do.data_ptr(), bh, s_q, s_kv, d, dv,
+                  scale=scale, scale_ptr=sb.data_ptr() if sb is not None else 0, k_layout=k_layout)
+    ctx.sync()
+    return do.cpu().numpy()
+
+
+@pytest.mark.parametrize("bh,s_q,s_kv,d,dv", [(2, 128, 128, 64, 64), (3, 100, 77, 48, 16), (1, 12, 3, 48, 16),
+                                              (4, 256, 512, 128, 128), (1, 9, 19, 19, 7), (2, 200, 300, 32, 40)])
+@pytest.mark.parametrize("k_layout", [0, 1])
+def test_attention_matches_float64(ctx, torch_cuda, bh, s_q, s_kv, d, dv, k_layout):
+    rng = np.random.default_rng(bh * 1000 + s_q + s_kv + d)
+    q = rng.standard_normal((bh, s_q, d)).astype(np.float32)
+    k = rng.standard_normal((bh, s_kv, d)).astype(np.float32)
+    v = rng.standard_normal((bh, s_kv, dv)).astype(np.float32)
+    kin = k if k_layout == 0 else np.ascontiguousarray(k.transpose(0, 2, 1))
+    got = run(ctx, torch_cuda, q, kin, v, k_layout=k_layout)
+    want = refs.attention_batched(q, k, v, math.sqrt(d))
+    ok, bad, err = refs.allclose_report(got, want, RTOL, ATOL)
+    assert ok, (bad, err)
+
+
+def test_attention_scale_from_device_buffer(ctx, torch_cuda):
+    """The IR passes the divisor as a one-element buffer (a01's div_c1 = 8)."""
+    rng = np.random.default_rng(1)
+    q, k, v = (rng.standard_normal((1, 64, 64)).astype(np.float32) for _ in range(3))
+    got = run(ctx, torch_cuda, q, k, v, scale_buf=8.0)
+    want = refs.attention_batched(q, k, v, 8.0)
+    ok, bad, err = refs.allclose_report(got, want, RTOL, ATOL)
+    assert ok, (bad, err)
+
+
+def test_attention_baseline_config_sampled_heads(ctx, torch_cuda):
+    """4 x 16 heads, S 2048, D 128: two heads checked in full against float64."""
+    workloads = pkg("workloads")
+    q, k, v = workloads.attention_inputs()
+    got = run(ctx, torch_cuda, q, k, v)
+    for h in (0, 37):
+        want = refs.attention_batched(q[h:h + 1], k[h:h + 1], v[h:h + 1], math.sqrt(128))
+        ok, bad, err = refs.allclose_report(got[h:h + 1], want, RTOL, ATOL)
+        assert ok, (h, bad, err)
+    assert np.isfinite(got).all()
