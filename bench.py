@@ -428,15 +428,13 @@ def init_dist():
 
 
 def run_ours(args) -> dict | None:
-    import datetime
-
     import torch
     rank, local, world = init_dist()
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        pkg("mgpu").init_from_env("nccl", timeout_s=120)
     runtime, api = pkg("runtime"), pkg("api")
     ctx = runtime.Context(local)
     w = make_workload(args.workload, rank, world)
