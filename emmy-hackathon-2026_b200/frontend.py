@@ -46,7 +46,7 @@ class Unsupported(ValueError):
 class KernelSpec:
     """A recognised kernel: which C-ABI entry point runs it and with what roles."""
 
-    kind: str                  # pointwise | row_softmax | matmul | attention
+    kind: str                  # pointwise | row_softmax | matmul | attention | row_reduce | row_norm
     entry: str
     node: str
     arg_order: list
@@ -78,6 +78,17 @@ class KernelSpec:
             ctx.attention(pointers[p["q"]], pointers[p["kt"]], pointers[p["v"]], pointers[p["out"]],
                           1, p["s_q"], p["s_kv"], p["d"], p["dv"], scale_ptr=pointers[p["scale"]],
                           k_layout=runtime.K_DS, stream=stream)
+        elif self.kind == "row_reduce":
+            buf = p["sum_div_buffer"]
+            ctx.row_op(runtime.ROW_SUM, pointers[p["x"]], pointers[p["out"]], p["rows"], p["cols"],
+                       sum_div=p["sum_div"], sum_div_ptr=pointers[buf] if buf else 0, stream=stream)
+        elif self.kind == "row_norm":
+            op = runtime.ROW_RMSNORM if p["op"] == "rmsnorm" else runtime.ROW_L2NORM
+            eb, cb = p["eps_buffer"], p["count_buffer"]
+            ctx.row_op(op, pointers[p["x"]], pointers[p["out"]], p["rows"], p["cols"],
+                       ms_div=float(p["cols"]) if p["op"] == "rmsnorm" else 1.0,
+                       ms_div_ptr=pointers[cb] if cb else 0, eps=p["eps"], eps_ptr=pointers[eb] if eb else 0,
+                       w=pointers[p["w"]] if p["w"] else 0, stream=stream)
         else:
             raise Unsupported(f"no launcher for {self.kind}")
 
@@ -185,11 +196,15 @@ def _estimate_statements(body, depth_limit=6) -> int:
     return count(body, 0)
 
 
-def certify(node, kernel, args, inputs, outputs, expected_fn, rtol=1e-9, atol=1e-12) -> dict:
+def certify(node, kernel, args, inputs, outputs, expected_fn, rtol=1e-9, atol=1e-12, fit=False,
+            seed=12345) -> dict:
     """Execute the IR on seeded random inputs and compare with ``expected_fn``.
 
     Every CTA is executed when the launch is small; otherwise the first, last
-    and two seeded random CTAs.  Returns the certificate record."""
+    and two seeded random CTAs.  With ``fit``, ``expected_fn(inputs, produced)``
+    also sees what the IR produced ({name: (values, written mask)}) so that a
+    family can first fit its free constants (an epsilon, a divisor) and then
+    must reproduce every written value with them.  Returns the certificate."""
     grid, block = math.prod(kernel["grid"]), math.prod(kernel["block"])
     per_lane = _estimate_statements(node.body)
     atomic = any(s.kind == "Write" and s.get("atomic") for s in walk(node.body))
@@ -201,7 +216,7 @@ def certify(node, kernel, args, inputs, outputs, expected_fn, rtol=1e-9, atol=1e
     else:
         rng = np.random.default_rng(7)
         ctas = sorted({0, grid - 1, *rng.integers(0, grid, SAMPLE_CTAS - 2).tolist()})
-    buffers = _random_inputs(args, inputs)
+    buffers = _random_inputs(args, inputs, seed)
     shapes = {name: _shape(args[name]) for name in args}
     for name in outputs:
         buffers[name] = np.full(shapes[name] or (1,), np.nan)
@@ -211,7 +226,12 @@ def certify(node, kernel, args, inputs, outputs, expected_fn, rtol=1e-9, atol=1e
         launch = irexec.execute(node.body, grid, block, ctas, buffers, shapes)
     except irexec.ExecError as exc:
         raise Unsupported(f"IR outside the executable subset: {exc}") from exc
-    expected = expected_fn({k: buffers[k] for k in inputs})
+    if fit:
+        produced = {name: (buffers[name].reshape(-1), launch.writes.get(name, np.zeros(1, np.int64)) > 0)
+                    for name in outputs}
+        expected = expected_fn({k: buffers[k] for k in inputs}, produced)
+    else:
+        expected = expected_fn({k: buffers[k] for k in inputs})
     checked = 0
     for name in outputs:
         counts = launch.writes.get(name)
@@ -407,11 +427,130 @@ def classify_attention(node, kernel, args, inputs, outputs):
     raise last or Unsupported("attention: shapes do not form softmax(q kt / s) v")
 
 
+# --------------------------------------------------------------------------- row family
+def _scalar_inputs(args, inputs):
+    return [n for n in inputs if _size(_shape(args[n])) == 1]
+
+
+def _bind_constant(args, scalars, value, rel=1e-9):
+    """A one-element metadata buffer holding ``value`` (so the kernel reads the
+    buffer at run time), else None."""
+    for name in scalars:
+        data = args[name].get("data")
+        if data is not None and abs(float(data[0]) - value) <= rel * max(1.0, abs(value)):
+            return name
+    return None
+
+
+def classify_row_reduce(node, kernel, args, inputs, outputs):
+    if len(outputs) != 1:
+        raise Unsupported("row_reduce: one output")
+    out = outputs[0]
+    scalars = _scalar_inputs(args, inputs)
+    mats = [n for n in inputs if n not in scalars]
+    if len(mats) != 1:
+        raise Unsupported("row_reduce: one data input")
+    x = mats[0]
+    xs, ys = _shape(args[x]), _shape(args[out])
+    if len(xs) == 2 and _size(ys) == xs[0] and xs[0] > 1:
+        rows, cols = xs
+    elif len(xs) == 1 and _size(ys) == 1:
+        rows, cols = 1, xs[0]
+    else:
+        raise Unsupported("row_reduce: output is not one value per row")
+    if not any(s.kind == "Accum" and s.op.name == "add" for s in walk(node.body)):
+        raise Unsupported("row_reduce: no additive fold")
+    fitted = {}
+
+    def expect(buf, produced):
+        sums = buf[x].reshape(rows, cols).sum(axis=1)
+        vals, written = produced[out]
+        ok = written & (np.abs(vals) > 1e-30)
+        if not ok.any():
+            raise Unsupported("row_reduce: no output to fit")
+        div = float(np.median(sums[ok] / vals[ok]))
+        fitted["div"] = div
+        return {out: sums / div}
+
+    cert = certify(node, kernel, args, inputs, outputs, expect, fit=True)
+    div = fitted["div"]
+    # A fitted constant must hold on fresh inputs too (one output value alone
+    # would fit any divisor).
+    certify(node, kernel, args, inputs, outputs,
+            lambda buf: {out: buf[x].reshape(rows, cols).sum(axis=1) / div}, seed=777)
+    ptr = _bind_constant(args, scalars, div)
+    if abs(div - round(div)) < 1e-9 * max(1.0, abs(div)):
+        div = float(round(div))
+    return {"op": "sum", "x": x, "out": out, "rows": rows, "cols": cols, "sum_div": div,
+            "sum_div_buffer": ptr}, cert
+
+
+def classify_row_norm(node, kernel, args, inputs, outputs):
+    if len(outputs) != 1:
+        raise Unsupported("row_norm: one output")
+    out = outputs[0]
+    shape = _shape(args[out])
+    if len(shape) != 2:
+        raise Unsupported("row_norm: rank-2 output")
+    rows, cols = shape
+    scalars = _scalar_inputs(args, inputs)
+    xs = [n for n in inputs if _shape(args[n]) == shape]
+    ws = [n for n in inputs if _shape(args[n]) == (cols,) and n not in scalars]
+    if len(xs) != 1 or len(ws) > 1 or len(xs) + len(ws) + len(scalars) != len(inputs):
+        raise Unsupported("row_norm: x [rows, cols], optional w [cols] and scalar buffers")
+    x = xs[0]
+    w = ws[0] if ws else None
+    if not any(s.kind == "Assign" and s.op.name in ("sqrt", "rsqrt") for s in walk(node.body)):
+        raise Unsupported("row_norm: no square root")
+    last = None
+    for op in ("rmsnorm", "l2norm"):
+        fitted = {}
+
+        def expect(buf, produced, op=op):
+            xv = buf[x].reshape(rows, cols)
+            wv = buf[w].reshape(1, cols) if w else np.ones((1, cols))
+            ms = (xv * xv).sum(axis=1, keepdims=True) / (cols if op == "rmsnorm" else 1)
+            vals, written = produced[out]
+            vals = vals.reshape(rows, cols)
+            mask = written.reshape(rows, cols) & (np.abs(vals) > 1e-12) & (np.abs(xv * wv) > 1e-6)
+            if not mask.any():
+                raise Unsupported("row_norm: nothing to fit")
+            eps = float(np.median((((xv * wv) / np.where(mask, vals, 1.0)) ** 2 - ms)[mask]))
+            fitted["eps"] = eps
+            return {out: xv * wv / np.sqrt(ms + eps)}
+        def recheck(buf, op=op):
+            xv = buf[x].reshape(rows, cols)
+            wv = buf[w].reshape(1, cols) if w else np.ones((1, cols))
+            ms = (xv * xv).sum(axis=1, keepdims=True) / (cols if op == "rmsnorm" else 1)
+            return {out: xv * wv / np.sqrt(ms + fitted["eps"])}
+        try:
+            cert = certify(node, kernel, args, inputs, outputs, expect, fit=True, rtol=1e-7, atol=1e-10)
+            certify(node, kernel, args, inputs, outputs, recheck, rtol=1e-7, atol=1e-10, seed=777)
+        except Unsupported as exc:
+            last = exc
+            continue
+        eps = fitted["eps"]
+        # prefer the IR's own literal when the fit reproduces it
+        for lit in (st.value.value for st in walk(node.body) if st.kind == "Let" and isinstance(st.value, Node)
+                    and st.value.kind == "Literal" and isinstance(st.value.value, float)):
+            if abs(lit - eps) <= 1e-6 * max(abs(lit), 1e-30):
+                eps = lit
+        if abs(eps) < 1e-12:
+            eps = 0.0
+        eps_buffer = _bind_constant(args, scalars, eps, rel=1e-6) if eps else None
+        count_buffer = _bind_constant(args, scalars, float(cols)) if op == "rmsnorm" else None
+        return {"op": op, "x": x, "w": w, "out": out, "rows": rows, "cols": cols, "eps": eps,
+                "eps_buffer": eps_buffer, "count_buffer": count_buffer}, cert
+    raise last or Unsupported("row_norm: neither rms nor l2 normalisation")
+
+
 FAMILIES = (
     ("pointwise", classify_pointwise),
     ("row_softmax", classify_row_softmax),
     ("matmul", classify_matmul),
     ("attention", classify_attention),
+    ("row_reduce", classify_row_reduce),
+    ("row_norm", classify_row_norm),
 )
 
 

@@ -196,6 +196,8 @@ class CTAExecutor:
 
     # --- memory -----------------------------------------------------------------
     def _flat(self, shape, index, env):
+        if len(index) == 0 and int(np.prod(shape)) == 1:
+            return np.zeros(self.nlanes, dtype=np.int64)
         if len(index) != len(shape):
             raise ExecError("index rank differs from buffer rank")
         flat = 0

@@ -20,7 +20,8 @@ import numpy as np
 from . import api, frontend, runtime
 
 DTYPES = {"f32": np.float32}
-PHASE_OF = {"pointwise": "pointwise", "row_softmax": "softmax", "matmul": "mma", "attention": "attention"}
+PHASE_OF = {"pointwise": "pointwise", "row_softmax": "softmax", "matmul": "mma", "attention": "attention",
+            "row_reduce": "rows", "row_norm": "rows"}
 
 
 def array_for(arg) -> np.ndarray:

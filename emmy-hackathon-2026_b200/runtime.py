@@ -37,6 +37,14 @@ class B2KError(RuntimeError):
         super().__init__(f"{call}: {STATUS_NAMES.get(status, status)}: {reason}")
 
 
+class RowParams(C.Structure):
+    _fields_ = [("op", C.c_int32), ("sum_div", C.c_float), ("sum_div_ptr", C.c_void_p), ("ms_div", C.c_float),
+                ("ms_div_ptr", C.c_void_p), ("eps", C.c_float), ("eps_ptr", C.c_void_p), ("w", C.c_void_p)]
+
+
+ROW_SUM, ROW_RMSNORM, ROW_L2NORM = 0, 1, 2
+
+
 class PwInsn(C.Structure):
     _fields_ = [("op", C.c_int32), ("a", C.c_int32), ("b", C.c_int32), ("c", C.c_int32), ("imm", C.c_float)]
 
@@ -66,6 +74,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_pointwise_f32": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _P], C.c_int),
     "b2k_row_softmax_f32": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_selective_exp_f32": ([_P, _P, _P, _I64, _P], C.c_int),
+    "b2k_row_op_f32": ([_P, C.POINTER(RowParams), _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
@@ -75,7 +84,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_timing_reset": ([_P], C.c_int),
 }
 
-PHASES = {"split": 0, "mma": 1, "pointwise": 2, "softmax": 3, "attention": 4}
+PHASES = {"split": 0, "mma": 1, "pointwise": 2, "softmax": 3, "attention": 4, "rows": 5}
 
 _lock = threading.Lock()
 _lib: C.CDLL | None = None
@@ -161,6 +170,14 @@ class Context:
                     ld_y: int | None = None, stream: int = 0) -> None:
         self.check(self.lib.b2k_row_softmax_f32(self.handle, x, y, rows, cols, ld_x or cols, ld_y or cols, stream),
                    "b2k_row_softmax_f32")
+
+    def row_op(self, op: int, x: int, y: int, rows: int, cols: int, *, ld_x: int | None = None,
+               ld_y: int | None = None, sum_div: float = 1.0, sum_div_ptr: int = 0, ms_div: float = 1.0,
+               ms_div_ptr: int = 0, eps: float = 0.0, eps_ptr: int = 0, w: int = 0, stream: int = 0) -> None:
+        params = RowParams(op, sum_div, sum_div_ptr or None, ms_div, ms_div_ptr or None, eps, eps_ptr or None,
+                           w or None)
+        self.check(self.lib.b2k_row_op_f32(self.handle, C.byref(params), x, y, rows, cols, ld_x or cols,
+                                           ld_y or cols, stream), "b2k_row_op_f32")
 
     def selective_exp(self, x: int, y: int, n: int, stream: int = 0) -> None:
         self.check(self.lib.b2k_selective_exp_f32(self.handle, x, y, n, stream), "b2k_selective_exp_f32")

@@ -75,8 +75,9 @@ int b2k_stream_sync(b2k_ctx *ctx, void *stream);
 #define B2K_PHASE_MMA 1       /* tcgen05 GEMM main kernel */
 #define B2K_PHASE_POINTWISE 2 /* pointwise programs */
 #define B2K_PHASE_SOFTMAX 3   /* row softmax */
-#define B2K_PHASE_ATTENTION 4 /* fused attention */
-#define B2K_PHASE_COUNT 5
+#define B2K_PHASE_ATTENTION 4 /* attention (all of its passes) */
+#define B2K_PHASE_ROWS 5      /* row reductions / norms */
+#define B2K_PHASE_COUNT 6
 int b2k_timing_enable(b2k_ctx *ctx, int on);
 int b2k_timing_read(b2k_ctx *ctx, int phase, double *total_ms, int64_t *launches);
 int b2k_timing_reset(b2k_ctx *ctx);
@@ -147,6 +148,32 @@ int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, const float *
  * with leading dimensions ld_x / ld_y (elements). */
 int b2k_row_softmax_f32(b2k_ctx *ctx, const float *x, float *y, int64_t rows, int64_t cols,
                         int64_t ld_x, int64_t ld_y, void *stream);
+
+/* --- row reductions and row norms -------------------------------------------
+ * Replaces the Emitter's merged vector row reduction (compile.py:4987-5165,
+ * shuffles and trees 8958-9268) and row-map reuse (compile.py:5511-5665) for
+ * the reduction / rmsnorm / l2norm kernels:
+ *   B2K_ROW_SUM      y[r]    = (sum_c x[r,c]) / div                 (div = *sum_div_ptr or sum_div)
+ *   B2K_ROW_RMSNORM  y[r,c]  = x[r,c] * w[c] / sqrt(sum_c x^2 / count + eps)
+ *   B2K_ROW_L2NORM   y[r,c]  = x[r,c] * w[c] / sqrt(sum_c x^2 + eps)
+ * count = *ms_div_ptr or ms_div, eps = *eps_ptr or eps; w may be NULL (1).
+ * A single row longer than 65,536 (a whole-array sum) is reduced by many CTAs
+ * and a fixed-order second pass. */
+#define B2K_ROW_SUM 0
+#define B2K_ROW_RMSNORM 1
+#define B2K_ROW_L2NORM 2
+typedef struct b2k_row_params {
+  int32_t op;
+  float sum_div;
+  const float *sum_div_ptr;
+  float ms_div;
+  const float *ms_div_ptr;
+  float eps;
+  const float *eps_ptr;
+  const float *w;
+} b2k_row_params;
+int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const float *x, float *y, int64_t rows,
+                   int64_t cols, int64_t ld_x, int64_t ld_y, void *stream);
 
 /* Elementwise selective exponential (compile.py:2953-2965); exposed for the
  * subnormal-range accuracy tests. */

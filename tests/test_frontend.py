@@ -18,7 +18,15 @@ RECOGNISED = {
     "atomic_matmul-0-b0bb43becf74": ["matmul"],
     "atomic_matmul_7x5x9-variant": ["matmul"],
     "attention-0-9170e7b0641d": [None, "row_softmax", "matmul"],
+    "f01_rmsnorm-6ab09ab4acc3": ["row_norm"],
     "f02-extra-cta-120bf007fb2d": ["row_softmax"],
+    "f03_l2norm-1e82d7e58a53": ["row_norm"],
+    "l2norm-0-e8f4437dd934": ["row_norm"],
+    "r01_array_sum-2ffefe7fee88": ["row_reduce"],
+    "r02_big_sum-a56bdb784a46": ["row_reduce"],
+    "r03_mean-6dfbe2bc925e": ["row_reduce"],
+    "r04_row_sum-5c2ba872d36e": ["row_reduce"],
+    "rmsnorm-0-09d6470c83d3": ["row_norm"],
     "f02_row_softmax-89d56c168a0b": ["row_softmax"],
     "full-segment16-274cb67281df": ["attention"],
     "full-segment16-44c6e3443740": ["attention"],
@@ -126,6 +134,25 @@ def test_matmul_with_truncated_k_rejected():
     fe = pkg("frontend")
     with pytest.raises(fe.Unsupported):
         fe.compile_path(next((CASES / "case-7-72f1deeac451").glob("*.ir.json")))
+
+
+def test_row_constants_bound_to_metadata_buffers():
+    """f01's count and epsilon live in one-element buffers; the kernel must read
+    them at run time rather than bake the fitted values."""
+    fe = pkg("frontend")
+    p = fe.compile_path(CASES / "f01_rmsnorm-6ab09ab4acc3" / "k_mean_cbd1de.ir.json").params
+    assert (p["op"], p["w"], p["eps_buffer"], p["count_buffer"]) == ("rmsnorm", "w", "add_c1", "mean_count")
+    p = fe.compile_path(CASES / "r03_mean-6dfbe2bc925e" / "k_mean_ffcca3.ir.json").params
+    assert (p["sum_div"], p["sum_div_buffer"]) == (32768.0, "mean_keepdim_count")
+    p = fe.compile_path(next((CASES / "rmsnorm-0-09d6470c83d3").glob("*.ir.json"))).params
+    assert p["eps"] == 1e-05 and p["eps_buffer"] is None
+
+
+def test_one_value_fit_is_not_enough():
+    """A one-output kernel computing 4*x[0] must not pass as a scaled sum."""
+    fe = pkg("frontend")
+    with pytest.raises(fe.Unsupported):
+        fe.compile_path(next((CASES / "axis-rebound-before-load-e5a00bcecf77").glob("*.ir.json")))
 
 
 def test_cli_contract(capsys):

@@ -112,3 +112,49 @@ def test_selective_exp_subnormal_range(ctx, torch_cuda):
     assert report["ok"], report
     sub = (x > -103.0) & (x < -88.0)
     assert np.all(got[sub] > 0.0), "subnormal results were flushed"
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 8192), (64, 1024), (7, 3), (3, 20000)])
+def test_row_norms_match_float64(ctx, torch_cuda, rows, cols):
+    runtime = pkg("runtime")
+    rng = np.random.default_rng(rows + cols)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    w = rng.standard_normal(cols).astype(np.float32)
+    dx, dw = dev(torch_cuda, x), dev(torch_cuda, w)
+    y = torch_cuda.empty_like(dx)
+    ctx.row_op(runtime.ROW_RMSNORM, dx.data_ptr(), y.data_ptr(), rows, cols, ms_div=float(cols), eps=1e-5,
+               w=dw.data_ptr())
+    ctx.sync()
+    ok, bad, err = refs.allclose_report(y.cpu().numpy(), refs.rmsnorm(x, w, 1e-5), 1e-3, 1e-4)
+    assert ok, (bad, err)
+    ctx.row_op(runtime.ROW_L2NORM, dx.data_ptr(), y.data_ptr(), rows, cols)
+    ctx.sync()
+    ok, bad, err = refs.allclose_report(y.cpu().numpy(), refs.l2norm(x), 1e-3, 1e-4)
+    assert ok, (bad, err)
+
+
+@pytest.mark.parametrize("n", [1, 1000, 65536, 65537, 1 << 24])
+def test_whole_array_sum_deterministic(ctx, torch_cuda, n):
+    runtime = pkg("runtime")
+    x = np.random.default_rng(n).standard_normal(n).astype(np.float32)
+    dx = dev(torch_cuda, x)
+    y = torch_cuda.empty(1, device="cuda")
+    results = []
+    for _ in range(2):
+        ctx.row_op(runtime.ROW_SUM, dx.data_ptr(), y.data_ptr(), 1, n)
+        ctx.sync()
+        results.append(y.cpu().numpy().copy())
+    assert results[0].tobytes() == results[1].tobytes()  # fixed combination order
+    ok, bad, err = refs.allclose_report(results[0], refs.array_sum(x), 1e-4, 1e-3)
+    assert ok, (bad, err)
+
+
+def test_row_sums_and_means(ctx, torch_cuda):
+    runtime = pkg("runtime")
+    x = np.random.default_rng(4).standard_normal((64, 512)).astype(np.float32)
+    dx = dev(torch_cuda, x)
+    y = torch_cuda.empty(64, device="cuda")
+    ctx.row_op(runtime.ROW_SUM, dx.data_ptr(), y.data_ptr(), 64, 512, sum_div=512.0)
+    ctx.sync()
+    ok, bad, err = refs.allclose_report(y.cpu().numpy(), (refs.row_sum(x) / 512).astype(np.float32), 1e-4, 1e-6)
+    assert ok, (bad, err)
