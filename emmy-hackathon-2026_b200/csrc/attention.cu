@@ -17,7 +17,16 @@ namespace {
 
 inline int64_t round32(int64_t x) { return (x + 31) / 32 * 32; }
 
+// Force the three-pass path even where the fused kernel applies (tests and
+// benchmarks compare the two).
+int g_attention_unfused = 0;
+
 }  // namespace
+
+extern "C" int b2k_attention_set_fused(int fused) {
+  g_attention_unfused = fused ? 0 : 1;
+  return B2K_OK;
+}
 
 size_t b2k_attention_workspace_floats(int64_t bh, int64_t s_q, int64_t s_kv, int64_t d, int64_t dv) {
   const int64_t dp = b2k::gemm_kpad(d), sp = b2k::gemm_kpad(s_kv);
@@ -39,6 +48,13 @@ extern "C" int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k
     return b2k::fail(ctx, B2K_EINVAL, "attention: extent exceeds 32-bit TMA coordinates");
   if (!scale_div_ptr && !(scale_div != 0.0f)) return b2k::fail(ctx, B2K_EINVAL, "attention: zero scale divisor");
   cudaStream_t s = (cudaStream_t)stream;
+  if (b2k::flash_supported(d, dv) && !g_attention_unfused) {
+    int status = b2k::reserve_workspace(ctx, b2k::flash_workspace_floats(bh, s_q, s_kv, d, dv) * sizeof(float), s);
+    if (status != B2K_OK) return status;
+    b2k::PhaseTimer timer(ctx, B2K_PHASE_ATTENTION, s);
+    return b2k::flash_attention(ctx, q, k, v, o, bh, s_q, s_kv, d, dv, scale_div, scale_div_ptr, k_layout,
+                                static_cast<float *>(ctx->workspace), s);
+  }
   int status = b2k::reserve_workspace(ctx, b2k_attention_workspace_floats(bh, s_q, s_kv, d, dv) * sizeof(float), s);
   if (status != B2K_OK) return status;
   const int64_t dp = b2k::gemm_kpad(d), sp = b2k::gemm_kpad(s_kv);

@@ -86,6 +86,13 @@ int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_
 int softmax_split_rows(b2k_ctx *ctx, const float *x, int64_t rows, int64_t cols, int64_t ld_x, float *hi,
                        float *lo, int64_t kp, cudaStream_t s);
 
+// Fused attention (flash.cu): supported head dims, scratch, launch.
+bool flash_supported(int64_t d, int64_t dv);
+size_t flash_workspace_floats(int64_t bh, int64_t s_q, int64_t s_kv, int64_t d, int64_t dv);
+int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v, float *o, int64_t bh, int64_t s_q,
+                    int64_t s_kv, int64_t d, int64_t dv, float scale_div, const float *scale_div_ptr, int k_layout,
+                    float *ws, cudaStream_t s);
+
 int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
               cudaStream_t s);

@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_row_op_f32": ([_P, C.POINTER(RowParams), _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
+    "b2k_attention_set_fused": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_timing_enable": ([_P, C.c_int], C.c_int),
@@ -84,7 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_timing_reset": ([_P], C.c_int),
 }
 
-PHASES = {"split": 0, "mma": 1, "pointwise": 2, "softmax": 3, "attention": 4, "rows": 5}
+PHASES = {"split": 0, "mma": 1, "pointwise": 2, "softmax": 3, "attention": 4, "rows": 5, "flash": 6}
 
 _lock = threading.Lock()
 _lib: C.CDLL | None = None

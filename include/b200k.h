@@ -77,7 +77,8 @@ int b2k_stream_sync(b2k_ctx *ctx, void *stream);
 #define B2K_PHASE_SOFTMAX 3   /* row softmax */
 #define B2K_PHASE_ATTENTION 4 /* attention (all of its passes) */
 #define B2K_PHASE_ROWS 5      /* row reductions / norms */
-#define B2K_PHASE_COUNT 6
+#define B2K_PHASE_FLASH 6     /* fused attention kernel */
+#define B2K_PHASE_COUNT 7
 int b2k_timing_enable(b2k_ctx *ctx, int on);
 int b2k_timing_read(b2k_ctx *ctx, int phase, double *total_ms, int64_t *launches);
 int b2k_timing_reset(b2k_ctx *ctx);
@@ -207,13 +208,17 @@ int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int6
  * is [bh][s_q][dv] (all row-major, contiguous).  k_layout B2K_K_SD: K is
  * [bh][s_kv][d]; B2K_K_DS: K is given transposed as [bh][d][s_kv] (the IR's
  * `kt`).  The divisor is *scale_div_ptr when that device pointer is non-NULL
- * (the IR's one-element `div_c1` buffer), else scale_div.  Uses context
- * scratch for the split operands, S and P. */
+ * (the IR's one-element `div_c1` buffer), else scale_div.  Head dims up to
+ * 128 (d and dv) run one fused kernel (S and P never leave the SM); larger
+ * ones run three batched passes through context scratch. */
 #define B2K_K_SD 0
 #define B2K_K_DS 1
 int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k, const float *v, float *o, int64_t bh,
                          int64_t s_q, int64_t s_kv, int64_t d, int64_t dv, float scale_div,
                          const float *scale_div_ptr, int32_t k_layout, void *stream);
+/* Process-wide switch: 1 (default) uses the fused kernel where head dims
+ * allow, 0 forces the three-pass path (for comparisons). */
+int b2k_attention_set_fused(int fused);
 
 /* The same GEMM for callers that cannot allocate device memory (code running
  * under CUDA-graph capture or a fixed memory plan, or memory owned by another

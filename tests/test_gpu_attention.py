@@ -43,6 +43,27 @@ def test_attention_matches_float64(ctx, torch_cuda, bh, s_q, s_kv, d, dv, k_layo
     assert ok, (bad, err)
 
 
+@pytest.mark.parametrize("bh,s_q,s_kv,d,dv", [(2, 300, 257, 128, 128), (1, 64, 64, 64, 64), (3, 129, 33, 100, 24)])
+def test_fused_and_three_pass_paths_agree(ctx, torch_cuda, bh, s_q, s_kv, d, dv):
+    runtime = pkg("runtime")
+    lib = runtime.library()
+    rng = np.random.default_rng(17 + s_q)
+    q = rng.standard_normal((bh, s_q, d)).astype(np.float32)
+    k = rng.standard_normal((bh, s_kv, d)).astype(np.float32)
+    v = rng.standard_normal((bh, s_kv, dv)).astype(np.float32)
+    want = refs.attention_batched(q, k, v, math.sqrt(d))
+    outs = []
+    try:
+        for fused in (1, 0):
+            lib.b2k_attention_set_fused(fused)
+            outs.append(run(ctx, torch_cuda, q, k, v))
+    finally:
+        lib.b2k_attention_set_fused(1)
+    for got in outs:
+        ok, bad, err = refs.allclose_report(got, want, RTOL, ATOL)
+        assert ok, (bad, err)
+
+
 def test_attention_scale_from_device_buffer(ctx, torch_cuda):
     """The IR passes the divisor as a one-element buffer (a01's div_c1 = 8)."""
     rng = np.random.default_rng(1)
