@@ -1,24 +1,33 @@
 // Fused attention, O = softmax(Q K^T / scale) V, both contractions 3xTF32 on
-// tcgen05, one CTA per (head, 128 query rows), streaming 32-key blocks.
+// tcgen05, one CTA per (head, 128 query rows), streaming 128-key blocks.
+//
+// A tf32 tcgen05.mma costs at least ~46 cycles whatever its N (measured on
+// B200: N = 32 runs at 35 % of the tensor rate, N = 64 at 67 %, N >= 128 at
+// 100 %), so every MMA here is N = 128: S_j = Q K_j^T over 128 keys and
+// O_j = P_j V_j over 128 output columns.
 //
 // The reference hoists one head's score rows into shared memory and runs the
 // softmax and the P.V fold in SIMT FP32 (compile.py:7009-7966, selective exp
 // 2953-2965).  Here nothing but Q, K, V and O touches HBM:
 //
 //   warp 0      TMA: Q_hi/Q_lo once (128 x Dp, four 128-byte-swizzled
-//               column blocks each), then per key block j the K_j tiles
-//               (32 keys x Dp) and the V_j^T tiles (Dv x 32 keys)
+//               column blocks each, resident), then through a 3-stage ring
+//               the chunks K_j[:, 32c..] (128 keys x 32 dims) and
+//               V_j^T[:, 32c..] (128 dims x 32 keys), hi and lo
 //   warp 1      TMEM allocator and MMA issuer: S_j = Q K_j^T (three TF32
-//               products per 8-wide step) into TMEM buffer j % 2, and
-//               O_j = P_j V_j into TMEM buffer j % 2; issue order
-//               S_0, S_1, O_0, S_2, O_1, ... so QK^T of the next block
-//               overlaps the softmax of this one
-//   warps 2..5  softmax, one thread per query row: S_j from TMEM, online max /
-//               sum with the selective exponential, P_j's TF32 halves into
-//               swizzled shared memory (the A operand of O_j), then the
-//               finished O_{j-1} from TMEM folded into the FP32 row
-//               accumulator O = O * alpha + O_{j-1} in registers (which also
-//               keeps the tensor core's accumulation error per block small)
+//               products per 8-wide step, both operands from shared memory)
+//               into TMEM, then, once the softmax has written P_j over S_j,
+//               O_j = P_j V_j with P_j read from TMEM into O buffer j % 2;
+//               S_{j+1} waits for O_j to finish reading P_j
+//   warps 2..9  softmax, two threads per query row (warpgroup 0 takes score
+//               columns 0-63 and output columns 0-63 of the row, warpgroup
+//               1 the rest): S_j from TMEM, online max / sum with the
+//               selective exponential (partial row max and sum exchanged
+//               through shared memory), P_j's TF32 halves into TMEM (the A
+//               operand of O_j), then the finished
+//               O_{j-1} from TMEM folded into the FP32 row accumulator
+//               O = O * alpha + O_{j-1} in registers (which also keeps the
+//               tensor core's accumulation error per block small)
 //
 // Each key block's products accumulate in a fresh TMEM buffer, so the
 // in-instruction accumulation error stays that of 48 (S) / 12 (O) MMAs.
@@ -33,16 +42,23 @@
 namespace {
 
 constexpr int BM = 128;        // query rows per CTA
-constexpr int BN = 32;         // keys per block
+constexpr int BN = 128;        // keys per block (every MMA is N = 128: full tensor rate)
 constexpr int DMAX = 128;      // head dims supported (padded to 32)
-constexpr int kThreads = 192;  // producer, MMA, 4 softmax warps
+constexpr int kStages = 3;     // ring of K / V chunks
+constexpr int kThreads = 320;  // producer, MMA, 8 softmax warps (two per TMEM lane quarter)
 
-constexpr int kSub = 128 * 32 * 4;                 // one [128 rows x 32 fp32] swizzled block (16 KB)
-constexpr int kQBytes = (DMAX / 32) * kSub;        // 64 KB per half
-constexpr int kKBytes = (DMAX / 32) * BN * 128;    // 16 KB per half
-constexpr int kVBytes = kSub;                      // Dv <= 128 rows x 32 keys: 16 KB per half
-constexpr int kPBytes = kSub;                      // 128 rows x 32 keys: 16 KB per half
-constexpr int kSmem = 2 * (kQBytes + kKBytes + kVBytes + kPBytes) + 1024;
+constexpr int kSub = 128 * 32 * 4;          // one [128 rows x 32 fp32] swizzled block (16 KB)
+constexpr int kQBytes = (DMAX / 32) * kSub; // 64 KB per half
+// Q (both halves, resident) + a ring of stages, each one K chunk [128 keys x
+// 32 dims] or one V^T chunk [128 dims x 32 keys], hi and lo: 128 + 96 KB.
+// The row-exchange arrays and barriers are static, so the dynamic buffer is
+// declared 1024-byte aligned (checked at run time) instead of carrying slack.
+constexpr int kSmem = 2 * kQBytes + kStages * 2 * kSub;
+
+// TMEM columns: S_j and then P_j's hi half share [0, 128); P_j's lo half
+// [128, 256); O buffers [256, 384) and [384, 512).
+constexpr uint32_t kColS = 0, kColPlo = 128;
+__host__ __device__ constexpr uint32_t o_col(int b) { return (uint32_t)(256 + b * 128); }
 
 struct FlashArgs {
   float *o;
@@ -59,36 +75,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
                         const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
                         const FlashArgs args) {
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full, k_full, k_empty, v_full, v_empty, p_full, p_empty, drain;
-  __shared__ __align__(8) uint64_t s_full[2], s_empty[2], o_full[2], o_empty[2];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t q_full, s_full, p_full, drain;
+  __shared__ __align__(8) uint64_t ring_full[kStages], ring_empty[kStages], o_full[2], o_empty[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_word;
+  __shared__ float part_max[2][BM], part_sum[2][BM];
 
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *q_hi = smem, *q_lo = q_hi + kQBytes;
-  uint8_t *k_hi = q_lo + kQBytes, *k_lo = k_hi + kKBytes;
-  uint8_t *v_hi = k_lo + kKBytes, *v_lo = v_hi + kVBytes;
-  uint8_t *p_hi = v_lo + kVBytes, *p_lo = p_hi + kPBytes;
+  uint8_t *q_hi = smem_raw, *q_lo = q_hi + kQBytes;
+  uint8_t *ring = q_lo + kQBytes;  // stage i: hi at ring + 2i*kSub, lo at ring + (2i+1)*kSub
+  auto st_hi = [&](int i) { return ring + (2 * i) * kSub; };
+  auto st_lo = [&](int i) { return ring + (2 * i + 1) * kSub; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
   const int64_t m0 = (int64_t)blockIdx.x * BM;
   const int nblocks = (int)((args.s_kv + BN - 1) / BN);
-  const int dblocks = args.dp / 32;
+  const int dblocks = args.dp / 32;      // K chunks per block
+  constexpr int kVChunks = BN / 32;      // V chunks per block
   volatile int *abort = &abort_word;
 
   if (threadIdx.x == 0) {
-    abort_word = 0;
-    uint64_t *singles[] = {&q_full, &k_full, &k_empty, &v_full, &v_empty, &p_empty, &drain};
-    for (uint64_t *b : singles) sm100::mbar_init(b, 1);
-    for (int i = 0; i < 2; ++i) {
-      sm100::mbar_init(&s_full[i], 1);
-      sm100::mbar_init(&s_empty[i], 4);  // one arrival per softmax warp
-      sm100::mbar_init(&o_full[i], 1);
-      sm100::mbar_init(&o_empty[i], 4);
+    // swizzled tiles need 1024-byte alignment: refuse to run (error word, no
+    // work) rather than compute garbage
+    abort_word = (sm100::smem_addr(smem_raw) & 1023u) ? 1 : 0;
+    if (abort_word) atomicOr(args.err, sm100::kSiteAttention);
+    sm100::mbar_init(&q_full, 1);
+    sm100::mbar_init(&s_full, 1);
+    sm100::mbar_init(&p_full, 8);  // one arrival per softmax warp
+    sm100::mbar_init(&drain, 1);
+    for (int i = 0; i < kStages; ++i) {
+      sm100::mbar_init(&ring_full[i], 1);
+      sm100::mbar_init(&ring_empty[i], 1);
     }
-    sm100::mbar_init(&p_full, 4);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&o_full[i], 1);
+      sm100::mbar_init(&o_empty[i], 8);
+    }
     sm100::fence_barrier_init();
   }
   if (warp == 1) sm100::tmem_alloc(&tmem_slot, 512);
@@ -96,38 +119,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  // TMEM columns: S buffers at [0, 32) and [32, 64); O buffers at [128, 256) and [256, 384).
-  auto s_col = [](int b) { return (uint32_t)(b * BN); };
-  auto o_col = [](int b) { return (uint32_t)(128 + b * 128); };
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer
+      // ---------------- TMA producer: Q once, then K_j chunks, V_j chunks, K_{j+1} ...
       sm100::mbar_arrive_expect_tx(&q_full, 2 * dblocks * kSub);
       for (int c = 0; c < dblocks; ++c) {
         sm100::tma_load_3d(q_hi + c * kSub, &map_qhi, &q_full, c * 32, (int)m0, head);
         sm100::tma_load_3d(q_lo + c * kSub, &map_qlo, &q_full, c * 32, (int)m0, head);
       }
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < nblocks; ++j) {
-        if (j > 0 && !sm100::mbar_wait(&k_empty, (j - 1) & 1, args.err, sm100::kSiteAttention, abort)) break;
-        sm100::mbar_arrive_expect_tx(&k_full, 2 * dblocks * BN * 128);
-        for (int c = 0; c < dblocks; ++c) {
-          sm100::tma_load_3d(k_hi + c * BN * 128, &map_khi, &k_full, c * 32, j * BN, head);
-          sm100::tma_load_3d(k_lo + c * BN * 128, &map_klo, &k_full, c * 32, j * BN, head);
+      int n = 0;  // chunks issued through the ring
+      bool ok = true;
+      for (int j = 0; ok && j < nblocks; ++j) {
+        for (int c = 0; ok && c < dblocks + kVChunks; ++c, ++n) {
+          const int i = n % kStages;
+          if (n >= kStages &&
+              !sm100::mbar_wait(&ring_empty[i], ((n / kStages) - 1) & 1, args.err, sm100::kSiteAttention, abort)) {
+            ok = false;
+            break;
+          }
+          sm100::mbar_arrive_expect_tx(&ring_full[i], 2 * kSub);
+          if (c < dblocks) {  // K chunk: keys j*BN.., dims c*32..
+            sm100::tma_load_3d(st_hi(i), &map_khi, &ring_full[i], c * 32, j * BN, head);
+            sm100::tma_load_3d(st_lo(i), &map_klo, &ring_full[i], c * 32, j * BN, head);
+          } else {            // V^T chunk: dims 0..127, keys j*BN + 32*(c - dblocks)..
+            const int x = j * BN + 32 * (c - dblocks);
+            sm100::tma_load_3d(st_hi(i), &map_vhi, &ring_full[i], x, 0, head);
+            sm100::tma_load_3d(st_lo(i), &map_vlo, &ring_full[i], x, 0, head);
+          }
         }
-        k_issued = j + 1;
-        if (j > 0 && !sm100::mbar_wait(&v_empty, (j - 1) & 1, args.err, sm100::kSiteAttention, abort)) break;
-        sm100::mbar_arrive_expect_tx(&v_full, 2 * kVBytes);
-        sm100::tma_load_3d(v_hi, &map_vhi, &v_full, j * BN, 0, head);
-        sm100::tma_load_3d(v_lo, &map_vlo, &v_full, j * BN, 0, head);
-        v_issued = j + 1;
       }
-      // drain loads in flight (budget only)
-      int never = 0;
+      int never = 0;  // drain loads in flight (budget only)
       sm100::mbar_wait(&q_full, 0, args.err, sm100::kSiteDrain, &never);
-      if (k_issued) sm100::mbar_wait(&k_full, (k_issued - 1) & 1, args.err, sm100::kSiteDrain, &never);
-      if (v_issued) sm100::mbar_wait(&v_full, (v_issued - 1) & 1, args.err, sm100::kSiteDrain, &never);
+      for (int m = n > kStages ? n - kStages : 0; m < n; ++m)
+        sm100::mbar_wait(&ring_full[m % kStages], (m / kStages) & 1, args.err, sm100::kSiteDrain, &never);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -135,160 +160,170 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_s = sm100::idesc_tf32(BM, BN);
       const uint32_t id_o = sm100::idesc_tf32(BM, args.n_pv);
       const uint32_t qh = sm100::smem_addr(q_hi), ql = sm100::smem_addr(q_lo);
-      const uint32_t kh = sm100::smem_addr(k_hi), kl = sm100::smem_addr(k_lo);
-      const uint32_t vh = sm100::smem_addr(v_hi), vl = sm100::smem_addr(v_lo);
-      const uint32_t ph = sm100::smem_addr(p_hi), pl = sm100::smem_addr(p_lo);
       bool ok = sm100::mbar_wait(&q_full, 0, args.err, sm100::kSiteAttention, abort);
-      auto issue_s = [&](int j) -> bool {
-        const int b = j & 1;
-        if (j >= 2 && !sm100::mbar_wait(&s_empty[b], ((j >> 1) - 1) & 1, args.err, sm100::kSiteAttention, abort))
-          return false;
-        if (!sm100::mbar_wait(&k_full, j & 1, args.err, sm100::kSiteAttention, abort)) return false;
+      int n = 0;  // ring chunks consumed
+      for (int j = 0; ok && j < nblocks; ++j) {
+        // S_j overwrites P_{j-1}'s hi half: wait until O_{j-1} has read it.
+        if (j >= 1 &&
+            !(ok = sm100::mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, args.err, sm100::kSiteAttention, abort)))
+          break;
         sm100::tc_fence_after();
-        const uint32_t d = tmem + s_col(b);
-        for (int k = 0; k < dblocks * 4; ++k) {
-          const uint32_t qa = (uint32_t)((k >> 2) * kSub + (k & 3) * 32);
-          const uint32_t ka = (uint32_t)((k >> 2) * BN * 128 + (k & 3) * 32);
-          const uint64_t dqh = sm100::desc_kmajor<128>(qh + qa), dql = sm100::desc_kmajor<128>(ql + qa);
-          const uint64_t dkh = sm100::desc_kmajor<128>(kh + ka), dkl = sm100::desc_kmajor<128>(kl + ka);
-          sm100::mma_tf32(d, dql, dkh, id_s, k == 0 ? 0u : 1u);
-          sm100::mma_tf32(d, dqh, dkl, id_s, 1u);
-          sm100::mma_tf32(d, dqh, dkh, id_s, 1u);
+        for (int c = 0; ok && c < dblocks; ++c, ++n) {
+          const int i = n % kStages;
+          if (!(ok = sm100::mbar_wait(&ring_full[i], (n / kStages) & 1, args.err, sm100::kSiteAttention, abort)))
+            break;
+          sm100::tc_fence_after();
+          const uint32_t kh = sm100::smem_addr(st_hi(i)), kl = sm100::smem_addr(st_lo(i));
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t qa = (uint32_t)(c * kSub + k * 32), ka = (uint32_t)(k * 32);
+            const uint64_t dqh = sm100::desc_kmajor<128>(qh + qa), dql = sm100::desc_kmajor<128>(ql + qa);
+            const uint64_t dkh = sm100::desc_kmajor<128>(kh + ka), dkl = sm100::desc_kmajor<128>(kl + ka);
+            sm100::mma_tf32(tmem + kColS, dql, dkh, id_s, (c == 0 && k == 0) ? 0u : 1u);
+            sm100::mma_tf32(tmem + kColS, dqh, dkl, id_s, 1u);
+            sm100::mma_tf32(tmem + kColS, dqh, dkh, id_s, 1u);
+          }
+          sm100::mma_commit(&ring_empty[i]);
         }
-        sm100::mma_commit(&k_empty);
-        sm100::mma_commit(&s_full[b]);
-        return true;
-      };
-      auto issue_o = [&](int j) -> bool {
+        if (!ok) break;
+        sm100::mma_commit(&s_full);
+        // O_j = P_j V_j once the softmax has written P_j into TMEM
         const int b = j & 1;
-        if (j >= 2 && !sm100::mbar_wait(&o_empty[b], ((j >> 1) - 1) & 1, args.err, sm100::kSiteAttention, abort))
-          return false;
-        if (!sm100::mbar_wait(&p_full, j & 1, args.err, sm100::kSiteAttention, abort)) return false;
-        if (!sm100::mbar_wait(&v_full, j & 1, args.err, sm100::kSiteAttention, abort)) return false;
+        if (j >= 2 &&
+            !(ok = sm100::mbar_wait(&o_empty[b], ((j >> 1) - 1) & 1, args.err, sm100::kSiteAttention, abort)))
+          break;
+        if (!(ok = sm100::mbar_wait(&p_full, j & 1, args.err, sm100::kSiteAttention, abort))) break;
         sm100::tc_fence_after();
-        const uint32_t d = tmem + o_col(b);
-        for (int k = 0; k < BN / 8; ++k) {
-          const uint32_t off = (uint32_t)(k * 32);
-          const uint64_t dph = sm100::desc_kmajor<128>(ph + off), dpl = sm100::desc_kmajor<128>(pl + off);
-          const uint64_t dvh = sm100::desc_kmajor<128>(vh + off), dvl = sm100::desc_kmajor<128>(vl + off);
-          sm100::mma_tf32(d, dpl, dvh, id_o, k == 0 ? 0u : 1u);
-          sm100::mma_tf32(d, dph, dvl, id_o, 1u);
-          sm100::mma_tf32(d, dph, dvh, id_o, 1u);
+        for (int c = 0; ok && c < kVChunks; ++c, ++n) {
+          const int i = n % kStages;
+          if (!(ok = sm100::mbar_wait(&ring_full[i], (n / kStages) & 1, args.err, sm100::kSiteAttention, abort)))
+            break;
+          sm100::tc_fence_after();
+          const uint32_t vh = sm100::smem_addr(st_hi(i)), vl = sm100::smem_addr(st_lo(i));
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t pcol = (uint32_t)(c * 32 + k * 8);
+            const uint64_t dvh = sm100::desc_kmajor<128>(vh + k * 32), dvl = sm100::desc_kmajor<128>(vl + k * 32);
+            sm100::mma_tf32_ts(tmem + o_col(b), tmem + kColPlo + pcol, dvh, id_o, (c == 0 && k == 0) ? 0u : 1u);
+            sm100::mma_tf32_ts(tmem + o_col(b), tmem + kColS + pcol, dvl, id_o, 1u);
+            sm100::mma_tf32_ts(tmem + o_col(b), tmem + kColS + pcol, dvh, id_o, 1u);
+          }
+          sm100::mma_commit(&ring_empty[i]);
         }
-        sm100::mma_commit(&p_empty);
-        sm100::mma_commit(&v_empty);
-        sm100::mma_commit(&o_full[b]);
-        return true;
-      };
-      for (int j = 0; ok && j <= nblocks; ++j) {
-        if (j < nblocks) ok = issue_s(j);
-        if (ok && j >= 1) ok = issue_o(j - 1);
+        if (ok) sm100::mma_commit(&o_full[b]);
       }
       sm100::mma_commit(&drain);
       int never = 0;
       sm100::mbar_wait(&drain, 0, args.err, sm100::kSiteDrain, &never);
     }
   } else {
-    // ---------------- softmax + O accumulation: thread = query row
+    // ---------------- softmax + O accumulation: two threads per query row
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // row within the tile == TMEM lane
+    const int wg = (warp - 2) >> 2;        // column half of the row
+    const int r = quarter * 32 + lane;     // row within the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float inv_scale = args.scale_ptr ? __frcp_rn(__ldg(args.scale_ptr)) : args.inv_scale;
-    constexpr int OC = 128;  // O columns held per thread (>= n_pv)
+    constexpr int SC = BN / 2;   // score columns per thread
+    constexpr int OC = 64;       // output columns per thread
+    const int sc0 = wg * SC, oc0 = wg * OC;
     float o_acc[OC];
 #pragma unroll
     for (int i = 0; i < OC; ++i) o_acc[i] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
-    uint8_t *prow_hi = p_hi + r * 128, *prow_lo = p_lo + r * 128;
-    for (int j = 0; j <= nblocks && ok; ++j) {
-      float alpha = 1.0f;
-      if (j < nblocks) {
-        const int b = j & 1;
-        ok = sm100::mbar_wait(&s_full[b], (j >> 1) & 1, args.err, sm100::kSiteAttention, abort);
-        if (!ok) break;
-        sm100::tc_fence_after();
-        uint32_t sr[32];
-        sm100::tmem_ld_32x32b_x32(tmem + lane_base + s_col(b), sr);
+    // Every thread runs every iteration and reaches both named barriers even
+    // after a failed wait (ok == false), so the two warpgroups never wait on
+    // each other forever; failed waits only skip work.
+    for (int j = 0; j < nblocks; ++j) {
+      ok = ok && sm100::mbar_wait(&s_full, j & 1, args.err, sm100::kSiteAttention, abort);
+      sm100::tc_fence_after();
+      uint32_t sr[SC];
+      {
+        uint32_t (&a)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[0]);
+        uint32_t (&b)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32]);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_base + kColS + (uint32_t)sc0, a);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_base + kColS + (uint32_t)sc0 + 32, b);
         sm100::tmem_ld_wait();
-        sm100::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&s_empty[b]);
-        float x[32];
-        float mx = m_run;
-        const int64_t c0 = (int64_t)j * BN;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          x[i] = (c0 + i < args.s_kv) ? __fmul_rn(__uint_as_float(sr[i]), inv_scale) : -INFINITY;
-          mx = fmaxf(mx, x[i]);
-        }
-        alpha = b2k_exp(__fsub_rn(m_run, mx));
-        float sum = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          x[i] = b2k_exp(__fsub_rn(x[i], mx));
-          sum += x[i];
-        }
-        l_run = __fadd_rn(__fmul_rn(l_run, alpha), sum);
-        m_run = mx;
-        // P_j into the swizzled A tile once O_{j-1}'s MMA has released it
-        if (j > 0) {
-          ok = sm100::mbar_wait(&p_empty, (j - 1) & 1, args.err, sm100::kSiteAttention, abort);
-          if (!ok) break;
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float4 h, l;
-          split_tf32(x[4 * c + 0], h.x, l.x);
-          split_tf32(x[4 * c + 1], h.y, l.y);
-          split_tf32(x[4 * c + 2], h.z, l.z);
-          split_tf32(x[4 * c + 3], h.w, l.w);
-          const int pos = (c ^ (r & 7)) * 16;
-          *reinterpret_cast<float4 *>(prow_hi + pos) = h;
-          *reinterpret_cast<float4 *>(prow_lo + pos) = l;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&p_full);
       }
-      if (j >= 1) {
-        // fold the finished O_{j-1} = P_{j-1} V_{j-1}
-        const int jb = j - 1, b = jb & 1;
-        ok = sm100::mbar_wait(&o_full[b], (jb >> 1) & 1, args.err, sm100::kSiteAttention, abort,
-                              3 * sm100::kWaitCycles);
-        if (!ok) break;
-        sm100::tc_fence_after();
+      float mx = -INFINITY;
+      const int64_t c0 = (int64_t)j * BN + sc0;
 #pragma unroll
-        for (int c = 0; c < OC; c += 32) {
-          if (c >= args.n_pv) break;  // warp-uniform
-          uint32_t orr[32];
-          sm100::tmem_ld_32x32b_x32(tmem + lane_base + o_col(b) + (uint32_t)c, orr);
+      for (int i = 0; i < SC; ++i) {
+        const float x = (c0 + i < args.s_kv) ? __fmul_rn(__uint_as_float(sr[i]), inv_scale) : -INFINITY;
+        sr[i] = __float_as_uint(x);
+        mx = fmaxf(mx, x);
+      }
+      part_max[wg][r] = mx;
+      sm100::named_barrier(1, 256);
+      mx = fmaxf(fmaxf(mx, part_max[wg ^ 1][r]), m_run);
+      const float alpha = b2k_exp(__fsub_rn(m_run, mx));
+      float sum = 0.0f;
+      uint32_t pl[SC];
+#pragma unroll
+      for (int i = 0; i < SC; ++i) {
+        const float v = b2k_exp(__fsub_rn(__uint_as_float(sr[i]), mx));
+        sum += v;
+        // probabilities are finite and in [0, 1]: the split needs no range guards
+        const uint32_t hv = (__float_as_uint(v) + 0x1000u) & 0xFFFFE000u;
+        sr[i] = hv;
+        pl[i] = (__float_as_uint(__fsub_rn(v, __uint_as_float(hv))) + 0x1000u) & 0xFFFFE000u;
+      }
+      part_sum[wg][r] = sum;
+      if (ok) {
+        // P_j's halves into TMEM: hi over S_j, lo beside it (the A operand of O_j)
+        uint32_t (&h0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[0]);
+        uint32_t (&h1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32]);
+        uint32_t (&l0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pl[0]);
+        uint32_t (&l1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pl[32]);
+        sm100::tmem_st_32x32b_x32(tmem + lane_base + kColS + (uint32_t)sc0, h0);
+        sm100::tmem_st_32x32b_x32(tmem + lane_base + kColS + (uint32_t)sc0 + 32, h1);
+        sm100::tmem_st_32x32b_x32(tmem + lane_base + kColPlo + (uint32_t)sc0, l0);
+        sm100::tmem_st_32x32b_x32(tmem + lane_base + kColPlo + (uint32_t)sc0 + 32, l1);
+        sm100::tmem_st_wait();
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && ok) sm100::mbar_arrive(&p_full);
+      sm100::named_barrier(2, 256);
+      l_run = __fadd_rn(__fmul_rn(l_run, alpha), __fadd_rn(part_sum[0][r], part_sum[1][r]));
+      m_run = mx;
+      // fold O_j = P_j V_j into the register accumulator
+      const int b = j & 1;
+      ok = ok && sm100::mbar_wait(&o_full[b], (j >> 1) & 1, args.err, sm100::kSiteAttention, abort,
+                                  3 * sm100::kWaitCycles);
+      if (ok) {
+        sm100::tc_fence_after();
+        if (oc0 < args.n_pv) {  // warp-uniform
+          uint32_t o0[32], o1[32];
+          const uint32_t ta = tmem + lane_base + o_col(b) + (uint32_t)oc0;
+          sm100::tmem_ld_32x32b_x32(ta, o0);
+          sm100::tmem_ld_32x32b_x32(ta + 32, o1);
           sm100::tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o_acc[c + i] = __fadd_rn(__fmul_rn(o_acc[c + i], alpha_prev), __uint_as_float(orr[i]));
+          for (int i = 0; i < 32; ++i) {
+            o_acc[i] = __fadd_rn(__fmul_rn(o_acc[i], alpha), __uint_as_float(o0[i]));
+            o_acc[32 + i] = __fadd_rn(__fmul_rn(o_acc[32 + i], alpha), __uint_as_float(o1[i]));
+          }
         }
         sm100::tc_fence_before();
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(&o_empty[b]);
       }
-      alpha_prev = alpha;
     }
     const int64_t row = m0 + r;
-    if (ok && row < args.s_q) {
+    if (ok && row < args.s_q && oc0 < args.dv) {
       const float inv_l = __frcp_rn(l_run);
       float *orow = args.o + ((int64_t)head * args.s_q + row) * args.dv;
       const bool vec = (args.dv % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.o) & 15) == 0);
       if (vec) {
 #pragma unroll
         for (int i = 0; i < OC; i += 4)
-          if (i < args.dv)
-            *reinterpret_cast<float4 *>(orow + i) =
+          if (oc0 + i < args.dv)
+            *reinterpret_cast<float4 *>(orow + oc0 + i) =
                 make_float4(__fmul_rn(o_acc[i], inv_l), __fmul_rn(o_acc[i + 1], inv_l), __fmul_rn(o_acc[i + 2], inv_l),
                             __fmul_rn(o_acc[i + 3], inv_l));
       } else {
 #pragma unroll
         for (int i = 0; i < OC; ++i)
-          if (i < args.dv) orow[i] = __fmul_rn(o_acc[i], inv_l);
+          if (oc0 + i < args.dv) orow[oc0 + i] = __fmul_rn(o_acc[i], inv_l);
       }
     }
   }
