@@ -48,6 +48,7 @@ extern "C" int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k
     return b2k::fail(ctx, B2K_EINVAL, "attention: extent exceeds 32-bit TMA coordinates");
   if (!scale_div_ptr && !(scale_div != 0.0f)) return b2k::fail(ctx, B2K_EINVAL, "attention: zero scale divisor");
   cudaStream_t s = (cudaStream_t)stream;
+  ctx->flags_epoch = 0;  // the workspace is reused below: GEMM stream-K flags must be reset next time
   if (b2k::flash_supported(d, dv) && !g_attention_unfused) {
     int status = b2k::reserve_workspace(ctx, b2k::flash_workspace_floats(bh, s_q, s_kv, d, dv) * sizeof(float), s);
     if (status != B2K_OK) return status;

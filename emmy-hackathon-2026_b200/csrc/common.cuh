@@ -22,6 +22,9 @@ struct b2k_ctx {
   size_t workspace_bytes = 0;
   // Device-side error word written by kernels whose bounded waits expire.
   unsigned int *error_flag = nullptr;
+  // Stream-K flag slots in the workspace and the epoch of the last GEMM.
+  unsigned *flags_ptr = nullptr;
+  unsigned flags_epoch = 0;
   // Optional per-phase CUDA-event timing (b2k_timing_*).
   bool timing = false;
   std::vector<cudaEvent_t> event_pool;
@@ -82,6 +85,16 @@ int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_
                     int64_t kp, float *hi, float *lo, cudaStream_t s);
 // C[z] = epilogue(A[z] * B[z]^T) for z < batch on pre-split operands; the
 // epilogue divides by *div_ptr (or div_value), adds bias[n], applies ReLU.
+// Scratch of the stream-K GEMM: per-CTA partial tiles and publication flags.
+struct StreamKScratch {
+  int grid;
+  float *partials;
+  unsigned *flags;
+  unsigned epoch;
+};
+bool streamk_pays(int64_t m, int64_t n, int64_t kp, int grid);
+size_t streamk_scratch_bytes(int grid);
+
 // Row softmax of x [rows, cols] written as TF32 hi/lo halves [rows][kp] (softmax.cu).
 int softmax_split_rows(b2k_ctx *ctx, const float *x, int64_t rows, int64_t cols, int64_t ld_x, float *hi,
                        float *lo, int64_t kp, cudaStream_t s);
@@ -95,7 +108,7 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
 
 int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
-              cudaStream_t s);
+              cudaStream_t s, const StreamKScratch *sk = nullptr);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

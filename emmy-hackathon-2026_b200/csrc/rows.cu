@@ -156,6 +156,7 @@ extern "C" int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const 
     const int parts = ctx->sm_count * 4;
     int status = b2k::reserve_workspace(ctx, (size_t)parts * sizeof(float), s);
     if (status != B2K_OK) return status;
+    ctx->flags_epoch = 0;  // GEMM stream-K flags share this scratch: reset them next time
     float *partials = static_cast<float *>(ctx->workspace);
     sum_partials<<<parts, kThreads, 0, s>>>(x, cols, partials);
     sum_finish<<<1, kThreads, 0, s>>>(a, partials, parts, y);

@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_row_op_f32": ([_P, C.POINTER(RowParams), _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
+    "b2k_gemm_set_streamk": ([C.c_int], C.c_int),
     "b2k_attention_set_fused": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
@@ -214,6 +215,9 @@ class Context:
 
     def set_gemm_variant(self, variant: int) -> None:
         self.check(self.lib.b2k_gemm_set_variant(variant), "b2k_gemm_set_variant")
+
+    def set_gemm_streamk(self, on: bool) -> None:
+        self.check(self.lib.b2k_gemm_set_streamk(int(bool(on))), "b2k_gemm_set_streamk")
 
     def sync(self, stream: int = 0) -> None:
         self.check(self.lib.b2k_stream_sync(self.handle, stream), "b2k_stream_sync")

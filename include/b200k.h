@@ -244,9 +244,16 @@ int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c, int64_t m,
 /* Select the GEMM kernel variant for subsequent calls (process-wide; for
  * tuning and benchmarking): 0 = 128x256 tile, 128-byte swizzle, 2 stages;
  * 1 = 128x256, 64-byte swizzle, 4 stages (default); 2 = 128x128, 128-byte
- * swizzle, 3 stages.  Outputs at most 128 columns wide always use 2.  No counterpart in the reference, whose plan
+ * swizzle, 3 stages; 3 = 128x192, 64-byte swizzle, 5 stages.  Outputs at
+ * most 128 columns wide always use 2.  No counterpart in the reference, whose plan
  * geometry comes from the IR. */
 int b2k_gemm_set_variant(int variant);
+/* Process-wide switch for the persistent stream-K schedule of the default
+ * variant (0 = off, the default; 1 = on): one CTA per SM takes an equal share
+ * of the (tile, K block) work instead of whole tiles, so a partial last wave
+ * of tiles does not idle SMs.  Off by default because it measured slower on
+ * B200 than one tile per CTA.  No counterpart in the reference. */
+int b2k_gemm_set_streamk(int on);
 
 #ifdef __cplusplus
 }

@@ -92,3 +92,40 @@ def test_gemm_4096_cubed(ctx, torch_cuda):
     # size-independent checksum: column sums of C equal (1^T A) B
     colsum = (a.astype(np.float64).sum(axis=0) @ b.astype(np.float64))
     np.testing.assert_allclose(got.astype(np.float64).sum(axis=0), colsum, rtol=1e-4, atol=1e-2)
+
+
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+@pytest.mark.parametrize("m,n,k", [(300, 520, 200), (128, 1024, 512), (1000, 257, 96)])
+def test_gemm_every_variant(ctx, torch_cuda, variant, m, n, k):
+    """Each tile/swizzle/stage variant gives the same normwise accuracy."""
+    rng = np.random.default_rng(variant * 1000 + m + n + k)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    ctx.set_gemm_variant(variant)
+    try:
+        got = run_gemm(ctx, torch_cuda, a, b)
+    finally:
+        ctx.set_gemm_variant(1)
+    assert tf32.normwise_error(got, a.astype(np.float64) @ b.astype(np.float64)) <= NORMWISE
+
+
+@pytest.mark.parametrize("m,n,k,b_layout", [(4096, 4096, 4096, 0), (4097, 1000, 777, 1), (1024, 2048, 512, 0),
+                                            (1000, 2000, 1000, 1)])
+def test_gemm_streamk_opt_in(ctx, torch_cuda, m, n, k, b_layout):
+    """The opt-in stream-K schedule (partial tiles combined through scratch)
+    matches whole-tile results to the 3xTF32 bound."""
+    rng = np.random.default_rng(m + 3 * n + 7 * k)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    ctx.set_gemm_streamk(True)
+    try:
+        got = run_gemm(ctx, torch_cuda, a, b, b_layout=b_layout, bias=bias, relu=True)
+        again = run_gemm(ctx, torch_cuda, a, b, b_layout=b_layout, bias=bias, relu=True)
+    finally:
+        ctx.set_gemm_streamk(False)
+    bm = b if b_layout == 0 else b.T
+    rows = np.random.default_rng(5).choice(m, min(m, 128), replace=False)
+    exact = np.maximum(a[rows].astype(np.float64) @ bm.astype(np.float64) + bias, 0.0)
+    assert tf32.normwise_error(got[rows], exact) <= NORMWISE
+    np.testing.assert_array_equal(got, again)  # fixed combination order
