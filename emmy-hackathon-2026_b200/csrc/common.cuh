@@ -77,6 +77,20 @@ struct SplitOperands {
   int64_t kp;
 };
 
+// In-kernel split GEMMs (gemm_fused.cu).  gemm_split_mode returns the
+// path a call takes under the b2k_gemm_set_fused_split switch: 0 = pre-pass
+// split of both operands, 1 = A split into TMEM inside the kernel with B
+// pre-split into `ops` (A must be TMA-readable: 16-byte aligned, row stride a
+// multiple of 4 elements, K >= 16), 2 = both operands split in shared memory
+// (B TMA-readable too; needs no scratch).
+int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb);
+// The tile variant selected with b2k_gemm_set_variant (2 = 128-wide tiles).
+int gemm_variant();
+int gemm_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const SplitOperands &ops, float *c, int64_t m,
+                int64_t n, int64_t ldc, const float *bias, int relu, cudaStream_t s);
+int gemm_smem_split(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                    int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu, cudaStream_t s);
+
 // Row-major [batch][rows, k] -> hi/lo [batch][rows][kp].
 int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t ld, int64_t bs, int64_t batch,
                int64_t kp, float *hi, float *lo, cudaStream_t s);
@@ -174,6 +188,31 @@ __device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
   const float r = __fsub_rn(x, h);
   hi = h;
   lo = __uint_as_float((__float_as_uint(r) + 0x1000u) & 0xFFFFE000u);
+}
+
+// split_tf32 of four values.  When every |x| is below 0x7F7FF000 (bit
+// pattern: finite, and rounding cannot carry into the exponent's all-ones
+// value) the special cases cannot arise and the split is two integer ops per
+// half; otherwise each value takes split_tf32.  Results are bit-identical.
+__device__ __forceinline__ void split_tf32x4(const float4 &x, float4 &hi, float4 &lo) {
+  const uint32_t b0 = __float_as_uint(x.x), b1 = __float_as_uint(x.y);
+  const uint32_t b2 = __float_as_uint(x.z), b3 = __float_as_uint(x.w);
+  const uint32_t mag = max(max(b0 & 0x7FFFFFFFu, b1 & 0x7FFFFFFFu), max(b2 & 0x7FFFFFFFu, b3 & 0x7FFFFFFFu));
+  if (mag < 0x7F7FF000u) {
+    hi.x = __uint_as_float((b0 + 0x1000u) & 0xFFFFE000u);
+    hi.y = __uint_as_float((b1 + 0x1000u) & 0xFFFFE000u);
+    hi.z = __uint_as_float((b2 + 0x1000u) & 0xFFFFE000u);
+    hi.w = __uint_as_float((b3 + 0x1000u) & 0xFFFFE000u);
+    lo.x = __uint_as_float((__float_as_uint(__fsub_rn(x.x, hi.x)) + 0x1000u) & 0xFFFFE000u);
+    lo.y = __uint_as_float((__float_as_uint(__fsub_rn(x.y, hi.y)) + 0x1000u) & 0xFFFFE000u);
+    lo.z = __uint_as_float((__float_as_uint(__fsub_rn(x.z, hi.z)) + 0x1000u) & 0xFFFFE000u);
+    lo.w = __uint_as_float((__float_as_uint(__fsub_rn(x.w, hi.w)) + 0x1000u) & 0xFFFFE000u);
+  } else {
+    split_tf32(x.x, hi.x, lo.x);
+    split_tf32(x.y, hi.y, lo.y);
+    split_tf32(x.z, hi.z, lo.z);
+    split_tf32(x.w, hi.w, lo.w);
+  }
 }
 
 __device__ __forceinline__ float warp_max(float v) {

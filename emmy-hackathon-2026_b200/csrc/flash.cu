@@ -38,6 +38,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace {
 
@@ -155,22 +156,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::mbar_wait(&ring_full[m % kStages], (m / kStages) & 1, args.err, sm100::kSiteDrain, &never);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
       // ---------------- MMA issuer
       const uint32_t id_s = sm100::idesc_tf32(BM, BN);
       const uint32_t id_o = sm100::idesc_tf32(BM, args.n_pv);
       const uint32_t qh = sm100::smem_addr(q_hi), ql = sm100::smem_addr(q_lo);
-      bool ok = sm100::mbar_wait(&q_full, 0, args.err, sm100::kSiteAttention, abort);
+      bool ok = sm100::mbar_wait_warp(&q_full, 0, args.err, sm100::kSiteAttention, abort);
       int n = 0;  // ring chunks consumed
       for (int j = 0; ok && j < nblocks; ++j) {
         // S_j overwrites P_{j-1}'s hi half: wait until O_{j-1} has read it.
         if (j >= 1 &&
-            !(ok = sm100::mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, args.err, sm100::kSiteAttention, abort)))
+            !(ok = sm100::mbar_wait_warp(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, args.err, sm100::kSiteAttention, abort)))
           break;
         sm100::tc_fence_after();
         for (int c = 0; ok && c < dblocks; ++c, ++n) {
           const int i = n % kStages;
-          if (!(ok = sm100::mbar_wait(&ring_full[i], (n / kStages) & 1, args.err, sm100::kSiteAttention, abort)))
+          if (!(ok = sm100::mbar_wait_warp(&ring_full[i], (n / kStages) & 1, args.err, sm100::kSiteAttention, abort)))
             break;
           sm100::tc_fence_after();
           const uint32_t kh = sm100::smem_addr(st_hi(i)), kl = sm100::smem_addr(st_lo(i));
@@ -189,13 +190,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // O_j = P_j V_j once the softmax has written P_j into TMEM
         const int b = j & 1;
         if (j >= 2 &&
-            !(ok = sm100::mbar_wait(&o_empty[b], ((j >> 1) - 1) & 1, args.err, sm100::kSiteAttention, abort)))
+            !(ok = sm100::mbar_wait_warp(&o_empty[b], ((j >> 1) - 1) & 1, args.err, sm100::kSiteAttention, abort)))
           break;
-        if (!(ok = sm100::mbar_wait(&p_full, j & 1, args.err, sm100::kSiteAttention, abort))) break;
+        if (!(ok = sm100::mbar_wait_warp(&p_full, j & 1, args.err, sm100::kSiteAttention, abort))) break;
         sm100::tc_fence_after();
         for (int c = 0; ok && c < kVChunks; ++c, ++n) {
           const int i = n % kStages;
-          if (!(ok = sm100::mbar_wait(&ring_full[i], (n / kStages) & 1, args.err, sm100::kSiteAttention, abort)))
+          if (!(ok = sm100::mbar_wait_warp(&ring_full[i], (n / kStages) & 1, args.err, sm100::kSiteAttention, abort)))
             break;
           sm100::tc_fence_after();
           const uint32_t vh = sm100::smem_addr(st_hi(i)), vl = sm100::smem_addr(st_lo(i));
@@ -335,23 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void *p = nullptr;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 // [batch][rows][inner] FP32, box [1][box_rows][32] with the 128-byte swizzle.
 int make_map(b2k_ctx *ctx, CUtensorMap *map, const float *base, int64_t inner, int64_t rows, int64_t batch,
              int box_rows) {
-  auto encode = encode_fn();
+  auto encode = b2k::tensor_map_encoder();
   if (!encode) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)inner * 4, (cuuint64_t)(rows * inner * 4)};

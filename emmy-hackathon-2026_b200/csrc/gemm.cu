@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace {
 
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::mbar_wait(&full_bar[kb % STAGES], (kb / STAGES) & 1, args.err, sm100::kSiteDrain, &never);
     }
   } else if (warp == 1) {
-    if (sm100::elect_lane0()) {
+    {
       // MMA issuer: chunk c accumulates into TMEM buffer c & 1.
       constexpr uint32_t idesc = sm100::idesc_tf32(BM, BN);
       for (int kb = 0; kb < num_kb; ++kb) {
@@ -219,10 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool first = (kb % Shape::kChunkBlocks) == 0;
         const bool last = ((kb + 1) % Shape::kChunkBlocks) == 0 || kb + 1 == num_kb;
         if (first && chunk >= 2 &&
-            !sm100::mbar_wait(&tmem_empty[buf], ((chunk >> 1) & 1) ^ 1, args.err, sm100::kSiteMmaFull, abort))
+            !sm100::mbar_wait_warp(&tmem_empty[buf], ((chunk >> 1) & 1) ^ 1, args.err, sm100::kSiteMmaFull, abort))
           break;
         const int s = kb % STAGES;
-        if (!sm100::mbar_wait(&full_bar[s], (kb / STAGES) & 1, args.err, sm100::kSiteMmaFull, abort)) break;
+        if (!sm100::mbar_wait_warp(&full_bar[s], (kb / STAGES) & 1, args.err, sm100::kSiteMmaFull, abort)) break;
         sm100::tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(buf * BN);
         const uint32_t ahi = sm100::smem_addr(a_hi(s)), alo = sm100::smem_addr(a_lo(s));
@@ -434,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::mbar_wait(&full_bar[k % STAGES], (k / STAGES) & 1, args.g.err, sm100::kSiteDrain, &never);
     }
   } else if (warp == 1) {
-    if (sm100::elect_lane0()) {
+    {
       // MMA issuer: a chunk ends at a multiple of CB K blocks or at the end of a segment.
       constexpr uint32_t idesc = sm100::idesc_tf32(BM, BN);
       int n = 0, chunk = 0;
@@ -449,11 +450,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool last = ((kb + 1) % CB) == 0 || kb + 1 == num_kb || u + 1 == u1;
         const int buf = chunk & 1;
         if (first && chunk >= 2 &&
-            !(ok = sm100::mbar_wait(&tmem_empty[buf], ((chunk >> 1) & 1) ^ 1, args.g.err, sm100::kSiteMmaFull,
+            !(ok = sm100::mbar_wait_warp(&tmem_empty[buf], ((chunk >> 1) & 1) ^ 1, args.g.err, sm100::kSiteMmaFull,
                                     abort)))
           break;
         const int s = n % STAGES;
-        if (!(ok = sm100::mbar_wait(&full_bar[s], (n / STAGES) & 1, args.g.err, sm100::kSiteMmaFull, abort))) break;
+        if (!(ok = sm100::mbar_wait_warp(&full_bar[s], (n / STAGES) & 1, args.g.err, sm100::kSiteMmaFull, abort))) break;
         sm100::tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(buf * BN);
         const uint32_t ahi = sm100::smem_addr(a_hi(s)), alo = sm100::smem_addr(a_lo(s));
@@ -598,25 +599,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // --- host side -------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void *p = nullptr;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 // K-major FP32 operand [batch][rows][Kp]: box [1, box_rows, SW/4] with the
 // SW-byte swizzle.
 int make_operand_map(b2k_ctx *ctx, CUtensorMap *map, const float *base, int64_t rows, int64_t Kp, int64_t batch,
                      int box_rows, int sw) {
-  auto encode = encode_fn();
+  auto encode = b2k::tensor_map_encoder();
   if (!encode) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)Kp * 4, (cuuint64_t)(rows * Kp * 4)};
@@ -747,15 +734,30 @@ int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int6
 
 }  // namespace b2k
 
-// Shared by the public entry points: split both operands into `ws` (A_hi,
-// A_lo: m x Kp; B_hi, B_lo: n x Kp) and run the tensor-core kernel.
+// Shared by the public entry points.  By default a TMA-readable A is split
+// inside the kernel (gemm_fused.cu) and only B is pre-split into `ws`;
+// otherwise both operands are split into `ws` (A_hi, A_lo: m x Kp; B_hi,
+// B_lo: n x Kp) and the kernel above runs.
 // `b_kmajor`: B is stored [n, K] (else [K, n]).
 int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                          int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu,
                          float *ws, cudaStream_t s, const b2k::StreamKScratch *sk) {
+  const int mode = b2k::gemm_split_mode(a, b, m, n, k, lda, ldb);
+  if (mode == 2) return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_kmajor, bias, relu, s);
   const int64_t kp = b2k::gemm_kpad(k);
-  b2k::SplitOperands ops{ws, ws + m * kp, ws + 2 * m * kp, ws + 2 * m * kp + n * kp, kp};
   int status;
+  if (mode == 1) {
+    // A is split inside the kernel (into TMEM); only B is pre-split.
+    b2k::SplitOperands ops{nullptr, nullptr, ws, ws + n * kp, kp};
+    {
+      b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
+      status = b_kmajor ? b2k::split_rows(ctx, b, n, k, ldb, n * ldb, 1, kp, ops.b_hi, ops.b_lo, s)
+                        : b2k::split_transpose(ctx, b, k, n, ldb, k * ldb, 1, kp, ops.b_hi, ops.b_lo, s);
+    }
+    if (status != B2K_OK) return status;
+    return b2k::gemm_tmem_a(ctx, a, k, lda, ops, c, m, n, ldc, bias, relu, s);
+  }
+  b2k::SplitOperands ops{ws, ws + m * kp, ws + 2 * m * kp, ws + 2 * m * kp + n * kp, kp};
   {
     b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
     status = b2k::split_rows(ctx, a, m, k, lda, m * lda, 1, kp, ops.a_hi, ops.a_lo, s);
@@ -767,6 +769,8 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
   if (status != B2K_OK) return status;
   return b2k::gemm_main(ctx, ops, m, n, 1, c, ldc, m * ldc, bias, relu, nullptr, 1.0f, s, sk);
 }
+
+int b2k::gemm_variant() { return g_gemm_variant; }
 
 extern "C" int b2k_gemm_set_variant(int variant) {
   if (variant < 0 || variant > 3) return B2K_EINVAL;
@@ -798,6 +802,8 @@ extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, flo
     if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: zero fill");
     return B2K_OK;
   }
+  if (b2k::gemm_split_mode(a, b, m, n, k, lda, ldb) == 2)  // needs no scratch
+    return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu, s);
   // scratch: split operands, then the stream-K partial slots and flags
   const size_t split_bytes = (b2k_gemm_workspace_bytes(m, n, k) + 255) & ~size_t(255);
   int status = b2k::reserve_workspace(ctx, split_bytes + b2k::streamk_scratch_bytes(ctx->sm_count), s);

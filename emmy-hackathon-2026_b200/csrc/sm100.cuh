@@ -21,6 +21,7 @@ enum WaitSite : unsigned {
   kSiteEpilogueAccum = 0x4,
   kSiteDrain = 0x8,
   kSiteAttention = 0x10,
+  kSiteConvert = 0x20,
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -145,29 +146,91 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor, kind::tf32, FP32 accumulate, both operands K-major.
-//   bits 4-5 D format (1 = F32), 7-9 A format (2 = TF32), 10-12 B format,
-//   15/16 A/B major (0 = K), 17-22 N >> 3, 24-28 M >> 4.
-__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(m >> 4) << 24);
+// Shared-memory matrix descriptor for an MN-major TF32 operand stored with
+// the 128-byte swizzle of 32-byte atoms (TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+// the only swizzle the tensor core accepts for MN-major 32-bit operands).
+// The operand is a grid of atoms, each 32 MN-consecutive elements (128 bytes)
+// by 4 K rows (512 bytes):
+//   bits 16-29 leading-dimension byte offset >> 4: stride between atoms along MN
+//   bits 32-45 stride byte offset >> 4: stride between atoms along K
+//   bits 61-63 layout 1 = SWIZZLE_128B_BASE32B
+// Atoms must sit on 512-byte boundaries.
+__device__ __forceinline__ uint64_t desc_mn_sw128_32b(uint32_t saddr, uint32_t mn_stride_bytes,
+                                                      uint32_t k_stride_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((mn_stride_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((k_stride_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(1u) << 61;
+  return d;
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+// Instruction descriptor, kind::tf32, FP32 accumulate.
+//   bits 4-5 D format (1 = F32), 7-9 A format (2 = TF32), 10-12 B format,
+//   15/16 A/B major (0 = K-major, 1 = MN-major), 17-22 N >> 3, 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool b_mn_major = false) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (b_mn_major ? (1u << 16) : 0u) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// 16-byte shared-memory load / store by 32-bit shared address.
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tcgen05.mma) before it signals a consumer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// --- tcgen05 issue ----------------------------------------------------------
+// The MMA and commit wrappers are WARP-WIDE: all 32 lanes of a converged warp
+// execute them with identical (warp-uniform) operands and elect.sync picks the
+// one lane that issues the instruction.  Measured on B200, keeping the MMA
+// issuer's loop warp-uniform this way issues six tf32 MMAs in ~150 cycles
+// instead of ~350 when one lane runs the loop alone, which is what lets a
+// 128 x 256 stage (768 tensor cycles) keep the tensor pipe busy.
+
+// D[tmem] (+)= A[smem] * B[smem]^T.
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-// Arrive on `bar` once every tcgen05.mma issued so far by this thread completes.
+// Arrive on `bar` once every tcgen05.mma issued so far by this warp completes.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar))
+      : "memory");
+}
+
+// mbar_wait by every lane of a warp, with a warp-uniform result (a lane whose
+// budget ran out makes the whole warp give up), so the warp stays converged
+// for the elect.sync of the wrappers above.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, unsigned *err, unsigned site,
+                                               volatile int *abort, long long budget = kWaitCycles) {
+  const bool ok = mbar_wait(bar, parity, err, site, abort, budget);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp receives its
@@ -207,6 +270,21 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// Store 4 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2,
+                                                  uint32_t r3) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
+}
+
+// Store 8 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 // Store 16 consecutive 32-bit columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -220,13 +298,14 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // D[tmem] (+)= A[tmem] * B[smem]^T: the A operand (M rows = TMEM lanes, K
-// 32-bit columns) is read from tensor memory.
+// 32-bit columns) is read from tensor memory.  Warp-wide, like mma_tf32.
 __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -78,6 +78,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
     "b2k_gemm_set_streamk": ([C.c_int], C.c_int),
+    "b2k_gemm_set_fused_split": ([C.c_int], C.c_int),
     "b2k_attention_set_fused": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
@@ -215,6 +216,11 @@ class Context:
 
     def set_gemm_variant(self, variant: int) -> None:
         self.check(self.lib.b2k_gemm_set_variant(variant), "b2k_gemm_set_variant")
+
+    def set_gemm_fused_split(self, mode: int) -> None:
+        """0 = pre-pass split of A and B, 1 = A split in-kernel into TMEM (default),
+        2 = A and B split in shared memory inside the kernel."""
+        self.check(self.lib.b2k_gemm_set_fused_split(int(mode)), "b2k_gemm_set_fused_split")
 
     def set_gemm_streamk(self, on: bool) -> None:
         self.check(self.lib.b2k_gemm_set_streamk(int(bool(on))), "b2k_gemm_set_streamk")

@@ -245,7 +245,9 @@ int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c, int64_t m,
  * tuning and benchmarking): 0 = 128x256 tile, 128-byte swizzle, 2 stages;
  * 1 = 128x256, 64-byte swizzle, 4 stages (default); 2 = 128x128, 128-byte
  * swizzle, 3 stages; 3 = 128x192, 64-byte swizzle, 5 stages.  Outputs at
- * most 128 columns wide always use 2.  No counterpart in the reference, whose plan
+ * most 128 columns wide always use 2.  For the in-kernel split kernels
+ * (b2k_gemm_set_fused_split) variant 2 selects 128-wide tiles and every
+ * other variant 192-wide ones.  No counterpart in the reference, whose plan
  * geometry comes from the IR. */
 int b2k_gemm_set_variant(int variant);
 /* Process-wide switch for the persistent stream-K schedule of the default
@@ -254,6 +256,21 @@ int b2k_gemm_set_variant(int variant);
  * of tiles does not idle SMs.  Off by default because it measured slower on
  * B200 than one tile per CTA.  No counterpart in the reference. */
 int b2k_gemm_set_streamk(int on);
+/* Process-wide choice of where b2k_gemm_tf32x3 (and the no-alloc variant)
+ * split operands into TF32 hi/lo halves:
+ *   1 (default)  A is staged raw by TMA and split inside the tensor-core
+ *                kernel into tensor memory, which the MMAs read A from; B is
+ *                split once by a pre-pass.  Needs A 16-byte aligned with a row
+ *                stride that is a multiple of 4 elements and K >= 16.
+ *   2            both operands staged raw and split in shared memory inside
+ *                the kernel (no pre-pass, no scratch; both operands must be
+ *                TMA-readable as above).  Measured slower on B200: the split
+ *                doubles the shared-memory traffic the tensor core competes for.
+ *   0            both operands split by the pre-pass.
+ * Calls whose operands do not meet a mode's conditions take the next mode
+ * down.  Returns B2K_EINVAL for other values.  No counterpart in the
+ * reference. */
+int b2k_gemm_set_fused_split(int mode);
 
 #ifdef __cplusplus
 }

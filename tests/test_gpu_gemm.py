@@ -102,10 +102,12 @@ def test_gemm_every_variant(ctx, torch_cuda, variant, m, n, k):
     a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
     b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
     ctx.set_gemm_variant(variant)
+    ctx.set_gemm_fused_split(0)  # variants select pre-pass kernels
     try:
         got = run_gemm(ctx, torch_cuda, a, b)
     finally:
         ctx.set_gemm_variant(1)
+        ctx.set_gemm_fused_split(1)
     assert tf32.normwise_error(got, a.astype(np.float64) @ b.astype(np.float64)) <= NORMWISE
 
 
@@ -119,13 +121,77 @@ def test_gemm_streamk_opt_in(ctx, torch_cuda, m, n, k, b_layout):
     b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
     bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
     ctx.set_gemm_streamk(True)
+    ctx.set_gemm_fused_split(0)  # stream-K is a schedule of the pre-pass kernel
     try:
         got = run_gemm(ctx, torch_cuda, a, b, b_layout=b_layout, bias=bias, relu=True)
         again = run_gemm(ctx, torch_cuda, a, b, b_layout=b_layout, bias=bias, relu=True)
     finally:
         ctx.set_gemm_streamk(False)
+        ctx.set_gemm_fused_split(1)
     bm = b if b_layout == 0 else b.T
     rows = np.random.default_rng(5).choice(m, min(m, 128), replace=False)
     exact = np.maximum(a[rows].astype(np.float64) @ bm.astype(np.float64) + bias, 0.0)
     assert tf32.normwise_error(got[rows], exact) <= NORMWISE
     np.testing.assert_array_equal(got, again)  # fixed combination order
+
+
+FUSED_CASES = [
+    (4096, 4096, 4096, 0), (1000, 1000, 776, 1), (300, 520, 200, 0), (257, 384, 1000, 0), (130, 96, 48, 1),
+    (130, 96, 48, 0), (64, 128, 16, 0), (33, 200, 20, 1), (512, 200, 36, 0), (2048, 4000, 300, 1),
+]
+
+
+@pytest.mark.parametrize("m,n,k,b_layout", FUSED_CASES)
+def test_gemm_split_modes_match_float64_and_each_other(ctx, torch_cuda, m, n, k, b_layout):
+    """The three split placements (0: pre-pass for A and B; 1: A split into
+    TMEM inside the kernel, B pre-split; 2: A and B split in shared memory,
+    B read K-major or MN-major) against float64, the 3xTF32 model and each
+    other on the same inputs.  Shapes cover ragged M, N and K, N <= 128 and
+    K = 16."""
+    rng = np.random.default_rng(m * 31 + n * 7 + k + b_layout)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    got = {}
+    try:
+        for mode in (0, 1, 2):
+            ctx.set_gemm_fused_split(mode)
+            got[mode] = run_gemm(ctx, torch_cuda, a, b, b_layout=b_layout, bias=bias, relu=True)
+    finally:
+        ctx.set_gemm_fused_split(1)
+    bm = b if b_layout == 0 else b.T
+    rows = np.arange(m) if m <= 512 else np.random.default_rng(1).choice(m, 256, replace=False)
+    exact = np.maximum(a[rows].astype(np.float64) @ bm.astype(np.float64) + bias, 0.0)
+    model = np.maximum(tf32.gemm_3xtf32(a, bm) + bias, 0.0) if m * n * k <= 1 << 24 else None
+    for mode in (1, 2):
+        assert tf32.normwise_error(got[mode][rows], exact) <= NORMWISE, mode
+        assert tf32.normwise_error(got[mode], got[0]) <= 1e-7, mode
+        if model is not None:
+            assert tf32.normwise_error(got[mode], model) <= 2e-6, mode
+
+
+def test_gemm_fused_split_special_values(ctx, torch_cuda):
+    """Max-finite times zero stays 0 and infinities propagate through the
+    in-kernel split as through the pre-pass split."""
+    a = np.full((128, 32), np.finfo(np.float32).max, dtype=np.float32)
+    b = np.zeros((32, 64), dtype=np.float32)
+    np.testing.assert_array_equal(run_gemm(ctx, torch_cuda, a, b), np.zeros((128, 64), np.float32))
+    # inf * (B's lo half = 0) is NaN in the hi*lo term, as in the reference's
+    # 3xTF32 model; the in-kernel split must match the pre-pass split exactly.
+    a = np.ones((128, 32), dtype=np.float32)
+    a[5, 3] = np.inf
+    a[9, 0] = np.nan
+    b = np.ones((32, 64), dtype=np.float32)
+    b[2, 7] = 1.5
+    got = {}
+    try:
+        for mode in (0, 1, 2):
+            ctx.set_gemm_fused_split(mode)
+            got[mode] = run_gemm(ctx, torch_cuda, a, b)
+    finally:
+        ctx.set_gemm_fused_split(1)
+    np.testing.assert_array_equal(got[1], got[0])
+    np.testing.assert_array_equal(got[2], got[0])
+    got = got[1]
+    finite = np.setdiff1d(np.arange(128), [5, 9])
+    np.testing.assert_array_equal(got[finite], (a[finite].astype(np.float64) @ b).astype(np.float32))
