@@ -73,6 +73,7 @@ struct FusedArgs {
 template <int BN>
 struct Slice {
   static constexpr int CPT = BN / 4;
+  static_assert(CPT % 8 == 0, "slice width");
   float acc[CPT];
   int quarter, slice, lane;
 
@@ -93,12 +94,20 @@ struct Slice {
     sm100::tc_fence_after();
     const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + slice * CPT);
 #pragma unroll
-    for (int j = 0; j < CPT; j += 16) {
+    for (int j = 0; j + 16 <= CPT; j += 16) {
       uint32_t r[16];
       sm100::tmem_ld_32x32b_x16(taddr + j, r);
       sm100::tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+    }
+    if constexpr (CPT % 16 != 0) {
+      constexpr int j = CPT - 8;
+      uint32_t r[8];
+      sm100::tmem_ld_32x32b_x8(taddr + j, r);
+      sm100::tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
     }
     sm100::tc_fence_before();
     __syncwarp();
@@ -158,7 +167,7 @@ struct TmemAShape {
   static_assert(kSmem <= 227 * 1024, "stage ring exceeds shared memory");
 };
 
-template <int BN>
+template <int BN, int G>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tmem_a_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
                        const __grid_constant__ CUtensorMap map_blo, const FusedArgs args) {
@@ -191,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::mbar_init(&full_bar[s], 1);
       sm100::mbar_init(&empty_bar[s], 1);
     }
-    for (int t = 0; t < Shape::kAStages; ++t) sm100::mbar_init(&a_full[t], kGroupWarps);
+    for (int t = 0; t < Shape::kAStages; ++t) sm100::mbar_init(&a_full[t], kWorkWarps / G);
     for (int b = 0; b < 2; ++b) {
       sm100::mbar_init(&tmem_full[b], 1);
       sm100::mbar_init(&tmem_empty[b], kWorkWarps);
@@ -265,10 +274,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::mbar_wait(&drain_bar, 0, args.err, sm100::kSiteDrain, &never);
     }
   } else {
-    // Split: thread (quarter q, lane l) owns A row 32q + l = TMEM lane 32q + l
-    // and splits all 16 K values of that row for its group's stages.
+    // Split: thread (quarter q, lane l) owns A row 32q + l = TMEM lane 32q + l.
+    // The 16 K values of a staged row are four 16-byte chunks; with G stage
+    // groups each of the 4 / G warps of a quarter in a group splits G chunks.
     Slice<BN> out(warp);
-    const int group = out.slice;
+    constexpr int kPerQuarter = 4 / G;  // warps of one quarter in one group
+    const int group = out.slice / kPerQuarter;
+    const int chunk0 = (out.slice % kPerQuarter) * G;
     const int row = out.quarter * 32 + out.lane;
     // Raw A rows are 64 bytes with the 64-byte TMA swizzle: 16-byte chunk c of
     // row r sits at chunk c ^ ((r >> 1) & 3) (conflict-free across 8 rows).
@@ -277,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = (uint32_t)(out.quarter * 32) << 16;
     bool ok = true;
     int folded = 0;
-    for (int kb = group; kb < num_kb && ok; kb += kGroups) {
+    for (int kb = group; kb < num_kb && ok; kb += G) {
       const int s = kb % Shape::kStages;
       if (!sm100::mbar_wait(&full_bar[s], (kb / Shape::kStages) & 1, args.err, sm100::kSiteConvert, abort)) {
         ok = false;
@@ -299,20 +311,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t src = sm100::smem_addr(a_raw(s)) + row_off;
       const uint32_t dst = tmem_a + lane_base + (uint32_t)(t * 32);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t h[8], l[8];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint32_t c = (uint32_t)(2 * half + q);
-          float4 hv, lv;
-          split_tf32x4(sm100::lds128(src + 16u * (c ^ swz)), hv, lv);
-          h[4 * q + 0] = __float_as_uint(hv.x), h[4 * q + 1] = __float_as_uint(hv.y);
-          h[4 * q + 2] = __float_as_uint(hv.z), h[4 * q + 3] = __float_as_uint(hv.w);
-          l[4 * q + 0] = __float_as_uint(lv.x), l[4 * q + 1] = __float_as_uint(lv.y);
-          l[4 * q + 2] = __float_as_uint(lv.z), l[4 * q + 3] = __float_as_uint(lv.w);
-        }
-        sm100::tmem_st_32x32b_x8(dst + 8 * half, h);
-        sm100::tmem_st_32x32b_x8(dst + 16 + 8 * half, l);
+      for (int q = 0; q < G; ++q) {
+        const uint32_t c = (uint32_t)(chunk0 + q);
+        float4 hv, lv;
+        split_tf32x4(sm100::lds128(src + 16u * (c ^ swz)), hv, lv);
+        sm100::tmem_st_32x32b_x4(dst + 4 * c, __float_as_uint(hv.x), __float_as_uint(hv.y), __float_as_uint(hv.z),
+                                 __float_as_uint(hv.w));
+        sm100::tmem_st_32x32b_x4(dst + 16 + 4 * c, __float_as_uint(lv.x), __float_as_uint(lv.y),
+                                 __float_as_uint(lv.z), __float_as_uint(lv.w));
       }
       sm100::tmem_st_wait();
       sm100::tc_fence_before();
@@ -536,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // --- host side -------------------------------------------------------------
-template <int BN>
+template <int BN, int G>
 int launch_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const b2k::SplitOperands &ops, float *c,
                   int64_t m, int64_t n, int64_t ldc, const float *bias, int relu, cudaStream_t s) {
   using Shape = TmemAShape<BN>;
@@ -550,7 +556,7 @@ int launch_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const b2
     status = b2k::make_map_2d(ctx, &map_blo, ops.b_lo, ops.kp, n, ops.kp, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B);
   if (status != B2K_OK) return status;
   FusedArgs args{c, bias, m, n, ldc, (int)(ops.kp / BK), relu, ctx->error_flag};
-  auto kernel = gemm_tmem_a_kernel<BN>;
+  auto kernel = gemm_tmem_a_kernel<BN, G>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (TMEM A): set smem");
   dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM), 1);
@@ -605,8 +611,9 @@ int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_
 int gemm_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const SplitOperands &ops, float *c, int64_t m,
                 int64_t n, int64_t ldc, const float *bias, int relu, cudaStream_t s) {
   PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
-  if (n <= 128 || gemm_variant() == 2) return launch_tmem_a<128>(ctx, a, k, lda, ops, c, m, n, ldc, bias, relu, s);
-  return launch_tmem_a<192>(ctx, a, k, lda, ops, c, m, n, ldc, bias, relu, s);
+  // Four stage groups measured fastest (vs. 2 and 1) on B200.
+  if (n <= 128 || gemm_variant() == 2) return launch_tmem_a<128, 4>(ctx, a, k, lda, ops, c, m, n, ldc, bias, relu, s);
+  return launch_tmem_a<192, 4>(ctx, a, k, lda, ops, c, m, n, ldc, bias, relu, s);
 }
 
 int gemm_smem_split(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
