@@ -77,7 +77,6 @@ class Workload:
     unit = ""
     bound = "hbm"
     phase = ""          # library timing phase of the dominant kernel
-    launches_per_step = 1
     profile = ""
 
     def __init__(self, rank: int, world: int):
@@ -113,7 +112,7 @@ class Workload:
 
 
 class Gemm(Workload):
-    name, unit, bound, phase, launches_per_step = "gemm", "TFLOP/s", "tensor", "mma", 3
+    name, unit, bound, phase = "gemm", "TFLOP/s", "tensor", "mma"
     profile = "gemm_tf32x3_4096"
 
     def __init__(self, rank, world, m=4096, n=4096, k=4096, ragged=False):
@@ -191,7 +190,7 @@ class Gemm(Workload):
 
 
 class Softmax(Workload):
-    name, unit, bound, phase, launches_per_step = "softmax", "GB/s", "hbm", "softmax", 1
+    name, unit, bound, phase = "softmax", "GB/s", "hbm", "softmax"
     profile = "row_softmax_4096x8192"
 
     def __init__(self, rank, world, rows=4096, cols=8192):
@@ -239,7 +238,7 @@ class Softmax(Workload):
 
 
 class Add(Workload):
-    name, unit, bound, phase, launches_per_step = "add", "GB/s", "hbm", "pointwise", 1
+    name, unit, bound, phase = "add", "GB/s", "hbm", "pointwise"
     profile = "pointwise_add_2e24"
 
     def __init__(self, rank, world, n=1 << 24):
@@ -290,7 +289,7 @@ class Add(Workload):
 
 
 class Attention(Workload):
-    name, unit, bound, phase, launches_per_step = "attention", "TFLOP/s", "tensor", "flash", 4
+    name, unit, bound, phase = "attention", "TFLOP/s", "tensor", "flash"
     profile = "attention_tf32x3_64x2048x128"
 
     def __init__(self, rank, world, bh=64, seq=2048, d=128):
@@ -463,11 +462,13 @@ def run_ours(args) -> dict | None:
     ctx.timing_reset()
     ctx.timing(True)
     barrier()
+    launches_before = ctx.kernel_launches()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(args.steps):
         w.step()
     stop.record()
+    launches = ctx.kernel_launches() - launches_before
     barrier()
     clocks = sampler.stop()
     ctx.sync()  # surfaces a device-side error status
@@ -527,7 +528,7 @@ def run_ours(args) -> dict | None:
                          "peak_basis": peak_note},
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "gpu_launches": w.launches_per_step * args.steps,
+            "gpu_launches": launches,
         }
     session.close()
     ctx.close()

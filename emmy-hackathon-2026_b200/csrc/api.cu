@@ -81,6 +81,12 @@ int b2k_timing_read(b2k_ctx *ctx, int phase, double *total_ms, int64_t *launches
   return B2K_OK;
 }
 
+int b2k_kernel_launches(b2k_ctx *ctx, int64_t *count) {
+  if (!ctx || !count) return B2K_EINVAL;
+  *count = ctx->kernel_launches;
+  return B2K_OK;
+}
+
 int b2k_timing_reset(b2k_ctx *ctx) {
   if (!ctx) return B2K_EINVAL;
   for (auto &list : ctx->phase_events) {

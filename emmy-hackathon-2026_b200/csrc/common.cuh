@@ -22,6 +22,8 @@ struct b2k_ctx {
   size_t workspace_bytes = 0;
   // Device-side error word written by kernels whose bounded waits expire.
   unsigned int *error_flag = nullptr;
+  // Kernels enqueued through this context (b2k_kernel_launches).
+  int64_t kernel_launches = 0;
   // Stream-K flag slots in the workspace and the epoch of the last GEMM.
   unsigned *flags_ptr = nullptr;
   unsigned flags_epoch = 0;
@@ -48,12 +50,13 @@ inline int cuda_fail(b2k_ctx *ctx, cudaError_t err, const char *what) {
   return fail(ctx, B2K_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
 }
 
-// Check the launch that was just enqueued (configuration errors only; the
-// kernel itself runs asynchronously).
-inline int check_launch(b2k_ctx *ctx, const char *what) {
+// Check the `launches` kernel launches just enqueued (configuration errors
+// only; the kernels themselves run asynchronously) and count them.
+inline int check_launch(b2k_ctx *ctx, const char *what, int launches = 1) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return cuda_fail(ctx, err, what);
   ctx->error.clear();
+  ctx->kernel_launches += launches;
   return B2K_OK;
 }
 

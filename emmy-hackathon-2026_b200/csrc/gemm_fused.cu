@@ -184,8 +184,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
-  const int64_t n0 = (int64_t)blockIdx.x * BN;
-  const int64_t m0 = (int64_t)blockIdx.y * BM;
+  // M-fastest raster: the CTAs resident at one time share a few B column
+  // tiles (B_hi/B_lo are twice A's size) and sweep A, so both stay in L2.
+  const int64_t m0 = (int64_t)blockIdx.x * BM;
+  const int64_t n0 = (int64_t)blockIdx.y * BN;
   const int num_kb = args.num_kb;
   const int num_chunks = (num_kb + kChunkBlocks - 1) / kChunkBlocks;
   volatile int *abort = &abort_word;
@@ -559,7 +561,8 @@ int launch_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const b2
   auto kernel = gemm_tmem_a_kernel<BN, G>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (TMEM A): set smem");
-  dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM), 1);
+  if ((n + BN - 1) / BN > 65535) return b2k::fail(ctx, B2K_EINVAL, "gemm: N exceeds %d", 65535 * BN);
+  dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN), 1);
   kernel<<<grid, kThreads, Shape::kSmem, s>>>(map_a, map_bhi, map_blo, args);
   return b2k::check_launch(ctx, "gemm (TMEM A) launch");
 }

@@ -208,6 +208,7 @@ extern "C" int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, co
   cudaStream_t s = (cudaStream_t)stream;
   b2k::PhaseTimer timer(ctx, B2K_PHASE_POINTWISE, s);
   int64_t done = 0;
+  int launches = 0;
   if (vector_ok && n >= 4) {
     const int64_t n4 = n >> 2;
     const int64_t per_block = (int64_t)kThreads * kUnroll;
@@ -216,12 +217,14 @@ extern "C" int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, co
     if (!launch_binary_fast(*program, inputs, out, n4, (int)blocks, s))
       pw_program_vec4<<<(int)blocks, kThreads, 0, s>>>(params);
     done = n4 << 2;
+    ++launches;
   }
   if (done < n) {
     const int64_t rest = n - done;
     const int64_t blocks = (rest + kThreads - 1) / kThreads;
     if (blocks > INT32_MAX) return b2k::fail(ctx, B2K_EINVAL, "pointwise: extent too large");
     pw_program_scalar<<<(int)blocks, kThreads, 0, s>>>(params, done);
+    ++launches;
   }
-  return b2k::check_launch(ctx, "pointwise launch");
+  return b2k::check_launch(ctx, "pointwise launch", launches);
 }

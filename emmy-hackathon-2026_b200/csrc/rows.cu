@@ -160,7 +160,7 @@ extern "C" int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const 
     float *partials = static_cast<float *>(ctx->workspace);
     sum_partials<<<parts, kThreads, 0, s>>>(x, cols, partials);
     sum_finish<<<1, kThreads, 0, s>>>(a, partials, parts, y);
-    return b2k::check_launch(ctx, "row_op sum launch");
+    return b2k::check_launch(ctx, "row_op sum launch", 2);
   }
   const bool vec = (cols % 4 == 0) && (ld_x % 4 == 0) && b2k::aligned16(x) &&
                    (params->op == B2K_ROW_SUM || ((ld_y % 4 == 0) && b2k::aligned16(y) &&

@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_timing_enable": ([_P, C.c_int], C.c_int),
     "b2k_timing_read": ([_P, C.c_int, C.POINTER(C.c_double), C.POINTER(_I64)], C.c_int),
     "b2k_timing_reset": ([_P], C.c_int),
+    "b2k_kernel_launches": ([C.c_void_p, C.POINTER(_I64)], C.c_int),
 }
 
 PHASES = {"split": 0, "mma": 1, "pointwise": 2, "softmax": 3, "attention": 4, "rows": 5, "flash": 6}
@@ -216,6 +217,12 @@ class Context:
 
     def set_gemm_variant(self, variant: int) -> None:
         self.check(self.lib.b2k_gemm_set_variant(variant), "b2k_gemm_set_variant")
+
+    def kernel_launches(self) -> int:
+        """Kernels this context has enqueued since it was created."""
+        count = _I64()
+        self.check(self.lib.b2k_kernel_launches(self.handle, C.byref(count)), "b2k_kernel_launches")
+        return int(count.value)
 
     def set_gemm_fused_split(self, mode: int) -> None:
         """0 = pre-pass split of A and B, 1 = A split in-kernel into TMEM (default),

@@ -70,7 +70,10 @@ int b2k_stream_sync(b2k_ctx *ctx, void *stream);
  * with CUDA events recorded on the caller's stream (the runner's event
  * timing, tools/local_runner.py:318-332, per kernel instead of per launch
  * request).  b2k_timing_read synchronises and sums the recorded intervals of
- * one phase; b2k_timing_reset forgets them. */
+ * one phase (`launches` = intervals: one per entry-point call of the phase,
+ * which may cover more than one kernel); b2k_timing_reset forgets them.
+ * b2k_kernel_launches returns how many kernels the context has enqueued
+ * since b2k_init (every launch is counted, timing enabled or not). */
 #define B2K_PHASE_SPLIT 0     /* 3xTF32 operand split pre-pass */
 #define B2K_PHASE_MMA 1       /* tcgen05 GEMM main kernel */
 #define B2K_PHASE_POINTWISE 2 /* pointwise programs */
@@ -82,6 +85,7 @@ int b2k_stream_sync(b2k_ctx *ctx, void *stream);
 int b2k_timing_enable(b2k_ctx *ctx, int on);
 int b2k_timing_read(b2k_ctx *ctx, int phase, double *total_ms, int64_t *launches);
 int b2k_timing_reset(b2k_ctx *ctx);
+int b2k_kernel_launches(b2k_ctx *ctx, int64_t *count);
 
 /* --- pointwise programs ---------------------------------------------------
  * Replaces the SIMT Emitter's pointwise lowering: Tile decode
