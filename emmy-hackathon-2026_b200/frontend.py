@@ -62,35 +62,48 @@ class KernelSpec:
                 "params": self.params, "zero_outputs": self.zero_outputs, "certificate": self.certificate}
 
     # --- launch -----------------------------------------------------------------
-    def launch(self, ctx, pointers: dict, stream: int = 0) -> None:
-        """Run on the GPU; ``pointers`` maps argument names to device addresses."""
-        from . import runtime
-        p = self.params
+    def descriptor(self):
+        """The b2k_kernel_desc of this kernel: its kind, and each operand role as
+        an index into the positional ``arg_order`` arguments."""
+        from . import runtime as rt
+        p, pos = self.params, {name: i for i, name in enumerate(self.arg_order)}
         if self.kind == "pointwise":
-            prog = runtime.make_program(len(p["inputs"]), [tuple(i) for i in p["insns"]], p["result"],
-                                        broadcast=tuple(i for i, b in enumerate(p["broadcast"]) if b))
-            ctx.pointwise(prog, [pointers[n] for n in p["inputs"]], pointers[p["output"]], p["n"], stream)
-        elif self.kind == "row_softmax":
-            ctx.row_softmax(pointers[p["x"]], pointers[p["out"]], p["rows"], p["cols"], stream=stream)
-        elif self.kind == "matmul":
-            ctx.gemm(pointers[p["a"]], pointers[p["b"]], pointers[p["out"]], p["m"], p["n"], p["k"], stream=stream)
-        elif self.kind == "attention":
-            ctx.attention(pointers[p["q"]], pointers[p["kt"]], pointers[p["v"]], pointers[p["out"]],
-                          1, p["s_q"], p["s_kv"], p["d"], p["dv"], scale_ptr=pointers[p["scale"]],
-                          k_layout=runtime.K_DS, stream=stream)
-        elif self.kind == "row_reduce":
-            buf = p["sum_div_buffer"]
-            ctx.row_op(runtime.ROW_SUM, pointers[p["x"]], pointers[p["out"]], p["rows"], p["cols"],
-                       sum_div=p["sum_div"], sum_div_ptr=pointers[buf] if buf else 0, stream=stream)
-        elif self.kind == "row_norm":
-            op = runtime.ROW_RMSNORM if p["op"] == "rmsnorm" else runtime.ROW_L2NORM
-            eb, cb = p["eps_buffer"], p["count_buffer"]
-            ctx.row_op(op, pointers[p["x"]], pointers[p["out"]], p["rows"], p["cols"],
-                       ms_div=float(p["cols"]) if p["op"] == "rmsnorm" else 1.0,
-                       ms_div_ptr=pointers[cb] if cb else 0, eps=p["eps"], eps_ptr=pointers[eb] if eb else 0,
-                       w=pointers[p["w"]] if p["w"] else 0, stream=stream)
-        else:
-            raise Unsupported(f"no launcher for {self.kind}")
+            prog = rt.make_program(len(p["inputs"]), [tuple(i) for i in p["insns"]], p["result"],
+                                   broadcast=tuple(i for i, b in enumerate(p["broadcast"]) if b))
+            roles = {i: pos[n] for i, n in enumerate(p["inputs"])}
+            roles[rt.ROLE_PW_OUT] = pos[p["output"]]
+            return rt.make_desc(rt.KIND_POINTWISE, roles, dims=(p["n"],), program=prog)
+        if self.kind == "row_softmax":
+            return rt.make_desc(rt.KIND_ROW_SOFTMAX, {0: pos[p["x"]], 1: pos[p["out"]]},
+                                dims=(p["rows"], p["cols"], p["cols"], p["cols"]))
+        if self.kind == "matmul":
+            return rt.make_desc(rt.KIND_GEMM, {0: pos[p["a"]], 1: pos[p["b"]], 2: pos[p["out"]]},
+                                dims=(p["m"], p["n"], p["k"], p["k"], p["n"], p["n"]), flags=(rt.B_KN, 0))
+        if self.kind == "attention":
+            return rt.make_desc(rt.KIND_ATTENTION, {0: pos[p["q"]], 1: pos[p["kt"]], 2: pos[p["v"]],
+                                                    3: pos[p["out"]], 4: pos[p["scale"]]},
+                                dims=(1, p["s_q"], p["s_kv"], p["d"], p["dv"]), flags=(rt.K_DS,))
+        if self.kind == "row_reduce":
+            roles = {0: pos[p["x"]], 1: pos[p["out"]]}
+            if p["sum_div_buffer"]:
+                roles[3] = pos[p["sum_div_buffer"]]
+            return rt.make_desc(rt.KIND_ROW_OP, roles, dims=(p["rows"], p["cols"], p["cols"], p["cols"]),
+                                flags=(rt.ROW_SUM,), values=(p["sum_div"], 1.0, 0.0))
+        if self.kind == "row_norm":
+            rms = p["op"] == "rmsnorm"
+            roles = {0: pos[p["x"]], 1: pos[p["out"]]}
+            for role, key in ((2, "w"), (4, "count_buffer"), (5, "eps_buffer")):
+                if p[key]:
+                    roles[role] = pos[p[key]]
+            return rt.make_desc(rt.KIND_ROW_OP, roles, dims=(p["rows"], p["cols"], p["cols"], p["cols"]),
+                                flags=(rt.ROW_RMSNORM if rms else rt.ROW_L2NORM,),
+                                values=(1.0, float(p["cols"]) if rms else 1.0, p["eps"]))
+        raise Unsupported(f"no launcher for {self.kind}")
+
+    def launch(self, ctx, pointers: dict, stream: int = 0) -> None:
+        """Run on the GPU through b2k_launch; ``pointers`` maps argument names to
+        device addresses (every recognised kernel takes only buffers)."""
+        ctx.launch(self.descriptor(), [int(pointers[name]) for name in self.arg_order], stream)
 
 
 # --------------------------------------------------------------------------- loading

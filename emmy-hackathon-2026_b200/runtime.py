@@ -45,6 +45,35 @@ class RowParams(C.Structure):
 ROW_SUM, ROW_RMSNORM, ROW_L2NORM = 0, 1, 2
 
 
+KIND_POINTWISE, KIND_ROW_SOFTMAX, KIND_ROW_OP, KIND_GEMM, KIND_ATTENTION = 1, 2, 3, 4, 5
+MAX_ROLES, NO_ARG, ROLE_PW_OUT = 12, -1, 8
+
+
+class KernelDesc(C.Structure):
+    """b2k_kernel_desc: which kernel runs and which positional arguments feed it."""
+    _fields_ = [("kind", C.c_int32), ("role", C.c_int32 * MAX_ROLES), ("dims", C.c_int64 * 6),
+                ("flags", C.c_int32 * 4), ("values", C.c_float * 4), ("program", C.c_void_p)]
+
+
+def make_desc(kind: int, roles: dict, dims=(), flags=(), values=(), program=None) -> KernelDesc:
+    """Descriptor with `roles` = {role: positional argument index}; unset roles are NO_ARG."""
+    desc = KernelDesc()
+    desc.kind = kind
+    for r in range(MAX_ROLES):
+        desc.role[r] = NO_ARG
+    for r, idx in roles.items():
+        desc.role[r] = idx
+    for i, v in enumerate(dims):
+        desc.dims[i] = int(v)
+    for i, v in enumerate(flags):
+        desc.flags[i] = int(v)
+    for i, v in enumerate(values):
+        desc.values[i] = float(v)
+    desc.program = C.cast(C.pointer(program), C.c_void_p) if program is not None else None
+    desc._program_ref = program  # keeps the program alive as long as the descriptor
+    return desc
+
+
 class PwInsn(C.Structure):
     _fields_ = [("op", C.c_int32), ("a", C.c_int32), ("b", C.c_int32), ("c", C.c_int32), ("imm", C.c_float)]
 
@@ -86,6 +115,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_timing_read": ([_P, C.c_int, C.POINTER(C.c_double), C.POINTER(_I64)], C.c_int),
     "b2k_timing_reset": ([_P], C.c_int),
     "b2k_kernel_launches": ([C.c_void_p, C.POINTER(_I64)], C.c_int),
+    "b2k_selftest_wait_timeout": ([C.c_void_p, _I64, C.c_void_p], C.c_int),
+    "b2k_launch": ([C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p), C.c_int32, C.c_void_p], C.c_int),
 }
 
 PHASES = {"split": 0, "mma": 1, "pointwise": 2, "softmax": 3, "attention": 4, "rows": 5, "flash": 6}
@@ -217,6 +248,14 @@ class Context:
 
     def set_gemm_variant(self, variant: int) -> None:
         self.check(self.lib.b2k_gemm_set_variant(variant), "b2k_gemm_set_variant")
+
+    def launch(self, desc: KernelDesc, arg_values: list, stream: int = 0) -> None:
+        """b2k_launch with the positional arguments in arg_order: ints are device
+        addresses, floats are f32 scalars (each passed as a pointer to its value,
+        the cuLaunchKernel params convention)."""
+        slots = [C.c_uint64(v) if isinstance(v, int) else C.c_float(v) for v in arg_values]
+        params = (C.c_void_p * max(1, len(slots)))(*[C.cast(C.pointer(x), C.c_void_p) for x in slots])
+        self.check(self.lib.b2k_launch(self.handle, C.byref(desc), params, len(slots), stream), "b2k_launch")
 
     def kernel_launches(self) -> int:
         """Kernels this context has enqueued since it was created."""

@@ -64,6 +64,14 @@ int b2k_memset(b2k_ctx *ctx, void *dst, int value, size_t bytes, void *stream);
 int b2k_host_alloc(b2k_ctx *ctx, void **ptr, size_t bytes);
 int b2k_host_free(b2k_ctx *ctx, void *ptr);
 int b2k_stream_sync(b2k_ctx *ctx, void *stream);
+/* Failure-detection self test: launches one kernel whose mbarrier wait can
+ * never complete and gives up after `budget_cycles` SM cycles (at most the
+ * kernels' own ~2 s budget), exactly as a stalled tensor-core kernel would.
+ * The following b2k_stream_sync returns B2K_ETIMEOUT and clears the device
+ * error word; the context stays usable.  No counterpart in the reference
+ * (its runner retires a worker process on any CUDA error,
+ * tools/local_runner.py:246-342). */
+int b2k_selftest_wait_timeout(b2k_ctx *ctx, int64_t budget_cycles, void *stream);
 
 /* --- per-phase timing -------------------------------------------------------
  * When enabled, every entry point brackets the kernels of each of its phases
@@ -223,6 +231,47 @@ int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k, const flo
 /* Process-wide switch: 1 (default) uses the fused kernel where head dims
  * allow, 0 forces the three-pass path (for comparisons). */
 int b2k_attention_set_fused(int fused);
+
+/* --- launch by descriptor ----------------------------------------------------
+ * The reference's runner launches a compiled kernel with
+ * cuLaunchKernel(fn, grid, block, smem, stream, params, NULL), `params` being
+ * pointers to the values of the positional meta.json arguments in arg_order
+ * (tools/local_runner.py:296-324; Emitter ABI binding compile.py:1995-2213).
+ * b2k_launch takes that same `args` array -- a device-pointer argument's slot
+ * points at its 64-bit address, an f32 scalar's slot at its value -- plus a
+ * descriptor naming the B200 kernel and which positional arguments feed it.
+ * The front end (frontend.py) fills the descriptor when it recognises an IR
+ * kernel; meta's grid/block are validated there, not obeyed (the sm_89
+ * geometry is not a B200 geometry).  zero_outputs stay with the caller, as in
+ * the reference's runner.  Every failure is reported before launching. */
+#define B2K_KIND_POINTWISE 1
+#define B2K_KIND_ROW_SOFTMAX 2
+#define B2K_KIND_ROW_OP 3
+#define B2K_KIND_GEMM_3XTF32 4
+#define B2K_KIND_ATTENTION_3XTF32 5
+#define B2K_MAX_ROLES 12
+#define B2K_NO_ARG (-1)
+#define B2K_ROLE_PW_OUT 8
+typedef struct b2k_kernel_desc {
+  int32_t kind;
+  /* Positional argument index of each operand role (B2K_NO_ARG if absent):
+   *   POINTWISE   roles 0..n_inputs-1 input streams, B2K_ROLE_PW_OUT output
+   *   ROW_SOFTMAX 0 x, 1 y
+   *   ROW_OP      0 x, 1 y, 2 weight, 3 sum-divisor buffer,
+   *               4 mean-square-divisor buffer, 5 epsilon buffer
+   *   GEMM_3XTF32 0 A, 1 B, 2 C, 3 bias
+   *   ATTENTION   0 Q, 1 K, 2 V, 3 O, 4 divisor buffer */
+  int32_t role[B2K_MAX_ROLES];
+  /* POINTWISE: n | ROW_*: rows, cols, ld_x, ld_y | GEMM: m, n, k, lda, ldb, ldc |
+   * ATTENTION: bh, s_q, s_kv, d, dv */
+  int64_t dims[6];
+  /* GEMM: b_layout, relu | ATTENTION: k_layout | ROW_OP: op */
+  int32_t flags[4];
+  /* ROW_OP: sum_div, ms_div, eps | ATTENTION: scale_div (when no buffer) */
+  float values[4];
+  const b2k_pw_program *program; /* POINTWISE */
+} b2k_kernel_desc;
+int b2k_launch(b2k_ctx *ctx, const b2k_kernel_desc *desc, void *const *args, int32_t nargs, void *stream);
 
 /* The same GEMM for callers that cannot allocate device memory (code running
  * under CUDA-graph capture or a fixed memory plan, or memory owned by another
