@@ -312,15 +312,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::tc_fence_after();
       const uint32_t src = sm100::smem_addr(a_raw(s)) + row_off;
       const uint32_t dst = tmem_a + lane_base + (uint32_t)(t * 32);
+      if constexpr (G == 4) {
+        // The whole 16-element row chunk: one 16-column store each for hi and lo.
+        uint32_t h[16], l[16];
+        float4 v[4];
 #pragma unroll
-      for (int q = 0; q < G; ++q) {
-        const uint32_t c = (uint32_t)(chunk0 + q);
-        float4 hv, lv;
-        split_tf32x4(sm100::lds128(src + 16u * (c ^ swz)), hv, lv);
-        sm100::tmem_st_32x32b_x4(dst + 4 * c, __float_as_uint(hv.x), __float_as_uint(hv.y), __float_as_uint(hv.z),
-                                 __float_as_uint(hv.w));
-        sm100::tmem_st_32x32b_x4(dst + 16 + 4 * c, __float_as_uint(lv.x), __float_as_uint(lv.y),
-                                 __float_as_uint(lv.z), __float_as_uint(lv.w));
+        for (int q = 0; q < 4; ++q) v[q] = sm100::lds128(src + 16u * ((uint32_t)q ^ swz));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float4 hv, lv;
+          split_tf32x4(v[q], hv, lv);
+          h[4 * q + 0] = __float_as_uint(hv.x), h[4 * q + 1] = __float_as_uint(hv.y);
+          h[4 * q + 2] = __float_as_uint(hv.z), h[4 * q + 3] = __float_as_uint(hv.w);
+          l[4 * q + 0] = __float_as_uint(lv.x), l[4 * q + 1] = __float_as_uint(lv.y);
+          l[4 * q + 2] = __float_as_uint(lv.z), l[4 * q + 3] = __float_as_uint(lv.w);
+        }
+        sm100::tmem_st_32x32b_x16(dst, h);
+        sm100::tmem_st_32x32b_x16(dst + 16, l);
+      } else {
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+          const uint32_t c = (uint32_t)(chunk0 + q);
+          float4 hv, lv;
+          split_tf32x4(sm100::lds128(src + 16u * (c ^ swz)), hv, lv);
+          sm100::tmem_st_32x32b_x4(dst + 4 * c, __float_as_uint(hv.x), __float_as_uint(hv.y), __float_as_uint(hv.z),
+                                   __float_as_uint(hv.w));
+          sm100::tmem_st_32x32b_x4(dst + 16 + 4 * c, __float_as_uint(lv.x), __float_as_uint(lv.y),
+                                   __float_as_uint(lv.z), __float_as_uint(lv.w));
+        }
       }
       sm100::tmem_st_wait();
       sm100::tc_fence_before();
