@@ -56,10 +56,12 @@ constexpr int kQBytes = (DMAX / 32) * kSub; // 64 KB per half
 // declared 1024-byte aligned (checked at run time) instead of carrying slack.
 constexpr int kSmem = 2 * kQBytes + kStages * 2 * kSub;
 
-// TMEM columns: S_j and then P_j's hi half share [0, 128); P_j's lo half
-// [128, 256); O buffers [256, 384) and [384, 512).
-constexpr uint32_t kColS = 0, kColPlo = 128;
-__host__ __device__ constexpr uint32_t o_col(int b) { return (uint32_t)(256 + b * 128); }
+// TMEM columns: two score buffers [0, 128) and [128, 256) -- S_j, then P_j's
+// hi half, in buffer j % 2 -- P_j's lo half [256, 384), O_j [384, 512).  With
+// two score buffers the tensor core computes S_{j+1} while the softmax warps
+// turn S_j into P_j.
+constexpr uint32_t kColPlo = 256, kColO = 384;
+__host__ __device__ constexpr uint32_t s_col(int j) { return (uint32_t)((j & 1) * 128); }
 
 struct FlashArgs {
   float *o;
@@ -77,8 +79,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
                         const FlashArgs args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full, s_full, p_full, drain;
-  __shared__ __align__(8) uint64_t ring_full[kStages], ring_empty[kStages], o_full[2], o_empty[2];
+  __shared__ __align__(8) uint64_t q_full, p_full, pv_done, drain;
+  __shared__ __align__(8) uint64_t ring_full[kStages], ring_empty[kStages], s_full[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_word;
   __shared__ float part_max[2][BM], part_sum[2][BM];
@@ -102,17 +104,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_word = (sm100::smem_addr(smem_raw) & 1023u) ? 1 : 0;
     if (abort_word) atomicOr(args.err, sm100::kSiteAttention);
     sm100::mbar_init(&q_full, 1);
-    sm100::mbar_init(&s_full, 1);
     sm100::mbar_init(&p_full, 8);  // one arrival per softmax warp
+    sm100::mbar_init(&pv_done, 1);
     sm100::mbar_init(&drain, 1);
     for (int i = 0; i < kStages; ++i) {
       sm100::mbar_init(&ring_full[i], 1);
       sm100::mbar_init(&ring_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      sm100::mbar_init(&o_full[i], 1);
-      sm100::mbar_init(&o_empty[i], 8);
-    }
+    for (int i = 0; i < 2; ++i) sm100::mbar_init(&s_full[i], 1);
     sm100::fence_barrier_init();
   }
   if (warp == 1) sm100::tmem_alloc(&tmem_slot, 512);
@@ -129,26 +128,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tma_load_3d(q_hi + c * kSub, &map_qhi, &q_full, c * 32, (int)m0, head);
         sm100::tma_load_3d(q_lo + c * kSub, &map_qlo, &q_full, c * 32, (int)m0, head);
       }
+      // Ring order = MMA order: K_0, then for each block j, K_{j+1} and V_j.
       int n = 0;  // chunks issued through the ring
       bool ok = true;
-      for (int j = 0; ok && j < nblocks; ++j) {
-        for (int c = 0; ok && c < dblocks + kVChunks; ++c, ++n) {
-          const int i = n % kStages;
-          if (n >= kStages &&
-              !sm100::mbar_wait(&ring_empty[i], ((n / kStages) - 1) & 1, args.err, sm100::kSiteAttention, abort)) {
-            ok = false;
-            break;
-          }
-          sm100::mbar_arrive_expect_tx(&ring_full[i], 2 * kSub);
-          if (c < dblocks) {  // K chunk: keys j*BN.., dims c*32..
-            sm100::tma_load_3d(st_hi(i), &map_khi, &ring_full[i], c * 32, j * BN, head);
-            sm100::tma_load_3d(st_lo(i), &map_klo, &ring_full[i], c * 32, j * BN, head);
-          } else {            // V^T chunk: dims 0..127, keys j*BN + 32*(c - dblocks)..
-            const int x = j * BN + 32 * (c - dblocks);
-            sm100::tma_load_3d(st_hi(i), &map_vhi, &ring_full[i], x, 0, head);
-            sm100::tma_load_3d(st_lo(i), &map_vlo, &ring_full[i], x, 0, head);
-          }
+      auto load_chunk = [&](bool is_k, int j, int c) {
+        const int i = n % kStages;
+        if (n >= kStages &&
+            !sm100::mbar_wait(&ring_empty[i], ((n / kStages) - 1) & 1, args.err, sm100::kSiteAttention, abort))
+          return false;
+        sm100::mbar_arrive_expect_tx(&ring_full[i], 2 * kSub);
+        if (is_k) {  // K chunk: keys j*BN.., dims c*32..
+          sm100::tma_load_3d(st_hi(i), &map_khi, &ring_full[i], c * 32, j * BN, head);
+          sm100::tma_load_3d(st_lo(i), &map_klo, &ring_full[i], c * 32, j * BN, head);
+        } else {     // V^T chunk: dims 0..127, keys j*BN + 32c..
+          const int x = j * BN + 32 * c;
+          sm100::tma_load_3d(st_hi(i), &map_vhi, &ring_full[i], x, 0, head);
+          sm100::tma_load_3d(st_lo(i), &map_vlo, &ring_full[i], x, 0, head);
         }
+        ++n;
+        return true;
+      };
+      for (int c = 0; ok && c < dblocks; ++c) ok = load_chunk(true, 0, c);
+      for (int j = 0; ok && j < nblocks; ++j) {
+        for (int c = 0; ok && j + 1 < nblocks && c < dblocks; ++c) ok = load_chunk(true, j + 1, c);
+        for (int c = 0; ok && c < kVChunks; ++c) ok = load_chunk(false, j, c);
       }
       int never = 0;  // drain loads in flight (budget only)
       sm100::mbar_wait(&q_full, 0, args.err, sm100::kSiteDrain, &never);
@@ -157,18 +160,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     {
-      // ---------------- MMA issuer
+      // ---------------- MMA issuer: S_0, then for each block j, S_{j+1}
+      // (into the other score buffer, overlapping softmax_j) and O_j = P_j V_j.
+      // S_{j+1} reuses the buffer P_{j-1} occupied; O_{j-1}'s MMAs, which read
+      // it, were issued earlier and tcgen05 MMAs of one issuer run in order.
       const uint32_t id_s = sm100::idesc_tf32(BM, BN);
       const uint32_t id_o = sm100::idesc_tf32(BM, args.n_pv);
       const uint32_t qh = sm100::smem_addr(q_hi), ql = sm100::smem_addr(q_lo);
       bool ok = sm100::mbar_wait_warp(&q_full, 0, args.err, sm100::kSiteAttention, abort);
       int n = 0;  // ring chunks consumed
-      for (int j = 0; ok && j < nblocks; ++j) {
-        // S_j overwrites P_{j-1}'s hi half: wait until O_{j-1} has read it.
-        if (j >= 1 &&
-            !(ok = sm100::mbar_wait_warp(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, args.err, sm100::kSiteAttention, abort)))
-          break;
-        sm100::tc_fence_after();
+      auto issue_s = [&](int j) {
         for (int c = 0; ok && c < dblocks; ++c, ++n) {
           const int i = n % kStages;
           if (!(ok = sm100::mbar_wait_warp(&ring_full[i], (n / kStages) & 1, args.err, sm100::kSiteAttention, abort)))
@@ -179,20 +180,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t qa = (uint32_t)(c * kSub + k * 32), ka = (uint32_t)(k * 32);
             const uint64_t dqh = sm100::desc_kmajor<128>(qh + qa), dql = sm100::desc_kmajor<128>(ql + qa);
             const uint64_t dkh = sm100::desc_kmajor<128>(kh + ka), dkl = sm100::desc_kmajor<128>(kl + ka);
-            sm100::mma_tf32(tmem + kColS, dql, dkh, id_s, (c == 0 && k == 0) ? 0u : 1u);
-            sm100::mma_tf32(tmem + kColS, dqh, dkl, id_s, 1u);
-            sm100::mma_tf32(tmem + kColS, dqh, dkh, id_s, 1u);
+            sm100::mma_tf32(tmem + s_col(j), dql, dkh, id_s, (c == 0 && k == 0) ? 0u : 1u);
+            sm100::mma_tf32(tmem + s_col(j), dqh, dkl, id_s, 1u);
+            sm100::mma_tf32(tmem + s_col(j), dqh, dkh, id_s, 1u);
           }
           sm100::mma_commit(&ring_empty[i]);
         }
-        if (!ok) break;
-        sm100::mma_commit(&s_full);
-        // O_j = P_j V_j once the softmax has written P_j into TMEM
-        const int b = j & 1;
-        if (j >= 2 &&
-            !(ok = sm100::mbar_wait_warp(&o_empty[b], ((j >> 1) - 1) & 1, args.err, sm100::kSiteAttention, abort)))
-          break;
-        if (!(ok = sm100::mbar_wait_warp(&p_full, j & 1, args.err, sm100::kSiteAttention, abort))) break;
+        if (ok) sm100::mma_commit(&s_full[j & 1]);
+      };
+      auto issue_pv = [&](int j) {
+        // once the softmax has written P_j into TMEM and folded O_{j-1}
+        if (!(ok = sm100::mbar_wait_warp(&p_full, j & 1, args.err, sm100::kSiteAttention, abort))) return;
         sm100::tc_fence_after();
         for (int c = 0; ok && c < kVChunks; ++c, ++n) {
           const int i = n % kStages;
@@ -203,13 +201,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k) {
             const uint32_t pcol = (uint32_t)(c * 32 + k * 8);
             const uint64_t dvh = sm100::desc_kmajor<128>(vh + k * 32), dvl = sm100::desc_kmajor<128>(vl + k * 32);
-            sm100::mma_tf32_ts(tmem + o_col(b), tmem + kColPlo + pcol, dvh, id_o, (c == 0 && k == 0) ? 0u : 1u);
-            sm100::mma_tf32_ts(tmem + o_col(b), tmem + kColS + pcol, dvl, id_o, 1u);
-            sm100::mma_tf32_ts(tmem + o_col(b), tmem + kColS + pcol, dvh, id_o, 1u);
+            sm100::mma_tf32_ts(tmem + kColO, tmem + kColPlo + pcol, dvh, id_o, (c == 0 && k == 0) ? 0u : 1u);
+            sm100::mma_tf32_ts(tmem + kColO, tmem + s_col(j) + pcol, dvl, id_o, 1u);
+            sm100::mma_tf32_ts(tmem + kColO, tmem + s_col(j) + pcol, dvh, id_o, 1u);
           }
           sm100::mma_commit(&ring_empty[i]);
         }
-        if (ok) sm100::mma_commit(&o_full[b]);
+        if (ok) sm100::mma_commit(&pv_done);
+      };
+      if (ok) issue_s(0);
+      for (int j = 0; ok && j < nblocks; ++j) {
+        if (j + 1 < nblocks) issue_s(j + 1);
+        if (ok) issue_pv(j);
       }
       sm100::mma_commit(&drain);
       int never = 0;
@@ -229,19 +232,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int i = 0; i < OC; ++i) o_acc[i] = 0.0f;
     float m_run = -INFINITY, l_run = 0.0f;
+    float alpha_prev = 1.0f;  // exp(m_{j-2} - m_{j-1}): the rescale O_{j-1} is folded with
     bool ok = true;
+    // Fold O_{j-1} = P_{j-1} V_{j-1} (TMEM) into the register accumulator once
+    // its MMAs are done; O's TMEM buffer is then free for O_j.
+    auto fold_o = [&](int jm1) {
+      ok = ok && sm100::mbar_wait(&pv_done, jm1 & 1, args.err, sm100::kSiteAttention, abort, 3 * sm100::kWaitCycles);
+      if (!ok) return;
+      sm100::tc_fence_after();
+      if (oc0 < args.n_pv) {  // warp-uniform
+        uint32_t o0[32], o1[32];
+        const uint32_t ta = tmem + lane_base + kColO + (uint32_t)oc0;
+        sm100::tmem_ld_32x32b_x32(ta, o0);
+        sm100::tmem_ld_32x32b_x32(ta + 32, o1);
+        sm100::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          o_acc[i] = __fadd_rn(__fmul_rn(o_acc[i], alpha_prev), __uint_as_float(o0[i]));
+          o_acc[32 + i] = __fadd_rn(__fmul_rn(o_acc[32 + i], alpha_prev), __uint_as_float(o1[i]));
+        }
+      }
+    };
     // Every thread runs every iteration and reaches both named barriers even
     // after a failed wait (ok == false), so the two warpgroups never wait on
     // each other forever; failed waits only skip work.
     for (int j = 0; j < nblocks; ++j) {
-      ok = ok && sm100::mbar_wait(&s_full, j & 1, args.err, sm100::kSiteAttention, abort);
+      ok = ok && sm100::mbar_wait(&s_full[j & 1], (j >> 1) & 1, args.err, sm100::kSiteAttention, abort);
       sm100::tc_fence_after();
       uint32_t sr[SC];
       {
         uint32_t (&a)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[0]);
         uint32_t (&b)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32]);
-        sm100::tmem_ld_32x32b_x32(tmem + lane_base + kColS + (uint32_t)sc0, a);
-        sm100::tmem_ld_32x32b_x32(tmem + lane_base + kColS + (uint32_t)sc0 + 32, b);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_base + s_col(j) + (uint32_t)sc0, a);
+        sm100::tmem_ld_32x32b_x32(tmem + lane_base + s_col(j) + (uint32_t)sc0 + 32, b);
         sm100::tmem_ld_wait();
       }
       float mx = -INFINITY;
@@ -268,14 +291,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         pl[i] = (__float_as_uint(__fsub_rn(v, __uint_as_float(hv))) + 0x1000u) & 0xFFFFE000u;
       }
       part_sum[wg][r] = sum;
+      // O_{j-1} must leave TMEM (and P_{j-1}'s lo half be consumed) before
+      // P_j's lo half and, later, O_j are written.
+      if (j >= 1) fold_o(j - 1);
       if (ok) {
-        // P_j's halves into TMEM: hi over S_j, lo beside it (the A operand of O_j)
+        // P_j's halves into TMEM: hi over S_j, lo in its own columns (the A operand of O_j)
         uint32_t (&h0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[0]);
         uint32_t (&h1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32]);
         uint32_t (&l0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pl[0]);
         uint32_t (&l1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pl[32]);
-        sm100::tmem_st_32x32b_x32(tmem + lane_base + kColS + (uint32_t)sc0, h0);
-        sm100::tmem_st_32x32b_x32(tmem + lane_base + kColS + (uint32_t)sc0 + 32, h1);
+        sm100::tmem_st_32x32b_x32(tmem + lane_base + s_col(j) + (uint32_t)sc0, h0);
+        sm100::tmem_st_32x32b_x32(tmem + lane_base + s_col(j) + (uint32_t)sc0 + 32, h1);
         sm100::tmem_st_32x32b_x32(tmem + lane_base + kColPlo + (uint32_t)sc0, l0);
         sm100::tmem_st_32x32b_x32(tmem + lane_base + kColPlo + (uint32_t)sc0 + 32, l1);
         sm100::tmem_st_wait();
@@ -286,29 +312,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::named_barrier(2, 256);
       l_run = __fadd_rn(__fmul_rn(l_run, alpha), __fadd_rn(part_sum[0][r], part_sum[1][r]));
       m_run = mx;
-      // fold O_j = P_j V_j into the register accumulator
-      const int b = j & 1;
-      ok = ok && sm100::mbar_wait(&o_full[b], (j >> 1) & 1, args.err, sm100::kSiteAttention, abort,
-                                  3 * sm100::kWaitCycles);
-      if (ok) {
-        sm100::tc_fence_after();
-        if (oc0 < args.n_pv) {  // warp-uniform
-          uint32_t o0[32], o1[32];
-          const uint32_t ta = tmem + lane_base + o_col(b) + (uint32_t)oc0;
-          sm100::tmem_ld_32x32b_x32(ta, o0);
-          sm100::tmem_ld_32x32b_x32(ta + 32, o1);
-          sm100::tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            o_acc[i] = __fadd_rn(__fmul_rn(o_acc[i], alpha), __uint_as_float(o0[i]));
-            o_acc[32 + i] = __fadd_rn(__fmul_rn(o_acc[32 + i], alpha), __uint_as_float(o1[i]));
-          }
-        }
-        sm100::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(&o_empty[b]);
-      }
+      alpha_prev = alpha;
     }
+    if (nblocks > 0) fold_o(nblocks - 1);
     const int64_t row = m0 + r;
     if (ok && row < args.s_q && oc0 < args.dv) {
       const float inv_l = __frcp_rn(l_run);
