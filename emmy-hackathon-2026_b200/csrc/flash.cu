@@ -1,10 +1,13 @@
 // Fused attention, O = softmax(Q K^T / scale) V, both contractions 3xTF32 on
 // tcgen05, one CTA per (head, 128 query rows), streaming 128-key blocks.
 //
-// A tf32 tcgen05.mma costs at least ~46 cycles whatever its N (measured on
-// B200: N = 32 runs at 35 % of the tensor rate, N = 64 at 67 %, N >= 128 at
-// 100 %), so every MMA here is N = 128: S_j = Q K_j^T over 128 keys and
-// O_j = P_j V_j over 128 output columns.
+// A tf32 tcgen05.mma with M = 128 reads its A operand (4 KB) from shared
+// memory every time, so narrow MMAs are bound by shared-memory bandwidth
+// (measured on B200: N = 32 runs at 35 % of the tensor rate, N = 64 at 67 %,
+// N >= 128 at 100 %); every MMA here is N = 128: S_j = Q K_j^T over 128 keys
+// and O_j = P_j V_j over 128 output columns.  Ring chunks are 32 wide (12
+// MMAs each): 16-wide chunks in a 6-deep ring measured slower, the issuer's
+// per-chunk wait and commit then costing about as much as the chunk's MMAs.
 //
 // The reference hoists one head's score rows into shared memory and runs the
 // softmax and the P.V fold in SIMT FP32 (compile.py:7009-7966, selective exp
@@ -13,24 +16,23 @@
 //   warp 0      TMA: Q_hi/Q_lo once (128 x Dp, four 128-byte-swizzled
 //               column blocks each, resident), then through a 3-stage ring
 //               the chunks K_j[:, 32c..] (128 keys x 32 dims) and
-//               V_j^T[:, 32c..] (128 dims x 32 keys), hi and lo
-//   warp 1      TMEM allocator and MMA issuer: S_j = Q K_j^T (three TF32
-//               products per 8-wide step, both operands from shared memory)
-//               into TMEM, then, once the softmax has written P_j over S_j,
-//               O_j = P_j V_j with P_j read from TMEM into O buffer j % 2;
-//               S_{j+1} waits for O_j to finish reading P_j
+//               V_j^T[:, 32c..] (128 dims x 32 keys), hi and lo, in the MMA
+//               issuer's order: K_0, then K_{j+1}, V_j for each j
+//   warp 1      TMEM allocator and MMA issuer (warp-wide, elect.sync):
+//               S_{j+1} = Q K_{j+1}^T into score buffer (j+1) % 2 while the
+//               softmax works on S_j, then O_j = P_j V_j (P_j read from TMEM)
+//               into the O buffer once the softmax has released P_j
 //   warps 2..9  softmax, two threads per query row (warpgroup 0 takes score
 //               columns 0-63 and output columns 0-63 of the row, warpgroup
 //               1 the rest): S_j from TMEM, online max / sum with the
 //               selective exponential (partial row max and sum exchanged
-//               through shared memory), P_j's TF32 halves into TMEM (the A
-//               operand of O_j), then the finished
-//               O_{j-1} from TMEM folded into the FP32 row accumulator
-//               O = O * alpha + O_{j-1} in registers (which also keeps the
-//               tensor core's accumulation error per block small)
+//               through shared memory), then the finished O_{j-1} folded
+//               into the FP32 row accumulator O = O * alpha + O_{j-1} in
+//               registers, then P_j's TF32 halves into TMEM (hi over S_j, lo
+//               in its own columns: the A operand of O_j)
 //
 // Each key block's products accumulate in a fresh TMEM buffer, so the
-// in-instruction accumulation error stays that of 48 (S) / 12 (O) MMAs.
+// in-instruction accumulation error stays that of 48 (S) / 48 (O) MMAs.
 // All mbarrier waits are bounded (sm100.cuh).
 #include <cudaTypedefs.h>
 
