@@ -63,8 +63,14 @@ struct FusedArgs {
   int64_t m, n, ldc;
   int num_kb;
   int relu;
+  int tma_c;  // C is written by TMA stores (16-byte aligned, ldc % 4 == 0)
   unsigned *err;
 };
+
+// C staging for the TMA store: the tile as [BN / 32] boxes of 128 rows x 32
+// FP32 (16 KB each) with the 128-byte swizzle, so the row-per-thread writes
+// of a warp hit eight distinct 16-byte chunks per 128 bytes (no conflicts).
+constexpr int kCBox = BM * 32 * 4;
 
 // Epilogue helpers shared by both kernels.  Work warp w holds the
 // accumulator of TMEM lane quarter w % 4 (rows) and column slice (w - 2) / 4
@@ -113,6 +119,27 @@ struct Slice {
     __syncwarp();
     if (lane == 0) sm100::mbar_arrive(&tmem_empty[buf]);
     return true;
+  }
+
+  // Bias -> ReLU -> the staging boxes in shared memory (see kCBox).
+  __device__ __forceinline__ void stage(uint8_t *staging, const FusedArgs &args, int64_t n0) {
+    const int row = quarter * 32 + lane;
+    const int c0 = slice * CPT;
+#pragma unroll
+    for (int j = 0; j < CPT; j += 4) {
+      float v[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float x = acc[j + q];
+        if (args.bias) x = __fadd_rn(x, (n0 + c0 + j + q < args.n) ? __ldg(args.bias + n0 + c0 + j + q) : 0.0f);
+        if (args.relu) x = x > 0.0f ? x : 0.0f;
+        v[q] = x;
+      }
+      const int col = c0 + j;
+      const uint32_t chunk = (uint32_t)((col & 31) >> 2) ^ (uint32_t)(row & 7);
+      sm100::sts128(sm100::smem_addr(staging + (col >> 5) * kCBox + row * 128 + chunk * 16),
+                    make_float4(v[0], v[1], v[2], v[3]));
+    }
   }
 
   __device__ __forceinline__ void store(const FusedArgs &args, int64_t m0, int64_t n0) {
@@ -170,7 +197,8 @@ struct TmemAShape {
 template <int BN, int G>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tmem_a_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
-                       const __grid_constant__ CUtensorMap map_blo, const FusedArgs args) {
+                       const __grid_constant__ CUtensorMap map_blo, const __grid_constant__ CUtensorMap map_c,
+                       const FusedArgs args) {
   using Shape = TmemAShape<BN>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[Shape::kStages];   // raw A + B hi/lo landed
@@ -357,7 +385,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = out.fold(folded, tmem_base, tmem_full, tmem_empty, args.err, abort);
       ++folded;
     }
-    if (ok) out.store(args, m0, n0);
+    if (args.tma_c) {
+      // The ring is idle once the last chunk is folded (every MMA, hence
+      // every load it consumed, is done): stage C there, one TMA store per box.
+      if (ok) out.stage(smem, args, n0);
+      sm100::fence_proxy_async_smem();
+      sm100::named_barrier(1, kWorkThreads);
+      if (threadIdx.x == 64 && ok) {
+#pragma unroll 1
+        for (int b = 0; b < BN / 32; ++b) sm100::tma_store_2d(&map_c, smem + b * kCBox, (int)n0 + 32 * b, (int)m0);
+        sm100::tma_store_flush();
+      }
+    } else if (ok) {
+      out.store(args, m0, n0);
+    }
   }
   sm100::tc_fence_before();
   __syncthreads();
@@ -576,13 +617,19 @@ int launch_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const b2
   if (status == B2K_OK)
     status = b2k::make_map_2d(ctx, &map_blo, ops.b_lo, ops.kp, n, ops.kp, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B);
   if (status != B2K_OK) return status;
-  FusedArgs args{c, bias, m, n, ldc, (int)(ops.kp / BK), relu, ctx->error_flag};
+  // C through TMA stores when it is TMA-writable, else row stores by the threads.
+  CUtensorMap map_c{};
+  const int tma_c = b2k::aligned16(c) && ldc % 4 == 0;
+  if (tma_c && (status = b2k::make_map_2d(ctx, &map_c, c, n, m, ldc, 32, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != B2K_OK)
+    return status;
+  static_assert((BN / 32) * kCBox <= Shape::kStages * Shape::kStage, "C staging exceeds the ring");
+  FusedArgs args{c, bias, m, n, ldc, (int)(ops.kp / BK), relu, tma_c, ctx->error_flag};
   auto kernel = gemm_tmem_a_kernel<BN, G>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (TMEM A): set smem");
   if ((n + BN - 1) / BN > 65535) return b2k::fail(ctx, B2K_EINVAL, "gemm: N exceeds %d", 65535 * BN);
   dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN), 1);
-  kernel<<<grid, kThreads, Shape::kSmem, s>>>(map_a, map_bhi, map_blo, args);
+  kernel<<<grid, kThreads, Shape::kSmem, s>>>(map_a, map_bhi, map_blo, map_c, args);
   return b2k::check_launch(ctx, "gemm (TMEM A) launch");
 }
 
@@ -596,7 +643,7 @@ int launch_smem_split(b2k_ctx *ctx, const float *a, const float *b, float *c, in
   status = B_MN ? b2k::make_map_2d(ctx, &map_b, b, n, k, ldb, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
                 : b2k::make_map_2d(ctx, &map_b, b, k, n, ldb, BK, BN, CU_TENSOR_MAP_SWIZZLE_64B);
   if (status != B2K_OK) return status;
-  FusedArgs args{c, bias, m, n, ldc, (int)((k + BK - 1) / BK), relu, ctx->error_flag};
+  FusedArgs args{c, bias, m, n, ldc, (int)((k + BK - 1) / BK), relu, 0, ctx->error_flag};
   auto kernel = gemm_smem_split_kernel<BN, B_MN>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (shared-memory split): set smem");
