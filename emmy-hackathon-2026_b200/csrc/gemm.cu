@@ -116,7 +116,13 @@ struct GemmArgs {
   int num_kb;
   int relu;
   unsigned *err;
+  int tma_c;  // C written by TMA stores from shared memory (main kernel only)
 };
+
+// C staging for the TMA store: BN / 32 boxes of 128 rows x 32 FP32 (16 KB)
+// with the 128-byte swizzle; a warp's row-per-thread 16-byte writes then hit
+// eight distinct chunks per 128 bytes, and TMA clips the ragged edges.
+constexpr int kCBox = BM * 32 * 4;
 
 template <int BN, int SW, int STAGES>
 struct GemmShape {
@@ -137,7 +143,7 @@ template <int BN, int SW, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                        const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
-                       const GemmArgs args) {
+                       const __grid_constant__ CUtensorMap map_c, const GemmArgs args) {
   using Shape = GemmShape<BN, SW, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
@@ -276,7 +282,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int64_t row = m0 + quarter * 32 + lane;
     const int64_t col0 = n0 + half * CPT;
-    if (ok && row < args.m && col0 < args.n) {
+    if (args.tma_c) {
+      // The ring is idle once the last chunk is folded: stage C there and
+      // write it with one TMA store per box.
+      if (ok) {
+        const float divisor = args.div_ptr ? __ldg(args.div_ptr) : args.div_value;
+        const bool divide = args.div_ptr != nullptr || args.div_value != 1.0f;
+        const int r = quarter * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < CPT; j += 4) {
+          float v[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float x = acc[j + q];
+            if (divide) x = __fdiv_rn(x, divisor);
+            if (args.bias) x = __fadd_rn(x, (col0 + j + q < args.n) ? __ldg(args.bias + col0 + j + q) : 0.0f);
+            if (args.relu) x = x > 0.0f ? x : 0.0f;
+            v[q] = x;
+          }
+          const int col = half * CPT + j;
+          const uint32_t chunk = (uint32_t)((col & 31) >> 2) ^ (uint32_t)(r & 7);
+          sm100::sts128(sm100::smem_addr(smem + (col >> 5) * kCBox + r * 128 + chunk * 16),
+                        make_float4(v[0], v[1], v[2], v[3]));
+        }
+      }
+      sm100::fence_proxy_async_smem();
+      sm100::named_barrier(1, 32 * kEpilogueWarps);
+      if (threadIdx.x == 64 && ok) {
+#pragma unroll 1
+        for (int b = 0; b < BN / 32; ++b)
+          sm100::tma_store_3d(&map_c, smem + b * kCBox, (int)n0 + 32 * b, (int)m0, (int)blockIdx.z);
+        sm100::tma_store_flush();
+      }
+    } else if (ok && row < args.m && col0 < args.n) {
       float *crow = args.c + (int64_t)blockIdx.z * args.batch_stride_c + row * args.ldc + col0;
       const float divisor = args.div_ptr ? __ldg(args.div_ptr) : args.div_value;
       const bool divide = args.div_ptr != nullptr || args.div_value != 1.0f;
@@ -627,11 +665,28 @@ int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, Gemm
   if ((status = make_operand_map(ctx, &maps[2], ops.b_hi, args.n, ops.kp, batch, BN, SW)) != B2K_OK) return status;
   if ((status = make_operand_map(ctx, &maps[3], ops.b_lo, args.n, ops.kp, batch, BN, SW)) != B2K_OK) return status;
   args.num_kb = (int)(ops.kp / Shape::BK);
+  // C through TMA stores when it is TMA-writable, else row stores by the threads.
+  CUtensorMap map_c{};
+  args.tma_c = b2k::aligned16(args.c) && args.ldc % 4 == 0 && (batch == 1 || args.batch_stride_c % 4 == 0);
+  if (args.tma_c) {
+    auto encode = b2k::tensor_map_encoder();
+    if (!encode) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[3] = {(cuuint64_t)args.n, (cuuint64_t)args.m, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)args.ldc * 4,
+                             (cuuint64_t)(batch == 1 ? args.m * args.ldc : args.batch_stride_c) * 4};
+    cuuint32_t box[3] = {32, (cuuint32_t)BM, 1};
+    cuuint32_t elem[3] = {1, 1, 1};
+    CUresult res = encode(&map_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, args.c, dims, strides, box, elem,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (res != CUDA_SUCCESS) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled (C) failed (%d)", (int)res);
+  }
+  static_assert((BN / 32) * kCBox <= STAGES * Shape::kStage, "C staging exceeds the ring");
   auto kernel = gemm_tf32x3_kernel<BN, SW, STAGES>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: set smem");
   dim3 grid((unsigned)((args.n + BN - 1) / BN), (unsigned)((args.m + BM - 1) / BM), (unsigned)batch);
-  kernel<<<grid, kThreads, Shape::kSmem, s>>>(maps[0], maps[1], maps[2], maps[3], args);
+  kernel<<<grid, kThreads, Shape::kSmem, s>>>(maps[0], maps[1], maps[2], maps[3], map_c, args);
   return b2k::check_launch(ctx, "gemm launch");
 }
 
@@ -719,7 +774,7 @@ int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int6
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
               cudaStream_t s, const StreamKScratch *sk) {
   if (batch > 65535) return fail(ctx, B2K_EINVAL, "gemm: batch exceeds 65535");
-  GemmArgs args{c, bias, div_ptr, div_value, m, n, ldc, batch_stride_c, 0, relu, ctx->error_flag};
+  GemmArgs args{c, bias, div_ptr, div_value, m, n, ldc, batch_stride_c, 0, relu, ctx->error_flag, 0};
   PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
   if (sk && batch == 1 && n > 128 && g_gemm_variant == 1 && streamk_pays(m, n, ops.kp, sk->grid))
     return launch_streamk<256, 64, 4>(ctx, ops, args, *sk, s);
