@@ -66,6 +66,7 @@ constexpr uint32_t kColPlo = 256, kColO = 384;
 __host__ __device__ constexpr uint32_t s_col(int j) { return (uint32_t)((j & 1) * 128); }
 
 struct FlashArgs {
+  int tma_o;  // O written by TMA stores from shared memory (16-byte aligned, dv % 4 == 0)
   float *o;
   int64_t s_q, s_kv, dv;
   int dp;          // padded head dim (multiple of 32, <= 128)
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_qhi, const __grid_constant__ CUtensorMap map_qlo,
                         const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
                         const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
-                        const FlashArgs args) {
+                        const __grid_constant__ CUtensorMap map_o, const FlashArgs args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, p_full, pv_done, drain;
   __shared__ __align__(8) uint64_t ring_full[kStages], ring_empty[kStages], s_full[2];
@@ -318,8 +319,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (nblocks > 0) fold_o(nblocks - 1);
     const int64_t row = m0 + r;
-    if (ok && row < args.s_q && oc0 < args.dv) {
-      const float inv_l = __frcp_rn(l_run);
+    const float inv_l = __frcp_rn(l_run);
+    if (args.tma_o) {
+      // Q's buffer is idle after the last block: stage the normalised O tile
+      // there as 128-byte-swizzled boxes of 128 rows x 32 columns and write it
+      // with TMA stores (coalesced, rows past s_q clipped).
+      if (ok) {
+#pragma unroll
+        for (int i = 0; i < OC; i += 4) {
+          const int col = oc0 + i;
+          const uint32_t chunk = (uint32_t)((col & 31) >> 2) ^ (uint32_t)(r & 7);
+          sm100::sts128(sm100::smem_addr(q_hi + (col >> 5) * kSub + r * 128 + chunk * 16),
+                        make_float4(__fmul_rn(o_acc[i], inv_l), __fmul_rn(o_acc[i + 1], inv_l),
+                                    __fmul_rn(o_acc[i + 2], inv_l), __fmul_rn(o_acc[i + 3], inv_l)));
+        }
+      }
+      sm100::fence_proxy_async_smem();
+      sm100::named_barrier(3, 256);
+      if (threadIdx.x == 64 && ok) {
+        for (int b = 0; b * 32 < args.dv; ++b) sm100::tma_store_3d(&map_o, q_hi + b * kSub, 32 * b, (int)m0, head);
+        sm100::tma_store_flush();
+      }
+    } else if (ok && row < args.s_q && oc0 < args.dv) {
       float *orow = args.o + ((int64_t)head * args.s_q + row) * args.dv;
       const bool vec = (args.dv % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.o) & 15) == 0);
       if (vec) {
@@ -392,13 +413,18 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   if ((status = make_map(ctx, &maps[3], k_lo, dp, s_kv, bh, BN)) != B2K_OK) return status;
   if ((status = make_map(ctx, &maps[4], v_hi, sp, dv, bh, 128)) != B2K_OK) return status;
   if ((status = make_map(ctx, &maps[5], v_lo, sp, dv, bh, 128)) != B2K_OK) return status;
-  FlashArgs args{o, s_q, s_kv, dv, (int)dp, (int)((dv + 15) / 16 * 16), 1.0f / scale_div, scale_div_ptr,
+  // O through TMA stores when it is TMA-writable, else row stores by the threads.
+  CUtensorMap map_o{};
+  const int tma_o = aligned16(o) && dv % 4 == 0;
+  if (tma_o && (status = make_map(ctx, &map_o, o, dv, s_q, bh, BM)) != B2K_OK) return status;
+  FlashArgs args{tma_o, o, s_q, s_kv, dv, (int)dp, (int)((dv + 15) / 16 * 16), 1.0f / scale_div, scale_div_ptr,
                  ctx->error_flag};
   cudaError_t err = cudaFuncSetAttribute(flash_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (err != cudaSuccess) return cuda_fail(ctx, err, "flash: set smem");
   dim3 grid((unsigned)((s_q + BM - 1) / BM), (unsigned)bh);
   PhaseTimer timer(ctx, B2K_PHASE_FLASH, s);
-  flash_tf32x3_kernel<<<grid, kThreads, kSmem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], args);
+  flash_tf32x3_kernel<<<grid, kThreads, kSmem, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], map_o,
+                                                     args);
   return check_launch(ctx, "flash launch");
 }
 
