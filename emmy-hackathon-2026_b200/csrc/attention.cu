@@ -17,14 +17,17 @@ namespace {
 
 inline int64_t round32(int64_t x) { return (x + 31) / 32 * 32; }
 
-// Force the three-pass path even where the fused kernel applies (tests and
-// benchmarks compare the two).
-int g_attention_unfused = 0;
+// 1 = fused kernel, one CTA per query tile (default), 2 = fused kernel on
+// CTA pairs, 0 = three passes (tests and benchmarks compare them).
+int g_attention_mode = 1;
 
 }  // namespace
 
-extern "C" int b2k_attention_set_fused(int fused) {
-  g_attention_unfused = fused ? 0 : 1;
+int b2k::attention_mode() { return g_attention_mode; }
+
+extern "C" int b2k_attention_set_fused(int mode) {
+  if (mode < 0 || mode > 2) return B2K_EINVAL;
+  g_attention_mode = mode;
   return B2K_OK;
 }
 
@@ -49,7 +52,7 @@ extern "C" int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k
   if (!scale_div_ptr && !(scale_div != 0.0f)) return b2k::fail(ctx, B2K_EINVAL, "attention: zero scale divisor");
   cudaStream_t s = (cudaStream_t)stream;
   ctx->flags_epoch = 0;  // the workspace is reused below: GEMM stream-K flags must be reset next time
-  if (b2k::flash_supported(d, dv) && !g_attention_unfused) {
+  if (b2k::flash_supported(d, dv) && g_attention_mode != 0) {
     int status = b2k::reserve_workspace(ctx, b2k::flash_workspace_floats(bh, s_q, s_kv, d, dv) * sizeof(float), s);
     if (status != B2K_OK) return status;
     b2k::PhaseTimer timer(ctx, B2K_PHASE_ATTENTION, s);

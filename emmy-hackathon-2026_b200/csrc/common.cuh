@@ -116,6 +116,8 @@ size_t streamk_scratch_bytes(int grid);
 int softmax_split_rows(b2k_ctx *ctx, const float *x, int64_t rows, int64_t cols, int64_t ld_x, float *hi,
                        float *lo, int64_t kp, cudaStream_t s);
 
+// Attention path chosen with b2k_attention_set_fused (attention.cu).
+int attention_mode();
 // Fused attention (flash.cu): supported head dims, scratch, launch.
 bool flash_supported(int64_t d, int64_t dv);
 size_t flash_workspace_floats(int64_t bh, int64_t s_q, int64_t s_kv, int64_t d, int64_t dv);

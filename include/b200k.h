@@ -228,9 +228,13 @@ int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int6
 int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k, const float *v, float *o, int64_t bh,
                          int64_t s_q, int64_t s_kv, int64_t d, int64_t dv, float scale_div,
                          const float *scale_div_ptr, int32_t k_layout, void *stream);
-/* Process-wide switch: 1 (default) uses the fused kernel where head dims
- * allow, 0 forces the three-pass path (for comparisons). */
-int b2k_attention_set_fused(int fused);
+/* Process-wide choice of attention path where head dims allow the fused
+ * kernel: 1 (default) the fused kernel with one CTA per query tile; 2 the
+ * fused kernel on CTA pairs (tcgen05 cta_group::2, M = 256: two query tiles
+ * of a head share every K / V chunk, each CTA loading half -- measured slower
+ * on B200 than 1); 0 the three-pass path (for comparisons).  Other values
+ * return B2K_EINVAL. */
+int b2k_attention_set_fused(int mode);
 
 /* --- launch by descriptor ----------------------------------------------------
  * The reference's runner launches a compiled kernel with

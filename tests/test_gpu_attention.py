@@ -43,8 +43,13 @@ def test_attention_matches_float64(ctx, torch_cuda, bh, s_q, s_kv, d, dv, k_layo
     assert ok, (bad, err)
 
 
-@pytest.mark.parametrize("bh,s_q,s_kv,d,dv", [(2, 300, 257, 128, 128), (1, 64, 64, 64, 64), (3, 129, 33, 100, 24)])
-def test_fused_and_three_pass_paths_agree(ctx, torch_cuda, bh, s_q, s_kv, d, dv):
+@pytest.mark.parametrize("bh,s_q,s_kv,d,dv", [(2, 300, 257, 128, 128), (1, 64, 64, 64, 64), (3, 129, 33, 100, 24),
+                                         (2, 256, 200, 128, 64), (1, 640, 384, 32, 128)])
+def test_attention_paths_agree(ctx, torch_cuda, bh, s_q, s_kv, d, dv):
+    """Fused kernel on CTA pairs (mode 2: odd tile counts leave a CTA with no
+    rows; dv <= 64 leaves the odd CTA's V half all zero), fused with one CTA
+    per tile (1, the default) and three passes (0) against float64 and each
+    other."""
     runtime = pkg("runtime")
     lib = runtime.library()
     rng = np.random.default_rng(17 + s_q)
@@ -54,14 +59,16 @@ def test_fused_and_three_pass_paths_agree(ctx, torch_cuda, bh, s_q, s_kv, d, dv)
     want = refs.attention_batched(q, k, v, math.sqrt(d))
     outs = []
     try:
-        for fused in (1, 0):
-            lib.b2k_attention_set_fused(fused)
+        for mode in (2, 1, 0):
+            assert lib.b2k_attention_set_fused(mode) == runtime.B2K_OK
             outs.append(run(ctx, torch_cuda, q, k, v))
     finally:
         lib.b2k_attention_set_fused(1)
     for got in outs:
         ok, bad, err = refs.allclose_report(got, want, RTOL, ATOL)
         assert ok, (bad, err)
+    np.testing.assert_allclose(outs[0], outs[1], rtol=1e-5, atol=1e-6)
+    assert lib.b2k_attention_set_fused(3) == runtime.B2K_EINVAL
 
 
 def test_attention_scale_from_device_buffer(ctx, torch_cuda):
