@@ -72,6 +72,9 @@ def profile_traffic(name: str) -> float | None:
 
 
 # --------------------------------------------------------------------------- workloads
+TIMING_EVERY = 8  # steps per sampled launch of the dominant kernel
+
+
 class Workload:
     name = ""
     unit = ""
@@ -142,11 +145,14 @@ class Gemm(Workload):
         self.dbias = torch.from_numpy(bias).cuda() if bias is not None else None
         self.dc = torch.empty((self.m, self.n), dtype=torch.float32, device="cuda")
         self.ctx = ctx
+        # the step's library call with its arguments converted once: every
+        # step still runs the whole GEMM (operand split + tensor-core kernel)
+        self.call = ctx.gemm_call(self.da.data_ptr(), self.db.data_ptr(), self.dc.data_ptr(), self.m, self.n,
+                                  self.k, b_layout=1 if self.ragged else 0,
+                                  bias=self.dbias.data_ptr() if self.dbias is not None else 0, relu=self.ragged)
 
     def step(self):
-        self.ctx.gemm(self.da.data_ptr(), self.db.data_ptr(), self.dc.data_ptr(), self.m, self.n, self.k,
-                      b_layout=1 if self.ragged else 0,
-                      bias=self.dbias.data_ptr() if self.dbias is not None else 0, relu=self.ragged)
+        self.call()
 
     def e2e_setup(self, session):
         a, b, bias = self.host
@@ -212,9 +218,10 @@ class Softmax(Workload):
         self.dx = torch.from_numpy(x).cuda()
         self.dy = torch.empty_like(self.dx)
         self.ctx = ctx
+        self.call = ctx.row_softmax_call(self.dx.data_ptr(), self.dy.data_ptr(), self.rows, self.cols)
 
     def step(self):
-        self.ctx.row_softmax(self.dx.data_ptr(), self.dy.data_ptr(), self.rows, self.cols)
+        self.call()
 
     def e2e_setup(self, session):
         self.session = session
@@ -261,9 +268,11 @@ class Add(Workload):
         self.dc = torch.empty_like(self.da)
         self.prog = pkg("runtime").make_program(2, [("add", 0, 1, 0, 0.0)], 2)
         self.ctx = ctx
+        self.call = ctx.pointwise_call(self.prog, [self.da.data_ptr(), self.db.data_ptr()], self.dc.data_ptr(),
+                                       self.n)
 
     def step(self):
-        self.ctx.pointwise(self.prog, [self.da.data_ptr(), self.db.data_ptr()], self.dc.data_ptr(), self.n)
+        self.call()
 
     def e2e_setup(self, session):
         self.session = session
@@ -317,10 +326,11 @@ class Attention(Workload):
         self.dq, self.dk, self.dv = (torch.from_numpy(t).cuda() for t in (q, k, v))
         self.do = torch.empty_like(self.dq)
         self.ctx = ctx
+        self.call = ctx.attention_call(self.dq.data_ptr(), self.dk.data_ptr(), self.dv.data_ptr(),
+                                       self.do.data_ptr(), self.bh, self.seq, self.seq, self.d, self.d)
 
     def step(self):
-        self.ctx.attention(self.dq.data_ptr(), self.dk.data_ptr(), self.dv.data_ptr(), self.do.data_ptr(),
-                           self.bh, self.seq, self.seq, self.d, self.d)
+        self.call()
 
     def e2e_setup(self, session):
         self.session = session
@@ -466,13 +476,20 @@ def run_ours(args) -> dict | None:
     sampler.start()
     time.sleep(0.3)
     ctx.timing_reset()
-    ctx.timing(True)
+    # The dominant kernel is timed with CUDA events on every TIMING_EVERY-th
+    # step of the timed region: an event pair between two kernels costs a few
+    # microseconds of idle GPU front end, which would inflate a 40-us step.
     barrier()
     launches_before = ctx.kernel_launches()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        sampled = i % TIMING_EVERY == 0
+        if sampled:
+            ctx.timing(True, phases=[w.phase])
         w.step()
+        if sampled:
+            ctx.timing(False)
     stop.record()
     launches = ctx.kernel_launches() - launches_before
     barrier()

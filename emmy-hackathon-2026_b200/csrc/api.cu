@@ -38,8 +38,11 @@ static cudaEvent_t take_event(b2k_ctx *ctx) {
   return e;
 }
 
+static bool g_pdl = true;
+bool pdl_enabled() { return g_pdl; }
+
 PhaseTimer::PhaseTimer(b2k_ctx *ctx, int phase, cudaStream_t stream) : ctx_(ctx), phase_(phase), stream_(stream) {
-  if (!ctx_->timing) return;
+  if (!ctx_->timing || !((ctx_->timing_mask >> phase) & 1u)) return;
   start_ = take_event(ctx_);
   if (start_) cudaEventRecord(start_, stream_);
 }
@@ -62,6 +65,17 @@ extern "C" {
 int b2k_timing_enable(b2k_ctx *ctx, int on) {
   if (!ctx) return B2K_EINVAL;
   ctx->timing = on != 0;
+  return B2K_OK;
+}
+
+int b2k_timing_select(b2k_ctx *ctx, uint32_t phase_mask) {
+  if (!ctx) return B2K_EINVAL;
+  ctx->timing_mask = phase_mask;
+  return B2K_OK;
+}
+
+int b2k_set_pdl(int on) {
+  b2k::g_pdl = on != 0;
   return B2K_OK;
 }
 

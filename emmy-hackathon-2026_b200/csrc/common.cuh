@@ -7,7 +7,9 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "b200k.h"
@@ -27,8 +29,10 @@ struct b2k_ctx {
   // Stream-K flag slots in the workspace and the epoch of the last GEMM.
   unsigned *flags_ptr = nullptr;
   unsigned flags_epoch = 0;
-  // Optional per-phase CUDA-event timing (b2k_timing_*).
+  // Optional per-phase CUDA-event timing (b2k_timing_*), for the phases
+  // whose bit is set in timing_mask.
   bool timing = false;
+  uint32_t timing_mask = ~0u;
   std::vector<cudaEvent_t> event_pool;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> phase_events[B2K_PHASE_COUNT];
 };
@@ -69,6 +73,46 @@ inline int make_current(b2k_ctx *ctx) {
 // Grow the context's scratch arena to at least `bytes`.
 int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream);
 
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device):
+// cudaFuncSetAttribute costs about a microsecond and a half of host time per
+// call, a noticeable share of a short GEMM's enqueue cost.
+inline cudaError_t set_max_smem(b2k_ctx *ctx, const void *kernel, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void *, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto &e : done)
+    if (e.first == kernel && e.second == ctx->device) return cudaSuccess;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess) done.emplace_back(kernel, ctx->device);
+  return err;
+}
+
+// Programmatic dependent launch (b2k_set_pdl, on by default): the kernels of
+// one operation (operand split, then the tensor-core kernel) are launched
+// with the programmatic-serialization attribute, so a kernel's CTAs may be
+// scheduled and run their set-up (barrier init, TMEM allocation, tensor-map
+// prefetch) while the previous kernel in the stream drains.  Every kernel
+// launched this way executes grid_dependency_wait() before it touches global
+// memory, which orders it after the previous kernel's completion and makes
+// that kernel's writes visible.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t s, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // --- 3xTF32 operand split and tensor-core GEMM (gemm.cu) ---------------------
 // K is zero-padded to a multiple of 32 in the split operands.
 inline int64_t gemm_kpad(int64_t k) { return (k + 31) / 32 * 32; }
@@ -97,6 +141,15 @@ int gemm_smem_split(b2k_ctx *ctx, const float *a, const float *b, float *c, int6
 // Row-major [batch][rows, k] -> hi/lo [batch][rows][kp].
 int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t ld, int64_t bs, int64_t batch,
                int64_t kp, float *hi, float *lo, cudaStream_t s);
+// One row-major operand [batch][rows, k] (row stride ld, batch stride bs)
+// and its hi/lo destination [batch][rows][kp].
+struct RowSplit {
+  const float *src;
+  int64_t rows, k, ld, bs, batch;
+  float *hi, *lo;
+};
+// Splits `a` and, when `b` is not null, `b` (same kp) in one launch.
+int split_rows2(b2k_ctx *ctx, const RowSplit &a, const RowSplit *b, int64_t kp, cudaStream_t s);
 // Row-major [batch][k, n] -> transposed hi/lo [batch][n][kp].
 int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_t ld, int64_t bs, int64_t batch,
                     int64_t kp, float *hi, float *lo, cudaStream_t s);
@@ -218,6 +271,15 @@ __device__ __forceinline__ void split_tf32x4(const float4 &x, float4 &hi, float4
     split_tf32(x.z, hi.z, lo.z);
     split_tf32(x.w, hi.w, lo.w);
   }
+}
+
+// Programmatic dependent launch, device side (see launch_kernel): wait until
+// the previous kernel in the stream has completed and its writes are
+// visible; allow the next kernel's CTAs to be scheduled.  Both are no-ops in
+// a kernel launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ float warp_max(float v) {

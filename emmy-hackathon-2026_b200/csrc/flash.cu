@@ -153,6 +153,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  // Nothing above touched global memory: under programmatic dependent
+  // launch the set-up overlaps the V split kernel's tail.
+  grid_dependency_wait();
+  grid_dependents_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -475,9 +479,14 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   float *k_hi = q_lo + bh * s_q * dp, *k_lo = k_hi + bh * s_kv * dp;
   float *v_hi = k_lo + bh * s_kv * dp, *v_lo = v_hi + bh * dv * sp;
   int status;
-  if ((status = split_rows(ctx, q, s_q, d, d, s_q * d, bh, dp, q_hi, q_lo, s)) != B2K_OK) return status;
-  status = k_layout == B2K_K_SD ? split_rows(ctx, k, s_kv, d, d, s_kv * d, bh, dp, k_hi, k_lo, s)
-                                : split_transpose(ctx, k, d, s_kv, s_kv, d * s_kv, bh, dp, k_hi, k_lo, s);
+  const RowSplit sq{q, s_q, d, d, s_q * d, bh, q_hi, q_lo};
+  if (k_layout == B2K_K_SD) {
+    // Q and K in one launch
+    const RowSplit sk{k, s_kv, d, d, s_kv * d, bh, k_hi, k_lo};
+    status = split_rows2(ctx, sq, &sk, dp, s);
+  } else if ((status = split_rows2(ctx, sq, nullptr, dp, s)) == B2K_OK) {
+    status = split_transpose(ctx, k, d, s_kv, s_kv, d * s_kv, bh, dp, k_hi, k_lo, s);
+  }
   if (status != B2K_OK) return status;
   if ((status = split_transpose(ctx, v, s_kv, dv, dv, s_kv * dv, bh, sp, v_hi, v_lo, s)) != B2K_OK) return status;
   // CTA pairs (mode 2) need at least two query tiles to pair up.  Measured on
@@ -502,7 +511,7 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   FlashArgs args{tma_o, o, s_q, s_kv, dv, (int)dp, (int)((dv + 15) / 16 * 16), 1.0f / scale_div, scale_div_ptr,
                  ctx->error_flag};
   auto kernel = pair ? flash_tf32x3_kernel<true> : flash_tf32x3_kernel<false>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  cudaError_t err = set_max_smem(ctx, (const void *)kernel, kSmem);
   if (err != cudaSuccess) return cuda_fail(ctx, err, "flash: set smem");
   PhaseTimer timer(ctx, B2K_PHASE_FLASH, s);
   cudaLaunchConfig_t config = {};
@@ -510,13 +519,15 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   config.blockDim = dim3(kThreads);
   config.dynamicSmemBytes = kSmem;
   config.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = pair ? 2 : 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   config.attrs = attr;
-  config.numAttrs = 1;
+  config.numAttrs = !pair && pdl_enabled() ? 2 : 1;
   err = cudaLaunchKernelEx(&config, kernel, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], map_o, args);
   if (err != cudaSuccess) return cuda_fail(ctx, err, "flash: launch");
   return check_launch(ctx, "flash launch");

@@ -19,6 +19,7 @@
 // All mbarrier waits are bounded (see sm100.cuh).
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -33,37 +34,50 @@ constexpr int KPAD = 32;  // K is zero-padded to a multiple of this in the split
 // --- split pre-pass --------------------------------------------------------
 // (the split rule split_tf32 lives in common.cuh)
 
-// Row-major [batch][rows, K] (row stride ld, batch stride bs) -> hi/lo
-// [batch][rows][Kp], zero padded along K.
-__global__ void __launch_bounds__(256) split_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t K,
-                                                         int64_t ld, int64_t bs, int64_t batch, int64_t Kp,
-                                                         float *__restrict__ hi, float *__restrict__ lo,
-                                                         int vec_src) {
-  const int64_t kp4 = Kp >> 2;
-  const int64_t per_batch = rows * kp4;
-  const int64_t total = batch * per_batch;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t b = i / per_batch;
-    const int64_t rem = i - b * per_batch;
-    const int64_t r = rem / kp4;
-    const int64_t k = (rem - r * kp4) << 2;
-    const float *row = src + b * bs + r * ld;
-    float v[4];
-    if (vec_src && k + 3 < K) {
-      const float4 t = *reinterpret_cast<const float4 *>(row + k);
-      v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+// Row-major operand rows -> hi/lo rows [R][Kp] (R = batch * rows), zero
+// padded along K.  A block is 8 rows x 32 float4 columns; blockIdx.x picks
+// the 128-column slice, blockIdx.y (strided) the 8-row tile, over the tiles
+// of job 0 and then of job 1, so two operands split in one launch.
+struct RowSplitJob {
+  const float *src;
+  float *hi, *lo;
+  int64_t rows;        // rows per batch entry (all rows when the batch is contiguous)
+  int64_t k, ld, bs;   // valid columns, row stride, batch stride (elements)
+  int64_t total_rows;  // batch * rows
+  int64_t tiles;       // 8-row tiles
+  int vec;             // rows 16-byte aligned: float4 loads
+};
+constexpr int kSplitRows = 8;
+
+__global__ void __launch_bounds__(256) split_rows_kernel(const RowSplitJob j0, const RowSplitJob j1, int64_t Kp) {
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const int64_t k = ((int64_t)blockIdx.x * 32 + threadIdx.x) * 4;
+  if (k >= Kp) return;
+  const int64_t tiles = j0.tiles + j1.tiles;
+  for (int64_t t = blockIdx.y; t < tiles; t += gridDim.y) {
+    const bool second = t >= j0.tiles;
+    const int64_t R = (second ? t - j0.tiles : t) * kSplitRows + threadIdx.y;
+    const int64_t total_rows = second ? j1.total_rows : j0.total_rows;
+    if (R >= total_rows) continue;
+    const int64_t rows = second ? j1.rows : j0.rows, K = second ? j1.k : j0.k;
+    const int64_t ld = second ? j1.ld : j0.ld, bs = second ? j1.bs : j0.bs;
+    const float *src = second ? j1.src : j0.src;
+    const float *row = rows == total_rows ? src + R * ld : src + (R / rows) * bs + (R % rows) * ld;
+    float4 v;
+    if ((second ? j1.vec : j0.vec) && k + 3 < K) {
+      v = __ldg(reinterpret_cast<const float4 *>(row + k));
     } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? row[k + j] : 0.0f;
+      v.x = k < K ? __ldg(row + k) : 0.0f;
+      v.y = k + 1 < K ? __ldg(row + k + 1) : 0.0f;
+      v.z = k + 2 < K ? __ldg(row + k + 2) : 0.0f;
+      v.w = k + 3 < K ? __ldg(row + k + 3) : 0.0f;
     }
     float4 h, l;
-    split_tf32(v[0], h.x, l.x);
-    split_tf32(v[1], h.y, l.y);
-    split_tf32(v[2], h.z, l.z);
-    split_tf32(v[3], h.w, l.w);
-    const int64_t o = (b * rows + r) * Kp + k;
-    *reinterpret_cast<float4 *>(hi + o) = h;
-    *reinterpret_cast<float4 *>(lo + o) = l;
+    split_tf32x4(v, h, l);
+    const int64_t o = R * Kp + k;
+    *reinterpret_cast<float4 *>((second ? j1.hi : j0.hi) + o) = h;
+    *reinterpret_cast<float4 *>((second ? j1.lo : j0.lo) + o) = l;
   }
 }
 
@@ -73,6 +87,8 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float *__res
                                                               int64_t ld, int64_t bs, int64_t Kp,
                                                               float *__restrict__ hi, float *__restrict__ lo) {
   __shared__ float tile[32][33];
+  grid_dependency_wait();
+  grid_dependents_launch();
   const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
   const float *base = src + (int64_t)blockIdx.z * bs;
   float *hb = hi + (int64_t)blockIdx.z * N * Kp, *lb = lo + (int64_t)blockIdx.z * N * Kp;
@@ -139,7 +155,10 @@ struct GemmShape {
   static_assert(kSmem <= 227 * 1024, "stage ring exceeds shared memory");
 };
 
-template <int BN, int SW, int STAGES>
+// TMA_C selects the C write path at compile time: one kernel holding both
+// paths needs more registers than the 168 a 320-thread CTA may use, and its
+// spills cost more than the whole epilogue.
+template <int BN, int SW, int STAGES, bool TMA_C>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                        const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
@@ -153,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_word;
+  __shared__ float bias_tile[BN];  // this tile's bias columns (TMA_C epilogue)
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
@@ -190,6 +210,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  // Nothing above touched global memory: under programmatic dependent
+  // launch the set-up overlaps the split kernel's tail.
+  grid_dependency_wait();
+  grid_dependents_launch();
 
   if (warp == 0) {
     if (sm100::elect_lane0()) {
@@ -260,6 +284,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     float acc[CPT];
 #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0.0f;
+    if (TMA_C && args.bias) {
+      // The tile's bias columns, read once while the first chunk accumulates;
+      // the staging loop then reads them as shared-memory broadcasts.
+      for (int i = threadIdx.x - 64; i < BN; i += 32 * kEpilogueWarps)
+        bias_tile[i] = n0 + i < args.n ? __ldg(args.bias + n0 + i) : 0.0f;
+      sm100::named_barrier(2, 32 * kEpilogueWarps);
+    }
     bool ok = true;
     for (int chunk = 0; chunk < num_chunks; ++chunk) {
       const int buf = chunk & 1;
@@ -268,13 +299,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       sm100::tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + half * CPT);
+      // 16 columns per load: CPT accumulators + 16 loaded values stay within
+      // the register budget of a 320-thread CTA (168), with no spills.
 #pragma unroll
-      for (int j = 0; j < CPT; j += 32) {
-        uint32_t r[32];
-        sm100::tmem_ld_32x32b_x32(taddr + j, r);
+      for (int j = 0; j < CPT; j += 16) {
+        uint32_t r[16];
+        sm100::tmem_ld_32x32b_x16(taddr + j, r);
         sm100::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+        for (int i = 0; i < 16; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
       }
       sm100::tc_fence_before();
       __syncwarp();
@@ -282,13 +315,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int64_t row = m0 + quarter * 32 + lane;
     const int64_t col0 = n0 + half * CPT;
-    if (args.tma_c) {
+    if constexpr (TMA_C) {
       // The ring is idle once the last chunk is folded: stage C there and
       // write it with one TMA store per box.
       if (ok) {
         const float divisor = args.div_ptr ? __ldg(args.div_ptr) : args.div_value;
         const bool divide = args.div_ptr != nullptr || args.div_value != 1.0f;
         const int r = quarter * 32 + lane;
+        const bool has_bias = args.bias != nullptr;
+        // Plain shared-memory stores (no asm memory clobber), so the compiler
+        // may overlap the iterations' arithmetic and stores freely.
 #pragma unroll
         for (int j = 0; j < CPT; j += 4) {
           float v[4];
@@ -296,14 +332,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < 4; ++q) {
             float x = acc[j + q];
             if (divide) x = __fdiv_rn(x, divisor);
-            if (args.bias) x = __fadd_rn(x, (col0 + j + q < args.n) ? __ldg(args.bias + col0 + j + q) : 0.0f);
+            if (has_bias) x = __fadd_rn(x, bias_tile[half * CPT + j + q]);
             if (args.relu) x = x > 0.0f ? x : 0.0f;
             v[q] = x;
           }
           const int col = half * CPT + j;
-          const uint32_t chunk = (uint32_t)((col & 31) >> 2) ^ (uint32_t)(r & 7);
-          sm100::sts128(sm100::smem_addr(smem + (col >> 5) * kCBox + r * 128 + chunk * 16),
-                        make_float4(v[0], v[1], v[2], v[3]));
+          const int chunk = ((col & 31) >> 2) ^ (r & 7);
+          *reinterpret_cast<float4 *>(smem + (col >> 5) * kCBox + r * 128 + chunk * 16) =
+              make_float4(v[0], v[1], v[2], v[3]);
         }
       }
       sm100::fence_proxy_async_smem();
@@ -320,22 +356,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool divide = args.div_ptr != nullptr || args.div_value != 1.0f;
       const bool vec = ((args.ldc & 3) == 0) && ((args.batch_stride_c & 3) == 0) &&
                        ((reinterpret_cast<uintptr_t>(args.c) & 15) == 0) && col0 + CPT <= args.n;
+      const int64_t ncols = args.n - col0;
+      // Four columns at a time, each group stored as soon as it is final.
 #pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        float x = acc[j];
-        if (divide) x = __fdiv_rn(x, divisor);
-        if (args.bias) x = __fadd_rn(x, (col0 + j < args.n) ? __ldg(args.bias + col0 + j) : 0.0f);
-        if (args.relu) x = x > 0.0f ? x : 0.0f;
-        acc[j] = x;
-      }
-      if (vec) {
+      for (int j = 0; j < CPT; j += 4) {
+        float v[4];
 #pragma unroll
-        for (int j = 0; j < CPT; j += 4)
-          *reinterpret_cast<float4 *>(crow + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-      } else {
+        for (int q = 0; q < 4; ++q) {
+          float x = acc[j + q];
+          if (divide) x = __fdiv_rn(x, divisor);
+          if (args.bias) x = __fadd_rn(x, (j + q < ncols) ? __ldg(args.bias + col0 + j + q) : 0.0f);
+          if (args.relu) x = x > 0.0f ? x : 0.0f;
+          v[q] = x;
+        }
+        if (vec) {
+          *reinterpret_cast<float4 *>(crow + j) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < CPT; ++j)
-          if (col0 + j < args.n) crow[j] = acc[j];
+          for (int q = 0; q < 4; ++q)
+            if (j + q < ncols) crow[j + q] = v[q];
+        }
       }
     }
   }
@@ -548,12 +588,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tc_fence_after();
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + half * CPT);
 #pragma unroll
-        for (int j = 0; j < CPT; j += 32) {
-          uint32_t r[32];
-          sm100::tmem_ld_32x32b_x32(taddr + j, r);
+        for (int j = 0; j < CPT; j += 16) {
+          uint32_t r[16];
+          sm100::tmem_ld_32x32b_x16(taddr + j, r);
           sm100::tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+          for (int i = 0; i < 16; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
         }
         sm100::tc_fence_before();
         __syncwarp();
@@ -682,11 +722,13 @@ int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, Gemm
     if (res != CUDA_SUCCESS) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled (C) failed (%d)", (int)res);
   }
   static_assert((BN / 32) * kCBox <= STAGES * Shape::kStage, "C staging exceeds the ring");
-  auto kernel = gemm_tf32x3_kernel<BN, SW, STAGES>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
+  auto kernel = args.tma_c ? gemm_tf32x3_kernel<BN, SW, STAGES, true> : gemm_tf32x3_kernel<BN, SW, STAGES, false>;
+  cudaError_t err = b2k::set_max_smem(ctx, (const void *)kernel, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: set smem");
   dim3 grid((unsigned)((args.n + BN - 1) / BN), (unsigned)((args.m + BM - 1) / BM), (unsigned)batch);
-  kernel<<<grid, kThreads, Shape::kSmem, s>>>(maps[0], maps[1], maps[2], maps[3], map_c, args);
+  err = b2k::launch_kernel(b2k::pdl_enabled(), kernel, grid, dim3(kThreads), Shape::kSmem, s, maps[0], maps[1],
+                           maps[2], maps[3], map_c, args);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm launch");
   return b2k::check_launch(ctx, "gemm launch");
 }
 
@@ -712,7 +754,7 @@ int launch_streamk(b2k_ctx *ctx, const b2k::SplitOperands &ops, GemmArgs g, cons
   args.flags = sk.flags;
   args.epoch = sk.epoch;
   auto kernel = gemm_streamk_kernel<BN, SW, STAGES>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
+  cudaError_t err = b2k::set_max_smem(ctx, (const void *)kernel, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm stream-K: set smem");
   const int grid = sk.grid;
   void *params[] = {(void *)&maps[0], (void *)&maps[1], (void *)&maps[2], (void *)&maps[3], (void *)&args};
@@ -755,18 +797,45 @@ size_t streamk_scratch_bytes(int grid) { return (size_t)grid * (128 * 256 + 1) *
 
 namespace b2k {
 
+static void fill_job(RowSplitJob &o, const RowSplit &r) {
+  // A batch stored back to back is one tall matrix: no per-row division.
+  const bool flat = r.batch == 1 || r.bs == r.rows * r.ld;
+  o.src = r.src;
+  o.hi = r.hi;
+  o.lo = r.lo;
+  o.total_rows = r.rows * r.batch;
+  o.rows = flat ? o.total_rows : r.rows;
+  o.k = r.k;
+  o.ld = r.ld;
+  o.bs = r.bs;
+  o.tiles = (o.total_rows + kSplitRows - 1) / kSplitRows;
+  o.vec = r.ld % 4 == 0 && (flat || r.bs % 4 == 0) && aligned16(r.src);
+}
+
+int split_rows2(b2k_ctx *ctx, const RowSplit &a, const RowSplit *b, int64_t kp, cudaStream_t s) {
+  RowSplitJob j[2] = {};
+  fill_job(j[0], a);
+  if (b) fill_job(j[1], *b);
+  const int64_t tiles = j[0].tiles + j[1].tiles;
+  if (tiles == 0 || kp == 0) return B2K_OK;
+  const dim3 grid((unsigned)((kp / 4 + 31) / 32), (unsigned)std::min<int64_t>(tiles, 65535));
+  cudaError_t err = launch_kernel(pdl_enabled(), split_rows_kernel, grid, dim3(32, kSplitRows), 0, s, j[0], j[1], kp);
+  if (err != cudaSuccess) return cuda_fail(ctx, err, "split_rows launch");
+  return check_launch(ctx, "split_rows launch");
+}
+
 int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t ld, int64_t bs, int64_t batch,
                int64_t kp, float *hi, float *lo, cudaStream_t s) {
-  const bool vec = (ld % 4 == 0) && (bs % 4 == 0) && aligned16(src);
-  split_rows_kernel<<<ctx->sm_count * 8, 256, 0, s>>>(src, rows, k, ld, bs, batch, kp, hi, lo, vec);
-  return check_launch(ctx, "split_rows launch");
+  return split_rows2(ctx, RowSplit{src, rows, k, ld, bs, batch, hi, lo}, nullptr, kp, s);
 }
 
 int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_t ld, int64_t bs, int64_t batch,
                     int64_t kp, float *hi, float *lo, cudaStream_t s) {
   if (batch > 65535) return fail(ctx, B2K_EINVAL, "split_transpose: batch exceeds 65535");
   dim3 grid((unsigned)((n + 31) / 32), (unsigned)((kp + 31) / 32), (unsigned)batch);
-  split_transpose_kernel<<<grid, 256, 0, s>>>(src, k, n, ld, bs, kp, hi, lo);
+  cudaError_t err = launch_kernel(pdl_enabled(), split_transpose_kernel, grid, dim3(256), 0, s, src, k, n, ld, bs, kp,
+                                  hi, lo);
+  if (err != cudaSuccess) return cuda_fail(ctx, err, "split_transpose launch");
   return check_launch(ctx, "split_transpose launch");
 }
 
@@ -815,10 +884,14 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
   b2k::SplitOperands ops{ws, ws + m * kp, ws + 2 * m * kp, ws + 2 * m * kp + n * kp, kp};
   {
     b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
-    status = b2k::split_rows(ctx, a, m, k, lda, m * lda, 1, kp, ops.a_hi, ops.a_lo, s);
-    if (status == B2K_OK) {
-      status = b_kmajor ? b2k::split_rows(ctx, b, n, k, ldb, n * ldb, 1, kp, ops.b_hi, ops.b_lo, s)
-                        : b2k::split_transpose(ctx, b, k, n, ldb, k * ldb, 1, kp, ops.b_hi, ops.b_lo, s);
+    const b2k::RowSplit sa{a, m, k, lda, m * lda, 1, ops.a_hi, ops.a_lo};
+    if (b_kmajor) {
+      // A and a K-major B in one launch
+      const b2k::RowSplit sb{b, n, k, ldb, n * ldb, 1, ops.b_hi, ops.b_lo};
+      status = b2k::split_rows2(ctx, sa, &sb, kp, s);
+    } else {
+      status = b2k::split_rows2(ctx, sa, nullptr, kp, s);
+      if (status == B2K_OK) status = b2k::split_transpose(ctx, b, k, n, ldb, k * ldb, 1, kp, ops.b_hi, ops.b_lo, s);
     }
   }
   if (status != B2K_OK) return status;

@@ -247,6 +247,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   sm100::tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
   const uint32_t tmem_a = tmem_base + Shape::kAccCols;  // A ring, lane 0
+  // Nothing above touched global memory: under programmatic dependent
+  // launch the set-up overlaps the B split kernel's tail.
+  grid_dependency_wait();
+  grid_dependents_launch();
 
   if (warp == 0) {
     if (sm100::elect_lane0()) {
@@ -625,11 +629,13 @@ int launch_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const b2
   static_assert((BN / 32) * kCBox <= Shape::kStages * Shape::kStage, "C staging exceeds the ring");
   FusedArgs args{c, bias, m, n, ldc, (int)(ops.kp / BK), relu, tma_c, ctx->error_flag};
   auto kernel = gemm_tmem_a_kernel<BN, G>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
+  cudaError_t err = b2k::set_max_smem(ctx, (const void *)kernel, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (TMEM A): set smem");
   if ((n + BN - 1) / BN > 65535) return b2k::fail(ctx, B2K_EINVAL, "gemm: N exceeds %d", 65535 * BN);
   dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN), 1);
-  kernel<<<grid, kThreads, Shape::kSmem, s>>>(map_a, map_bhi, map_blo, map_c, args);
+  err = b2k::launch_kernel(b2k::pdl_enabled(), kernel, grid, dim3(kThreads), Shape::kSmem, s, map_a, map_bhi, map_blo,
+                           map_c, args);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (TMEM A) launch");
   return b2k::check_launch(ctx, "gemm (TMEM A) launch");
 }
 
@@ -645,7 +651,7 @@ int launch_smem_split(b2k_ctx *ctx, const float *a, const float *b, float *c, in
   if (status != B2K_OK) return status;
   FusedArgs args{c, bias, m, n, ldc, (int)((k + BK - 1) / BK), relu, 0, ctx->error_flag};
   auto kernel = gemm_smem_split_kernel<BN, B_MN>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
+  cudaError_t err = b2k::set_max_smem(ctx, (const void *)kernel, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (shared-memory split): set smem");
   dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM), 1);
   kernel<<<grid, kThreads, Shape::kSmem, s>>>(map_a, map_b, args);

@@ -112,6 +112,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_timing_enable": ([_P, C.c_int], C.c_int),
+    "b2k_timing_select": ([_P, C.c_uint32], C.c_int),
+    "b2k_set_pdl": ([C.c_int], C.c_int),
     "b2k_timing_read": ([_P, C.c_int, C.POINTER(C.c_double), C.POINTER(_I64)], C.c_int),
     "b2k_timing_reset": ([_P], C.c_int),
     "b2k_kernel_launches": ([C.c_void_p, C.POINTER(_I64)], C.c_int),
@@ -156,6 +158,29 @@ def make_program(n_inputs: int, insns: list[tuple], result: int, broadcast=()) -
     for i, (op, a, b, c, imm) in enumerate(insns):
         prog.insns[i] = PwInsn(OPCODES[op] if isinstance(op, str) else int(op), a, b, c, float(imm))
     return prog
+
+
+class BoundCall:
+    """One library call with its arguments converted to C types once.
+
+    Calling it re-issues the same call -- the same kernels on the same
+    buffers, every step doing the full work -- without converting Python
+    arguments again, which is most of the host cost of a short call made
+    from Python.  Raises :class:`B2KError` on a failed status, like the
+    methods of :class:`Context`.
+    """
+
+    def __init__(self, ctx: "Context", name: str, args: tuple, keep: tuple = ()):
+        fn = getattr(ctx.lib, name)
+        converted = [a if isinstance(a, (C._SimpleCData, C._Pointer, C.Array)) or type(a).__name__ == "CArgObject"
+                     else t(a) for t, a in zip(fn.argtypes, args)]
+        self._fn, self._args, self._keep = fn, tuple(converted), keep
+        self._ctx, self._name = ctx, name
+
+    def __call__(self) -> None:
+        status = self._fn(*self._args)
+        if status != B2K_OK:
+            self._ctx.check(status, self._name)
 
 
 class Context:
@@ -217,23 +242,57 @@ class Context:
     def selective_exp(self, x: int, y: int, n: int, stream: int = 0) -> None:
         self.check(self.lib.b2k_selective_exp_f32(self.handle, x, y, n, stream), "b2k_selective_exp_f32")
 
-    def gemm(self, a: int, b: int, c: int, m: int, n: int, k: int, *, b_layout: int = B_KN,
-             lda: int | None = None, ldb: int | None = None, ldc: int | None = None,
-             bias: int = 0, relu: bool = False, stream: int = 0) -> None:
+    def _gemm_args(self, a, b, c, m, n, k, b_layout=B_KN, lda=None, ldb=None, ldc=None, bias=0, relu=False,
+                   stream=0) -> tuple:
         lda = k if lda is None else lda
         ldb = (n if b_layout == B_KN else k) if ldb is None else ldb
         ldc = n if ldc is None else ldc
-        self.check(self.lib.b2k_gemm_tf32x3(self.handle, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias or None,
-                                            int(relu), stream), "b2k_gemm_tf32x3")
+        return (self.handle, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias or None, int(relu), stream)
+
+    def gemm(self, a: int, b: int, c: int, m: int, n: int, k: int, *, b_layout: int = B_KN,
+             lda: int | None = None, ldb: int | None = None, ldc: int | None = None,
+             bias: int = 0, relu: bool = False, stream: int = 0) -> None:
+        self.check(self.lib.b2k_gemm_tf32x3(*self._gemm_args(a, b, c, m, n, k, b_layout, lda, ldb, ldc, bias, relu,
+                                                             stream)), "b2k_gemm_tf32x3")
+
+    def gemm_call(self, a: int, b: int, c: int, m: int, n: int, k: int, **kw) -> "BoundCall":
+        """:meth:`gemm` with its arguments converted once (see :class:`BoundCall`)."""
+        return BoundCall(self, "b2k_gemm_tf32x3", self._gemm_args(a, b, c, m, n, k, **kw))
+
+    def _attention_args(self, q, k, v, o, bh, s_q, s_kv, d, dv, scale=None, scale_ptr=0, k_layout=K_SD,
+                        stream=0) -> tuple:
+        div = float(d) ** 0.5 if scale is None else float(scale)
+        return (self.handle, q, k, v, o, bh, s_q, s_kv, d, dv, div, scale_ptr or None, k_layout, stream)
 
     def attention(self, q: int, k: int, v: int, o: int, bh: int, s_q: int, s_kv: int, d: int, dv: int, *,
                   scale: float | None = None, scale_ptr: int = 0, k_layout: int = K_SD, stream: int = 0) -> None:
         """O = softmax(Q K^T / scale) V per head; scale defaults to sqrt(d)."""
-        div = float(d) ** 0.5 if scale is None else float(scale)
-        self.check(self.lib.b2k_attention_tf32x3(self.handle, q, k, v, o, bh, s_q, s_kv, d, dv, div,
-                                                 scale_ptr or None, k_layout, stream), "b2k_attention_tf32x3")
+        self.check(self.lib.b2k_attention_tf32x3(*self._attention_args(q, k, v, o, bh, s_q, s_kv, d, dv, scale,
+                                                                       scale_ptr, k_layout, stream)),
+                   "b2k_attention_tf32x3")
 
-    def timing(self, on: bool) -> None:
+    def attention_call(self, q: int, k: int, v: int, o: int, bh: int, s_q: int, s_kv: int, d: int, dv: int,
+                       **kw) -> "BoundCall":
+        """:meth:`attention` with its arguments converted once."""
+        return BoundCall(self, "b2k_attention_tf32x3", self._attention_args(q, k, v, o, bh, s_q, s_kv, d, dv, **kw))
+
+    def row_softmax_call(self, x: int, y: int, rows: int, cols: int, ld_x: int | None = None,
+                         ld_y: int | None = None, stream: int = 0) -> "BoundCall":
+        """:meth:`row_softmax` with its arguments converted once."""
+        return BoundCall(self, "b2k_row_softmax_f32", (self.handle, x, y, rows, cols, ld_x or cols, ld_y or cols,
+                                                        stream))
+
+    def pointwise_call(self, program: PwProgram, inputs: list[int], out: int, n: int,
+                       stream: int = 0) -> "BoundCall":
+        """:meth:`pointwise` with its arguments converted once."""
+        arr = (_P * max(1, len(inputs)))(*inputs)
+        return BoundCall(self, "b2k_pointwise_f32", (self.handle, C.byref(program), arr, out, n, stream),
+                         keep=(program, arr))
+
+    def timing(self, on: bool, phases: list[str] | None = None) -> None:
+        """Enable per-phase event timing, for `phases` only when given."""
+        mask = 0xFFFFFFFF if phases is None else sum(1 << PHASES[p] for p in phases)
+        self.check(self.lib.b2k_timing_select(self.handle, mask), "b2k_timing_select")
         self.check(self.lib.b2k_timing_enable(self.handle, int(on)), "b2k_timing_enable")
 
     def timing_read(self, phase: str) -> tuple[float, int]:
@@ -270,6 +329,10 @@ class Context:
 
     def set_gemm_streamk(self, on: bool) -> None:
         self.check(self.lib.b2k_gemm_set_streamk(int(bool(on))), "b2k_gemm_set_streamk")
+
+    def set_pdl(self, on: bool) -> None:
+        """Programmatic dependent launch between a call's kernels (process-wide, default on)."""
+        self.check(self.lib.b2k_set_pdl(int(bool(on))), "b2k_set_pdl")
 
     def sync(self, stream: int = 0) -> None:
         self.check(self.lib.b2k_stream_sync(self.handle, stream), "b2k_stream_sync")

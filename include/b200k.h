@@ -91,9 +91,24 @@ int b2k_selftest_wait_timeout(b2k_ctx *ctx, int64_t budget_cycles, void *stream)
 #define B2K_PHASE_FLASH 6     /* fused attention kernel */
 #define B2K_PHASE_COUNT 7
 int b2k_timing_enable(b2k_ctx *ctx, int on);
+/* Restrict timing to the phases whose bit (1 << B2K_PHASE_*) is set in
+ * `phase_mask` (default: all).  Each timed phase costs two event records
+ * per call, and an event between two kernels of one call serialises them
+ * (see b2k_set_pdl), so a caller timing one kernel should select only its
+ * phase. */
+int b2k_timing_select(b2k_ctx *ctx, uint32_t phase_mask);
 int b2k_timing_read(b2k_ctx *ctx, int phase, double *total_ms, int64_t *launches);
 int b2k_timing_reset(b2k_ctx *ctx);
 int b2k_kernel_launches(b2k_ctx *ctx, int64_t *count);
+
+/* --- launch overlap -----------------------------------------------------------
+ * Process-wide switch (default on): the kernels of a split-then-multiply
+ * operation (GEMM, fused attention) are launched with programmatic
+ * dependent launch, so the tensor-core kernel's CTAs are scheduled and run
+ * their set-up while the split kernel drains, and the next call's split
+ * overlaps this call's tail.  Results are identical either way; the switch
+ * exists for comparisons.  No counterpart in the reference. */
+int b2k_set_pdl(int on);
 
 /* --- pointwise programs ---------------------------------------------------
  * Replaces the SIMT Emitter's pointwise lowering: Tile decode
