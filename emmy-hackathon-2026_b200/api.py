@@ -107,20 +107,60 @@ class Session:
         self.ctx.pointwise(program, [t.ptr for t in inputs], out.ptr, out.size, stream=self.stream)
 
     # --- end to end from host arrays --------------------------------------------
+    # One library call per operation: the inputs are copied in slab by slab on
+    # a copy stream, each slab computes as soon as it has landed, and finished
+    # output slabs are copied out on a second copy stream (b2k_*_host).  The
+    # calls are asynchronous: `out` is complete after :meth:`sync`.  Host
+    # arrays from :meth:`pinned` give full copy/compute overlap.
+    @staticmethod
+    def _host_in(x: np.ndarray) -> np.ndarray:
+        x = np.asarray(x)
+        if x.dtype != F32 or not x.flags.c_contiguous:
+            raise ValueError("host inputs must be C-contiguous float32 arrays")
+        return x
+
+    @staticmethod
+    def _host_out(out: np.ndarray | None, shape: tuple) -> np.ndarray:
+        if out is None:
+            return np.empty(shape, F32)
+        if out.dtype != F32 or not out.flags.c_contiguous or out.shape != tuple(shape):
+            raise ValueError(f"output must be a C-contiguous float32 array of shape {tuple(shape)}")
+        return out
+
     def gemm_host(self, a: np.ndarray, b: np.ndarray, out: np.ndarray | None = None, *, b_layout: str = "kn",
-                  bias: np.ndarray | None = None, relu: bool = False, buffers: dict | None = None) -> np.ndarray:
-        """Copy A, B (and bias) in, run the GEMM, copy C out.  ``buffers``
-        (a dict) caches the device allocations across calls of one shape."""
-        buffers = {} if buffers is None else buffers
+                  bias: np.ndarray | None = None, relu: bool = False) -> np.ndarray:
+        a, b = self._host_in(a), self._host_in(b)
         m, k = a.shape
         n = b.shape[1] if b_layout == "kn" else b.shape[0]
-        if "a" not in buffers:
-            buffers.update(a=self.empty(a.shape), b=self.empty(b.shape), c=self.empty((m, n)),
-                           bias=self.empty(bias.shape) if bias is not None else None)
-        self.upload(a, buffers["a"])
-        self.upload(b, buffers["b"])
-        if bias is not None:
-            self.upload(bias, buffers["bias"])
-        self.gemm(buffers["a"], buffers["b"], buffers["c"], b_layout=b_layout, bias=buffers["bias"], relu=relu)
-        out = self.download(buffers["c"], out)
+        out = self._host_out(out, (m, n))
+        bias = self._host_in(bias) if bias is not None else None
+        self.ctx.gemm_host(a.ctypes.data, b.ctypes.data, out.ctypes.data, m, n, k,
+                           b_layout=runtime.B_KN if b_layout == "kn" else runtime.B_NK,
+                           bias=bias.ctypes.data if bias is not None else 0, relu=relu, stream=self.stream)
+        return out
+
+    def row_softmax_host(self, x: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        x = self._host_in(x)
+        rows, cols = x.shape
+        out = self._host_out(out, x.shape)
+        self.ctx.row_softmax_host(x.ctypes.data, out.ctypes.data, rows, cols, stream=self.stream)
+        return out
+
+    def pointwise_host(self, program, inputs: list[np.ndarray], out: np.ndarray) -> np.ndarray:
+        inputs = [self._host_in(t) for t in inputs]
+        out = self._host_out(out, out.shape)
+        self.ctx.pointwise_host(program, [t.ctypes.data for t in inputs], out.ctypes.data, out.size,
+                                stream=self.stream)
+        return out
+
+    def attention_host(self, q: np.ndarray, k: np.ndarray, v: np.ndarray, out: np.ndarray | None = None, *,
+                       scale: float | None = None, k_layout: str = "sd") -> np.ndarray:
+        """q [bh, s_q, d], k [bh, s_kv, d] (or [bh, d, s_kv] with k_layout "ds"), v [bh, s_kv, dv]."""
+        q, k, v = self._host_in(q), self._host_in(k), self._host_in(v)
+        bh, s_q, d = q.shape
+        s_kv, dv = v.shape[1], v.shape[2]
+        out = self._host_out(out, (bh, s_q, dv))
+        self.ctx.attention_host(q.ctypes.data, k.ctypes.data, v.ctypes.data, out.ctypes.data, bh, s_q, s_kv, d, dv,
+                                scale=scale, k_layout=runtime.K_SD if k_layout == "sd" else runtime.K_DS,
+                                stream=self.stream)
         return out

@@ -157,6 +157,12 @@ int b2k_destroy(b2k_ctx *ctx) {
   cudaSetDevice(ctx->device);
   b2k_timing_reset(ctx);
   for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
+  if (ctx->copy_in) cudaStreamSynchronize(ctx->copy_in);
+  if (ctx->copy_out) cudaStreamSynchronize(ctx->copy_out);
+  for (cudaEvent_t e : ctx->sync_events) cudaEventDestroy(e);
+  if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
+  if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
+  if (ctx->staging) cudaFree(ctx->staging);
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->error_flag) cudaFree(ctx->error_flag);
   delete ctx;

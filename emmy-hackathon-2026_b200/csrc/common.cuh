@@ -26,6 +26,12 @@ struct b2k_ctx {
   unsigned int *error_flag = nullptr;
   // Kernels enqueued through this context (b2k_kernel_launches).
   int64_t kernel_launches = 0;
+  // Pipelined host-array calls (host.cu): copy streams, dependency events
+  // (reused across calls) and the device staging arena.
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  std::vector<cudaEvent_t> sync_events;
+  void *staging = nullptr;
+  size_t staging_bytes = 0;
   // Stream-K flag slots in the workspace and the epoch of the last GEMM.
   unsigned *flags_ptr = nullptr;
   unsigned flags_epoch = 0;

@@ -111,6 +111,10 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_attention_set_fused": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
+    "b2k_row_softmax_f32_host": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
+    "b2k_pointwise_f32_host": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _P], C.c_int),
+    "b2k_gemm_tf32x3_host": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
+    "b2k_attention_tf32x3_host": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I32, _P], C.c_int),
     "b2k_timing_enable": ([_P, C.c_int], C.c_int),
     "b2k_timing_select": ([_P, C.c_uint32], C.c_int),
     "b2k_set_pdl": ([C.c_int], C.c_int),
@@ -288,6 +292,30 @@ class Context:
         arr = (_P * max(1, len(inputs)))(*inputs)
         return BoundCall(self, "b2k_pointwise_f32", (self.handle, C.byref(program), arr, out, n, stream),
                          keep=(program, arr))
+
+    # --- pipelined host-array calls: the same operations on HOST pointers, with
+    # the copies in, the kernels and the copies out overlapped slab by slab.
+    def row_softmax_host(self, x: int, y: int, rows: int, cols: int, ld_x: int | None = None,
+                         ld_y: int | None = None, stream: int = 0) -> None:
+        self.check(self.lib.b2k_row_softmax_f32_host(self.handle, x, y, rows, cols, ld_x or cols, ld_y or cols,
+                                                     stream), "b2k_row_softmax_f32_host")
+
+    def pointwise_host(self, program: PwProgram, inputs: list[int], out: int, n: int, stream: int = 0) -> None:
+        arr = (_P * max(1, len(inputs)))(*inputs)
+        self.check(self.lib.b2k_pointwise_f32_host(self.handle, C.byref(program), arr, out, n, stream),
+                   "b2k_pointwise_f32_host")
+
+    def gemm_host(self, a: int, b: int, c: int, m: int, n: int, k: int, *, b_layout: int = B_KN,
+                  lda: int | None = None, ldb: int | None = None, ldc: int | None = None,
+                  bias: int = 0, relu: bool = False, stream: int = 0) -> None:
+        self.check(self.lib.b2k_gemm_tf32x3_host(*self._gemm_args(a, b, c, m, n, k, b_layout, lda, ldb, ldc, bias,
+                                                                  relu, stream)), "b2k_gemm_tf32x3_host")
+
+    def attention_host(self, q: int, k: int, v: int, o: int, bh: int, s_q: int, s_kv: int, d: int, dv: int, *,
+                       scale: float | None = None, k_layout: int = K_SD, stream: int = 0) -> None:
+        div = float(d) ** 0.5 if scale is None else float(scale)
+        self.check(self.lib.b2k_attention_tf32x3_host(self.handle, q, k, v, o, bh, s_q, s_kv, d, dv, div, k_layout,
+                                                      stream), "b2k_attention_tf32x3_host")
 
     def timing(self, on: bool, phases: list[str] | None = None) -> None:
         """Enable per-phase event timing, for `phases` only when given."""

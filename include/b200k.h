@@ -344,6 +344,31 @@ int b2k_gemm_set_streamk(int on);
  * reference. */
 int b2k_gemm_set_fused_split(int mode);
 
+/* --- pipelined host-array calls ----------------------------------------------
+ * The runner's per-request host flow -- copy every input in, launch, copy
+ * every output out (tools/local_runner.py:287-338) -- as one call that
+ * overlaps the three.  Arguments are HOST pointers with the meaning of the
+ * device entry point of the same name.  Inputs are cut into slabs (rows of
+ * the softmax or of A, element ranges, batch*heads); slab i is copied in on
+ * a context-owned host-to-device stream, its kernels run on `stream` once it
+ * has landed, and its output is copied out on a device-to-host stream while
+ * later slabs compute and copy in.  Device staging memory belongs to the
+ * context.  Asynchronous like the device entry points: the host outputs are
+ * complete once `stream` is synchronised (b2k_stream_sync).  Host buffers
+ * should be page-locked (b2k_host_alloc); pageable buffers work with less
+ * overlap.  Results equal the device entry points' bit for bit. */
+int b2k_row_softmax_f32_host(b2k_ctx *ctx, const float *x, float *y, int64_t rows, int64_t cols, int64_t ld_x,
+                             int64_t ld_y, void *stream);
+int b2k_pointwise_f32_host(b2k_ctx *ctx, const b2k_pw_program *program, const float *const *inputs, float *out,
+                           int64_t n, void *stream);
+int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                         int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
+                         void *stream);
+/* Host variant of b2k_attention_tf32x3 with the scale divisor by value. */
+int b2k_attention_tf32x3_host(b2k_ctx *ctx, const float *q, const float *k, const float *v, float *o, int64_t bh,
+                              int64_t s_q, int64_t s_kv, int64_t d, int64_t dv, float scale_div, int32_t k_layout,
+                              void *stream);
+
 #ifdef __cplusplus
 }
 #endif
