@@ -6,6 +6,8 @@ import ctypes
 import re
 import subprocess
 
+import pytest
+
 from conftest import ROOT, pkg
 
 HEADER = ROOT / "include" / "b200k.h"
@@ -42,3 +44,31 @@ def test_runtime_binds_every_declared_symbol():
 def test_version_without_gpu():
     runtime = pkg("runtime")
     assert runtime.library().b2k_version() == 100
+
+
+def test_bound_call_converts_once_and_checks_status():
+    """BoundCall against a C function with the library's calling pattern
+    (libc abs: the status is the return value)."""
+    import ctypes as C
+    import ctypes.util
+
+    rt = pkg("runtime")
+    libc = C.CDLL(ctypes.util.find_library("c"))
+    libc.abs.argtypes, libc.abs.restype = [C.c_int], C.c_int
+    seen = []
+
+    class FakeCtx:
+        lib = libc
+
+        def check(self, status, call):
+            seen.append((status, call))
+            raise rt.B2KError(status, "failed", call)
+
+    ok = rt.BoundCall(FakeCtx(), "abs", (0,))
+    ok()
+    ok()
+    assert seen == []
+    bad = rt.BoundCall(FakeCtx(), "abs", (-7,))
+    with pytest.raises(rt.B2KError):
+        bad()
+    assert seen == [(7, "abs")]
