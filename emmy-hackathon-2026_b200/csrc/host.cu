@@ -11,9 +11,10 @@
 // host-to-device stream; the caller's stream waits for it (event) and runs
 // the slab's kernels; the device-to-host stream waits for those and copies
 // slab i's output out while slab i+1 computes and slab i+2 is copied in.
-// PCIe and C2C links are full duplex and the B200 has separate copy engines
-// per direction, so the call costs about max(bytes in, bytes out) / link
-// bandwidth plus one slab of compute and copy-out, instead of their sum.
+// The host link is full duplex and the B200 has copy engines per direction
+// (measured on the B200 box: 55 GB/s one way, 42 GB/s each way when both
+// run), so the call costs about the link time of its bytes plus one slab of
+// compute and copy-out, instead of the sum of copy-in, compute and copy-out.
 //
 // Device memory for the staged operands is a context-owned arena; the split
 // operands of the GEMM use the context workspace as the device entry points
@@ -32,14 +33,22 @@ namespace b2k {
 namespace {
 
 constexpr size_t kAlign = 256;
-constexpr size_t kSlabBytes = size_t(8) << 20;  // target input bytes per slab
 constexpr int kMaxSlabs = 32;
+// Target input bytes per slab, per operation, measured on B200 (4 / 8 / 16 /
+// 32 MB tried): small GEMM slabs shorten the exposed last slab (the compute
+// of 256 rows of A and their copy-out); attention wants slabs of at least
+// six heads of 2048 queries (96 CTAs) per launch; the streaming kernels are
+// flat between 8 and 16 MB.
+constexpr size_t kSlabStream = size_t(8) << 20;
+constexpr size_t kSlabGemm = size_t(4) << 20;
+constexpr size_t kSlabAttention = size_t(16) << 20;
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// Slabs for `total_in` input bytes, at least 1, at most min(kMaxSlabs, units).
-int64_t slab_count(size_t total_in, int64_t units) {
-  const int64_t s = (int64_t)((total_in + kSlabBytes - 1) / kSlabBytes);
+// Slabs of about `target` bytes for `total_in` input bytes, at least 1, at
+// most min(kMaxSlabs, units).
+int64_t slab_count(size_t total_in, int64_t units, size_t target) {
+  const int64_t s = (int64_t)((total_in + target - 1) / target);
   return std::max<int64_t>(1, std::min<int64_t>({s, (int64_t)kMaxSlabs, units}));
 }
 
@@ -180,7 +189,7 @@ int b2k_row_softmax_f32_host(b2k_ctx *ctx, const float *x, float *y, int64_t row
   B2K_TRY(b2k::reserve_staging(ctx, carve.used, s));
   char *base = static_cast<char *>(ctx->staging);
   float *dx = reinterpret_cast<float *>(base + ox), *dy = reinterpret_cast<float *>(base + oy);
-  const int64_t slabs = b2k::slab_count(row_bytes * rows, rows);
+  const int64_t slabs = b2k::slab_count(row_bytes * rows, rows, b2k::kSlabStream);
   const int64_t per = (rows + slabs - 1) / slabs;
   b2k::Pipe pipe(ctx, s);
   B2K_TRY(pipe.begin());
@@ -220,7 +229,8 @@ int b2k_pointwise_f32_host(b2k_ctx *ctx, const b2k_pw_program *program, const fl
   B2K_TRY(b2k::reserve_staging(ctx, carve.used, s));
   char *base = static_cast<char *>(ctx->staging);
   // Slabs of a multiple of 1024 elements keep every slab 16-byte aligned.
-  const int64_t slabs = b2k::slab_count(std::max<size_t>(streamed, (size_t)n * 4), (n + 1023) / 1024);
+  const int64_t slabs =
+      b2k::slab_count(std::max<size_t>(streamed, (size_t)n * 4), (n + 1023) / 1024, b2k::kSlabStream);
   const int64_t per = ((n + slabs - 1) / slabs + 1023) / 1024 * 1024;
   b2k::Pipe pipe(ctx, s);
   B2K_TRY(pipe.begin());
@@ -270,7 +280,7 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
   float *dc = reinterpret_cast<float *>(base + oc);
   const float *dbias = bias ? reinterpret_cast<float *>(base + obias) : nullptr;
   // Slabs of rows of A (multiples of the 128-row tile).
-  const int64_t slabs = b2k::slab_count((size_t)m * k * 4, (m + 127) / 128);
+  const int64_t slabs = b2k::slab_count((size_t)m * k * 4, (m + 127) / 128, b2k::kSlabGemm);
   const int64_t per = ((m + slabs - 1) / slabs + 127) / 128 * 128;
   b2k::Pipe pipe(ctx, s);
   if (k == 0 || b2k::gemm_split_mode(da, db, per, n, k, k, b_cols) == 2) {
@@ -342,7 +352,7 @@ int b2k_attention_tf32x3_host(b2k_ctx *ctx, const float *q, const float *k, cons
   char *base = static_cast<char *>(ctx->staging);
   float *dq = reinterpret_cast<float *>(base + oq), *dk = reinterpret_cast<float *>(base + ok);
   float *dvv = reinterpret_cast<float *>(base + ov), *dout = reinterpret_cast<float *>(base + oo);
-  const int64_t slabs = b2k::slab_count((hq + hk + hv) * bh * 4, bh);
+  const int64_t slabs = b2k::slab_count((hq + hk + hv) * bh * 4, bh, b2k::kSlabAttention);
   const int64_t per = (bh + slabs - 1) / slabs;
   b2k::Pipe pipe(ctx, s);
   B2K_TRY(pipe.begin());
