@@ -27,6 +27,7 @@ host cores.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import importlib
 import json
 import os
@@ -73,6 +74,21 @@ def profile_traffic(name: str) -> float | None:
 
 # --------------------------------------------------------------------------- workloads
 TIMING_EVERY = 8  # steps per sampled launch of the dominant kernel
+
+
+@contextlib.contextmanager
+def stdout_to_stderr():
+    """Point file descriptor 1 at stderr for the duration (libraries that
+    write to the C-level stdout included)."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    try:
+        os.dup2(2, 1)
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
 
 
 class Workload:
@@ -438,7 +454,11 @@ def run_ours(args) -> dict | None:
     dist = None
     if world > 1:
         import torch.distributed as dist
-        pkg("mgpu").init_from_env("nccl", timeout_s=120)
+        # NCCL prints its version on stdout while the communicator comes up;
+        # stdout must carry only the JSON line, so send that to stderr.
+        with stdout_to_stderr():
+            pkg("mgpu").init_from_env("nccl", timeout_s=120)
+            dist.barrier()
     runtime, api = pkg("runtime"), pkg("api")
     ctx = runtime.Context(local)
     w = make_workload(args.workload, rank, world)
