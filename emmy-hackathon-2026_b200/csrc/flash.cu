@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < OC; i += 4) {
           const int col = oc0 + i;
           const uint32_t chunk = (uint32_t)((col & 31) >> 2) ^ (uint32_t)(r & 7);
-          sm100::sts128(sm100::smem_addr(q_hi + (col >> 5) * kSub + r * 128 + chunk * 16),
+          sm100::sts128_relaxed(sm100::smem_addr(q_hi + (col >> 5) * kSub + r * 128 + chunk * 16),
                         make_float4(__fmul_rn(o_acc[i], inv_l), __fmul_rn(o_acc[i + 1], inv_l),
                                     __fmul_rn(o_acc[i + 2], inv_l), __fmul_rn(o_acc[i + 3], inv_l)));
         }

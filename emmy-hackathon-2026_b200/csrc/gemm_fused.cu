@@ -137,8 +137,10 @@ struct Slice {
       }
       const int col = c0 + j;
       const uint32_t chunk = (uint32_t)((col & 31) >> 2) ^ (uint32_t)(row & 7);
-      sm100::sts128(sm100::smem_addr(staging + (col >> 5) * kCBox + row * 128 + chunk * 16),
-                    make_float4(v[0], v[1], v[2], v[3]));
+      // no compiler memory barrier: the bias loads of later groups may be
+      // issued ahead of this store
+      sm100::sts128_relaxed(sm100::smem_addr(staging + (col >> 5) * kCBox + row * 128 + chunk * 16),
+                            make_float4(v[0], v[1], v[2], v[3]));
     }
   }
 
@@ -345,22 +347,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t src = sm100::smem_addr(a_raw(s)) + row_off;
       const uint32_t dst = tmem_a + lane_base + (uint32_t)(t * 32);
       if constexpr (G == 4) {
-        // The whole 16-element row chunk: one 16-column store each for hi and lo.
-        uint32_t h[16], l[16];
+        // The whole 16-element row chunk, loaded at once, split and stored
+        // in two halves of 8 columns each for hi and lo: with the 48
+        // accumulators this stays inside the 96 registers a 576-thread CTA
+        // may use (16-column halves spilled).
         float4 v[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) v[q] = sm100::lds128(src + 16u * ((uint32_t)q ^ swz));
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float4 hv, lv;
-          split_tf32x4(v[q], hv, lv);
-          h[4 * q + 0] = __float_as_uint(hv.x), h[4 * q + 1] = __float_as_uint(hv.y);
-          h[4 * q + 2] = __float_as_uint(hv.z), h[4 * q + 3] = __float_as_uint(hv.w);
-          l[4 * q + 0] = __float_as_uint(lv.x), l[4 * q + 1] = __float_as_uint(lv.y);
-          l[4 * q + 2] = __float_as_uint(lv.z), l[4 * q + 3] = __float_as_uint(lv.w);
+        for (int half = 0; half < 2; ++half) {
+          uint32_t h[8], l[8];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            float4 hv, lv;
+            split_tf32x4(v[2 * half + q], hv, lv);
+            h[4 * q + 0] = __float_as_uint(hv.x), h[4 * q + 1] = __float_as_uint(hv.y);
+            h[4 * q + 2] = __float_as_uint(hv.z), h[4 * q + 3] = __float_as_uint(hv.w);
+            l[4 * q + 0] = __float_as_uint(lv.x), l[4 * q + 1] = __float_as_uint(lv.y);
+            l[4 * q + 2] = __float_as_uint(lv.z), l[4 * q + 3] = __float_as_uint(lv.w);
+          }
+          sm100::tmem_st_32x32b_x8(dst + 8 * half, h);
+          sm100::tmem_st_32x32b_x8(dst + 16 + 8 * half, l);
         }
-        sm100::tmem_st_32x32b_x16(dst, h);
-        sm100::tmem_st_32x32b_x16(dst + 16, l);
       } else {
 #pragma unroll
         for (int q = 0; q < G; ++q) {

@@ -214,6 +214,13 @@ __device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
                : "memory");
 }
 
+// 16-byte shared-memory store without a compiler memory barrier: loads and
+// arithmetic may be scheduled around it (volatile asms keep their order).
+// A later fence_proxy_async_smem() or barrier orders it before consumers.
+__device__ __forceinline__ void sts128_relaxed(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w));
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (TMA, tcgen05.mma) before it signals a consumer.
 __device__ __forceinline__ void fence_proxy_async_smem() {
