@@ -81,6 +81,7 @@ struct FlashRing {
 
 struct FlashArgs {
   int tma_o;  // O written by TMA stores from shared memory (16-byte aligned, dv % 4 == 0)
+  int q_raw;  // map_qhi is raw FP32 Q: the CTA splits its Q tile in shared memory
   float *o;
   int64_t s_q, s_kv, dv;
   int dp;          // padded head dim (multiple of 32, <= 128)
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Ring = FlashRing<PAIR>;
   constexpr int kStages = Ring::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full, p_full, pv_done, drain;
+  __shared__ __align__(8) uint64_t q_full, q_ready, p_full, pv_done, drain;
   __shared__ __align__(8) uint64_t ring_full[kStages], ring_empty[kStages], s_full[2];
   // CTA pair: the peer CTA's Q and ring stages landed (forwarded to the even CTA).
   __shared__ __align__(8) uint64_t peer_q, peer_ready[kStages];
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_word = (sm100::smem_addr(smem_raw) & 1023u) ? 1 : 0;
     if (abort_word) atomicOr(args.err, sm100::kSiteAttention);
     sm100::mbar_init(&q_full, 1);
+    sm100::mbar_init(&q_ready, 8);             // one arrival per softmax warp (raw Q split)
     sm100::mbar_init(&p_full, PAIR ? 16 : 8);  // one arrival per softmax warp (of both CTAs)
     sm100::mbar_init(&peer_q, 1);
     sm100::mbar_init(&pv_done, 1);
@@ -161,10 +163,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer: Q once, then K_j chunks, V_j chunks, K_{j+1} ...
-      sm100::mbar_arrive_expect_tx(&q_full, 2 * dblocks * kSub);
-      for (int c = 0; c < dblocks; ++c) {
-        sm100::tma_load_3d(q_hi + c * kSub, &map_qhi, &q_full, c * 32, (int)m0, head);
-        sm100::tma_load_3d(q_lo + c * kSub, &map_qlo, &q_full, c * 32, (int)m0, head);
+      if (!PAIR && args.q_raw) {
+        // raw Q into the hi buffer; the softmax warps split it in place
+        sm100::mbar_arrive_expect_tx(&q_full, dblocks * kSub);
+        for (int c = 0; c < dblocks; ++c) sm100::tma_load_3d(q_hi + c * kSub, &map_qhi, &q_full, c * 32, (int)m0, head);
+      } else {
+        sm100::mbar_arrive_expect_tx(&q_full, 2 * dblocks * kSub);
+        for (int c = 0; c < dblocks; ++c) {
+          sm100::tma_load_3d(q_hi + c * kSub, &map_qhi, &q_full, c * 32, (int)m0, head);
+          sm100::tma_load_3d(q_lo + c * kSub, &map_qlo, &q_full, c * 32, (int)m0, head);
+        }
       }
       // Ring order = MMA order: K_0, then for each block j, K_{j+1} and V_j.
       int n = 0;  // chunks issued through the ring
@@ -238,7 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                abort);
         return true;
       };
-      bool ok = sm100::mbar_wait_warp(&q_full, 0, args.err, sm100::kSiteAttention, abort);
+      bool ok = !PAIR && args.q_raw ? sm100::mbar_wait_warp(&q_ready, 0, args.err, sm100::kSiteAttention, abort)
+                                    : sm100::mbar_wait_warp(&q_full, 0, args.err, sm100::kSiteAttention, abort);
       if constexpr (PAIR) ok = ok && sm100::mbar_wait_cluster_warp(&peer_q, 0, args.err, sm100::kSiteAttention, abort);
       int n = 0;  // ring chunks consumed
       auto issue_s = [&](int j) {
@@ -324,6 +333,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
+    if (!PAIR && args.q_raw) {
+      // Split the raw Q tile in place: Q_hi over the raw values, Q_lo in its
+      // own buffer, the same 128-byte-swizzled [128 rows x 32] boxes the
+      // MMAs read.  Warpgroup wg takes boxes wg, wg + 2, ...; each thread its
+      // row's eight 16-byte chunks of a box (chunk c of row r sits at
+      // c ^ (r & 7): conflict-free across the warp).
+      ok = sm100::mbar_wait(&q_full, 0, args.err, sm100::kSiteAttention, abort);
+      if (ok) {
+        for (int c = wg; c < dblocks; c += 2) {
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const uint32_t off = (uint32_t)(c * kSub + r * 128 + ((ch ^ (r & 7)) << 4));
+            float4 hv, lv;
+            split_tf32x4(sm100::lds128(sm100::smem_addr(q_hi) + off), hv, lv);
+            sm100::sts128(sm100::smem_addr(q_hi) + off, hv);
+            sm100::sts128(sm100::smem_addr(q_lo) + off, lv);
+          }
+        }
+        sm100::fence_proxy_async_smem();  // the MMAs read Q through the async proxy
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&q_ready);
+    }
     // Every thread runs every iteration and reaches both named barriers even
     // after a failed wait (ok == false), so the two warpgroups never wait on
     // each other forever; failed waits only skip work.
@@ -479,16 +511,6 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   float *k_hi = q_lo + bh * s_q * dp, *k_lo = k_hi + bh * s_kv * dp;
   float *v_hi = k_lo + bh * s_kv * dp, *v_lo = v_hi + bh * dv * sp;
   int status;
-  const RowSplit sq{q, s_q, d, d, s_q * d, bh, q_hi, q_lo};
-  if (k_layout == B2K_K_SD) {
-    // Q and K in one launch
-    const RowSplit sk{k, s_kv, d, d, s_kv * d, bh, k_hi, k_lo};
-    status = split_rows2(ctx, sq, &sk, dp, s);
-  } else if ((status = split_rows2(ctx, sq, nullptr, dp, s)) == B2K_OK) {
-    status = split_transpose(ctx, k, d, s_kv, s_kv, d * s_kv, bh, dp, k_hi, k_lo, s);
-  }
-  if (status != B2K_OK) return status;
-  if ((status = split_transpose(ctx, v, s_kv, dv, dv, s_kv * dv, bh, sp, v_hi, v_lo, s)) != B2K_OK) return status;
   // CTA pairs (mode 2) need at least two query tiles to pair up.  Measured on
   // B200 (64 heads x 2048 x 2048 x 128): 11.4 k cycles per key block on pairs
   // against 8.9 k on single CTAs -- the pair MMAs' S and PV phases take
@@ -496,9 +518,24 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   // the default.
   const int64_t tiles = (s_q + BM - 1) / BM;
   const bool pair = attention_mode() == 2 && tiles >= 2;
+  // A single CTA loads its Q tile once and can split it in shared memory:
+  // that needs raw Q TMA-readable with whole 32-column boxes (d % 32 == 0,
+  // 16-byte aligned) and saves the pre-pass writing and the kernel reading
+  // Q's hi/lo copies.  Otherwise Q is split by the pre-pass like K.
+  const bool q_raw = !pair && d % 32 == 0 && aligned16(q);
+  const RowSplit sq{q, s_q, d, d, s_q * d, bh, q_hi, q_lo};
+  const RowSplit sk{k, s_kv, d, d, s_kv * d, bh, k_hi, k_lo};
+  if (k_layout == B2K_K_SD) {
+    // Q (unless split in the kernel) and K in one launch
+    status = q_raw ? split_rows2(ctx, sk, nullptr, dp, s) : split_rows2(ctx, sq, &sk, dp, s);
+  } else if ((status = q_raw ? B2K_OK : split_rows2(ctx, sq, nullptr, dp, s)) == B2K_OK) {
+    status = split_transpose(ctx, k, d, s_kv, s_kv, d * s_kv, bh, dp, k_hi, k_lo, s);
+  }
+  if (status != B2K_OK) return status;
+  if ((status = split_transpose(ctx, v, s_kv, dv, dv, s_kv * dv, bh, sp, v_hi, v_lo, s)) != B2K_OK) return status;
   const int rows = pair ? FlashRing<true>::kRows : FlashRing<false>::kRows;
   CUtensorMap maps[6];
-  if ((status = make_map(ctx, &maps[0], q_hi, dp, s_q, bh, BM)) != B2K_OK) return status;
+  if ((status = make_map(ctx, &maps[0], q_raw ? q : q_hi, q_raw ? d : dp, s_q, bh, BM)) != B2K_OK) return status;
   if ((status = make_map(ctx, &maps[1], q_lo, dp, s_q, bh, BM)) != B2K_OK) return status;
   if ((status = make_map(ctx, &maps[2], k_hi, dp, s_kv, bh, rows)) != B2K_OK) return status;
   if ((status = make_map(ctx, &maps[3], k_lo, dp, s_kv, bh, rows)) != B2K_OK) return status;
@@ -508,8 +545,8 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   CUtensorMap map_o{};
   const int tma_o = aligned16(o) && dv % 4 == 0;
   if (tma_o && (status = make_map(ctx, &map_o, o, dv, s_q, bh, BM)) != B2K_OK) return status;
-  FlashArgs args{tma_o, o, s_q, s_kv, dv, (int)dp, (int)((dv + 15) / 16 * 16), 1.0f / scale_div, scale_div_ptr,
-                 ctx->error_flag};
+  FlashArgs args{tma_o, (int)q_raw, o, s_q, s_kv, dv, (int)dp, (int)((dv + 15) / 16 * 16), 1.0f / scale_div,
+                 scale_div_ptr, ctx->error_flag};
   auto kernel = pair ? flash_tf32x3_kernel<true> : flash_tf32x3_kernel<false>;
   cudaError_t err = set_max_smem(ctx, (const void *)kernel, kSmem);
   if (err != cudaSuccess) return cuda_fail(ctx, err, "flash: set smem");
