@@ -82,31 +82,70 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const RowSplitJob j0, c
 }
 
 // Row-major B [batch][K, N] (row stride ld, batch stride bs) -> transposed
-// hi/lo [batch][N][Kp] (K-major), zero padded.  blockIdx.z is the batch.
+// hi/lo [batch][N][Kp] (K-major), zero padded.  A block moves a 32 (k) x 128
+// (n) tile: rows of 128 n read as float4 (VEC: 16-byte aligned rows), then
+// per output row n its 32 k written as eight float4 of hi and of lo.  In
+// shared memory element (k, n) sits at k * 128 + (n ^ 4 * (k / 4)): the
+// float4 writes of a row and the column reads (lanes over k / 4 and four n)
+// are both free of bank conflicts.  blockIdx.z is the batch.
+constexpr int kTrK = 32, kTrN = 128;
+
+__device__ __forceinline__ int tr_col(int k, int n) { return n ^ ((k >> 2) << 2); }
+
+template <bool VEC>
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float *__restrict__ src, int64_t K, int64_t N,
                                                               int64_t ld, int64_t bs, int64_t Kp,
                                                               float *__restrict__ hi, float *__restrict__ lo) {
-  __shared__ float tile[32][33];
+  __shared__ __align__(16) float tile[kTrK * kTrN];
   grid_dependency_wait();
   grid_dependents_launch();
-  const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
+  const int64_t k0 = (int64_t)blockIdx.y * kTrK, n0 = (int64_t)blockIdx.x * kTrN;
   const float *base = src + (int64_t)blockIdx.z * bs;
   float *hb = hi + (int64_t)blockIdx.z * N * Kp, *lb = lo + (int64_t)blockIdx.z * N * Kp;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const int t = threadIdx.x;
+  {
+    // load: thread t covers n = 4 (t % 32) .. +3 of rows k = t / 32 + 8 i
+    const int nl = 4 * (t & 31);
+    const int64_t n = n0 + nl;
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-    const int64_t k = k0 + ty + i, n = n0 + tx;
-    tile[ty + i][tx] = (k < K && n < N) ? base[k * ld + n] : 0.0f;
+    for (int i = 0; i < kTrK; i += 8) {
+      const int kl = (t >> 5) + i;
+      const int64_t k = k0 + kl;
+      float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (k < K) {
+        const float *row = base + k * ld;
+        if (VEC && n + 3 < N) {
+          v = __ldg(reinterpret_cast<const float4 *>(row + n));
+        } else {
+          v.x = n < N ? __ldg(row + n) : 0.0f;
+          v.y = n + 1 < N ? __ldg(row + n + 1) : 0.0f;
+          v.z = n + 2 < N ? __ldg(row + n + 2) : 0.0f;
+          v.w = n + 3 < N ? __ldg(row + n + 3) : 0.0f;
+        }
+      }
+      *reinterpret_cast<float4 *>(&tile[kl * kTrN + tr_col(kl, nl)]) = v;
+    }
   }
   __syncthreads();
+  {
+    // store: thread t writes k = 4 (t % 8) .. +3 of output rows n = t / 8 + 32 i
+    const int kl = 4 * (t & 7);
+    const int64_t k = k0 + kl;
+    if (k < Kp) {  // Kp is a multiple of 32: the float4 never straddles it
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-    const int64_t n = n0 + ty + i, k = k0 + tx;
-    if (n < N && k < Kp) {
-      float h, l;
-      split_tf32(tile[tx][ty + i], h, l);
-      hb[n * Kp + k] = h;
-      lb[n * Kp + k] = l;
+      for (int i = 0; i < kTrN; i += 32) {
+        const int nl = (t >> 3) + i;
+        const int64_t n = n0 + nl;
+        if (n < N) {
+          const int c = tr_col(kl, nl);  // the same column for k .. k + 3
+          const float4 v = make_float4(tile[kl * kTrN + c], tile[(kl + 1) * kTrN + c], tile[(kl + 2) * kTrN + c],
+                                       tile[(kl + 3) * kTrN + c]);
+          float4 h, l;
+          split_tf32x4(v, h, l);
+          *reinterpret_cast<float4 *>(hb + n * Kp + k) = h;
+          *reinterpret_cast<float4 *>(lb + n * Kp + k) = l;
+        }
+      }
     }
   }
 }
@@ -832,9 +871,12 @@ int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t 
 int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_t ld, int64_t bs, int64_t batch,
                     int64_t kp, float *hi, float *lo, cudaStream_t s) {
   if (batch > 65535) return fail(ctx, B2K_EINVAL, "split_transpose: batch exceeds 65535");
-  dim3 grid((unsigned)((n + 31) / 32), (unsigned)((kp + 31) / 32), (unsigned)batch);
-  cudaError_t err = launch_kernel(pdl_enabled(), split_transpose_kernel, grid, dim3(256), 0, s, src, k, n, ld, bs, kp,
-                                  hi, lo);
+  dim3 grid((unsigned)((n + kTrN - 1) / kTrN), (unsigned)((kp + kTrK - 1) / kTrK), (unsigned)batch);
+  const bool vec = ld % 4 == 0 && (batch == 1 || bs % 4 == 0) && aligned16(src);
+  cudaError_t err = vec ? launch_kernel(pdl_enabled(), split_transpose_kernel<true>, grid, dim3(256), 0, s, src, k, n,
+                                        ld, bs, kp, hi, lo)
+                        : launch_kernel(pdl_enabled(), split_transpose_kernel<false>, grid, dim3(256), 0, s, src, k,
+                                        n, ld, bs, kp, hi, lo);
   if (err != cudaSuccess) return cuda_fail(ctx, err, "split_transpose launch");
   return check_launch(ctx, "split_transpose launch");
 }
