@@ -35,19 +35,22 @@ constexpr int KPAD = 32;  // K is zero-padded to a multiple of this in the split
 // (the split rule split_tf32 lives in common.cuh)
 
 // Row-major operand rows -> hi/lo rows [R][Kp] (R = batch * rows), zero
-// padded along K.  A block is 8 rows x 32 float4 columns; blockIdx.x picks
-// the 128-column slice, blockIdx.y (strided) the 8-row tile, over the tiles
-// of job 0 and then of job 1, so two operands split in one launch.
+// padded along K.  A block is 32 rows x 32 float4 columns: blockIdx.x picks
+// the 128-column slice, blockIdx.y (strided) the 32-row tile, over the tiles
+// of job 0 and then of job 1, so two operands split in one launch.  Each
+// thread loads its four rows (threadIdx.y + 8 u) before it splits and stores
+// any, so four 16-byte loads per thread are in flight.
 struct RowSplitJob {
   const float *src;
   float *hi, *lo;
   int64_t rows;        // rows per batch entry (all rows when the batch is contiguous)
   int64_t k, ld, bs;   // valid columns, row stride, batch stride (elements)
   int64_t total_rows;  // batch * rows
-  int64_t tiles;       // 8-row tiles
+  int64_t tiles;       // row tiles
   int vec;             // rows 16-byte aligned: float4 loads
 };
-constexpr int kSplitRows = 8;
+constexpr int kSplitRows = 32;  // rows per tile
+constexpr int kSplitRowsPerThread = kSplitRows / 8;
 
 __global__ void __launch_bounds__(256) split_rows_kernel(const RowSplitJob j0, const RowSplitJob j1, int64_t Kp) {
   grid_dependency_wait();
@@ -57,27 +60,40 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const RowSplitJob j0, c
   const int64_t tiles = j0.tiles + j1.tiles;
   for (int64_t t = blockIdx.y; t < tiles; t += gridDim.y) {
     const bool second = t >= j0.tiles;
-    const int64_t R = (second ? t - j0.tiles : t) * kSplitRows + threadIdx.y;
+    const int64_t R0 = (second ? t - j0.tiles : t) * kSplitRows + threadIdx.y;
     const int64_t total_rows = second ? j1.total_rows : j0.total_rows;
-    if (R >= total_rows) continue;
     const int64_t rows = second ? j1.rows : j0.rows, K = second ? j1.k : j0.k;
     const int64_t ld = second ? j1.ld : j0.ld, bs = second ? j1.bs : j0.bs;
     const float *src = second ? j1.src : j0.src;
-    const float *row = rows == total_rows ? src + R * ld : src + (R / rows) * bs + (R % rows) * ld;
-    float4 v;
-    if ((second ? j1.vec : j0.vec) && k + 3 < K) {
-      v = __ldg(reinterpret_cast<const float4 *>(row + k));
-    } else {
-      v.x = k < K ? __ldg(row + k) : 0.0f;
-      v.y = k + 1 < K ? __ldg(row + k + 1) : 0.0f;
-      v.z = k + 2 < K ? __ldg(row + k + 2) : 0.0f;
-      v.w = k + 3 < K ? __ldg(row + k + 3) : 0.0f;
+    const bool vec = (second ? j1.vec : j0.vec) && k + 3 < K;
+    float4 v[kSplitRowsPerThread];
+#pragma unroll
+    for (int u = 0; u < kSplitRowsPerThread; ++u) {
+      const int64_t R = R0 + 8 * u;
+      v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (R < total_rows) {
+        const float *row = rows == total_rows ? src + R * ld : src + (R / rows) * bs + (R % rows) * ld;
+        if (vec) {
+          v[u] = __ldg(reinterpret_cast<const float4 *>(row + k));
+        } else {
+          v[u].x = k < K ? __ldg(row + k) : 0.0f;
+          v[u].y = k + 1 < K ? __ldg(row + k + 1) : 0.0f;
+          v[u].z = k + 2 < K ? __ldg(row + k + 2) : 0.0f;
+          v[u].w = k + 3 < K ? __ldg(row + k + 3) : 0.0f;
+        }
+      }
     }
-    float4 h, l;
-    split_tf32x4(v, h, l);
-    const int64_t o = R * Kp + k;
-    *reinterpret_cast<float4 *>((second ? j1.hi : j0.hi) + o) = h;
-    *reinterpret_cast<float4 *>((second ? j1.lo : j0.lo) + o) = l;
+    float *hi = second ? j1.hi : j0.hi, *lo = second ? j1.lo : j0.lo;
+#pragma unroll
+    for (int u = 0; u < kSplitRowsPerThread; ++u) {
+      const int64_t R = R0 + 8 * u;
+      if (R < total_rows) {
+        float4 h, l;
+        split_tf32x4(v[u], h, l);
+        *reinterpret_cast<float4 *>(hi + R * Kp + k) = h;
+        *reinterpret_cast<float4 *>(lo + R * Kp + k) = l;
+      }
+    }
   }
 }
 
@@ -858,7 +874,7 @@ int split_rows2(b2k_ctx *ctx, const RowSplit &a, const RowSplit *b, int64_t kp, 
   const int64_t tiles = j[0].tiles + j[1].tiles;
   if (tiles == 0 || kp == 0) return B2K_OK;
   const dim3 grid((unsigned)((kp / 4 + 31) / 32), (unsigned)std::min<int64_t>(tiles, 65535));
-  cudaError_t err = launch_kernel(pdl_enabled(), split_rows_kernel, grid, dim3(32, kSplitRows), 0, s, j[0], j[1], kp);
+  cudaError_t err = launch_kernel(pdl_enabled(), split_rows_kernel, grid, dim3(32, kSplitRows / kSplitRowsPerThread), 0, s, j[0], j[1], kp);
   if (err != cudaSuccess) return cuda_fail(ctx, err, "split_rows launch");
   return check_launch(ctx, "split_rows launch");
 }
