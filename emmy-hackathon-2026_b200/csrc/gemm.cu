@@ -9,14 +9,19 @@
 // Pipeline (per CTA, one 128 x BN output tile):
 //   split pre-pass   A -> A_hi, A_lo ; B -> B_hi, B_lo (K-major, K padded to 32),
 //                    once per GEMM instead of once per element per K step
+//                    (A and a K-major B in one launch)
 //   warp 0           TMA producer: four swizzled tiles (A/B hi/lo) per stage
-//   warp 1           TMEM allocator + single-thread tcgen05.mma issuer:
-//                    per 8-wide K step, lo*hi, hi*lo and hi*hi into one
-//                    FP32 TMEM accumulator (128 lanes x BN columns) per
-//                    256-wide K chunk, double-buffered
+//   warp 1           TMEM allocator + MMA issuer (the whole warp runs the
+//                    loop, one elected lane issues): per 8-wide K step,
+//                    lo*hi, hi*lo and hi*hi into one FP32 TMEM accumulator
+//                    (128 lanes x BN columns) per 256-wide K chunk,
+//                    double-buffered
 //   warps 2..9       epilogue: fold each chunk into FP32 registers, then
-//                    bias -> ReLU -> global stores
-// All mbarrier waits are bounded (see sm100.cuh).
+//                    bias -> ReLU -> C staged in shared memory -> TMA stores
+//                    (row stores when C is not TMA-writable)
+// The tensor-core kernel is launched with programmatic dependent launch: its
+// set-up overlaps the split kernel's tail.  All mbarrier waits are bounded
+// (see sm100.cuh).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -29,7 +34,6 @@
 namespace {
 
 constexpr int BM = 128;
-constexpr int KPAD = 32;  // K is zero-padded to a multiple of this in the split operands
 
 // --- split pre-pass --------------------------------------------------------
 // (the split rule split_tf32 lives in common.cuh)

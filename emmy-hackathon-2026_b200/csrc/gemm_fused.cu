@@ -439,7 +439,8 @@ struct SmemSplitShape {
   static constexpr int kVecB = kTileB / 16;
   // MN-major B: boxes of 32 N x BK K (2 KB); each box is four 512-byte
   // swizzle atoms stacked along K.
-  static constexpr int kBoxB = B_MN ? 32 * BK * 4 : 0;
+  static constexpr int kBoxB = 32 * BK * 4;
+  static_assert(kBoxB % 512 == 0, "MN-major B boxes hold whole swizzle atoms");
   static_assert(BN == 128 || BN == 192, "BN");
   static_assert(kVecA % kGroupThreads == 0 && kVecB % kGroupThreads == 0, "split work split");
   static_assert(kChunkBlocks > kFoldLag, "fold lag");

@@ -95,7 +95,7 @@ class Pipe {
       if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&ctx_->copy_out, cudaStreamNonBlocking);
       if (err != cudaSuccess) return cuda_fail(ctx_, err, "pipeline: stream creation");
     }
-    cudaEvent_t entry;
+    cudaEvent_t entry = nullptr;
     int status = mark(s_, &entry);
     if (status == B2K_OK) status = wait(ctx_->copy_in, entry);
     if (status == B2K_OK) status = wait(ctx_->copy_out, entry);
@@ -112,19 +112,19 @@ class Pipe {
 
   // The compute stream waits for everything copied in so far.
   int landed() {
-    cudaEvent_t e;
+    cudaEvent_t e = nullptr;
     int status = mark(ctx_->copy_in, &e);
     return status == B2K_OK ? wait(s_, e) : status;
   }
   // The copy-out stream waits for everything computed so far.
   int computed() {
-    cudaEvent_t e;
+    cudaEvent_t e = nullptr;
     int status = mark(s_, &e);
     return status == B2K_OK ? wait(ctx_->copy_out, e) : status;
   }
   // The caller's stream waits for the last copy-out.
   int end() {
-    cudaEvent_t e;
+    cudaEvent_t e = nullptr;
     int status = mark(ctx_->copy_out, &e);
     return status == B2K_OK ? wait(s_, e) : status;
   }
@@ -142,7 +142,7 @@ class Pipe {
   // Events are reused across calls: a wait binds to the record made before it.
   int mark(cudaStream_t st, cudaEvent_t *out) {
     if (next_ == ctx_->sync_events.size()) {
-      cudaEvent_t e;
+      cudaEvent_t e = nullptr;
       cudaError_t err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
       if (err != cudaSuccess) return cuda_fail(ctx_, err, "pipeline: event creation");
       ctx_->sync_events.push_back(e);
