@@ -116,6 +116,20 @@ class Workload:
     def cpu_once(self, rows: int) -> tuple[float, str]:
         raise NotImplementedError
 
+    def cpu_extras(self) -> dict:
+        """One-core figure of the same float64 sample (BLAS held to one thread),
+        and, for the GEMMs, the reference's own 3xTF32 model timed on a small
+        shape and extrapolated by flop."""
+        extras = {}
+        try:
+            from threadpoolctl import threadpool_limits
+            with threadpool_limits(limits=1):
+                v, what = self.cpu_sample(max_seconds=2.0, rows=self.reference_rows)
+            extras["single_core"] = {"value": round(v, 5), "unit": self.unit, "sample": what}
+        except ImportError:
+            pass
+        return extras
+
     def cpu_sample(self, max_seconds: float = 12.0, rows: int | None = None) -> tuple[float, str]:
         """Repeat the oracle's float64 evaluation of a bounded sample for about
         `max_seconds`; returns (throughput in the metric's unit, description)."""
@@ -187,6 +201,24 @@ class Gemm(Workload):
     def e2e_step(self):
         self.session.gemm_host(self.pa, self.pb, self.pc, b_layout="nk" if self.ragged else "kn",
                                bias=self.pbias, relu=self.ragged)
+
+    def cpu_extras(self):
+        extras = super().cpu_extras()
+        # tf32_emitter.py:64-96's model (per-8-K atom, three FP32 accumulators),
+        # restated in oracle/tf32.py, on a 256^3 slab: its cost is linear in flop.
+        tf32 = importlib.import_module("oracle.tf32")
+        rng = np.random.default_rng(5)
+        a = rng.uniform(-1, 1, (256, 256)).astype(np.float32)
+        b = rng.uniform(-1, 1, (256, 256)).astype(np.float32)
+        reps, t0 = 0, time.perf_counter()
+        while reps < 3 or time.perf_counter() - t0 < 1.0:
+            tf32.simulate_matmul(a, b)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        extras["tf32_model"] = {"value": round(2.0 * 256 ** 3 / dt / scale(self.unit), 6), "unit": self.unit,
+                                "sample": f"{reps} x oracle/tf32.simulate_matmul 256x256x256 (the reference's "
+                                          "3xTF32 model, tf32_emitter.py:64-96), extrapolated by flop"}
+        return extras
 
     def cpu_once(self, rows):
         # The oracle's float64 equations (refs.matmul / refs.matmul_bias_relu)
@@ -560,6 +592,7 @@ def run_ours(args) -> dict | None:
             v, sample = w.cpu_sample()
             cpu = {"value": round(v, 4), "unit": w.unit, "cores": os.cpu_count(), "kind": "port",
                    "sample": sample + " (oracle/refs.py float64 equations, NumPy/BLAS threads = all cores)"}
+            cpu.update(w.cpu_extras())
         result = {
             "metric": METRIC, "value": round(value, 3), "unit": w.unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
@@ -616,7 +649,7 @@ def run_reference(args) -> dict | None:
             "config": w.config(),
             "cpu_baseline": {"value": round(value, 4), "unit": w.unit, "cores": os.cpu_count(), "kind": "port",
                              "sample": samples + " per step (oracle/refs.py float64 equations of "
-                                                 "tools/research_cases.py:74-103)"},
+                                                 "tools/research_cases.py:74-103)", **w.cpu_extras()},
             "e2e": {"value": round(value, 4), "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
