@@ -290,9 +290,22 @@ class Softmax(Workload):
     default_rows = 512
     reference_rows = 64
 
+    def subnormal_exp_args(self) -> int:
+        """How many exp arguments x - rowmax of this input give a subnormal
+        FP32 result (arguments in [-103.28, -87.34]): the range the selective
+        exponential exists for."""
+        if getattr(self, "_subnormal", None) is None:
+            x = getattr(self, "host", None)
+            if x is None:
+                x = pkg("workloads").softmax_input(self.rows, self.cols)
+            t = x - x.max(axis=1, keepdims=True)
+            self._subnormal = int(np.count_nonzero((t >= -103.28) & (t < -87.34)))
+        return self._subnormal
+
     def config(self):
         return {"workload": "row_softmax", "rows": self.rows * self.world, "rows_per_gpu": self.rows,
                 "cols": self.cols, "inputs": "N(0,16), 1% set to -100, seeded",
+                "exp_args_in_subnormal_range": self.subnormal_exp_args(),
                 "l2": "inputs larger than L2", "parallelism": f"dp{self.world} (rows per GPU)"}
 
 
