@@ -375,40 +375,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t row = m0 + quarter * 32 + lane;
     const int64_t col0 = n0 + half * CPT;
     if constexpr (TMA_C) {
-      // The ring is idle once the last chunk is folded: stage C there and
-      // write it with one TMA store per box.
-      if (ok) {
-        const float divisor = args.div_ptr ? __ldg(args.div_ptr) : args.div_value;
-        const bool divide = args.div_ptr != nullptr || args.div_value != 1.0f;
-        const int r = quarter * 32 + lane;
-        const bool has_bias = args.bias != nullptr;
-        // Plain shared-memory stores (no asm memory clobber), so the compiler
-        // may overlap the iterations' arithmetic and stores freely.
+      // The ring is idle once the last chunk is folded: stage C there, one
+      // 128 x 32 box at a time per column half, and let the half's first
+      // thread store each box as soon as its four warps have written it, so
+      // the stores overlap the staging of the next box.
+      const float divisor = args.div_ptr ? __ldg(args.div_ptr) : args.div_value;
+      const bool divide = args.div_ptr != nullptr || args.div_value != 1.0f;
+      const int r = quarter * 32 + lane;
+      const bool has_bias = args.bias != nullptr;
+      const bool leader = threadIdx.x == (unsigned)(64 + 128 * half);
 #pragma unroll
-        for (int j = 0; j < CPT; j += 4) {
-          float v[4];
+      for (int b = 0; b < CPT / 32; ++b) {
+        if (ok) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float x = acc[j + q];
-            if (divide) x = __fdiv_rn(x, divisor);
-            if (has_bias) x = __fadd_rn(x, bias_tile[half * CPT + j + q]);
-            if (args.relu) x = x > 0.0f ? x : 0.0f;
-            v[q] = x;
+          for (int j = 32 * b; j < 32 * b + 32; j += 4) {
+            float v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float x = acc[j + q];
+              if (divide) x = __fdiv_rn(x, divisor);
+              if (has_bias) x = __fadd_rn(x, bias_tile[half * CPT + j + q]);
+              if (args.relu) x = x > 0.0f ? x : 0.0f;
+              v[q] = x;
+            }
+            const int col = half * CPT + j;
+            const int chunk = ((col & 31) >> 2) ^ (r & 7);
+            *reinterpret_cast<float4 *>(smem + (col >> 5) * kCBox + r * 128 + chunk * 16) =
+                make_float4(v[0], v[1], v[2], v[3]);
           }
-          const int col = half * CPT + j;
-          const int chunk = ((col & 31) >> 2) ^ (r & 7);
-          *reinterpret_cast<float4 *>(smem + (col >> 5) * kCBox + r * 128 + chunk * 16) =
-              make_float4(v[0], v[1], v[2], v[3]);
+        }
+        sm100::fence_proxy_async_smem();
+        sm100::named_barrier(3 + half * 4 + b, 128);  // this half's four warps
+        if (leader && ok) {
+          const int box = half * (CPT / 32) + b;
+          sm100::tma_store_3d(&map_c, smem + box * kCBox, (int)n0 + 32 * box, (int)m0, (int)blockIdx.z);
         }
       }
-      sm100::fence_proxy_async_smem();
-      sm100::named_barrier(1, 32 * kEpilogueWarps);
-      if (threadIdx.x == 64 && ok) {
-#pragma unroll 1
-        for (int b = 0; b < BN / 32; ++b)
-          sm100::tma_store_3d(&map_c, smem + b * kCBox, (int)n0 + 32 * b, (int)m0, (int)blockIdx.z);
-        sm100::tma_store_flush();
-      }
+      if (leader && ok) sm100::tma_store_flush();
     } else if (ok && row < args.m && col0 < args.n) {
       float *crow = args.c + (int64_t)blockIdx.z * args.batch_stride_c + row * args.ldc + col0;
       const float divisor = args.div_ptr ? __ldg(args.div_ptr) : args.div_value;
