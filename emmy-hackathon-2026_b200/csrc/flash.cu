@@ -428,23 +428,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (args.tma_o) {
       // Q's buffer is idle after the last block: stage the normalised O tile
       // there as 128-byte-swizzled boxes of 128 rows x 32 columns and write it
-      // with TMA stores (coalesced, rows past s_q clipped).
-      if (ok) {
+      // with TMA stores (coalesced, rows past s_q clipped).  Each warpgroup
+      // stages its two boxes one at a time; its first thread stores a box as
+      // soon as the group's four warps have written it.
+      const bool leader = threadIdx.x == (unsigned)(64 + 128 * wg);
 #pragma unroll
-        for (int i = 0; i < OC; i += 4) {
-          const int col = oc0 + i;
-          const uint32_t chunk = (uint32_t)((col & 31) >> 2) ^ (uint32_t)(r & 7);
-          sm100::sts128_relaxed(sm100::smem_addr(q_hi + (col >> 5) * kSub + r * 128 + chunk * 16),
-                        make_float4(__fmul_rn(o_acc[i], inv_l), __fmul_rn(o_acc[i + 1], inv_l),
-                                    __fmul_rn(o_acc[i + 2], inv_l), __fmul_rn(o_acc[i + 3], inv_l)));
+      for (int b = 0; b < OC / 32; ++b) {
+        const int box = oc0 / 32 + b;
+        if (ok) {
+#pragma unroll
+          for (int i = 32 * b; i < 32 * b + 32; i += 4) {
+            const int col = oc0 + i;
+            const uint32_t chunk = (uint32_t)((col & 31) >> 2) ^ (uint32_t)(r & 7);
+            sm100::sts128_relaxed(sm100::smem_addr(q_hi + (col >> 5) * kSub + r * 128 + chunk * 16),
+                                  make_float4(__fmul_rn(o_acc[i], inv_l), __fmul_rn(o_acc[i + 1], inv_l),
+                                              __fmul_rn(o_acc[i + 2], inv_l), __fmul_rn(o_acc[i + 3], inv_l)));
+          }
         }
+        sm100::fence_proxy_async_smem();
+        sm100::named_barrier(4 + 2 * wg + b, 128);  // this warpgroup's four warps
+        if (leader && ok && box * 32 < args.dv)
+          sm100::tma_store_3d(&map_o, q_hi + box * kSub, 32 * box, (int)m0, head);
       }
-      sm100::fence_proxy_async_smem();
-      sm100::named_barrier(3, 256);
-      if (threadIdx.x == 64 && ok) {
-        for (int b = 0; b * 32 < args.dv; ++b) sm100::tma_store_3d(&map_o, q_hi + b * kSub, 32 * b, (int)m0, head);
-        sm100::tma_store_flush();
-      }
+      if (leader && ok) sm100::tma_store_flush();
     } else if (ok && row < args.s_q && oc0 < args.dv) {
       float *orow = args.o + ((int64_t)head * args.s_q + row) * args.dv;
       const bool vec = (args.dv % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.o) & 15) == 0);
