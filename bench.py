@@ -492,6 +492,43 @@ def init_dist():
     return rank, local, world
 
 
+def strong_scaling_gemm(ctx, torch, dist, rank, world, barrier, max_over_ranks, steps=10, warmup=3) -> dict:
+    """One 4096^3 GEMM split by rows of A over the ranks (mgpu.sharded_gemm):
+    NCCL broadcasts B from rank 0, each rank multiplies its row slab with the
+    C-ABI GEMM, NCCL all-gathers C.  Device-timed with CUDA events around the
+    whole call, max over ranks."""
+    mgpu, workloads = pkg("mgpu"), pkg("workloads")
+    m = n = k = 4096
+    a, b = workloads.gemm_inputs(m, n, k)
+    shard = mgpu.partition(m, world, rank, align=128)
+    a_rows = torch.from_numpy(a[shard.start:shard.start + shard.count]).cuda()
+    b_dev = torch.from_numpy(b).cuda() if rank == 0 else torch.empty((k, n), device="cuda")
+
+    def compute(a_part, b_full):
+        c_part = torch.empty((a_part.shape[0], n), device="cuda")
+        ctx.gemm(a_part.data_ptr(), b_full.data_ptr(), c_part.data_ptr(), a_part.shape[0], n, k)
+        return c_part
+
+    for _ in range(warmup):
+        mgpu.sharded_gemm(a_rows, b_dev, m, rank, world, compute, torch, device="cuda")
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        c = mgpu.sharded_gemm(a_rows, b_dev, m, rank, world, compute, torch, device="cuda")
+    e1.record()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+    # size-independent check of the gathered C: its column sums equal (1^T A) B
+    col = c.double().sum(dim=0).cpu().numpy()
+    want = a.astype(np.float64).sum(axis=0) @ b.astype(np.float64)
+    rel = float(np.max(np.abs(col - want)) / np.max(np.abs(want)))
+    return {"value": round(2.0 * m * n * k / (ms / 1e3) / 1e12, 3), "unit": "TFLOP/s", "ms_per_gemm": round(ms, 4),
+            "n_gpus": world, "steps": steps, "problem": "one 4096x4096x4096 GEMM (strong scaling)",
+            "collectives": "NCCL broadcast of B (64 MiB) from rank 0, all_gather of C row slabs (64 MiB)",
+            "column_sum_rel_err": rel}
+
+
 def run_ours(args) -> dict | None:
     import torch
     rank, local, world = init_dist()
@@ -577,6 +614,10 @@ def run_ours(args) -> dict | None:
     session.sync()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    # --- strong scaling of one 4096^3 GEMM over NCCL (multi-GPU GEMM runs) ---------
+    strong = None
+    if world > 1 and isinstance(w, Gemm) and not w.ragged:
+        strong = strong_scaling_gemm(ctx, torch, dist, rank, world, barrier, max_over_ranks)
     # --- report ------------------------------------------------------------------
     result = None
     if rank == 0:
@@ -621,6 +662,7 @@ def run_ours(args) -> dict | None:
                          "peak_basis": peak_note},
             "cpu_baseline": cpu,
             "clocks": clocks,
+            **({"strong_scaling_nccl": strong} if strong else {}),
             "gpu_launches": launches,
         }
     session.close()
