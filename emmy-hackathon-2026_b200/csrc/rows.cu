@@ -134,20 +134,66 @@ __global__ void __launch_bounds__(kThreads) sum_finish(const RowArgs a, const fl
   if (threadIdx.x == 0) y[0] = row_scale(a, acc);
 }
 
+// Row folds with a non-additive operator (max, min, product), one CTA per
+// row: thread-strided fold, shfl.xor butterfly, then the warps' partials in
+// warp order -- a fixed order, so repeated runs are bit-identical.
+template <int OP>
+__device__ __forceinline__ float fold_op(float a, float b) {
+  if constexpr (OP == B2K_ROW_MAX) return fmaxf(a, b);
+  else if constexpr (OP == B2K_ROW_MIN) return fminf(a, b);
+  else return __fmul_rn(a, b);
+}
+
+template <int OP>
+__device__ __forceinline__ float fold_identity() {
+  if constexpr (OP == B2K_ROW_MAX) return -INFINITY;
+  else if constexpr (OP == B2K_ROW_MIN) return INFINITY;
+  else return 1.0f;
+}
+
+template <int OP>
+__global__ void __launch_bounds__(kThreads) rows_fold(const float *__restrict__ x, float *__restrict__ y,
+                                                      int64_t cols, int64_t ldx) {
+  __shared__ float red[kWarps];
+  const float *xr = x + (int64_t)blockIdx.x * ldx;
+  float acc = fold_identity<OP>();
+  for (int64_t c = threadIdx.x; c < cols; c += kThreads) acc = fold_op<OP>(acc, __ldg(xr + c));
+#pragma unroll
+  for (int offset = 16; offset > 0; offset >>= 1) acc = fold_op<OP>(acc, __shfl_xor_sync(0xffffffffu, acc, offset));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = red[0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) r = fold_op<OP>(r, red[w]);
+    y[blockIdx.x] = r;
+  }
+}
+
 }  // namespace
 
 extern "C" int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const float *x, float *y, int64_t rows,
                               int64_t cols, int64_t ld_x, int64_t ld_y, void *stream) {
   B2K_CHECK_CTX(ctx);
   if (!params) return b2k::fail(ctx, B2K_EINVAL, "row_op: null params");
-  if (params->op != B2K_ROW_SUM && params->op != B2K_ROW_RMSNORM && params->op != B2K_ROW_L2NORM)
+  if (params->op < B2K_ROW_SUM || params->op > B2K_ROW_PROD)
     return b2k::fail(ctx, B2K_EINVAL, "row_op: unknown op %d", params->op);
+  const bool reduction = params->op == B2K_ROW_SUM || params->op >= B2K_ROW_MAX;  // one value per row
   if (rows < 0 || cols < 0) return b2k::fail(ctx, B2K_EINVAL, "row_op: negative extent");
   if (rows == 0) return B2K_OK;
   if (!x || !y) return b2k::fail(ctx, B2K_EINVAL, "row_op: null buffer");
-  if (ld_x < cols || (params->op != B2K_ROW_SUM && ld_y < cols))
+  if (ld_x < cols || (!reduction && ld_y < cols))
     return b2k::fail(ctx, B2K_EINVAL, "row_op: leading dimension < cols");
   if (rows > INT32_MAX) return b2k::fail(ctx, B2K_EINVAL, "row_op: too many rows");
+  if (params->op >= B2K_ROW_MAX) {
+    cudaStream_t s = (cudaStream_t)stream;
+    b2k::PhaseTimer timer(ctx, B2K_PHASE_ROWS, s);
+    const int grid = (int)rows;
+    if (params->op == B2K_ROW_MAX) rows_fold<B2K_ROW_MAX><<<grid, kThreads, 0, s>>>(x, y, cols, ld_x);
+    else if (params->op == B2K_ROW_MIN) rows_fold<B2K_ROW_MIN><<<grid, kThreads, 0, s>>>(x, y, cols, ld_x);
+    else rows_fold<B2K_ROW_PROD><<<grid, kThreads, 0, s>>>(x, y, cols, ld_x);
+    return b2k::check_launch(ctx, "row_op fold launch");
+  }
   const RowArgs a{params->op,  params->sum_div, params->sum_div_ptr, params->ms_div,
                   params->ms_div_ptr, params->eps, params->eps_ptr,     params->w};
   cudaStream_t s = (cudaStream_t)stream;

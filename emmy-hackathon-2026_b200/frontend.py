@@ -87,8 +87,9 @@ class KernelSpec:
             roles = {0: pos[p["x"]], 1: pos[p["out"]]}
             if p["sum_div_buffer"]:
                 roles[3] = pos[p["sum_div_buffer"]]
+            op = {"sum": rt.ROW_SUM, "max": rt.ROW_MAX, "min": rt.ROW_MIN, "prod": rt.ROW_PROD}[p["op"]]
             return rt.make_desc(rt.KIND_ROW_OP, roles, dims=(p["rows"], p["cols"], p["cols"], p["cols"]),
-                                flags=(rt.ROW_SUM,), values=(p["sum_div"], 1.0, 0.0))
+                                flags=(op,), values=(p["sum_div"], 1.0, 0.0))
         if self.kind == "row_norm":
             rms = p["op"] == "rmsnorm"
             roles = {0: pos[p["x"]], 1: pos[p["out"]]}
@@ -471,8 +472,25 @@ def classify_row_reduce(node, kernel, args, inputs, outputs):
         rows, cols = 1, xs[0]
     else:
         raise Unsupported("row_reduce: output is not one value per row")
-    if not any(s.kind == "Accum" and s.op.name == "add" for s in walk(node.body)):
-        raise Unsupported("row_reduce: no additive fold")
+    # The fold's operator: the ops of the Accum statements and of the
+    # combine steps of warp shuffles / halving trees.  Only additive folds
+    # carry a divisor (sum, mean); max / min / product must match exactly.
+    fold_ops = set()
+    for s in walk(node.body):
+        if s.kind == "Accum":
+            fold_ops.add(s.op.name)
+        elif s.kind in ("WarpShuffle", "TreeHalve"):
+            fold_ops.update(c.op.name for c in s.get("combine_states") or () if c.kind == "Assign")
+    fold_ops.discard("copy")
+    if fold_ops in ({"maximum"}, {"minimum"}, {"multiply"}):
+        op = {"maximum": "max", "minimum": "min", "multiply": "prod"}[fold_ops.pop()]
+        fold = {"max": np.max, "min": np.min, "prod": np.prod}[op]
+        cert = certify(node, kernel, args, inputs, outputs,
+                       lambda buf: {out: fold(buf[x].reshape(rows, cols), axis=1)})
+        return {"op": op, "x": x, "out": out, "rows": rows, "cols": cols, "sum_div": 1.0,
+                "sum_div_buffer": None}, cert
+    if "add" not in fold_ops:
+        raise Unsupported("row_reduce: no additive, max, min or product fold")
     fitted = {}
 
     def expect(buf, produced):

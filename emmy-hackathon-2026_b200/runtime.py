@@ -42,7 +42,7 @@ class RowParams(C.Structure):
                 ("ms_div_ptr", C.c_void_p), ("eps", C.c_float), ("eps_ptr", C.c_void_p), ("w", C.c_void_p)]
 
 
-ROW_SUM, ROW_RMSNORM, ROW_L2NORM = 0, 1, 2
+ROW_SUM, ROW_RMSNORM, ROW_L2NORM, ROW_MAX, ROW_MIN, ROW_PROD = 0, 1, 2, 3, 4, 5
 
 
 KIND_POINTWISE, KIND_ROW_SOFTMAX, KIND_ROW_OP, KIND_GEMM, KIND_ATTENTION = 1, 2, 3, 4, 5

@@ -184,12 +184,18 @@ int b2k_row_softmax_f32(b2k_ctx *ctx, const float *x, float *y, int64_t rows, in
  *   B2K_ROW_SUM      y[r]    = (sum_c x[r,c]) / div                 (div = *sum_div_ptr or sum_div)
  *   B2K_ROW_RMSNORM  y[r,c]  = x[r,c] * w[c] / sqrt(sum_c x^2 / count + eps)
  *   B2K_ROW_L2NORM   y[r,c]  = x[r,c] * w[c] / sqrt(sum_c x^2 + eps)
+ *   B2K_ROW_MAX      y[r]    = max_c x[r,c]    (IEEE maxNum: a NaN loses to a number)
+ *   B2K_ROW_MIN      y[r]    = min_c x[r,c]    (IEEE minNum)
+ *   B2K_ROW_PROD     y[r]    = prod_c x[r,c]   (FP32 products in a fixed tree order)
  * count = *ms_div_ptr or ms_div, eps = *eps_ptr or eps; w may be NULL (1).
  * A single row longer than 65,536 (a whole-array sum) is reduced by many CTAs
  * and a fixed-order second pass. */
 #define B2K_ROW_SUM 0
 #define B2K_ROW_RMSNORM 1
 #define B2K_ROW_L2NORM 2
+#define B2K_ROW_MAX 3
+#define B2K_ROW_MIN 4
+#define B2K_ROW_PROD 5
 typedef struct b2k_row_params {
   int32_t op;
   float sum_div;

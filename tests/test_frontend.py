@@ -18,6 +18,10 @@ RECOGNISED = {
     "atomic_matmul-0-b0bb43becf74": ["matmul"],
     "atomic_matmul_7x5x9-variant": ["matmul"],
     "attention-0-9170e7b0641d": [None, "row_softmax", "matmul"],
+    "case-08-e4ac354528a2": ["row_reduce"],
+    "case-14-fff293a2235c": ["row_reduce"],
+    "case-22-da018f96fc2e": ["row_reduce"],
+    "case-30-061d7084b729": ["row_reduce"],
     "f01_rmsnorm-6ab09ab4acc3": ["row_norm"],
     "f02-extra-cta-120bf007fb2d": ["row_softmax"],
     "f03_l2norm-1e82d7e58a53": ["row_norm"],

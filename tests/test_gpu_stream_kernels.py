@@ -158,3 +158,31 @@ def test_row_sums_and_means(ctx, torch_cuda):
     ctx.sync()
     ok, bad, err = refs.allclose_report(y.cpu().numpy(), (refs.row_sum(x) / 512).astype(np.float32), 1e-4, 1e-6)
     assert ok, (bad, err)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 127), (3, 4), (64, 1000), (5, 70000)])
+def test_row_max_min_prod(ctx, torch_cuda, rows, cols):
+    """Non-additive row folds: max and min exact, product within FP32
+    rounding of a fixed-order tree (inputs near 1 keep it finite)."""
+    runtime = pkg("runtime")
+    rng = np.random.default_rng(rows * 7 + cols)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    x[:, ::7] = -np.inf if cols > 8 else x[:, ::7]  # max must skip -inf entries
+    near_one = (1.0 + rng.uniform(-1e-3, 1e-3, (rows, cols))).astype(np.float32)
+    dx, dn = dev(torch_cuda, x), dev(torch_cuda, near_one)
+    y = torch_cuda.empty(rows, device="cuda")
+    ctx.row_op(runtime.ROW_MAX, dx.data_ptr(), y.data_ptr(), rows, cols)
+    ctx.sync()
+    assert np.array_equal(y.cpu().numpy(), x.max(axis=1))
+    ctx.row_op(runtime.ROW_MIN, dx.data_ptr(), y.data_ptr(), rows, cols)
+    ctx.sync()
+    assert np.array_equal(y.cpu().numpy(), x.min(axis=1))
+    ctx.row_op(runtime.ROW_PROD, dn.data_ptr(), y.data_ptr(), rows, cols)
+    ctx.sync()
+    want = near_one.astype(np.float64).prod(axis=1)
+    np.testing.assert_allclose(y.cpu().numpy(), want, rtol=cols * 2.0 ** -23, atol=0)
+    # the same launch twice gives the same bits (fixed combine order)
+    first = y.clone()
+    ctx.row_op(runtime.ROW_PROD, dn.data_ptr(), y.data_ptr(), rows, cols)
+    ctx.sync()
+    assert torch_cuda.equal(first, y)
