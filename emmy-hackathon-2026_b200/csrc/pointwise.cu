@@ -68,6 +68,8 @@ __device__ __forceinline__ float run_program(const b2k_pw_program &p, const floa
 }
 
 __global__ void __launch_bounds__(kThreads) pw_program_vec4(const __grid_constant__ PwParams p) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   const int64_t n4 = p.n >> 2;
   const int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x;
   float scalars[B2K_PW_MAX_INPUTS];
@@ -97,6 +99,8 @@ __global__ void __launch_bounds__(kThreads) pw_program_vec4(const __grid_constan
 // Scalar path: unaligned streams and the (n mod 4) tail of the vector path.
 __global__ void __launch_bounds__(kThreads) pw_program_scalar(const __grid_constant__ PwParams p,
                                                               int64_t start) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   const int64_t i = start + (int64_t)blockIdx.x * kThreads + threadIdx.x;
   if (i >= p.n) return;
   float values[B2K_PW_MAX_INPUTS];
@@ -110,6 +114,8 @@ template <int OP, bool BA, bool BB>
 __global__ void __launch_bounds__(kThreads) pw_binary_vec4(const float *__restrict__ a,
                                                            const float *__restrict__ b,
                                                            float *__restrict__ out, int64_t n4) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   const int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x;
   const float sa = BA ? __ldg(a) : 0.0f, sb = BB ? __ldg(b) : 0.0f;
   float4 va[kUnroll], vb[kUnroll];
@@ -138,10 +144,13 @@ __global__ void __launch_bounds__(kThreads) pw_binary_vec4(const float *__restri
 template <int OP>
 void launch_binary(bool ba, bool bb, const float *a, const float *b, float *out, int64_t n4, int blocks,
                    cudaStream_t s) {
-  if (ba && bb) pw_binary_vec4<OP, true, true><<<blocks, kThreads, 0, s>>>(a, b, out, n4);
-  else if (ba) pw_binary_vec4<OP, true, false><<<blocks, kThreads, 0, s>>>(a, b, out, n4);
-  else if (bb) pw_binary_vec4<OP, false, true><<<blocks, kThreads, 0, s>>>(a, b, out, n4);
-  else pw_binary_vec4<OP, false, false><<<blocks, kThreads, 0, s>>>(a, b, out, n4);
+  // programmatic dependent launch: back-to-back launches hide each other's
+  // launch latency and tail (each kernel waits for its predecessor first)
+  const bool pdl = b2k::pdl_enabled();
+  if (ba && bb) b2k::launch_kernel(pdl, pw_binary_vec4<OP, true, true>, dim3(blocks), dim3(kThreads), 0, s, a, b, out, n4);
+  else if (ba) b2k::launch_kernel(pdl, pw_binary_vec4<OP, true, false>, dim3(blocks), dim3(kThreads), 0, s, a, b, out, n4);
+  else if (bb) b2k::launch_kernel(pdl, pw_binary_vec4<OP, false, true>, dim3(blocks), dim3(kThreads), 0, s, a, b, out, n4);
+  else b2k::launch_kernel(pdl, pw_binary_vec4<OP, false, false>, dim3(blocks), dim3(kThreads), 0, s, a, b, out, n4);
 }
 
 bool launch_binary_fast(const b2k_pw_program &p, const float *const *in, float *out, int64_t n4, int blocks,
@@ -215,7 +224,7 @@ extern "C" int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, co
     const int64_t blocks = (n4 + per_block - 1) / per_block;
     if (blocks > INT32_MAX) return b2k::fail(ctx, B2K_EINVAL, "pointwise: extent too large");
     if (!launch_binary_fast(*program, inputs, out, n4, (int)blocks, s))
-      pw_program_vec4<<<(int)blocks, kThreads, 0, s>>>(params);
+      b2k::launch_kernel(b2k::pdl_enabled(), pw_program_vec4, dim3((unsigned)blocks), dim3(kThreads), 0, s, params);
     done = n4 << 2;
     ++launches;
   }
@@ -223,7 +232,8 @@ extern "C" int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, co
     const int64_t rest = n - done;
     const int64_t blocks = (rest + kThreads - 1) / kThreads;
     if (blocks > INT32_MAX) return b2k::fail(ctx, B2K_EINVAL, "pointwise: extent too large");
-    pw_program_scalar<<<(int)blocks, kThreads, 0, s>>>(params, done);
+    b2k::launch_kernel(b2k::pdl_enabled(), pw_program_scalar, dim3((unsigned)blocks), dim3(kThreads), 0, s, params,
+                       done);
     ++launches;
   }
   return b2k::check_launch(ctx, "pointwise launch", launches);

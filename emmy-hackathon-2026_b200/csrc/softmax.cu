@@ -83,6 +83,8 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_vec(const float *__rest
                                                              int64_t cols4, int64_t ldx) {
   __shared__ float red_max[kWarps];
   __shared__ float red_sum[kWarps];
+  grid_dependency_wait();
+  grid_dependents_launch();
   const int64_t row = blockIdx.x;
   const float4 *xr = reinterpret_cast<const float4 *>(x + row * ldx);
   float4 v[VPT];
@@ -131,6 +133,8 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_vec(const float *__rest
 template <class Sink>
 __global__ void __launch_bounds__(kThreads) softmax_rows_generic(const float *__restrict__ x, const Sink sink,
                                                                  int64_t cols, int64_t ldx) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   __shared__ float red_max[kWarps];
   __shared__ float red_sum[kWarps];
   const int64_t row = blockIdx.x;
@@ -151,12 +155,16 @@ void launch_rows(const float *x, const Sink &sink, int64_t rows, int64_t cols, i
                  cudaStream_t s) {
   const int64_t cols4 = cols / 4;
   const int grid = (int)rows;
-  if (vec && cols4 <= kThreads * 1) softmax_rows_vec<1><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
-  else if (vec && cols4 <= kThreads * 2) softmax_rows_vec<2><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
-  else if (vec && cols4 <= kThreads * 4) softmax_rows_vec<4><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
-  else if (vec && cols4 <= kThreads * 8) softmax_rows_vec<8><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
-  else if (vec && cols4 <= kThreads * 16) softmax_rows_vec<16><<<grid, kThreads, 0, s>>>(x, sink, cols4, ld_x);
-  else softmax_rows_generic<<<grid, kThreads, 0, s>>>(x, sink, cols, ld_x);
+  // programmatic dependent launch: back-to-back launches hide each other's
+  // launch latency and tail (each kernel waits for its predecessor first)
+  const bool pdl = b2k::pdl_enabled();
+  const dim3 g((unsigned)grid), b(kThreads);
+  if (vec && cols4 <= kThreads * 1) b2k::launch_kernel(pdl, softmax_rows_vec<1, Sink>, g, b, 0, s, x, sink, cols4, ld_x);
+  else if (vec && cols4 <= kThreads * 2) b2k::launch_kernel(pdl, softmax_rows_vec<2, Sink>, g, b, 0, s, x, sink, cols4, ld_x);
+  else if (vec && cols4 <= kThreads * 4) b2k::launch_kernel(pdl, softmax_rows_vec<4, Sink>, g, b, 0, s, x, sink, cols4, ld_x);
+  else if (vec && cols4 <= kThreads * 8) b2k::launch_kernel(pdl, softmax_rows_vec<8, Sink>, g, b, 0, s, x, sink, cols4, ld_x);
+  else if (vec && cols4 <= kThreads * 16) b2k::launch_kernel(pdl, softmax_rows_vec<16, Sink>, g, b, 0, s, x, sink, cols4, ld_x);
+  else b2k::launch_kernel(pdl, softmax_rows_generic<Sink>, g, b, 0, s, x, sink, cols, ld_x);
 }
 
 __global__ void selective_exp_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t n) {
