@@ -50,6 +50,8 @@ __device__ __forceinline__ float row_scale(const RowArgs &a, float acc) {
 template <int VPT>
 __global__ void __launch_bounds__(kThreads) rows_vec(const RowArgs a, const float *__restrict__ x, float *__restrict__ y,
                                                      int64_t cols4, int64_t ldx, int64_t ldy) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   __shared__ float red[kWarps];
   const int64_t row = blockIdx.x;
   const float4 *xr = reinterpret_cast<const float4 *>(x + row * ldx);
@@ -90,6 +92,8 @@ __global__ void __launch_bounds__(kThreads) rows_vec(const RowArgs a, const floa
 __global__ void __launch_bounds__(kThreads) rows_generic(const RowArgs a, const float *__restrict__ x,
                                                          float *__restrict__ y, int64_t cols, int64_t ldx,
                                                          int64_t ldy) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   __shared__ float red[kWarps];
   const int64_t row = blockIdx.x;
   const float *xr = x + row * ldx;
@@ -116,6 +120,8 @@ __global__ void __launch_bounds__(kThreads) rows_generic(const RowArgs a, const 
 // fixed order and writes one partial.
 __global__ void __launch_bounds__(kThreads) sum_partials(const float *__restrict__ x, int64_t n,
                                                          float *__restrict__ partials) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   __shared__ float red[kWarps];
   float acc = 0.0f;
   const int64_t stride = (int64_t)gridDim.x * kThreads;
@@ -127,6 +133,8 @@ __global__ void __launch_bounds__(kThreads) sum_partials(const float *__restrict
 // Stage 2: one CTA sums the partials in index order.
 __global__ void __launch_bounds__(kThreads) sum_finish(const RowArgs a, const float *__restrict__ partials, int count,
                                                        float *__restrict__ y) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   __shared__ float red[kWarps];
   float acc = 0.0f;
   for (int i = threadIdx.x; i < count; i += kThreads) acc += partials[i];
@@ -154,6 +162,8 @@ __device__ __forceinline__ float fold_identity() {
 template <int OP>
 __global__ void __launch_bounds__(kThreads) rows_fold(const float *__restrict__ x, float *__restrict__ y,
                                                       int64_t cols, int64_t ldx) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   __shared__ float red[kWarps];
   const float *xr = x + (int64_t)blockIdx.x * ldx;
   float acc = fold_identity<OP>();
@@ -189,9 +199,11 @@ extern "C" int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const 
     cudaStream_t s = (cudaStream_t)stream;
     b2k::PhaseTimer timer(ctx, B2K_PHASE_ROWS, s);
     const int grid = (int)rows;
-    if (params->op == B2K_ROW_MAX) rows_fold<B2K_ROW_MAX><<<grid, kThreads, 0, s>>>(x, y, cols, ld_x);
-    else if (params->op == B2K_ROW_MIN) rows_fold<B2K_ROW_MIN><<<grid, kThreads, 0, s>>>(x, y, cols, ld_x);
-    else rows_fold<B2K_ROW_PROD><<<grid, kThreads, 0, s>>>(x, y, cols, ld_x);
+    const bool pdl = b2k::pdl_enabled();
+    const dim3 g((unsigned)grid), b(kThreads);
+    if (params->op == B2K_ROW_MAX) b2k::launch_kernel(pdl, rows_fold<B2K_ROW_MAX>, g, b, 0, s, x, y, cols, ld_x);
+    else if (params->op == B2K_ROW_MIN) b2k::launch_kernel(pdl, rows_fold<B2K_ROW_MIN>, g, b, 0, s, x, y, cols, ld_x);
+    else b2k::launch_kernel(pdl, rows_fold<B2K_ROW_PROD>, g, b, 0, s, x, y, cols, ld_x);
     return b2k::check_launch(ctx, "row_op fold launch");
   }
   const RowArgs a{params->op,  params->sum_div, params->sum_div_ptr, params->ms_div,
@@ -204,8 +216,9 @@ extern "C" int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const 
     if (status != B2K_OK) return status;
     ctx->flags_epoch = 0;  // GEMM stream-K flags share this scratch: reset them next time
     float *partials = static_cast<float *>(ctx->workspace);
-    sum_partials<<<parts, kThreads, 0, s>>>(x, cols, partials);
-    sum_finish<<<1, kThreads, 0, s>>>(a, partials, parts, y);
+    b2k::launch_kernel(b2k::pdl_enabled(), sum_partials, dim3(parts), dim3(kThreads), 0, s, x, cols, partials);
+    b2k::launch_kernel(b2k::pdl_enabled(), sum_finish, dim3(1), dim3(kThreads), 0, s, a, (const float *)partials,
+                       parts, y);
     return b2k::check_launch(ctx, "row_op sum launch", 2);
   }
   const bool vec = (cols % 4 == 0) && (ld_x % 4 == 0) && b2k::aligned16(x) &&
@@ -213,11 +226,13 @@ extern "C" int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const 
                                                   (!params->w || b2k::aligned16(params->w))));
   const int64_t cols4 = cols / 4;
   const int grid = (int)rows;
-  if (vec && cols4 <= kThreads) rows_vec<1><<<grid, kThreads, 0, s>>>(a, x, y, cols4, ld_x, ld_y);
-  else if (vec && cols4 <= kThreads * 2) rows_vec<2><<<grid, kThreads, 0, s>>>(a, x, y, cols4, ld_x, ld_y);
-  else if (vec && cols4 <= kThreads * 4) rows_vec<4><<<grid, kThreads, 0, s>>>(a, x, y, cols4, ld_x, ld_y);
-  else if (vec && cols4 <= kThreads * 8) rows_vec<8><<<grid, kThreads, 0, s>>>(a, x, y, cols4, ld_x, ld_y);
-  else if (vec && cols4 <= kThreads * 16) rows_vec<16><<<grid, kThreads, 0, s>>>(a, x, y, cols4, ld_x, ld_y);
-  else rows_generic<<<grid, kThreads, 0, s>>>(a, x, y, cols, ld_x, ld_y);
+  const bool pdl = b2k::pdl_enabled();
+  const dim3 g((unsigned)grid), b(kThreads);
+  if (vec && cols4 <= kThreads) b2k::launch_kernel(pdl, rows_vec<1>, g, b, 0, s, a, x, y, cols4, ld_x, ld_y);
+  else if (vec && cols4 <= kThreads * 2) b2k::launch_kernel(pdl, rows_vec<2>, g, b, 0, s, a, x, y, cols4, ld_x, ld_y);
+  else if (vec && cols4 <= kThreads * 4) b2k::launch_kernel(pdl, rows_vec<4>, g, b, 0, s, a, x, y, cols4, ld_x, ld_y);
+  else if (vec && cols4 <= kThreads * 8) b2k::launch_kernel(pdl, rows_vec<8>, g, b, 0, s, a, x, y, cols4, ld_x, ld_y);
+  else if (vec && cols4 <= kThreads * 16) b2k::launch_kernel(pdl, rows_vec<16>, g, b, 0, s, a, x, y, cols4, ld_x, ld_y);
+  else b2k::launch_kernel(pdl, rows_generic, g, b, 0, s, a, x, y, cols, ld_x, ld_y);
   return b2k::check_launch(ctx, "row_op launch");
 }

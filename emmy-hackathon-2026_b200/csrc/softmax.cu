@@ -168,6 +168,8 @@ void launch_rows(const float *x, const Sink &sink, int64_t rows, int64_t cols, i
 }
 
 __global__ void selective_exp_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t n) {
+  grid_dependency_wait();
+  grid_dependents_launch();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = b2k_exp(x[i]);
 }
@@ -210,6 +212,7 @@ extern "C" int b2k_selective_exp_f32(b2k_ctx *ctx, const float *x, float *y, int
   if (!x || !y) return b2k::fail(ctx, B2K_EINVAL, "selective_exp: null buffer");
   const int64_t blocks = (n + 255) / 256;
   if (blocks > INT32_MAX) return b2k::fail(ctx, B2K_EINVAL, "selective_exp: extent too large");
-  selective_exp_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(x, y, n);
+  b2k::launch_kernel(b2k::pdl_enabled(), selective_exp_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                     (cudaStream_t)stream, x, y, n);
   return b2k::check_launch(ctx, "selective_exp launch");
 }
