@@ -13,8 +13,10 @@
 // softmax and the P.V fold in SIMT FP32 (compile.py:7009-7966, selective exp
 // 2953-2965).  Here nothing but Q, K, V and O touches HBM:
 //
-//   warp 0      TMA: Q_hi/Q_lo once (128 x Dp, four 128-byte-swizzled
-//               column blocks each, resident), then through a 3-stage ring
+//   warp 0      TMA: Q once (128 x Dp, four 128-byte-swizzled column
+//               blocks, resident; raw when d % 32 == 0 -- the softmax warps
+//               then split it into Q_hi/Q_lo in place before the first S
+//               MMA -- else the pre-split hi/lo copies), then through a 3-stage ring
 //               the chunks K_j[:, 32c..] (128 keys x 32 dims) and
 //               V_j^T[:, 32c..] (128 dims x 32 keys), hi and lo, in the MMA
 //               issuer's order: K_0, then K_{j+1}, V_j for each j
@@ -29,7 +31,9 @@
 //               through shared memory), then the finished O_{j-1} folded
 //               into the FP32 row accumulator O = O * alpha + O_{j-1} in
 //               registers, then P_j's TF32 halves into TMEM (hi over S_j, lo
-//               in its own columns: the A operand of O_j)
+//               in its own columns: the A operand of O_j); at the end the
+//               normalised O tile, staged in Q's buffer and TMA-stored box
+//               by box
 //
 // Each key block's products accumulate in a fresh TMEM buffer, so the
 // in-instruction accumulation error stays that of 48 (S) / 48 (O) MMAs.
