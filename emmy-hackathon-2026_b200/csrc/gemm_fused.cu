@@ -32,11 +32,14 @@
 //       cycles): measured about 2x slower than the pre-pass kernel, so it is
 //       kept for comparison only (b2k_gemm_set_fused_split(2)).
 //
-// Roles (576 threads): warp 0 TMA producer, warp 1 TMEM allocator + single
-// MMA issuer, warps 2..17 split + epilogue: all sixteen fold each finished
-// 256-wide K chunk of the TMEM accumulator into FP32 registers with
-// round-to-nearest adds, then bias -> ReLU -> stores; the split is shared out
-// by stage in four groups of four warps.  All waits are bounded.
+// Roles (576 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
+// issuer (the whole warp runs the loop, one elected lane issues), warps
+// 2..17 split + epilogue: all sixteen fold each finished 256-wide K chunk of
+// the TMEM accumulator into FP32 registers with round-to-nearest adds, then
+// bias -> ReLU -> C staged in shared memory and written by TMA stores; the
+// split is shared out by stage in four groups of four warps.  The kernel is
+// launched with programmatic dependent launch (its set-up overlaps the B
+// split's tail).  All waits are bounded.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
