@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 backend's hot path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|softmax|add|ragged]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|softmax|add|ragged|attention]
                     [--impl ours|reference]
 
 A step is one pass of the hot path over one batch of synthetic input:
