@@ -36,6 +36,7 @@ from .ir import Graph, GraphNode, IRError, Node, static_int, walk
 
 FULL_EXECUTION_BUDGET = 4_000_000     # lanes x statements below which every CTA is executed
 SAMPLE_CTAS = 4
+PREFIX_CANDIDATES = 6                 # K-prefix contractions tried per operand order
 
 
 class Unsupported(ValueError):
@@ -78,7 +79,8 @@ class KernelSpec:
                                 dims=(p["rows"], p["cols"], p["cols"], p["cols"]))
         if self.kind == "matmul":
             return rt.make_desc(rt.KIND_GEMM, {0: pos[p["a"]], 1: pos[p["b"]], 2: pos[p["out"]]},
-                                dims=(p["m"], p["n"], p["k"], p["k"], p["n"], p["n"]), flags=(rt.B_KN, 0))
+                                dims=(p["m"], p["n"], p["k"], p.get("lda", p["k"]), p.get("ldb", p["n"]), p["n"]),
+                                flags=(rt.B_KN, 0))
         if self.kind == "attention":
             return rt.make_desc(rt.KIND_ATTENTION, {0: pos[p["q"]], 1: pos[p["kt"]], 2: pos[p["v"]],
                                                     3: pos[p["out"]], 4: pos[p["scale"]]},
@@ -401,13 +403,42 @@ def classify_matmul(node, kernel, args, inputs, outputs):
         sa, sb = _shape(args[a]), _shape(args[b])
         if sa[1] != sb[0] or (sa[0], sb[1]) != oshape:
             continue
-        try:
-            cert = certify(node, kernel, args, inputs, outputs, lambda buf: {out: buf[a] @ buf[b]})
-        except Unsupported as exc:
-            last = exc
-            continue
-        return {"a": a, "b": b, "out": out, "m": sa[0], "n": sb[1], "k": sa[1]}, cert
+        # The whole shared dimension first; then, if the IR bounds its K loop
+        # below it (a guard ``kk < 63`` over 65 columns), each static integer
+        # of the body smaller than K, largest first, as a prefix contraction
+        # A[:, :k] @ B[:k, :] -- the GEMM reads it through lda / ldb.
+        prefixes = sorted((v for v in _int_literals(node.body) if 0 < v < sa[1]), reverse=True)[:PREFIX_CANDIDATES]
+        for k in [sa[1]] + prefixes:
+            try:
+                cert = certify(node, kernel, args, inputs, outputs,
+                               lambda buf, k=k: {out: buf[a][:, :k] @ buf[b][:k, :]})
+            except Unsupported as exc:
+                last = last or exc
+                continue
+            return {"a": a, "b": b, "out": out, "m": sa[0], "n": sb[1], "k": k, "lda": sa[1], "ldb": sb[1]}, cert
     raise last or Unsupported("matmul: operand shapes do not contract to the output")
+
+
+def _int_literals(body) -> set:
+    """The distinct static integers (``Literal`` and ``Dim`` values) anywhere in
+    ``body``, expressions included."""
+    seen: set = set()
+
+    def visit(value):
+        if isinstance(value, Node):
+            if value.kind in ("Literal", "Dim") and isinstance(value.get("value"), int) \
+                    and not isinstance(value.get("value"), bool):
+                seen.add(value.get("value"))
+            for v in value.positional:
+                visit(v)
+            for v in value.fields.values():
+                visit(v)
+        elif isinstance(value, (tuple, list)):
+            for v in value:
+                visit(v)
+
+    visit(body)
+    return seen
 
 
 # --------------------------------------------------------------------------- attention

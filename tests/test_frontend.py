@@ -22,6 +22,7 @@ RECOGNISED = {
     "case-14-fff293a2235c": ["row_reduce"],
     "case-22-da018f96fc2e": ["row_reduce"],
     "case-30-061d7084b729": ["row_reduce"],
+    "case-7-72f1deeac451": ["matmul"],
     "f01_rmsnorm-6ab09ab4acc3": ["row_norm"],
     "f02-extra-cta-120bf007fb2d": ["row_softmax"],
     "f03_l2norm-1e82d7e58a53": ["row_norm"],
@@ -133,11 +134,28 @@ def test_wrong_semantics_rejected(tmp_path):
     assert [i[0] for i in spec.params["insns"]] == ["subtract"]  # ... of the IR's own op
 
 
-def test_matmul_with_truncated_k_rejected():
-    """case-7 contracts only the first 63 of 65 K columns: not A @ B."""
+def test_matmul_over_k_prefix():
+    """case-7 contracts only the first 63 of 65 K columns: recognised as
+    A[:, :63] @ B[:63, :] read through lda = 65, never as the full A @ B."""
     fe = pkg("frontend")
+    spec = fe.compile_path(next((CASES / "case-7-72f1deeac451").glob("*.ir.json")))
+    p = spec.params
+    assert (spec.kind, p["m"], p["n"], p["k"], p["lda"], p["ldb"]) == ("matmul", 64, 32, 63, 65, 32)
+
+
+def test_matmul_prefix_needs_the_certificate(tmp_path):
+    """A K guard that is not a prefix (every other column) fits no candidate."""
+    fe = pkg("frontend")
+    folder = _copy_case(tmp_path, "case-7-72f1deeac451")
+    path = next(folder.glob("*.ir.json"))
+    text = path.read_text()
+    guard = "BinaryExpr(op='<', left=Var(name='kk'), right=Literal(value=63, dtype='int'))"
+    assert guard in text
+    odd = ("BinaryExpr(op='==', left=BinaryExpr(op='%', left=Var(name='kk'), right=Literal(value=2, dtype='int')), "
+           "right=Literal(value=0, dtype='int'))")
+    path.write_text(text.replace(guard, odd))
     with pytest.raises(fe.Unsupported):
-        fe.compile_path(next((CASES / "case-7-72f1deeac451").glob("*.ir.json")))
+        fe.compile_path(path)
 
 
 def test_row_constants_bound_to_metadata_buffers():
