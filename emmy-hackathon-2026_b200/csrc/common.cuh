@@ -135,8 +135,12 @@ struct SplitOperands {
 // split of both operands, 1 = A split into TMEM inside the kernel with B
 // pre-split into `ops` (A must be TMA-readable: 16-byte aligned, row stride a
 // multiple of 4 elements, K >= 16), 2 = both operands split in shared memory
-// (B TMA-readable too; needs no scratch).
-int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb);
+// (B TMA-readable too; needs no scratch).  Under the default switch the
+// choice between 0 and 1 also weighs their tilings over `sms` SMs.
+int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                    int sms);
+// Tile width (columns) of the pre-pass kernel gemm_main picks for n columns.
+int main_tile_width(int64_t n);
 // The tile variant selected with b2k_gemm_set_variant (2 = 128-wide tiles).
 int gemm_variant();
 int gemm_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const SplitOperands &ops, float *c, int64_t m,

@@ -39,11 +39,14 @@ constexpr int BM = 128;
 // (the split rule split_tf32 lives in common.cuh)
 
 // Row-major operand rows -> hi/lo rows [R][Kp] (R = batch * rows), zero
-// padded along K.  A block is 32 rows x 32 float4 columns: blockIdx.x picks
-// the 128-column slice, blockIdx.y (strided) the 32-row tile, over the tiles
+// padded along K.  A block is 16 rows x 32 float4 columns: blockIdx.x picks
+// the 128-column slice, blockIdx.y (strided) the 16-row tile, over the tiles
 // of job 0 and then of job 1, so two operands split in one launch.  Each
-// thread loads its four rows (threadIdx.y + 8 u) before it splits and stores
-// any, so four 16-byte loads per thread are in flight.
+// thread loads its two rows (threadIdx.y + 8 u) before it splits and stores
+// either.  Two rows per thread (37 registers, six blocks per SM) measured
+// 1.6 % faster on the ragged 4097 x 1000 x 777 GEMM than four rows (56
+// registers, four blocks per SM); bounding the registers further spilled or
+// ran slower.
 struct RowSplitJob {
   const float *src;
   float *hi, *lo;
@@ -53,7 +56,7 @@ struct RowSplitJob {
   int64_t tiles;       // row tiles
   int vec;             // rows 16-byte aligned: float4 loads
 };
-constexpr int kSplitRows = 32;  // rows per tile
+constexpr int kSplitRows = 16;  // rows per tile
 constexpr int kSplitRowsPerThread = kSplitRows / 8;
 
 __global__ void __launch_bounds__(256) split_rows_kernel(const RowSplitJob j0, const RowSplitJob j1, int64_t Kp) {
@@ -904,6 +907,15 @@ int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_
   return check_launch(ctx, "split_transpose launch");
 }
 
+int main_tile_width(int64_t n) {
+  if (n <= 128) return 128;
+  switch (g_gemm_variant) {
+    case 2: return 128;
+    case 3: return 192;
+    default: return 256;
+  }
+}
+
 int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
               cudaStream_t s, const StreamKScratch *sk) {
@@ -931,7 +943,7 @@ int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int6
 int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                          int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu,
                          float *ws, cudaStream_t s, const b2k::StreamKScratch *sk) {
-  const int mode = b2k::gemm_split_mode(a, b, m, n, k, lda, ldb);
+  const int mode = b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count);
   if (mode == 2) return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_kmajor, bias, relu, s);
   const int64_t kp = b2k::gemm_kpad(k);
   int status;
@@ -995,7 +1007,7 @@ extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, flo
     if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: zero fill");
     return B2K_OK;
   }
-  if (b2k::gemm_split_mode(a, b, m, n, k, lda, ldb) == 2)  // needs no scratch
+  if (b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count) == 2)  // needs no scratch
     return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu, s);
   // scratch: split operands, then the stream-K partial slots and flags
   const size_t split_bytes = (b2k_gemm_workspace_bytes(m, n, k) + 255) & ~size_t(255);

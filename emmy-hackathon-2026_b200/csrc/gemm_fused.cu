@@ -15,7 +15,8 @@
 // 960 128-byte wavefronts per 768 MMA cycles and runs at the predicted 80 %).
 // Two kernels:
 //
-//   gemm_tmem_a_kernel (default)  A is split into TENSOR memory: each split
+//   gemm_tmem_a_kernel (default unless the pre-pass kernel's wider tiles
+//       cover the output in enough fewer waves)  A is split into TENSOR memory: each split
 //       thread owns one A row (one TMEM lane), reads one raw 16-byte chunk of
 //       the staged row, splits it and writes hi and lo with tcgen05.st; the
 //       MMAs take A from TMEM (tcgen05.mma ... [a_tmem]), so A costs one
@@ -673,11 +674,12 @@ int launch_smem_split(b2k_ctx *ctx, const float *a, const float *b, float *c, in
 }  // namespace
 
 // 0 = pre-pass split of both operands, 1 = A split into TMEM inside the
-// kernel + B pre-pass (default), 2 = both split in shared memory.
+// kernel + B pre-pass where that tiles no worse (default), 2 = both split in
+// shared memory, 3 = A split into TMEM wherever TMA can read A.
 static int g_split_mode = 1;
 
 extern "C" int b2k_gemm_set_fused_split(int mode) {
-  if (mode < 0 || mode > 2) return B2K_EINVAL;
+  if (mode < 0 || mode > 3) return B2K_EINVAL;
   g_split_mode = mode;
   return B2K_OK;
 }
@@ -688,10 +690,28 @@ namespace b2k {
 // its row stride is a multiple of 4 elements.
 static bool tma_readable(const float *p, int64_t ld) { return aligned16(p) && (ld % 4 == 0); }
 
-int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb) {
+// Each CTA of either kernel computes one 128-row tile, so a call takes about
+// (waves of tiles over the SMs) x (tile width) x K.  The in-kernel split
+// (tiles 192 wide) is kept unless the pre-pass kernel (256 wide) needs 10 %
+// less by that estimate: it also saves the pre-pass over A.  Measured on
+// B200: 4096^3 takes 5 waves x 192 against 4 x 256, and the in-kernel split
+// is 7 % faster; 4097 x 1000 x 776 takes 2 waves x 192 (198 tiles on 148
+// SMs) against 1 x 256, and the pre-pass kernel is 35 % faster.
+static bool prepass_tiles_better(int64_t m, int64_t n, int sms) {
+  if (sms <= 0) return false;
+  const int64_t bn1 = (n <= 128 || gemm_variant() == 2) ? 128 : 192, bn0 = main_tile_width(n);
+  const int64_t rows = (m + BM - 1) / BM;
+  const int64_t cost1 = (rows * ((n + bn1 - 1) / bn1) + sms - 1) / sms * bn1;
+  const int64_t cost0 = (rows * ((n + bn0 - 1) / bn0) + sms - 1) / sms * bn0;
+  return 10 * cost1 > 11 * cost0;
+}
+
+int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                    int sms) {
   if (g_split_mode == 0 || k < BK || m > INT32_MAX - BM || n > INT32_MAX - 256 || k > INT32_MAX - 64) return 0;
   if (!tma_readable(a, lda)) return 0;
   if (g_split_mode == 2) return tma_readable(b, ldb) ? 2 : 1;
+  if (g_split_mode == 1 && prepass_tiles_better(m, n, sms)) return 0;
   return 1;
 }
 

@@ -283,7 +283,10 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
   const int64_t slabs = b2k::slab_count((size_t)m * k * 4, (m + 127) / 128, b2k::kSlabGemm);
   const int64_t per = ((m + slabs - 1) / slabs + 127) / 128 * 128;
   b2k::Pipe pipe(ctx, s);
-  if (k == 0 || b2k::gemm_split_mode(da, db, per, n, k, k, b_cols) == 2) {
+  // The kernel is chosen for the whole call's m, as b2k_gemm_tf32x3 chooses
+  // it, so that the result equals the device entry point's bit for bit.
+  const int mode = k == 0 ? 0 : b2k::gemm_split_mode(da, db, m, n, k, k, b_cols, ctx->sm_count);
+  if (k == 0 || mode == 2) {
     // No split operands to share between slabs: each slab is a whole GEMM.
     B2K_TRY(pipe.begin());
     B2K_TRY(pipe.in(db, (size_t)b_cols * 4, b, (size_t)ldb * 4, (size_t)b_cols * 4, b_rows));
@@ -301,7 +304,7 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
   // B is split once into the workspace; each slab then splits its rows of A
   // (pre-pass path) or reads them raw (A split into TMEM inside the kernel).
   const int64_t kp = b2k::gemm_kpad(k);
-  const bool tmem_a = b2k::gemm_split_mode(da, db, per, n, k, k, b_cols) == 1;
+  const bool tmem_a = mode == 1;
   B2K_TRY(b2k::reserve_workspace(ctx, (size_t)(2 * n * kp + (tmem_a ? 0 : 2 * per * kp)) * 4, s));
   ctx->flags_epoch = 0;  // the workspace is reused: stream-K flags must be reset by the next device GEMM
   float *ws = static_cast<float *>(ctx->workspace);

@@ -351,8 +351,9 @@ class Context:
         return int(count.value)
 
     def set_gemm_fused_split(self, mode: int) -> None:
-        """0 = pre-pass split of A and B, 1 = A split in-kernel into TMEM (default),
-        2 = A and B split in shared memory inside the kernel."""
+        """0 = pre-pass split of A and B; 3 = A split in-kernel into TMEM; 1 (default)
+        = 3 unless the pre-pass kernel's wider tiles need fewer waves; 2 = A and
+        B split in shared memory inside the kernel."""
         self.check(self.lib.b2k_gemm_set_fused_split(int(mode)), "b2k_gemm_set_fused_split")
 
     def set_gemm_streamk(self, on: bool) -> None:

@@ -336,18 +336,24 @@ int b2k_gemm_set_variant(int variant);
 int b2k_gemm_set_streamk(int on);
 /* Process-wide choice of where b2k_gemm_tf32x3 (and the no-alloc variant)
  * split operands into TF32 hi/lo halves:
- *   1 (default)  A is staged raw by TMA and split inside the tensor-core
- *                kernel into tensor memory, which the MMAs read A from; B is
- *                split once by a pre-pass.  Needs A 16-byte aligned with a row
- *                stride that is a multiple of 4 elements and K >= 16.
+ *   3            A is staged raw by TMA and split inside the tensor-core
+ *                kernel into tensor memory, which the MMAs read A from (128 x
+ *                192 tiles); B is split once by a pre-pass.  Needs A 16-byte
+ *                aligned with a row stride that is a multiple of 4 elements and
+ *                K >= 16.
+ *   1 (default)  3 where A qualifies, unless the pre-pass kernel's 128 x 256
+ *                tiles cover the output in enough fewer waves over the SMs
+ *                that (waves x tile width) drops by more than 10 %: then 0.
+ *                (4097 x 1000 tiles as 198 tiles of 192 -- two waves on 148
+ *                SMs -- or 132 tiles of 256 -- one wave.)
  *   2            both operands staged raw and split in shared memory inside
  *                the kernel (no pre-pass, no scratch; both operands must be
  *                TMA-readable as above).  Measured slower on B200: the split
  *                doubles the shared-memory traffic the tensor core competes for.
  *   0            both operands split by the pre-pass.
- * Calls whose operands do not meet a mode's conditions take the next mode
- * down.  Returns B2K_EINVAL for other values.  No counterpart in the
- * reference. */
+ * Calls whose operands do not meet a mode's conditions take the pre-pass path
+ * (2 falls back to 3 when only B is not TMA-readable).  Returns B2K_EINVAL
+ * for other values.  No counterpart in the reference. */
 int b2k_gemm_set_fused_split(int mode);
 
 /* --- pipelined host-array calls ----------------------------------------------

@@ -138,23 +138,24 @@ def test_gemm_streamk_opt_in(ctx, torch_cuda, m, n, k, b_layout):
 FUSED_CASES = [
     (4096, 4096, 4096, 0), (1000, 1000, 776, 1), (300, 520, 200, 0), (257, 384, 1000, 0), (130, 96, 48, 1),
     (130, 96, 48, 0), (64, 128, 16, 0), (33, 200, 20, 1), (512, 200, 36, 0), (2048, 4000, 300, 1),
+    (4097, 1000, 776, 1),  # mode 1 takes the pre-pass kernel: one wave of 256-wide tiles
 ]
 
 
 @pytest.mark.parametrize("m,n,k,b_layout", FUSED_CASES)
 def test_gemm_split_modes_match_float64_and_each_other(ctx, torch_cuda, m, n, k, b_layout):
-    """The three split placements (0: pre-pass for A and B; 1: A split into
+    """The three split placements (0: pre-pass for A and B; 3: A split into
     TMEM inside the kernel, B pre-split; 2: A and B split in shared memory,
-    B read K-major or MN-major) against float64, the 3xTF32 model and each
-    other on the same inputs.  Shapes cover ragged M, N and K, N <= 128 and
-    K = 16."""
+    B read K-major or MN-major) and the default choice between 0 and 3 (1)
+    against float64, the 3xTF32 model and each other on the same inputs.
+    Shapes cover ragged M, N and K, N <= 128 and K = 16."""
     rng = np.random.default_rng(m * 31 + n * 7 + k + b_layout)
     a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
     b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
     bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
     got = {}
     try:
-        for mode in (0, 1, 2):
+        for mode in (0, 1, 2, 3):
             ctx.set_gemm_fused_split(mode)
             got[mode] = run_gemm(ctx, torch_cuda, a, b, b_layout=b_layout, bias=bias, relu=True)
     finally:
@@ -163,7 +164,7 @@ def test_gemm_split_modes_match_float64_and_each_other(ctx, torch_cuda, m, n, k,
     rows = np.arange(m) if m <= 512 else np.random.default_rng(1).choice(m, 256, replace=False)
     exact = np.maximum(a[rows].astype(np.float64) @ bm.astype(np.float64) + bias, 0.0)
     model = np.maximum(tf32.gemm_3xtf32(a, bm) + bias, 0.0) if m * n * k <= 1 << 24 else None
-    for mode in (1, 2):
+    for mode in (1, 2, 3):
         assert tf32.normwise_error(got[mode][rows], exact) <= NORMWISE, mode
         assert tf32.normwise_error(got[mode], got[0]) <= 1e-7, mode
         if model is not None:
@@ -185,13 +186,13 @@ def test_gemm_fused_split_special_values(ctx, torch_cuda):
     b[2, 7] = 1.5
     got = {}
     try:
-        for mode in (0, 1, 2):
+        for mode in (0, 1, 2, 3):
             ctx.set_gemm_fused_split(mode)
             got[mode] = run_gemm(ctx, torch_cuda, a, b)
     finally:
         ctx.set_gemm_fused_split(1)
-    np.testing.assert_array_equal(got[1], got[0])
-    np.testing.assert_array_equal(got[2], got[0])
+    for mode in (1, 2, 3):
+        np.testing.assert_array_equal(got[mode], got[0])
     got = got[1]
     finite = np.setdiff1d(np.arange(128), [5, 9])
     np.testing.assert_array_equal(got[finite], (a[finite].astype(np.float64) @ b).astype(np.float32))

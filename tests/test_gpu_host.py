@@ -89,6 +89,8 @@ GEMM_CASES = [
     (640, 384, 256, "kn", False, 0),
     (640, 384, 256, "kn", True, 2),       # whole GEMM per slab
     (5, 7, 3, "kn", False, 1),
+    (2304, 1024, 1024, "kn", False, 3),   # A split into TMEM, forced
+    (4097, 1000, 776, "nk", True, 1),     # aligned A, but the pre-pass kernel tiles in fewer waves
 ]
 
 
