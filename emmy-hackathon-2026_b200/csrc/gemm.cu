@@ -942,8 +942,11 @@ int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int6
 // `b_kmajor`: B is stored [n, K] (else [K, n]).
 int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                          int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu,
-                         float *ws, cudaStream_t s, const b2k::StreamKScratch *sk) {
-  const int mode = b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count);
+                         float *ws, cudaStream_t s, const b2k::StreamKScratch *sk, const float *div_ptr,
+                         float div_value) {
+  // A divided product runs on the pre-pass kernel, whose epilogue divides.
+  const bool divide = div_ptr != nullptr || div_value != 1.0f;
+  const int mode = divide ? 0 : b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count);
   if (mode == 2) return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_kmajor, bias, relu, s);
   const int64_t kp = b2k::gemm_kpad(k);
   int status;
@@ -972,7 +975,7 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
     }
   }
   if (status != B2K_OK) return status;
-  return b2k::gemm_main(ctx, ops, m, n, 1, c, ldc, m * ldc, bias, relu, nullptr, 1.0f, s, sk);
+  return b2k::gemm_main(ctx, ops, m, n, 1, c, ldc, m * ldc, bias, relu, div_ptr, div_value, s, sk);
 }
 
 int b2k::gemm_variant() { return g_gemm_variant; }
@@ -987,9 +990,10 @@ size_t b2k_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   return (size_t)(2 * (m + n) * b2k::gemm_kpad(k)) * sizeof(float);
 }
 
-extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n,
-                               int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout,
-                               const float *bias, int32_t relu, void *stream) {
+// Validation, scratch and dispatch shared by b2k_gemm_tf32x3 and its scaled form.
+static int gemm_entry(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                      int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
+                      const float *div_ptr, float div_value, void *stream) {
   B2K_CHECK_CTX(ctx);
   if (m < 0 || n < 0 || k < 0) return b2k::fail(ctx, B2K_EINVAL, "gemm: negative extent");
   if (b_layout != B2K_B_KN && b_layout != B2K_B_NK) return b2k::fail(ctx, B2K_EINVAL, "gemm: bad b_layout");
@@ -1000,14 +1004,16 @@ extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, flo
   if (m > INT32_MAX - 256 || n > INT32_MAX - 256 || k > INT32_MAX - 64)
     return b2k::fail(ctx, B2K_EINVAL, "gemm: extent exceeds 32-bit TMA coordinates");
   cudaStream_t s = (cudaStream_t)stream;
+  const bool divide = div_ptr != nullptr || div_value != 1.0f;
   if (k == 0) {
     // Empty contraction: C = epilogue(0).
     if (bias) return b2k::fail(ctx, B2K_EUNSUPPORTED, "gemm: bias with K = 0");
+    if (divide) return b2k::fail(ctx, B2K_EUNSUPPORTED, "gemm: divisor with K = 0");
     cudaError_t err = cudaMemset2DAsync(c, (size_t)ldc * 4, 0, (size_t)n * 4, (size_t)m, s);
     if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: zero fill");
     return B2K_OK;
   }
-  if (b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count) == 2)  // needs no scratch
+  if (!divide && b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count) == 2)  // needs no scratch
     return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu, s);
   // scratch: split operands, then the stream-K partial slots and flags
   const size_t split_bytes = (b2k_gemm_workspace_bytes(m, n, k) + 255) & ~size_t(255);
@@ -1027,5 +1033,18 @@ extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, flo
   sk.epoch = ++ctx->flags_epoch;
   if (sk.epoch == 0) sk.epoch = ctx->flags_epoch = 1;
   return b2k_gemm_tf32x3_impl(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu,
-                              static_cast<float *>(ctx->workspace), s, &sk);
+                              static_cast<float *>(ctx->workspace), s, &sk, div_ptr, div_value);
+}
+
+extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n,
+                               int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout,
+                               const float *bias, int32_t relu, void *stream) {
+  return gemm_entry(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu, nullptr, 1.0f, stream);
+}
+
+extern "C" int b2k_gemm_tf32x3_scaled(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n,
+                                      int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout,
+                                      const float *bias, int32_t relu, const float *div_ptr, float div_value,
+                                      void *stream) {
+  return gemm_entry(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu, div_ptr, div_value, stream);
 }

@@ -59,11 +59,20 @@ extern "C" int b2k_launch(b2k_ctx *ctx, const b2k_kernel_desc *d, void *const *a
                             d->dims[3], stream);
     }
     case B2K_KIND_GEMM_3XTF32:
-      need(0), need(1), need(2), maybe(3);
+      need(0), need(1), need(2), maybe(3), maybe(4);
       if (st != B2K_OK) return st;
+      if (p[4])  // the product divided by a one-element buffer
+        return b2k_gemm_tf32x3_scaled(ctx, (const float *)p[0], (const float *)p[1], (float *)p[2], d->dims[0],
+                                      d->dims[1], d->dims[2], d->dims[3], d->dims[4], d->dims[5], d->flags[0],
+                                      (const float *)p[3], d->flags[1], (const float *)p[4], 1.0f, stream);
       return b2k_gemm_tf32x3(ctx, (const float *)p[0], (const float *)p[1], (float *)p[2], d->dims[0], d->dims[1],
                              d->dims[2], d->dims[3], d->dims[4], d->dims[5], d->flags[0], (const float *)p[3],
                              d->flags[1], stream);
+    case B2K_KIND_AXIS_REDUCE:
+      need(0), need(1), maybe(3);
+      if (st != B2K_OK) return st;
+      return b2k_axis_reduce_f32(ctx, d->flags[0], (const float *)p[0], (float *)p[1], d->dims[0], d->dims[1],
+                                 d->dims[2], d->values[0], (const float *)p[3], stream);
     case B2K_KIND_ATTENTION_3XTF32:
       need(0), need(1), need(2), need(3), maybe(4);
       if (st != B2K_OK) return st;

@@ -180,7 +180,58 @@ __global__ void __launch_bounds__(kThreads) rows_fold(const float *__restrict__ 
   }
 }
 
+// Fold over the middle axis of [batch][s][cols]: one thread per output
+// column j, folding i = 0 .. s-1 in order (the IR's serial Loop + Accum over
+// that axis).  Consecutive threads hold consecutive columns, so every step of
+// every fold is one coalesced read of a row segment; the loop is unrolled so
+// that several rows' loads are in flight ahead of the dependent fold.
+template <int OP>
+__global__ void __launch_bounds__(kThreads) axis_fold(const float *__restrict__ x, float *__restrict__ y,
+                                                      int64_t batch, int64_t s_len, int64_t cols,
+                                                      const float *div_ptr, float div) {
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const int64_t j = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  if (j >= cols) return;
+  for (int64_t b = blockIdx.y; b < batch; b += gridDim.y) {
+    const float *xb = x + b * s_len * cols + j;
+    float acc = OP == B2K_ROW_SUM ? 0.0f : fold_identity<OP>();
+#pragma unroll 8
+    for (int64_t i = 0; i < s_len; ++i) {
+      const float v = __ldg(xb + i * cols);
+      acc = OP == B2K_ROW_SUM ? __fadd_rn(acc, v) : fold_op<OP>(acc, v);
+    }
+    if (OP == B2K_ROW_SUM) {
+      const float d = div_ptr ? __ldg(div_ptr) : div;
+      if (div_ptr || d != 1.0f) acc = __fdiv_rn(acc, d);
+    }
+    y[b * cols + j] = acc;
+  }
+}
+
 }  // namespace
+
+extern "C" int b2k_axis_reduce_f32(b2k_ctx *ctx, int32_t op, const float *x, float *y, int64_t batch, int64_t s,
+                                   int64_t cols, float div, const float *div_ptr, void *stream) {
+  B2K_CHECK_CTX(ctx);
+  if (op != B2K_ROW_SUM && op != B2K_ROW_MAX && op != B2K_ROW_MIN && op != B2K_ROW_PROD)
+    return b2k::fail(ctx, B2K_EINVAL, "axis_reduce: op %d is not a fold", op);
+  if (batch < 0 || s < 0 || cols < 0) return b2k::fail(ctx, B2K_EINVAL, "axis_reduce: negative extent");
+  if (batch == 0 || cols == 0) return B2K_OK;
+  if (!y || (s > 0 && !x)) return b2k::fail(ctx, B2K_EINVAL, "axis_reduce: null buffer");
+  if ((cols + kThreads - 1) / kThreads > INT32_MAX) return b2k::fail(ctx, B2K_EINVAL, "axis_reduce: too many columns");
+  cudaStream_t st = (cudaStream_t)stream;
+  b2k::PhaseTimer timer(ctx, B2K_PHASE_ROWS, st);
+  const dim3 g((unsigned)((cols + kThreads - 1) / kThreads), (unsigned)std::min<int64_t>(batch, 65535)), b(kThreads);
+  const bool pdl = b2k::pdl_enabled();
+  switch (op) {
+    case B2K_ROW_SUM: b2k::launch_kernel(pdl, axis_fold<B2K_ROW_SUM>, g, b, 0, st, x, y, batch, s, cols, div_ptr, div); break;
+    case B2K_ROW_MAX: b2k::launch_kernel(pdl, axis_fold<B2K_ROW_MAX>, g, b, 0, st, x, y, batch, s, cols, div_ptr, div); break;
+    case B2K_ROW_MIN: b2k::launch_kernel(pdl, axis_fold<B2K_ROW_MIN>, g, b, 0, st, x, y, batch, s, cols, div_ptr, div); break;
+    default: b2k::launch_kernel(pdl, axis_fold<B2K_ROW_PROD>, g, b, 0, st, x, y, batch, s, cols, div_ptr, div); break;
+  }
+  return b2k::check_launch(ctx, "axis_reduce launch");
+}
 
 extern "C" int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const float *x, float *y, int64_t rows,
                               int64_t cols, int64_t ld_x, int64_t ld_y, void *stream) {

@@ -47,7 +47,7 @@ class Unsupported(ValueError):
 class KernelSpec:
     """A recognised kernel: which C-ABI entry point runs it and with what roles."""
 
-    kind: str                  # pointwise | row_softmax | matmul | attention | row_reduce | row_norm
+    kind: str                  # pointwise | row_softmax | matmul | attention | row_reduce | row_norm | axis_reduce
     entry: str
     node: str
     arg_order: list
@@ -78,7 +78,10 @@ class KernelSpec:
             return rt.make_desc(rt.KIND_ROW_SOFTMAX, {0: pos[p["x"]], 1: pos[p["out"]]},
                                 dims=(p["rows"], p["cols"], p["cols"], p["cols"]))
         if self.kind == "matmul":
-            return rt.make_desc(rt.KIND_GEMM, {0: pos[p["a"]], 1: pos[p["b"]], 2: pos[p["out"]]},
+            roles = {0: pos[p["a"]], 1: pos[p["b"]], 2: pos[p["out"]]}
+            if p.get("div_buffer"):
+                roles[4] = pos[p["div_buffer"]]
+            return rt.make_desc(rt.KIND_GEMM, roles,
                                 dims=(p["m"], p["n"], p["k"], p.get("lda", p["k"]), p.get("ldb", p["n"]), p["n"]),
                                 flags=(rt.B_KN, 0))
         if self.kind == "attention":
@@ -92,6 +95,13 @@ class KernelSpec:
             op = {"sum": rt.ROW_SUM, "max": rt.ROW_MAX, "min": rt.ROW_MIN, "prod": rt.ROW_PROD}[p["op"]]
             return rt.make_desc(rt.KIND_ROW_OP, roles, dims=(p["rows"], p["cols"], p["cols"], p["cols"]),
                                 flags=(op,), values=(p["sum_div"], 1.0, 0.0))
+        if self.kind == "axis_reduce":
+            roles = {0: pos[p["x"]], 1: pos[p["out"]]}
+            if p["sum_div_buffer"]:
+                roles[3] = pos[p["sum_div_buffer"]]
+            op = {"sum": rt.ROW_SUM, "max": rt.ROW_MAX, "min": rt.ROW_MIN, "prod": rt.ROW_PROD}[p["op"]]
+            return rt.make_desc(rt.KIND_AXIS_REDUCE, roles, dims=(p["batch"], p["s"], p["cols"]), flags=(op,),
+                                values=(p["sum_div"],))
         if self.kind == "row_norm":
             rms = p["op"] == "rmsnorm"
             roles = {0: pos[p["x"]], 1: pos[p["out"]]}
@@ -393,8 +403,15 @@ def classify_matmul(node, kernel, args, inputs, outputs):
         raise Unsupported("matmul: one output")
     out = outputs[0]
     mats = [n for n in inputs if len(_shape(args[n])) == 2]
-    if len(mats) != 2 or len(inputs) != 2:
-        raise Unsupported("matmul: two rank-2 inputs")
+    # An optional one-element buffer divides the product (scores = x @ y / scale[0]).
+    extra = [n for n in inputs if n not in mats]
+    if len(mats) != 2 or len(extra) > 1 or (extra and _size(_shape(args[extra[0]])) != 1):
+        raise Unsupported("matmul: two rank-2 inputs (and at most a one-element divisor)")
+    div = extra[0] if extra else None
+
+    def product(buf, a, b, k):
+        c = buf[a][:, :k] @ buf[b][:k, :]
+        return c / float(buf[div].reshape(-1)[0]) if div else c
     oshape = _shape(args[out])
     if len(oshape) != 2:
         raise Unsupported("matmul: rank-2 output")
@@ -411,11 +428,12 @@ def classify_matmul(node, kernel, args, inputs, outputs):
         for k in [sa[1]] + prefixes:
             try:
                 cert = certify(node, kernel, args, inputs, outputs,
-                               lambda buf, k=k: {out: buf[a][:, :k] @ buf[b][:k, :]})
+                               lambda buf, k=k, a=a, b=b: {out: product(buf, a, b, k)})
             except Unsupported as exc:
                 last = last or exc
                 continue
-            return {"a": a, "b": b, "out": out, "m": sa[0], "n": sb[1], "k": k, "lda": sa[1], "ldb": sb[1]}, cert
+            return {"a": a, "b": b, "out": out, "m": sa[0], "n": sb[1], "k": k, "lda": sa[1], "ldb": sb[1],
+                    "div_buffer": div}, cert
     raise last or Unsupported("matmul: operand shapes do not contract to the output")
 
 
@@ -487,6 +505,20 @@ def _bind_constant(args, scalars, value, rel=1e-9):
     return None
 
 
+def _fold_ops(node) -> set:
+    """The fold's operator: the ops of the Accum statements and of the combine
+    steps of warp shuffles / halving trees.  Only additive folds carry a
+    divisor (sum, mean); max / min / product must match exactly."""
+    fold_ops = set()
+    for s in walk(node.body):
+        if s.kind == "Accum":
+            fold_ops.add(s.op.name)
+        elif s.kind in ("WarpShuffle", "TreeHalve"):
+            fold_ops.update(c.op.name for c in s.get("combine_states") or () if c.kind == "Assign")
+    fold_ops.discard("copy")
+    return fold_ops
+
+
 def classify_row_reduce(node, kernel, args, inputs, outputs):
     if len(outputs) != 1:
         raise Unsupported("row_reduce: one output")
@@ -503,16 +535,7 @@ def classify_row_reduce(node, kernel, args, inputs, outputs):
         rows, cols = 1, xs[0]
     else:
         raise Unsupported("row_reduce: output is not one value per row")
-    # The fold's operator: the ops of the Accum statements and of the
-    # combine steps of warp shuffles / halving trees.  Only additive folds
-    # carry a divisor (sum, mean); max / min / product must match exactly.
-    fold_ops = set()
-    for s in walk(node.body):
-        if s.kind == "Accum":
-            fold_ops.add(s.op.name)
-        elif s.kind in ("WarpShuffle", "TreeHalve"):
-            fold_ops.update(c.op.name for c in s.get("combine_states") or () if c.kind == "Assign")
-    fold_ops.discard("copy")
+    fold_ops = _fold_ops(node)
     if fold_ops in ({"maximum"}, {"minimum"}, {"multiply"}):
         op = {"maximum": "max", "minimum": "min", "multiply": "prod"}[fold_ops.pop()]
         fold = {"max": np.max, "min": np.min, "prod": np.prod}[op]
@@ -544,6 +567,51 @@ def classify_row_reduce(node, kernel, args, inputs, outputs):
     if abs(div - round(div)) < 1e-9 * max(1.0, abs(div)):
         div = float(round(div))
     return {"op": "sum", "x": x, "out": out, "rows": rows, "cols": cols, "sum_div": div,
+            "sum_div_buffer": ptr}, cert
+
+
+def classify_axis_reduce(node, kernel, args, inputs, outputs):
+    """A fold over the middle axis: x [batch, s, cols] -> out [batch, cols]
+    (the IR's serial Loop + Accum over s for every (batch, column) cell)."""
+    if len(outputs) != 1:
+        raise Unsupported("axis_reduce: one output")
+    out = outputs[0]
+    scalars = _scalar_inputs(args, inputs)
+    mats = [n for n in inputs if n not in scalars]
+    if len(mats) != 1:
+        raise Unsupported("axis_reduce: one data input")
+    x = mats[0]
+    xs, ys = _shape(args[x]), _shape(args[out])
+    if len(xs) != 3 or (tuple(ys) != (xs[0], xs[2]) and not (xs[0] == 1 and tuple(ys) == (xs[2],))):
+        raise Unsupported("axis_reduce: x [batch, s, cols] -> out [batch, cols]")
+    batch, s_len, cols = xs
+    fold_ops = _fold_ops(node)
+    if fold_ops in ({"maximum"}, {"minimum"}, {"multiply"}):
+        op = {"maximum": "max", "minimum": "min", "multiply": "prod"}[fold_ops.pop()]
+        fold = {"max": np.max, "min": np.min, "prod": np.prod}[op]
+        cert = certify(node, kernel, args, inputs, outputs, lambda buf: {out: fold(buf[x], axis=1)})
+        return {"op": op, "x": x, "out": out, "batch": batch, "s": s_len, "cols": cols, "sum_div": 1.0,
+                "sum_div_buffer": None}, cert
+    if "add" not in fold_ops:
+        raise Unsupported("axis_reduce: no additive, max, min or product fold")
+    fitted = {}
+
+    def expect(buf, produced):
+        sums = buf[x].sum(axis=1).reshape(-1)
+        vals, written = produced[out]
+        ok = written & (np.abs(vals) > 1e-30)
+        if not ok.any():
+            raise Unsupported("axis_reduce: no output to fit")
+        fitted["div"] = float(np.median(sums[ok] / vals[ok]))
+        return {out: sums / fitted["div"]}
+
+    cert = certify(node, kernel, args, inputs, outputs, expect, fit=True)
+    div = fitted["div"]
+    certify(node, kernel, args, inputs, outputs, lambda buf: {out: buf[x].sum(axis=1) / div}, seed=777)
+    ptr = _bind_constant(args, scalars, div)
+    if abs(div - round(div)) < 1e-9 * max(1.0, abs(div)):
+        div = float(round(div))
+    return {"op": "sum", "x": x, "out": out, "batch": batch, "s": s_len, "cols": cols, "sum_div": div,
             "sum_div_buffer": ptr}, cert
 
 
@@ -613,6 +681,7 @@ FAMILIES = (
     ("attention", classify_attention),
     ("row_reduce", classify_row_reduce),
     ("row_norm", classify_row_norm),
+    ("axis_reduce", classify_axis_reduce),
 )
 
 

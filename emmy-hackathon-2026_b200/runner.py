@@ -21,7 +21,7 @@ from . import api, frontend, runtime
 
 DTYPES = {"f32": np.float32}
 PHASE_OF = {"pointwise": "pointwise", "row_softmax": "softmax", "matmul": "mma", "attention": "attention",
-            "row_reduce": "rows", "row_norm": "rows"}
+            "row_reduce": "rows", "row_norm": "rows", "axis_reduce": "rows"}
 
 
 def array_for(arg) -> np.ndarray:

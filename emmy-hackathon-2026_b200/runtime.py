@@ -45,7 +45,7 @@ class RowParams(C.Structure):
 ROW_SUM, ROW_RMSNORM, ROW_L2NORM, ROW_MAX, ROW_MIN, ROW_PROD = 0, 1, 2, 3, 4, 5
 
 
-KIND_POINTWISE, KIND_ROW_SOFTMAX, KIND_ROW_OP, KIND_GEMM, KIND_ATTENTION = 1, 2, 3, 4, 5
+KIND_POINTWISE, KIND_ROW_SOFTMAX, KIND_ROW_OP, KIND_GEMM, KIND_ATTENTION, KIND_AXIS_REDUCE = 1, 2, 3, 4, 5, 6
 MAX_ROLES, NO_ARG, ROLE_PW_OUT = 12, -1, 8
 
 
@@ -105,6 +105,9 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_selective_exp_f32": ([_P, _P, _P, _I64, _P], C.c_int),
     "b2k_row_op_f32": ([_P, C.POINTER(RowParams), _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
+    "b2k_gemm_tf32x3_scaled": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P, C.c_float,
+                                _P], C.c_int),
+    "b2k_axis_reduce_f32": ([_P, _I32, _P, _P, _I64, _I64, _I64, C.c_float, _P, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
     "b2k_gemm_set_streamk": ([C.c_int], C.c_int),
     "b2k_gemm_set_fused_split": ([C.c_int], C.c_int),
@@ -243,6 +246,12 @@ class Context:
         self.check(self.lib.b2k_row_op_f32(self.handle, C.byref(params), x, y, rows, cols, ld_x or cols,
                                            ld_y or cols, stream), "b2k_row_op_f32")
 
+    def axis_reduce(self, op: int, x: int, y: int, batch: int, s: int, cols: int, *, div: float = 1.0,
+                    div_ptr: int = 0, stream: int = 0) -> None:
+        """y[b][j] = fold over i < s of x[b][i][j] (ROW_SUM / ROW_MAX / ROW_MIN / ROW_PROD)."""
+        self.check(self.lib.b2k_axis_reduce_f32(self.handle, op, x, y, batch, s, cols, div, div_ptr or None, stream),
+                   "b2k_axis_reduce_f32")
+
     def selective_exp(self, x: int, y: int, n: int, stream: int = 0) -> None:
         self.check(self.lib.b2k_selective_exp_f32(self.handle, x, y, n, stream), "b2k_selective_exp_f32")
 
@@ -258,6 +267,14 @@ class Context:
              bias: int = 0, relu: bool = False, stream: int = 0) -> None:
         self.check(self.lib.b2k_gemm_tf32x3(*self._gemm_args(a, b, c, m, n, k, b_layout, lda, ldb, ldc, bias, relu,
                                                              stream)), "b2k_gemm_tf32x3")
+
+    def gemm_scaled(self, a: int, b: int, c: int, m: int, n: int, k: int, *, div_ptr: int = 0,
+                    div_value: float = 1.0, b_layout: int = B_KN, lda: int | None = None, ldb: int | None = None,
+                    ldc: int | None = None, bias: int = 0, relu: bool = False, stream: int = 0) -> None:
+        """C = relu?((A B) / div + bias), div = *div_ptr (device) or div_value."""
+        args = self._gemm_args(a, b, c, m, n, k, b_layout, lda, ldb, ldc, bias, relu, stream)
+        self.check(self.lib.b2k_gemm_tf32x3_scaled(*args[:-1], div_ptr or None, div_value, args[-1]),
+                   "b2k_gemm_tf32x3_scaled")
 
     def gemm_call(self, a: int, b: int, c: int, m: int, n: int, k: int, **kw) -> "BoundCall":
         """:meth:`gemm` with its arguments converted once (see :class:`BoundCall`)."""

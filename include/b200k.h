@@ -206,6 +206,15 @@ typedef struct b2k_row_params {
   const float *eps_ptr;
   const float *w;
 } b2k_row_params;
+/* Fold over the middle axis of x [batch][s][cols] (contiguous):
+ *   y[b][j] = fold_{i < s} x[b][i][j]      (y [batch][cols], contiguous)
+ * op: B2K_ROW_SUM (the sum divided by *div_ptr when non-NULL, else by div:
+ * a mean for div = s), B2K_ROW_MAX, B2K_ROW_MIN (IEEE maxNum / minNum) or
+ * B2K_ROW_PROD.  Each output folds i = 0, 1, ... in order, as the IR's serial
+ * Loop + Accum over that axis (the reference interpreter,
+ * tests/test_research_cases.py:103-160).  s = 0 gives the fold's identity. */
+int b2k_axis_reduce_f32(b2k_ctx *ctx, int32_t op, const float *x, float *y, int64_t batch, int64_t s, int64_t cols,
+                        float div, const float *div_ptr, void *stream);
 int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const float *x, float *y, int64_t rows,
                    int64_t cols, int64_t ld_x, int64_t ld_y, void *stream);
 
@@ -232,6 +241,17 @@ int b2k_selective_exp_f32(b2k_ctx *ctx, const float *x, float *y, int64_t n, voi
 int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                     int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
                     void *stream);
+
+/* b2k_gemm_tf32x3 with the product divided before the epilogue:
+ *   C = relu?((A B) / div + bias),  div = *div_ptr (a one-element device
+ *   buffer, read on the device) when div_ptr is non-NULL, else div_value.
+ * The division is FP32 round-to-nearest of each accumulated element, as the
+ * IR's `divide` of a contraction result (the scaled-score kernel of an
+ * attention pipeline: scores = x @ y / scale[0]).  Takes the pre-pass split
+ * path.  K = 0 returns B2K_EUNSUPPORTED. */
+int b2k_gemm_tf32x3_scaled(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                           int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
+                           const float *div_ptr, float div_value, void *stream);
 
 /* --- attention ----------------------------------------------------------------
  * Replaces the reference's fused SIMT attention lowering (compile.py:7009-7966:
@@ -274,6 +294,7 @@ int b2k_attention_set_fused(int mode);
 #define B2K_KIND_ROW_OP 3
 #define B2K_KIND_GEMM_3XTF32 4
 #define B2K_KIND_ATTENTION_3XTF32 5
+#define B2K_KIND_AXIS_REDUCE 6
 #define B2K_MAX_ROLES 12
 #define B2K_NO_ARG (-1)
 #define B2K_ROLE_PW_OUT 8
@@ -284,15 +305,17 @@ typedef struct b2k_kernel_desc {
    *   ROW_SOFTMAX 0 x, 1 y
    *   ROW_OP      0 x, 1 y, 2 weight, 3 sum-divisor buffer,
    *               4 mean-square-divisor buffer, 5 epsilon buffer
-   *   GEMM_3XTF32 0 A, 1 B, 2 C, 3 bias
-   *   ATTENTION   0 Q, 1 K, 2 V, 3 O, 4 divisor buffer */
+   *   GEMM_3XTF32 0 A, 1 B, 2 C, 3 bias, 4 divisor buffer (b2k_gemm_tf32x3_scaled)
+   *   ATTENTION   0 Q, 1 K, 2 V, 3 O, 4 divisor buffer
+   *   AXIS_REDUCE 0 x, 1 y, 3 divisor buffer */
   int32_t role[B2K_MAX_ROLES];
   /* POINTWISE: n | ROW_*: rows, cols, ld_x, ld_y | GEMM: m, n, k, lda, ldb, ldc |
-   * ATTENTION: bh, s_q, s_kv, d, dv */
+   * ATTENTION: bh, s_q, s_kv, d, dv | AXIS_REDUCE: batch, s, cols */
   int64_t dims[6];
-  /* GEMM: b_layout, relu | ATTENTION: k_layout | ROW_OP: op */
+  /* GEMM: b_layout, relu | ATTENTION: k_layout | ROW_OP, AXIS_REDUCE: op */
   int32_t flags[4];
-  /* ROW_OP: sum_div, ms_div, eps | ATTENTION: scale_div (when no buffer) */
+  /* ROW_OP: sum_div, ms_div, eps | ATTENTION: scale_div (when no buffer) |
+   * AXIS_REDUCE: sum divisor (when no buffer) */
   float values[4];
   const b2k_pw_program *program; /* POINTWISE */
 } b2k_kernel_desc;

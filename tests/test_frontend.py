@@ -17,7 +17,12 @@ RECOGNISED = {
     "a02_attention_128-69db4e7f597c": ["attention"],
     "atomic_matmul-0-b0bb43becf74": ["matmul"],
     "atomic_matmul_7x5x9-variant": ["matmul"],
-    "attention-0-9170e7b0641d": [None, "row_softmax", "matmul"],
+    "attention-0-9170e7b0641d": ["matmul", "row_softmax", "matmul"],
+    "canonical-tail-1575656197e9": ["axis_reduce"],
+    "canonical-tail-c37693f91a72": ["axis_reduce"],
+    "nondivisible-counter-21171f5ca6c3": ["axis_reduce"],
+    "short-ring-7bb9d9c27732": ["axis_reduce"],
+    "short-ring-b8c0079b7d44": ["axis_reduce"],
     "case-08-e4ac354528a2": ["row_reduce"],
     "case-14-fff293a2235c": ["row_reduce"],
     "case-22-da018f96fc2e": ["row_reduce"],
@@ -141,6 +146,30 @@ def test_matmul_over_k_prefix():
     spec = fe.compile_path(next((CASES / "case-7-72f1deeac451").glob("*.ir.json")))
     p = spec.params
     assert (spec.kind, p["m"], p["n"], p["k"], p["lda"], p["ldb"]) == ("matmul", 64, 32, 63, 65, 32)
+
+
+def test_scaled_scores_read_the_divisor_buffer():
+    """attention-0's first kernel is scores = x @ y / scale[0]: a GEMM whose
+    epilogue divides by the one-element buffer, read at run time."""
+    fe = pkg("frontend")
+    folder = CASES / "attention-0-9170e7b0641d"
+    spec = fe.compile_path(folder / "k_scores_238734.ir.json")
+    p = spec.params
+    assert (spec.kind, p["a"], p["b"], p["div_buffer"], p["m"], p["n"], p["k"]) == (
+        "matmul", "x_992187", "y_390031", "scale_236779", 3, 33, 33)
+    desc = spec.descriptor()
+    assert desc.role[4] == spec.arg_order.index("scale_236779")
+
+
+@pytest.mark.parametrize("name, batch, s, cols", [("canonical-tail-1575656197e9", 2, 9, 64),
+                                                  ("short-ring-b8c0079b7d44", 3, 1, 64)])
+def test_middle_axis_sum(name, batch, s, cols):
+    """out[b, j] = sum_i x[b, i, j], whatever ring or counter the IR stages it through."""
+    fe = pkg("frontend")
+    spec = fe.compile_path(next((CASES / name).glob("*.ir.json")))
+    p = spec.params
+    assert (spec.kind, p["op"], p["batch"], p["s"], p["cols"], p["sum_div"]) == ("axis_reduce", "sum", batch, s, cols,
+                                                                                  1.0)
 
 
 def test_matmul_prefix_needs_the_certificate(tmp_path):

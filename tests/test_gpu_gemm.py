@@ -196,3 +196,48 @@ def test_gemm_fused_split_special_values(ctx, torch_cuda):
     got = got[1]
     finite = np.setdiff1d(np.arange(128), [5, 9])
     np.testing.assert_array_equal(got[finite], (a[finite].astype(np.float64) @ b).astype(np.float32))
+
+
+@pytest.mark.parametrize("m,n,k,b_layout", [(3, 33, 33, 0), (300, 520, 200, 0), (1000, 257, 96, 1),
+                                            (4096, 1024, 512, 0)])
+def test_gemm_scaled_divides_before_the_epilogue(ctx, torch_cuda, m, n, k, b_layout):
+    """b2k_gemm_tf32x3_scaled: C = relu((A B) / div + bias), the divisor read
+    from a one-element device buffer or given by value."""
+    torch = torch_cuda
+    rng = np.random.default_rng(m + n + k)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    bm = (b if b_layout == 0 else b.T).astype(np.float64)
+    div = np.float32(5.7445626)  # sqrt(33)
+    da, db, dbias = dev(torch, a), dev(torch, b), dev(torch, bias)
+    ddiv = dev(torch, np.array([div], np.float32))
+    exact = np.maximum(a.astype(np.float64) @ bm / np.float64(div) + bias, 0.0)
+    for by_buffer in (True, False):
+        dc = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+        ctx.gemm_scaled(da.data_ptr(), db.data_ptr(), dc.data_ptr(), m, n, k, b_layout=b_layout,
+                        div_ptr=ddiv.data_ptr() if by_buffer else 0, div_value=1.0 if by_buffer else float(div),
+                        bias=dbias.data_ptr(), relu=True)
+        ctx.sync()
+        got = dc.cpu().numpy()
+        assert tf32.normwise_error(got, exact) <= NORMWISE, by_buffer
+        ok, bad, err = refs.allclose_report(got, exact.astype(np.float32), 1e-3, 1e-3)
+        assert ok, (bad, err)
+
+
+def test_gemm_scaled_with_unit_divisor_equals_gemm(ctx, torch_cuda):
+    """Dividing by a buffer holding 1 changes no bit of the pre-pass GEMM."""
+    torch = torch_cuda
+    rng = np.random.default_rng(11)
+    a, b = rng.uniform(-1, 1, (640, 300)).astype(np.float32), rng.uniform(-1, 1, (300, 384)).astype(np.float32)
+    da, db, one = dev(torch, a), dev(torch, b), dev(torch, np.ones(1, np.float32))
+    c1 = torch.empty((640, 384), device="cuda")
+    c2 = torch.empty((640, 384), device="cuda")
+    ctx.set_gemm_fused_split(0)
+    try:
+        ctx.gemm(da.data_ptr(), db.data_ptr(), c1.data_ptr(), 640, 384, 300)
+        ctx.gemm_scaled(da.data_ptr(), db.data_ptr(), c2.data_ptr(), 640, 384, 300, div_ptr=one.data_ptr())
+        ctx.sync()
+    finally:
+        ctx.set_gemm_fused_split(1)
+    assert torch.equal(c1, c2)

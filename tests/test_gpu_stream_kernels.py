@@ -186,3 +186,45 @@ def test_row_max_min_prod(ctx, torch_cuda, rows, cols):
     ctx.row_op(runtime.ROW_PROD, dn.data_ptr(), y.data_ptr(), rows, cols)
     ctx.sync()
     assert torch_cuda.equal(first, y)
+
+
+@pytest.mark.parametrize("batch,s,cols", [(2, 9, 64), (3, 1, 64), (1, 2, 32), (5, 300, 1000), (70000, 3, 5),
+                                          (4, 0, 7)])
+def test_axis_reduce(ctx, torch_cuda, batch, s, cols):
+    """Folds over the middle axis of [batch, s, cols]: the sum (and a mean
+    through a divisor buffer) in order over s, max / min exact, the product
+    within FP32 rounding; s = 0 gives each fold's identity."""
+    runtime = pkg("runtime")
+    rng = np.random.default_rng(batch + 7 * s + cols)
+    x = rng.standard_normal((batch, s, cols)).astype(np.float32)
+    near_one = (1.0 + rng.uniform(-1e-3, 1e-3, (batch, s, cols))).astype(np.float32)
+    dx, dn = dev(torch_cuda, x), dev(torch_cuda, near_one)
+    y = torch_cuda.full((batch, cols), float("nan"), device="cuda")
+
+    def run(op, src, **kw):
+        ctx.axis_reduce(op, src.data_ptr(), y.data_ptr(), batch, s, cols, **kw)
+        ctx.sync()
+        return y.cpu().numpy()
+
+    seq = np.zeros((batch, cols), np.float32)  # the serial FP32 fold the IR describes
+    for i in range(s):
+        seq = seq + x[:, i, :]
+    assert np.array_equal(run(runtime.ROW_SUM, dx), seq)
+    div = dev(torch_cuda, np.array([max(s, 1)], np.float32))
+    assert np.array_equal(run(runtime.ROW_SUM, dx, div_ptr=div.data_ptr()), seq / np.float32(max(s, 1)))
+    assert np.array_equal(run(runtime.ROW_SUM, dx, div=4.0), seq / np.float32(4.0))
+    want_max = x.max(axis=1) if s else np.full((batch, cols), -np.inf, np.float32)
+    want_min = x.min(axis=1) if s else np.full((batch, cols), np.inf, np.float32)
+    assert np.array_equal(run(runtime.ROW_MAX, dx), want_max)
+    assert np.array_equal(run(runtime.ROW_MIN, dx), want_min)
+    np.testing.assert_allclose(run(runtime.ROW_PROD, dn), near_one.astype(np.float64).prod(axis=1),
+                               rtol=max(s, 1) * 2.0 ** -23, atol=0)
+
+
+def test_axis_reduce_rejects_bad_arguments(ctx, torch_cuda):
+    runtime = pkg("runtime")
+    y = torch_cuda.empty(4, device="cuda")
+    with pytest.raises(runtime.B2KError):
+        ctx.axis_reduce(runtime.ROW_RMSNORM, y.data_ptr(), y.data_ptr(), 1, 1, 4)
+    with pytest.raises(runtime.B2KError):
+        ctx.axis_reduce(runtime.ROW_SUM, y.data_ptr(), y.data_ptr(), 1, -1, 4)

@@ -74,7 +74,16 @@ def test_compile_outside_the_families(server):
 
 
 def test_pipeline_with_an_unrecognised_kernel(server):
-    status, reply = _call(server, "/compile", _case_body("attention-0-9170e7b0641d"))
+    """attention-0 is recognised kernel by kernel; with its softmax's
+    exponentials turned into square roots one kernel matches no family and
+    the whole pipeline is refused."""
+    body = _case_body("attention-0-9170e7b0641d")
+    status, reply = _call(server, "/compile", body)
+    assert status == 200 and reply["ok"] and [k["kind"] for k in reply["kernels"]] == ["matmul", "row_softmax",
+                                                                                         "matmul"]
+    graph = json.dumps(body["irs"]["k_probs_104771"]).replace("ElementwiseImpl('exp')", "ElementwiseImpl('sqrt')")
+    body["irs"]["k_probs_104771"] = json.loads(graph)
+    status, reply = _call(server, "/compile", body)
     assert status == 200 and not reply["ok"] and reply["stage"] == "compile"
 
 
@@ -140,7 +149,7 @@ def test_run_given_and_seeded_inputs(server):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", ["m02_matmul_rect-aeb1568894b7", "f02_row_softmax-89d56c168a0b",
-                                  "a01_attention-c10866af73f8"])
+                                  "a01_attention-c10866af73f8", "attention-0-9170e7b0641d"])
 def test_run_matches_expected(server, name):
     oracle = pytest.importorskip("oracle.refs")
     folder = CASES / name
