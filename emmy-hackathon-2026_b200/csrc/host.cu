@@ -215,8 +215,20 @@ int b2k_pointwise_f32_host(b2k_ctx *ctx, const b2k_pw_program *program, const fl
   if (n == 0) return B2K_OK;
   for (int i = 0; i < program->n_inputs; ++i)
     if (!inputs[i]) return b2k::fail(ctx, B2K_EINVAL, "pointwise_host: null input %d", i);
+  for (int i = 0; i < program->n_inputs; ++i)
+    if (!program->broadcast[i] && program->offset[i] < 0)
+      return b2k::fail(ctx, B2K_EINVAL, "pointwise_host: input %d has a negative offset", i);
   cudaStream_t s = (cudaStream_t)stream;
   const int ni = program->n_inputs;
+  // Shifted windows are applied on the host side: each stream's slab is
+  // copied from its shifted start into compact device staging, and the
+  // device program reads the staging at offset 0.
+  b2k_pw_program staged = *program;
+  const float *src[B2K_PW_MAX_INPUTS] = {};
+  for (int i = 0; i < ni; ++i) {
+    src[i] = program->broadcast[i] ? inputs[i] : inputs[i] + program->offset[i];
+    staged.offset[i] = 0;
+  }
   b2k::Carve carve;
   size_t off_in[B2K_PW_MAX_INPUTS];
   size_t streamed = 0;
@@ -235,7 +247,7 @@ int b2k_pointwise_f32_host(b2k_ctx *ctx, const b2k_pw_program *program, const fl
   b2k::Pipe pipe(ctx, s);
   B2K_TRY(pipe.begin());
   for (int i = 0; i < ni; ++i)
-    if (program->broadcast[i]) B2K_TRY(pipe.in(base + off_in[i], 4, inputs[i], 4, 4, 1));
+    if (program->broadcast[i]) B2K_TRY(pipe.in(base + off_in[i], 4, src[i], 4, 4, 1));
   for (int64_t e0 = 0; e0 < n; e0 += per) {
     const int64_t ne = std::min(per, n - e0);
     const float *dev_in[B2K_PW_MAX_INPUTS];
@@ -244,13 +256,13 @@ int b2k_pointwise_f32_host(b2k_ctx *ctx, const b2k_pw_program *program, const fl
       if (program->broadcast[i]) {
         dev_in[i] = d;
       } else {
-        B2K_TRY(pipe.in(d + e0, (size_t)ne * 4, inputs[i] + e0, (size_t)ne * 4, (size_t)ne * 4, 1));
+        B2K_TRY(pipe.in(d + e0, (size_t)ne * 4, src[i] + e0, (size_t)ne * 4, (size_t)ne * 4, 1));
         dev_in[i] = d + e0;
       }
     }
     B2K_TRY(pipe.landed());
     float *dout = reinterpret_cast<float *>(base + off_out) + e0;
-    B2K_TRY(b2k_pointwise_f32(ctx, program, dev_in, dout, ne, stream));
+    B2K_TRY(b2k_pointwise_f32(ctx, &staged, dev_in, dout, ne, stream));
     B2K_TRY(pipe.computed());
     B2K_TRY(pipe.out(out + e0, (size_t)ne * 4, dout, (size_t)ne * 4, (size_t)ne * 4, 1));
   }

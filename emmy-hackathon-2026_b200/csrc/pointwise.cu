@@ -208,11 +208,16 @@ extern "C" int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, co
   params.out = out;
   params.n = n;
   bool vector_ok = b2k::aligned16(out);
+  // Each stream's first element: its base, shifted by the program's offset.
+  const float *in[B2K_PW_MAX_INPUTS] = {};
   for (int i = 0; i < B2K_PW_MAX_INPUTS; ++i) params.in[i] = nullptr;
   for (int i = 0; i < program->n_inputs; ++i) {
     if (!inputs[i]) return b2k::fail(ctx, B2K_EINVAL, "pointwise: input %d is null", i);
-    params.in[i] = inputs[i];
-    if (!program->broadcast[i]) vector_ok = vector_ok && b2k::aligned16(inputs[i]);
+    if (!program->broadcast[i] && program->offset[i] < 0)
+      return b2k::fail(ctx, B2K_EINVAL, "pointwise: input %d has a negative offset", i);
+    in[i] = program->broadcast[i] ? inputs[i] : inputs[i] + program->offset[i];
+    params.in[i] = in[i];
+    if (!program->broadcast[i]) vector_ok = vector_ok && b2k::aligned16(in[i]);
   }
   cudaStream_t s = (cudaStream_t)stream;
   b2k::PhaseTimer timer(ctx, B2K_PHASE_POINTWISE, s);
@@ -223,7 +228,7 @@ extern "C" int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, co
     const int64_t per_block = (int64_t)kThreads * kUnroll;
     const int64_t blocks = (n4 + per_block - 1) / per_block;
     if (blocks > INT32_MAX) return b2k::fail(ctx, B2K_EINVAL, "pointwise: extent too large");
-    if (!launch_binary_fast(*program, inputs, out, n4, (int)blocks, s))
+    if (!launch_binary_fast(*program, in, out, n4, (int)blocks, s))
       b2k::launch_kernel(b2k::pdl_enabled(), pw_program_vec4, dim3((unsigned)blocks), dim3(kThreads), 0, s, params);
     done = n4 << 2;
     ++launches;

@@ -70,7 +70,8 @@ class KernelSpec:
         p, pos = self.params, {name: i for i, name in enumerate(self.arg_order)}
         if self.kind == "pointwise":
             prog = rt.make_program(len(p["inputs"]), [tuple(i) for i in p["insns"]], p["result"],
-                                   broadcast=tuple(i for i, b in enumerate(p["broadcast"]) if b))
+                                   broadcast=tuple(i for i, b in enumerate(p["broadcast"]) if b),
+                                   offsets=tuple(p.get("offsets", ())))
             roles = {i: pos[n] for i, n in enumerate(p["inputs"])}
             roles[rt.ROLE_PW_OUT] = pos[p["output"]]
             return rt.make_desc(rt.KIND_POINTWISE, roles, dims=(p["n"],), program=prog)
@@ -282,11 +283,43 @@ _PW_OPS = {"add", "subtract", "multiply", "divide", "maximum", "minimum", "negat
            "rsqrt", "exp", "relu", "abs", "copy", "greater", "greater_equal", "less", "less_equal", "where"}
 
 
+def _affine(expr, axis):
+    """(coefficient, constant) of an index expression that is affine in the
+    Tile axis ``axis`` (Var, integer Literal, +, -, *), else None."""
+    def ev(e, x):
+        if isinstance(e, Node):
+            if e.kind == "Literal" and isinstance(e.value, int) and not isinstance(e.value, bool):
+                return e.value
+            if e.kind == "Var" and e.name == axis:
+                return x
+            if e.kind == "BinaryExpr" and e.op in ("+", "-", "*"):
+                a, b = ev(e.left, x), ev(e.right, x)
+                if a is None or b is None:
+                    return None
+                return a + b if e.op == "+" else a - b if e.op == "-" else a * b
+        return None
+    f0, f1, f2 = ev(expr, 0), ev(expr, 1), ev(expr, 2)
+    if f0 is None or f1 is None or f2 is None or f2 - f1 != f1 - f0:
+        return None
+    return f1 - f0, f0
+
+
 def _pointwise_program(node, args, inputs, output):
-    """Straight-line per-element program of a pointwise Tile (lane 0 of its write)."""
+    """Straight-line per-element program of a pointwise Tile.
+
+    Lanes of a vector group (grouped loads and writes of k adjacent elements,
+    or unrolled copies) are matched by element position: a load of element
+    ``c x + d + k`` feeding the value written at ``c x + w + k`` reads its
+    input at offset ``d - w`` from the output element (the runtime-aligned
+    vector groups of compile.py:1425-1600, 8586-8661, including windows that
+    start off the vector boundary).  Every written value must compute the
+    same program."""
     if len(node.body) != 1 or node.body[0].kind != "Tile":
         raise Unsupported("pointwise: body is not one Tile")
     tile = node.body[0]
+    axes = tile.axes
+    axis = axes[0].name if len(axes) == 1 else None
+    n_out = _size(_shape(args[output]))
     defs: dict = {}
     writes = []
 
@@ -299,11 +332,18 @@ def _pointwise_program(node, args, inputs, output):
             else:
                 yield st
 
+    def position(index):
+        if axis is None or len(index) != 1:
+            return None
+        return _affine(index[0], axis)
+
     for s in flatten(tile.body):
         if s.kind == "Load":
-            if len(s.names) != 1:
-                raise Unsupported("pointwise: grouped load")
-            defs[s.names[0]] = ("in", s.input)
+            pos = position(s.index)
+            for k, name in enumerate(s.names):
+                defs[name] = ("load", s.input, None if pos is None else (pos[0], pos[1] + k))
+            if len(s.names) > 1 and pos is None:
+                raise Unsupported("pointwise: grouped load at a non-affine index")
         elif s.kind == "Let":
             if isinstance(s.value, Node) and s.value.kind == "Literal" and isinstance(s.value.value, (int, float)):
                 defs[s.name] = ("const", float(s.value.value))
@@ -312,29 +352,58 @@ def _pointwise_program(node, args, inputs, output):
         elif s.kind == "Assign":
             if s.op.name not in _PW_OPS:
                 raise Unsupported(f"pointwise: op {s.op.name!r}")
-            defs[s.name] = ("op", s.op.name, tuple(defs[a] for a in s.args))
+            defs[s.name] = ("op", s.op.name, tuple(s.args))
         elif s.kind == "Write":
             if s.output != output or s.get("atomic"):
                 raise Unsupported("pointwise: unexpected write")
-            writes.append(s)
+            pos = position(s.index)
+            for k, v in enumerate(s.values):
+                writes.append((v, None if pos is None else (pos[0], pos[1] + k)))
         else:
             raise Unsupported(f"pointwise: statement {s.kind}")
     if not writes:
         raise Unsupported("pointwise: no write")
-    trees = [defs[v] for w in writes for v in w.values]
+
+    def tree(name, wpos):
+        d = defs.get(name)
+        if d is None:
+            raise Unsupported(f"pointwise: {name!r} is not defined in the Tile")
+        if d[0] == "const":
+            return d
+        if d[0] == "op":
+            return ("op", d[1], tuple(tree(a, wpos) for a in d[2]))
+        src, lpos = d[1], d[2]
+        if _size(_shape(args[src])) == 1 and n_out != 1:
+            return ("in", src, 0)                       # scalar buffer: broadcast
+        if lpos is None or wpos is None:
+            return ("in", src, 0)                       # elementwise by position; the certificate decides
+        if lpos[0] != wpos[0]:
+            raise Unsupported("pointwise: load and write advance at different strides")
+        return ("in", src, lpos[1] - wpos[1])
+
+    trees = [tree(v, wpos) for v, wpos in writes]
     if any(t != trees[0] for t in trees):
         raise Unsupported("pointwise: lanes compute different programs")
-    # compile lane 0's tree into the register program of b2k_pointwise_f32
-    order: list = []
-    slots: dict = {}
+
+    leaves: set = set()
+
+    def collect(t):
+        if t[0] == "in":
+            leaves.add((t[1], t[2]))
+        elif t[0] == "op":
+            for c in t[2]:
+                collect(c)
+    collect(trees[0])
+    # one input stream per (buffer, window offset), in argument order
+    streams = sorted(leaves, key=lambda sw: (inputs.index(sw[0]), sw[1]))
     insns: list = []
-    streams = [n for n in inputs]
+    slots: dict = {}
 
     def emit(t):
         if t in slots:
             return slots[t]
         if t[0] == "in":
-            return streams.index(t[1])
+            return streams.index((t[1], t[2]))
         if t[0] == "const":
             insns.append(("const", 0, 0, 0, t[1]))
         else:
@@ -345,15 +414,20 @@ def _pointwise_program(node, args, inputs, output):
         return slots[t]
 
     result = emit(trees[0])
-    broadcast = [1 if _size(_shape(args[n])) == 1 and _size(_shape(args[output])) != 1 else 0 for n in streams]
-    return {"inputs": streams, "insns": insns, "result": result, "broadcast": broadcast, "output": output,
-            "n": _size(_shape(args[output]))}
+    names = [name for name, _ in streams]
+    offsets = [off for _, off in streams]
+    broadcast = [1 if _size(_shape(args[nm])) == 1 and n_out != 1 else 0 for nm in names]
+    return {"inputs": names, "offsets": offsets, "insns": insns, "result": result, "broadcast": broadcast,
+            "output": output, "n": n_out}
 
 
 def _eval_program(params, buffers):
     n = params["n"]
-    regs = [np.broadcast_to(buffers[name].reshape(-1)[:1] if b else buffers[name].reshape(-1), (n,))
-            for name, b in zip(params["inputs"], params["broadcast"])]
+    regs = []
+    for name, off, b in zip(params["inputs"], params.get("offsets", [0] * len(params["inputs"])),
+                            params["broadcast"]):
+        flat = buffers[name].reshape(-1)
+        regs.append(np.broadcast_to(flat[:1], (n,)) if b else flat[off:off + n])
     for op, a, b, c, imm in params["insns"]:
         if op == "const":
             regs.append(np.full(n, imm))
@@ -367,12 +441,13 @@ def classify_pointwise(node, kernel, args, inputs, outputs):
         raise Unsupported("pointwise: needs inputs and one output")
     out = outputs[0]
     n = _size(_shape(args[out]))
-    for name in inputs:
-        if _size(_shape(args[name])) not in (1, n):
-            raise Unsupported("pointwise: input size differs from the output's")
-    if len(inputs) > 8:
-        raise Unsupported("pointwise: more than 8 input streams")
     params = _pointwise_program(node, args, inputs, out)
+    if len(params["inputs"]) > 8:
+        raise Unsupported("pointwise: more than 8 input streams")
+    for name, off, b in zip(params["inputs"], params["offsets"], params["broadcast"]):
+        size = _size(_shape(args[name]))
+        if not b and (off < 0 or size < n + off or (off == 0 and size != n)):
+            raise Unsupported("pointwise: input size differs from the output's")
     cert = certify(node, kernel, args, inputs, outputs, lambda b: {out: _eval_program(params, b)})
     return params, cert
 

@@ -80,7 +80,8 @@ class PwInsn(C.Structure):
 
 class PwProgram(C.Structure):
     _fields_ = [("n_inputs", C.c_int32), ("n_insns", C.c_int32), ("result", C.c_int32),
-                ("broadcast", C.c_int32 * PW_MAX_INPUTS), ("insns", PwInsn * PW_MAX_INSNS)]
+                ("broadcast", C.c_int32 * PW_MAX_INPUTS), ("offset", C.c_int32 * PW_MAX_INPUTS),
+                ("insns", PwInsn * PW_MAX_INSNS)]
 
 
 _P, _I32, _I64, _SZ, _F = C.c_void_p, C.c_int32, C.c_int64, C.c_size_t, C.c_float
@@ -154,14 +155,16 @@ def exported_symbols() -> list[str]:
     return list(SIGNATURES)
 
 
-def make_program(n_inputs: int, insns: list[tuple], result: int, broadcast=()) -> PwProgram:
-    """Build a :class:`PwProgram`; ``insns`` are ``(opname, a, b, c, imm)`` tuples."""
+def make_program(n_inputs: int, insns: list[tuple], result: int, broadcast=(), offsets=()) -> PwProgram:
+    """Build a :class:`PwProgram`; ``insns`` are ``(opname, a, b, c, imm)`` tuples;
+    ``offsets[r]`` shifts input stream r's window (element i reads i + offset)."""
     if n_inputs > PW_MAX_INPUTS or len(insns) > PW_MAX_INSNS:
         raise ValueError("pointwise program exceeds the kernel's register budget")
     prog = PwProgram()
     prog.n_inputs, prog.n_insns, prog.result = n_inputs, len(insns), result
     for i in range(PW_MAX_INPUTS):
         prog.broadcast[i] = 1 if i in tuple(broadcast) else 0
+        prog.offset[i] = int(offsets[i]) if i < len(offsets) else 0
     for i, (op, a, b, c, imm) in enumerate(insns):
         prog.insns[i] = PwInsn(OPCODES[op] if isinstance(op, str) else int(op), a, b, c, float(imm))
     return prog

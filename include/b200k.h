@@ -158,12 +158,17 @@ typedef struct b2k_pw_program {
   int32_t n_insns;                         /* instructions; insn i writes register n_inputs+i */
   int32_t result;                          /* register stored to the output */
   int32_t broadcast[B2K_PW_MAX_INPUTS];    /* 1: input is a scalar buffer read at element 0 */
+  int32_t offset[B2K_PW_MAX_INPUTS];       /* >= 0: input i is read at element i + offset[i]
+                                              (a shifted window; ignored for broadcast inputs) */
   b2k_pw_insn insns[B2K_PW_MAX_INSNS];
 } b2k_pw_program;
 
-/* out[i] = program(inputs[0][i], inputs[1][i], ...) for i in [0, n).
- * Non-broadcast inputs and out must hold n FP32 elements; 16-byte vector
- * accesses are used when every stream is 16-byte aligned. */
+/* out[i] = program(inputs[0][i + offset[0]], inputs[1][i + offset[1]], ...)
+ * for i in [0, n).  Non-broadcast input r must hold n + offset[r] FP32
+ * elements, out n; 16-byte vector accesses are used when every stream (its
+ * base plus offset) is 16-byte aligned, element accesses otherwise -- the
+ * runtime alignment fallback of the reference's vector groups
+ * (compile.py:1425-1600, 8586-8661). */
 int b2k_pointwise_f32(b2k_ctx *ctx, const b2k_pw_program *program, const float *const *inputs,
                       float *out, int64_t n, void *stream);
 

@@ -27,6 +27,7 @@ RECOGNISED = {
     "case-14-fff293a2235c": ["row_reduce"],
     "case-22-da018f96fc2e": ["row_reduce"],
     "case-30-061d7084b729": ["row_reduce"],
+    "case-4-b24c76efd4ba": ["pointwise"],
     "case-7-72f1deeac451": ["matmul"],
     "f01_rmsnorm-6ab09ab4acc3": ["row_norm"],
     "f02-extra-cta-120bf007fb2d": ["row_softmax"],
@@ -146,6 +147,18 @@ def test_matmul_over_k_prefix():
     spec = fe.compile_path(next((CASES / "case-7-72f1deeac451").glob("*.ir.json")))
     p = spec.params
     assert (spec.kind, p["m"], p["n"], p["k"], p["lda"], p["ldb"]) == ("matmul", 64, 32, 63, 65, 32)
+
+
+def test_vector_group_windows():
+    """case-4 loads 4-wide groups at elements 4c + 1 and 4c + 2 and writes at
+    4c: out[i] = x[i + 1] + y[i + 2], two streams with window offsets."""
+    fe = pkg("frontend")
+    spec = fe.compile_path(next((CASES / "case-4-b24c76efd4ba").glob("*.ir.json")))
+    p = spec.params
+    assert dict(zip(p["inputs"], p["offsets"])) == {"x_799729": 1, "y_221412": 2}
+    assert p["n"] == 260 and p["insns"] == [("add", 1, 0, 0, 0.0)]
+    prog = spec.descriptor().program
+    assert prog is not None
 
 
 def test_scaled_scores_read_the_divisor_buffer():

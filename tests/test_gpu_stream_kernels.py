@@ -228,3 +228,28 @@ def test_axis_reduce_rejects_bad_arguments(ctx, torch_cuda):
         ctx.axis_reduce(runtime.ROW_RMSNORM, y.data_ptr(), y.data_ptr(), 1, 1, 4)
     with pytest.raises(runtime.B2KError):
         ctx.axis_reduce(runtime.ROW_SUM, y.data_ptr(), y.data_ptr(), 1, -1, 4)
+
+
+@pytest.mark.parametrize("n", [260, 1 << 20, 1000003])
+def test_pointwise_windows(ctx, torch_cuda, n):
+    """Input streams read at element offsets (shifted windows): out[i] =
+    x[i + 1] * y[i + 2] + x[i], bit-exact against NumPy, through the device
+    entry point and the host-array call."""
+    runtime = pkg("runtime")
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal(n + 1).astype(np.float32)
+    y = rng.standard_normal(n + 2).astype(np.float32)
+    prog = runtime.make_program(3, [("multiply", 0, 1, 0, 0.0), ("add", 3, 2, 0, 0.0)], 4, offsets=(1, 2, 0))
+    want = x[1:n + 1] * y[2:n + 2] + x[:n]
+    dx, dy = dev(torch_cuda, x), dev(torch_cuda, y)
+    out = torch_cuda.empty(n, device="cuda")
+    ctx.pointwise(prog, [dx.data_ptr(), dy.data_ptr(), dx.data_ptr()], out.data_ptr(), n)
+    ctx.sync()
+    assert np.array_equal(out.cpu().numpy(), want)
+    got = np.empty(n, np.float32)
+    ctx.pointwise_host(prog, [x.ctypes.data, y.ctypes.data, x.ctypes.data], got.ctypes.data, n)
+    ctx.sync()
+    assert np.array_equal(got, want)
+    bad = runtime.make_program(1, [("copy", 0, 0, 0, 0.0)], 1, offsets=(-1,))
+    with pytest.raises(runtime.B2KError):
+        ctx.pointwise(bad, [dx.data_ptr()], out.data_ptr(), n)
