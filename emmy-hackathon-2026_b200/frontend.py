@@ -82,9 +82,11 @@ class KernelSpec:
             roles = {0: pos[p["a"]], 1: pos[p["b"]], 2: pos[p["out"]]}
             if p.get("div_buffer"):
                 roles[4] = pos[p["div_buffer"]]
+            b_nk = p.get("b_nk", False)
             return rt.make_desc(rt.KIND_GEMM, roles,
-                                dims=(p["m"], p["n"], p["k"], p.get("lda", p["k"]), p.get("ldb", p["n"]), p["n"]),
-                                flags=(rt.B_KN, 0))
+                                dims=(p["m"], p["n"], p["k"], p.get("lda", p["k"]),
+                                      p.get("ldb", p["k"] if b_nk else p["n"]), p["n"]),
+                                flags=(rt.B_NK if b_nk else rt.B_KN, 0))
         if self.kind == "attention":
             return rt.make_desc(rt.KIND_ATTENTION, {0: pos[p["q"]], 1: pos[p["kt"]], 2: pos[p["v"]],
                                                     3: pos[p["out"]], 4: pos[p["scale"]]},
@@ -484,16 +486,20 @@ def classify_matmul(node, kernel, args, inputs, outputs):
         raise Unsupported("matmul: two rank-2 inputs (and at most a one-element divisor)")
     div = extra[0] if extra else None
 
-    def product(buf, a, b, k):
-        c = buf[a][:, :k] @ buf[b][:k, :]
+    def product(buf, a, b, k, b_nk):
+        c = buf[a][:, :k] @ (buf[b][:, :k].T if b_nk else buf[b][:k, :])
         return c / float(buf[div].reshape(-1)[0]) if div else c
     oshape = _shape(args[out])
     if len(oshape) != 2:
         raise Unsupported("matmul: rank-2 output")
     last = None
-    for a, b in ((mats[0], mats[1]), (mats[1], mats[0])):
+    # B stored [K, N] (b_nk False) or transposed [N, K] (the IR's y^T), each
+    # operand order; square shapes fit several and the certificate decides.
+    for a, b, b_nk in ((mats[0], mats[1], False), (mats[1], mats[0], False),
+                       (mats[0], mats[1], True), (mats[1], mats[0], True)):
         sa, sb = _shape(args[a]), _shape(args[b])
-        if sa[1] != sb[0] or (sa[0], sb[1]) != oshape:
+        kb, nb = (sb[1], sb[0]) if b_nk else (sb[0], sb[1])
+        if sa[1] != kb or (sa[0], nb) != oshape:
             continue
         # The whole shared dimension first; then, if the IR bounds its K loop
         # below it (a guard ``kk < 63`` over 65 columns), each static integer
@@ -503,12 +509,12 @@ def classify_matmul(node, kernel, args, inputs, outputs):
         for k in [sa[1]] + prefixes:
             try:
                 cert = certify(node, kernel, args, inputs, outputs,
-                               lambda buf, k=k, a=a, b=b: {out: product(buf, a, b, k)})
+                               lambda buf, k=k, a=a, b=b, t=b_nk: {out: product(buf, a, b, k, t)})
             except Unsupported as exc:
                 last = last or exc
                 continue
-            return {"a": a, "b": b, "out": out, "m": sa[0], "n": sb[1], "k": k, "lda": sa[1], "ldb": sb[1],
-                    "div_buffer": div}, cert
+            return {"a": a, "b": b, "out": out, "m": sa[0], "n": nb, "k": k, "lda": sa[1], "ldb": sb[1],
+                    "b_nk": b_nk, "div_buffer": div}, cert
     raise last or Unsupported("matmul: operand shapes do not contract to the output")
 
 

@@ -161,6 +161,41 @@ def test_vector_group_windows():
     assert prog is not None
 
 
+def transposed_matmul_case(tmp_path):
+    """matmul-2 rewritten to read its right operand transposed: y stored
+    [16, 31] and loaded at (col, kk), so out = x @ y^T."""
+    folder = _copy_case(tmp_path, "matmul-2-cc1c8cef5b4d")
+    path = next(folder.glob("*.ir.json"))
+    graph = json.loads(path.read_text())
+    graph["nodes"]["y_637842"]["outputs"][0]["shape"] = [16, 31]
+    body = graph["nodes"]["out_511255"]["op_fields"]["body"][0]
+    old = "input='y_637842', index=(Var(name='kk'), Var(name='col'))"
+    assert old in body
+    graph["nodes"]["out_511255"]["op_fields"]["body"][0] = body.replace(
+        old, "input='y_637842', index=(Var(name='col'), Var(name='kk'))")
+    path.write_text(json.dumps(graph))
+    meta = json.loads((folder / "meta.json").read_text())
+    for arg in meta["kernels"][0]["args"]:
+        if arg["name"] == "y_637842":
+            arg["shape"] = [16, 31]
+    (folder / "meta.json").write_text(json.dumps(meta))
+    for name in ("inputs.npz", "expected.npz"):
+        (folder / name).unlink()
+    return folder, path
+
+
+def test_matmul_with_transposed_operand(tmp_path):
+    fe = pkg("frontend")
+    rt = pkg("runtime")
+    _, path = transposed_matmul_case(tmp_path)
+    spec = fe.compile_path(path)
+    p = spec.params
+    assert (spec.kind, p["a"], p["b"], p["b_nk"], p["m"], p["n"], p["k"], p["ldb"]) == (
+        "matmul", "x_786334", "y_637842", True, 3, 16, 31, 31)
+    desc = spec.descriptor()
+    assert desc.flags[0] == rt.B_NK and tuple(desc.dims[:6]) == (3, 16, 31, 31, 31, 16)
+
+
 def test_scaled_scores_read_the_divisor_buffer():
     """attention-0's first kernel is scores = x @ y / scale[0]: a GEMM whose
     epilogue divides by the one-element buffer, read at run time."""

@@ -53,3 +53,19 @@ def test_runner_seeded_request(session):
     x1 = np.random.default_rng(1).standard_normal(1024).astype(np.float32)
     assert result["outputs"]["add"]["values"] == (x0 + x1).tolist()
     assert result["median_us"] is not None and result["median_us"] > 0
+
+
+def test_transposed_operand_matmul_runs(session, tmp_path):
+    """A recognised x @ y^T (y stored [n, k]) through the runner on the GPU
+    against float64 at the matmul tolerance."""
+    from test_frontend import transposed_matmul_case
+    runner = pkg("runner")
+    folder, _ = transposed_matmul_case(tmp_path)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((3, 31)).astype(np.float32)
+    y = rng.standard_normal((16, 31)).astype(np.float32)
+    result, arrays = runner.Pipeline(folder).run(session, inputs={"x_786334": x, "y_637842": y}, warmup=1, iters=2)
+    assert result["ok"] and result["kernels"] == ["matmul"]
+    want = x.astype(np.float64) @ y.astype(np.float64).T
+    ok, bad, err = refs.allclose_report(arrays["out_511255"].reshape(3, 16), want.astype(np.float32), 1e-3, 1e-3)
+    assert ok, (bad, err)
