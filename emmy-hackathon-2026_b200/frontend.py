@@ -82,11 +82,13 @@ class KernelSpec:
             roles = {0: pos[p["a"]], 1: pos[p["b"]], 2: pos[p["out"]]}
             if p.get("div_buffer"):
                 roles[4] = pos[p["div_buffer"]]
+            if p.get("bias"):
+                roles[3] = pos[p["bias"]]
             b_nk = p.get("b_nk", False)
             return rt.make_desc(rt.KIND_GEMM, roles,
                                 dims=(p["m"], p["n"], p["k"], p.get("lda", p["k"]),
                                       p.get("ldb", p["k"] if b_nk else p["n"]), p["n"]),
-                                flags=(rt.B_NK if b_nk else rt.B_KN, 0))
+                                flags=(rt.B_NK if b_nk else rt.B_KN, int(bool(p.get("relu")))))
         if self.kind == "attention":
             return rt.make_desc(rt.KIND_ATTENTION, {0: pos[p["q"]], 1: pos[p["kt"]], 2: pos[p["v"]],
                                                     3: pos[p["out"]], 4: pos[p["scale"]]},
@@ -480,18 +482,30 @@ def classify_matmul(node, kernel, args, inputs, outputs):
         raise Unsupported("matmul: one output")
     out = outputs[0]
     mats = [n for n in inputs if len(_shape(args[n])) == 2]
-    # An optional one-element buffer divides the product (scores = x @ y / scale[0]).
-    extra = [n for n in inputs if n not in mats]
-    if len(mats) != 2 or len(extra) > 1 or (extra and _size(_shape(args[extra[0]])) != 1):
-        raise Unsupported("matmul: two rank-2 inputs (and at most a one-element divisor)")
-    div = extra[0] if extra else None
-
-    def product(buf, a, b, k, b_nk):
-        c = buf[a][:, :k] @ (buf[b][:, :k].T if b_nk else buf[b][:k, :])
-        return c / float(buf[div].reshape(-1)[0]) if div else c
     oshape = _shape(args[out])
     if len(oshape) != 2:
         raise Unsupported("matmul: rank-2 output")
+    # Epilogue operands the GEMM applies in this order: a one-element divisor
+    # (scores = x @ y / scale[0]), a bias over the output columns, then ReLU
+    # when the IR applies one (tf32_emitter's plans carry only `copy`; the C
+    # ABI's epilogue is the ragged config's bias + ReLU).
+    extra = [n for n in inputs if n not in mats]
+    divs = [n for n in extra if _size(_shape(args[n])) == 1]
+    biases = [n for n in extra if n not in divs and _shape(args[n]) == (oshape[1],)]
+    if len(mats) != 2 or len(divs) > 1 or len(biases) > 1 or len(divs) + len(biases) != len(extra):
+        raise Unsupported("matmul: two rank-2 inputs (and at most a divisor and a bias)")
+    div = divs[0] if divs else None
+    bias = biases[0] if biases else None
+    ops = {s.op.name for s in walk(node.body) if s.kind == "Assign"}
+    relus = (False, True) if ops & {"relu", "maximum"} else (False,)
+
+    def product(buf, a, b, k, b_nk, relu):
+        c = buf[a][:, :k] @ (buf[b][:, :k].T if b_nk else buf[b][:k, :])
+        if div:
+            c = c / float(buf[div].reshape(-1)[0])
+        if bias:
+            c = c + buf[bias].reshape(1, -1)
+        return np.maximum(c, 0.0) if relu else c
     last = None
     # B stored [K, N] (b_nk False) or transposed [N, K] (the IR's y^T), each
     # operand order; square shapes fit several and the certificate decides.
@@ -506,15 +520,15 @@ def classify_matmul(node, kernel, args, inputs, outputs):
         # of the body smaller than K, largest first, as a prefix contraction
         # A[:, :k] @ B[:k, :] -- the GEMM reads it through lda / ldb.
         prefixes = sorted((v for v in _int_literals(node.body) if 0 < v < sa[1]), reverse=True)[:PREFIX_CANDIDATES]
-        for k in [sa[1]] + prefixes:
+        for k, relu in [(k, r) for k in [sa[1]] + prefixes for r in relus]:
             try:
                 cert = certify(node, kernel, args, inputs, outputs,
-                               lambda buf, k=k, a=a, b=b, t=b_nk: {out: product(buf, a, b, k, t)})
+                               lambda buf, k=k, a=a, b=b, t=b_nk, r=relu: {out: product(buf, a, b, k, t, r)})
             except Unsupported as exc:
                 last = last or exc
                 continue
             return {"a": a, "b": b, "out": out, "m": sa[0], "n": nb, "k": k, "lda": sa[1], "ldb": sb[1],
-                    "b_nk": b_nk, "div_buffer": div}, cert
+                    "b_nk": b_nk, "div_buffer": div, "bias": bias, "relu": relu}, cert
     raise last or Unsupported("matmul: operand shapes do not contract to the output")
 
 

@@ -184,6 +184,55 @@ def transposed_matmul_case(tmp_path):
     return folder, path
 
 
+F32 = "DataType(name='f32', np=dtype('float32'), nbytes=4)"
+
+
+def bias_relu_matmul_case(tmp_path, relu=True):
+    """matmul-2 rewritten with the ragged config's epilogue: out =
+    relu(x @ y + bias[col]) (or without the ReLU), bias a [16] input."""
+    folder = _copy_case(tmp_path, "matmul-2-cc1c8cef5b4d")
+    path = next(folder.glob("*.ir.json"))
+    graph = json.loads(path.read_text())
+    node = graph["nodes"]["out_511255"]
+    body = node["op_fields"]["body"][0]
+    write = "Write(output='out_511255', index=(Var(name='row'), Var(name='col')), values=('total',)"
+    assert write in body
+    epilogue = (f"Load(names=('bv',), input='bias_1', index=(Var(name='col'),), dtype={F32}), "
+                f"Assign(name='biased', op=ElementwiseImpl('add'), args=('total', 'bv'), dtype={F32}), ")
+    result = "biased"
+    if relu:
+        epilogue += f"Assign(name='act', op=ElementwiseImpl('relu'), args=('biased',), dtype={F32}), "
+        result = "act"
+    node["op_fields"]["body"][0] = body.replace(
+        write, epilogue + f"Write(output='out_511255', index=(Var(name='row'), Var(name='col')), values=('{result}',)")
+    node["inputs"].append("bias_1")
+    graph["inputs"].append("bias_1")
+    graph["nodes"]["bias_1"] = {"inputs": [], "op": "InputOp", "op_fields": {},
+                                "outputs": [{"dtype": "f32", "name": "bias_1", "shape": [16]}]}
+    path.write_text(json.dumps(graph))
+    meta = json.loads((folder / "meta.json").read_text())
+    meta["graph_inputs"].append("bias_1")
+    kernel = meta["kernels"][0]
+    kernel["arg_order"].insert(1, "bias_1")
+    kernel["args"].append({"dtype": "f32", "name": "bias_1", "shape": [16]})
+    (folder / "meta.json").write_text(json.dumps(meta))
+    for name in ("inputs.npz", "expected.npz"):
+        (folder / name).unlink()
+    return folder, path
+
+
+@pytest.mark.parametrize("relu", [True, False])
+def test_matmul_bias_relu_epilogue(tmp_path, relu):
+    fe = pkg("frontend")
+    rt = pkg("runtime")
+    _, path = bias_relu_matmul_case(tmp_path, relu)
+    spec = fe.compile_path(path)
+    p = spec.params
+    assert (spec.kind, p["bias"], p["relu"], p["b_nk"]) == ("matmul", "bias_1", relu, False)
+    desc = spec.descriptor()
+    assert desc.role[3] == spec.arg_order.index("bias_1") and desc.flags[1] == int(relu)
+
+
 def test_matmul_with_transposed_operand(tmp_path):
     fe = pkg("frontend")
     rt = pkg("runtime")

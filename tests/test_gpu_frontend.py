@@ -69,3 +69,22 @@ def test_transposed_operand_matmul_runs(session, tmp_path):
     want = x.astype(np.float64) @ y.astype(np.float64).T
     ok, bad, err = refs.allclose_report(arrays["out_511255"].reshape(3, 16), want.astype(np.float32), 1e-3, 1e-3)
     assert ok, (bad, err)
+
+
+@pytest.mark.parametrize("relu", [True, False])
+def test_bias_relu_matmul_runs(session, tmp_path, relu):
+    """A recognised relu(x @ y + bias) IR through the runner on the GPU."""
+    from test_frontend import bias_relu_matmul_case
+    runner = pkg("runner")
+    folder, _ = bias_relu_matmul_case(tmp_path, relu)
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((3, 31)).astype(np.float32)
+    y = rng.standard_normal((31, 16)).astype(np.float32)
+    bias = rng.standard_normal(16).astype(np.float32)
+    result, arrays = runner.Pipeline(folder).run(session, inputs={"x_786334": x, "y_637842": y, "bias_1": bias},
+                                                 warmup=1, iters=2)
+    assert result["ok"]
+    want = x.astype(np.float64) @ y.astype(np.float64) + bias
+    want = np.maximum(want, 0.0) if relu else want
+    ok, bad, err = refs.allclose_report(arrays["out_511255"].reshape(3, 16), want.astype(np.float32), 1e-3, 1e-3)
+    assert ok, (bad, err)
