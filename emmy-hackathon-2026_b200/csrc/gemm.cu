@@ -1042,6 +1042,50 @@ extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, flo
   return gemm_entry(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu, nullptr, 1.0f, stream);
 }
 
+extern "C" int b2k_gemm_tf32x3_batched(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t batch,
+                                       int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                                       int64_t stride_a, int64_t stride_b, int64_t stride_c, int32_t b_layout,
+                                       const float *bias, int32_t relu, void *stream) {
+  B2K_CHECK_CTX(ctx);
+  if (batch < 0 || m < 0 || n < 0 || k < 0) return b2k::fail(ctx, B2K_EINVAL, "gemm_batched: negative extent");
+  if (b_layout != B2K_B_KN && b_layout != B2K_B_NK) return b2k::fail(ctx, B2K_EINVAL, "gemm_batched: bad b_layout");
+  if (batch == 0 || m == 0 || n == 0) return B2K_OK;
+  if (batch == 1)
+    return gemm_entry(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu, nullptr, 1.0f, stream);
+  if (!a || !b || !c) return b2k::fail(ctx, B2K_EINVAL, "gemm_batched: null buffer");
+  const bool b_nk = b_layout == B2K_B_NK;
+  if (lda < k || ldc < n || ldb < (b_nk ? k : n))
+    return b2k::fail(ctx, B2K_EINVAL, "gemm_batched: leading dimension too small");
+  if (stride_a < m * lda || stride_b < (b_nk ? n : k) * ldb || stride_c < m * ldc)
+    return b2k::fail(ctx, B2K_EINVAL, "gemm_batched: batch stride smaller than a matrix");
+  if (batch > 65535) return b2k::fail(ctx, B2K_EINVAL, "gemm_batched: batch exceeds 65535");
+  if (m > INT32_MAX - 256 || n > INT32_MAX - 256 || k > INT32_MAX - 64)
+    return b2k::fail(ctx, B2K_EINVAL, "gemm_batched: extent exceeds 32-bit TMA coordinates");
+  if (k == 0) return b2k::fail(ctx, B2K_EUNSUPPORTED, "gemm_batched: K = 0");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t kp = b2k::gemm_kpad(k);
+  int status = b2k::reserve_workspace(ctx, (size_t)(2 * (m + n) * kp * batch) * sizeof(float), s);
+  if (status != B2K_OK) return status;
+  ctx->flags_epoch = 0;  // the stream-K flags share this scratch: reset them next time
+  float *ws = static_cast<float *>(ctx->workspace);
+  // [batch][rows][kp] hi/lo halves, the layout the kernel's 3-D tensor maps walk
+  b2k::SplitOperands ops{ws, ws + batch * m * kp, ws + 2 * batch * m * kp, ws + 2 * batch * m * kp + batch * n * kp,
+                         kp};
+  {
+    b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
+    const b2k::RowSplit sa{a, m, k, lda, stride_a, batch, ops.a_hi, ops.a_lo};
+    if (b_nk) {
+      const b2k::RowSplit sb{b, n, k, ldb, stride_b, batch, ops.b_hi, ops.b_lo};
+      status = b2k::split_rows2(ctx, sa, &sb, kp, s);
+    } else {
+      status = b2k::split_rows2(ctx, sa, nullptr, kp, s);
+      if (status == B2K_OK) status = b2k::split_transpose(ctx, b, k, n, ldb, stride_b, batch, kp, ops.b_hi, ops.b_lo, s);
+    }
+  }
+  if (status != B2K_OK) return status;
+  return b2k::gemm_main(ctx, ops, m, n, batch, c, ldc, stride_c, bias, relu, nullptr, 1.0f, s, nullptr);
+}
+
 extern "C" int b2k_gemm_tf32x3_scaled(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n,
                                       int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout,
                                       const float *bias, int32_t relu, const float *div_ptr, float div_value,

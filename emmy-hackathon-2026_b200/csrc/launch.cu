@@ -68,6 +68,15 @@ extern "C" int b2k_launch(b2k_ctx *ctx, const b2k_kernel_desc *d, void *const *a
       return b2k_gemm_tf32x3(ctx, (const float *)p[0], (const float *)p[1], (float *)p[2], d->dims[0], d->dims[1],
                              d->dims[2], d->dims[3], d->dims[4], d->dims[5], d->flags[0], (const float *)p[3],
                              d->flags[1], stream);
+    case B2K_KIND_GEMM_BATCHED: {
+      need(0), need(1), need(2), maybe(3);
+      if (st != B2K_OK) return st;
+      const int64_t bt = d->dims[0], m = d->dims[1], n = d->dims[2], k = d->dims[3];
+      const bool nk = d->flags[0] == B2K_B_NK;
+      return b2k_gemm_tf32x3_batched(ctx, (const float *)p[0], (const float *)p[1], (float *)p[2], bt, m, n, k, k,
+                                     nk ? k : n, n, m * k, n * k, m * n, d->flags[0], (const float *)p[3],
+                                     d->flags[1], stream);
+    }
     case B2K_KIND_AXIS_REDUCE:
       need(0), need(1), maybe(3);
       if (st != B2K_OK) return st;

@@ -78,6 +78,12 @@ class KernelSpec:
         if self.kind == "row_softmax":
             return rt.make_desc(rt.KIND_ROW_SOFTMAX, {0: pos[p["x"]], 1: pos[p["out"]]},
                                 dims=(p["rows"], p["cols"], p["cols"], p["cols"]))
+        if self.kind == "matmul" and p.get("batch"):
+            roles = {0: pos[p["a"]], 1: pos[p["b"]], 2: pos[p["out"]]}
+            if p.get("bias"):
+                roles[3] = pos[p["bias"]]
+            return rt.make_desc(rt.KIND_GEMM_BATCHED, roles, dims=(p["batch"], p["m"], p["n"], p["k"]),
+                                flags=(rt.B_NK if p["b_nk"] else rt.B_KN, int(bool(p["relu"]))))
         if self.kind == "matmul":
             roles = {0: pos[p["a"]], 1: pos[p["b"]], 2: pos[p["out"]]}
             if p.get("div_buffer"):
@@ -477,10 +483,47 @@ def classify_row_softmax(node, kernel, args, inputs, outputs):
 
 
 # --------------------------------------------------------------------------- matmul
+def _classify_batched_matmul(node, kernel, args, inputs, out):
+    """x [B, M, K] @ y [B, K, N] (or y [B, N, K] transposed) -> out [B, M, N],
+    optionally + bias [N] and ReLU: a batch of independent contractions run
+    by b2k_gemm_tf32x3_batched."""
+    oshape = _shape(args[out])
+    mats = [n for n in inputs if len(_shape(args[n])) == 3]
+    extra = [n for n in inputs if n not in mats]
+    if len(mats) != 2 or len(extra) > 1 or (extra and _shape(args[extra[0]]) != (oshape[2],)):
+        raise Unsupported("matmul: two rank-3 inputs (and at most a bias)")
+    bias = extra[0] if extra else None
+    ops = {s.op.name for s in walk(node.body) if s.kind == "Assign"}
+    relus = (False, True) if ops & {"relu", "maximum"} else (False,)
+    last = None
+    for a, b, b_nk in ((mats[0], mats[1], False), (mats[1], mats[0], False),
+                       (mats[0], mats[1], True), (mats[1], mats[0], True)):
+        sa, sb = _shape(args[a]), _shape(args[b])
+        kb, nb = (sb[2], sb[1]) if b_nk else (sb[1], sb[2])
+        if sa[0] != sb[0] or sa[0] != oshape[0] or sa[2] != kb or (sa[1], nb) != tuple(oshape[1:]):
+            continue
+        for relu in relus:
+            def expect(buf, a=a, b=b, t=b_nk, r=relu):
+                c = np.einsum("bmk,bnk->bmn" if t else "bmk,bkn->bmn", buf[a], buf[b])
+                if bias:
+                    c = c + buf[bias].reshape(1, 1, -1)
+                return {out: np.maximum(c, 0.0) if r else c}
+            try:
+                cert = certify(node, kernel, args, inputs, [out], expect)
+            except Unsupported as exc:
+                last = last or exc
+                continue
+            return {"a": a, "b": b, "out": out, "batch": sa[0], "m": sa[1], "n": nb, "k": sa[2], "b_nk": b_nk,
+                    "div_buffer": None, "bias": bias, "relu": relu}, cert
+    raise last or Unsupported("matmul: batched operand shapes do not contract to the output")
+
+
 def classify_matmul(node, kernel, args, inputs, outputs):
     if len(outputs) != 1:
         raise Unsupported("matmul: one output")
     out = outputs[0]
+    if len(_shape(args[out])) == 3:
+        return _classify_batched_matmul(node, kernel, args, inputs, out)
     mats = [n for n in inputs if len(_shape(args[n])) == 2]
     oshape = _shape(args[out])
     if len(oshape) != 2:

@@ -45,7 +45,8 @@ class RowParams(C.Structure):
 ROW_SUM, ROW_RMSNORM, ROW_L2NORM, ROW_MAX, ROW_MIN, ROW_PROD = 0, 1, 2, 3, 4, 5
 
 
-KIND_POINTWISE, KIND_ROW_SOFTMAX, KIND_ROW_OP, KIND_GEMM, KIND_ATTENTION, KIND_AXIS_REDUCE = 1, 2, 3, 4, 5, 6
+(KIND_POINTWISE, KIND_ROW_SOFTMAX, KIND_ROW_OP, KIND_GEMM, KIND_ATTENTION, KIND_AXIS_REDUCE,
+ KIND_GEMM_BATCHED) = 1, 2, 3, 4, 5, 6, 7
 MAX_ROLES, NO_ARG, ROLE_PW_OUT = 12, -1, 8
 
 
@@ -109,6 +110,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_gemm_tf32x3_scaled": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P, C.c_float,
                                 _P], C.c_int),
     "b2k_axis_reduce_f32": ([_P, _I32, _P, _P, _I64, _I64, _I64, C.c_float, _P, _P], C.c_int),
+    "b2k_gemm_tf32x3_batched": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I32,
+                                 _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
     "b2k_gemm_set_streamk": ([C.c_int], C.c_int),
     "b2k_gemm_set_fused_split": ([C.c_int], C.c_int),
@@ -278,6 +281,14 @@ class Context:
         args = self._gemm_args(a, b, c, m, n, k, b_layout, lda, ldb, ldc, bias, relu, stream)
         self.check(self.lib.b2k_gemm_tf32x3_scaled(*args[:-1], div_ptr or None, div_value, args[-1]),
                    "b2k_gemm_tf32x3_scaled")
+
+    def gemm_batched(self, a: int, b: int, c: int, batch: int, m: int, n: int, k: int, *, b_layout: int = B_KN,
+                     bias: int = 0, relu: bool = False, stream: int = 0) -> None:
+        """C[i] = relu?(A[i] B[i] + bias) over contiguous [batch][rows][cols] operands."""
+        ldb = n if b_layout == B_KN else k
+        self.check(self.lib.b2k_gemm_tf32x3_batched(self.handle, a, b, c, batch, m, n, k, k, ldb, n, m * k, n * k,
+                                                    m * n, b_layout, bias or None, int(relu), stream),
+                   "b2k_gemm_tf32x3_batched")
 
     def gemm_call(self, a: int, b: int, c: int, m: int, n: int, k: int, **kw) -> "BoundCall":
         """:meth:`gemm` with its arguments converted once (see :class:`BoundCall`)."""

@@ -258,6 +258,18 @@ int b2k_gemm_tf32x3_scaled(b2k_ctx *ctx, const float *a, const float *b, float *
                            int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
                            const float *div_ptr, float div_value, void *stream);
 
+/* A batch of independent GEMMs with the arithmetic and epilogue of
+ * b2k_gemm_tf32x3: C[i] = relu?(A[i] B[i] + bias) for i < batch, A[i] at
+ * a + i * stride_a (elements), B[i] at b + i * stride_b, C[i] at
+ * c + i * stride_c; bias (optional, n columns) is shared by the batch.  Each
+ * stride must cover its matrix (stride_a >= m * lda, ...).  Replaces the
+ * batched contractions the reference's tensor-core plan rejects
+ * (tensor_core.py:284).  batch <= 65535; takes the pre-pass split path. */
+int b2k_gemm_tf32x3_batched(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t batch, int64_t m,
+                            int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a,
+                            int64_t stride_b, int64_t stride_c, int32_t b_layout, const float *bias, int32_t relu,
+                            void *stream);
+
 /* --- attention ----------------------------------------------------------------
  * Replaces the reference's fused SIMT attention lowering (compile.py:7009-7966:
  * hoisted score rows, selective-exp softmax, P.V fold) for every head of a
@@ -300,6 +312,7 @@ int b2k_attention_set_fused(int mode);
 #define B2K_KIND_GEMM_3XTF32 4
 #define B2K_KIND_ATTENTION_3XTF32 5
 #define B2K_KIND_AXIS_REDUCE 6
+#define B2K_KIND_GEMM_BATCHED 7
 #define B2K_MAX_ROLES 12
 #define B2K_NO_ARG (-1)
 #define B2K_ROLE_PW_OUT 8
@@ -312,12 +325,13 @@ typedef struct b2k_kernel_desc {
    *               4 mean-square-divisor buffer, 5 epsilon buffer
    *   GEMM_3XTF32 0 A, 1 B, 2 C, 3 bias, 4 divisor buffer (b2k_gemm_tf32x3_scaled)
    *   ATTENTION   0 Q, 1 K, 2 V, 3 O, 4 divisor buffer
-   *   AXIS_REDUCE 0 x, 1 y, 3 divisor buffer */
+   *   AXIS_REDUCE 0 x, 1 y, 3 divisor buffer
+   *   GEMM_BATCHED 0 A, 1 B, 2 C, 3 bias (contiguous [batch][rows][cols] operands) */
   int32_t role[B2K_MAX_ROLES];
   /* POINTWISE: n | ROW_*: rows, cols, ld_x, ld_y | GEMM: m, n, k, lda, ldb, ldc |
-   * ATTENTION: bh, s_q, s_kv, d, dv | AXIS_REDUCE: batch, s, cols */
+   * ATTENTION: bh, s_q, s_kv, d, dv | AXIS_REDUCE: batch, s, cols | GEMM_BATCHED: batch, m, n, k */
   int64_t dims[6];
-  /* GEMM: b_layout, relu | ATTENTION: k_layout | ROW_OP, AXIS_REDUCE: op */
+  /* GEMM, GEMM_BATCHED: b_layout, relu | ATTENTION: k_layout | ROW_OP, AXIS_REDUCE: op */
   int32_t flags[4];
   /* ROW_OP: sum_div, ms_div, eps | ATTENTION: scale_div (when no buffer) |
    * AXIS_REDUCE: sum divisor (when no buffer) */

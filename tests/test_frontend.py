@@ -233,6 +233,50 @@ def test_matmul_bias_relu_epilogue(tmp_path, relu):
     assert desc.role[3] == spec.arg_order.index("bias_1") and desc.flags[1] == int(relu)
 
 
+def batched_matmul_case(tmp_path, batch=2):
+    """matmul-2 rewritten as a batch of contractions: a third Tile axis `bat`
+    indexes x [B, 3, 31], y [B, 31, 16] and out [B, 3, 16]."""
+    folder = _copy_case(tmp_path, "matmul-2-cc1c8cef5b4d")
+    path = next(folder.glob("*.ir.json"))
+    graph = json.loads(path.read_text())
+    node = graph["nodes"]["out_511255"]
+    body = node["op_fields"]["body"][0]
+    for old, new in (
+            ("Tile(axes=(Axis(name='row'", f"Tile(axes=(Axis(name='bat', extent=Dim({batch}), window=None), Axis(name='row'"),
+            ("input='x_786334', index=(Var(name='row'), Var(name='kk'))",
+             "input='x_786334', index=(Var(name='bat'), Var(name='row'), Var(name='kk'))"),
+            ("input='y_637842', index=(Var(name='kk'), Var(name='col'))",
+             "input='y_637842', index=(Var(name='bat'), Var(name='kk'), Var(name='col'))"),
+            ("Write(output='out_511255', index=(Var(name='row'), Var(name='col'))",
+             "Write(output='out_511255', index=(Var(name='bat'), Var(name='row'), Var(name='col'))")):
+        assert old in body
+        body = body.replace(old, new)
+    node["op_fields"]["body"][0] = body
+    shapes = {"x_786334": [batch, 3, 31], "y_637842": [batch, 31, 16], "out_511255": [batch, 3, 16]}
+    for name, shape in shapes.items():
+        graph["nodes"][name]["outputs"][0]["shape"] = shape
+    path.write_text(json.dumps(graph))
+    meta = json.loads((folder / "meta.json").read_text())
+    for arg in meta["kernels"][0]["args"]:
+        arg["shape"] = shapes[arg["name"]]
+    (folder / "meta.json").write_text(json.dumps(meta))
+    for name in ("inputs.npz", "expected.npz"):
+        (folder / name).unlink()
+    return folder, path
+
+
+def test_batched_matmul(tmp_path):
+    fe = pkg("frontend")
+    rt = pkg("runtime")
+    _, path = batched_matmul_case(tmp_path)
+    spec = fe.compile_path(path)
+    p = spec.params
+    assert (spec.kind, p["batch"], p["m"], p["n"], p["k"], p["b_nk"], p["relu"]) == ("matmul", 2, 3, 16, 31, False,
+                                                                                        False)
+    desc = spec.descriptor()
+    assert desc.kind == rt.KIND_GEMM_BATCHED and tuple(desc.dims[:4]) == (2, 3, 16, 31)
+
+
 def test_matmul_with_transposed_operand(tmp_path):
     fe = pkg("frontend")
     rt = pkg("runtime")

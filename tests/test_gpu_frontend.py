@@ -88,3 +88,18 @@ def test_bias_relu_matmul_runs(session, tmp_path, relu):
     want = np.maximum(want, 0.0) if relu else want
     ok, bad, err = refs.allclose_report(arrays["out_511255"].reshape(3, 16), want.astype(np.float32), 1e-3, 1e-3)
     assert ok, (bad, err)
+
+
+def test_batched_matmul_runs(session, tmp_path):
+    """A recognised batched contraction (x [2, 3, 31] @ y [2, 31, 16]) through the runner."""
+    from test_frontend import batched_matmul_case
+    runner = pkg("runner")
+    folder, _ = batched_matmul_case(tmp_path)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((2, 3, 31)).astype(np.float32)
+    y = rng.standard_normal((2, 31, 16)).astype(np.float32)
+    result, arrays = runner.Pipeline(folder).run(session, inputs={"x_786334": x, "y_637842": y}, warmup=1, iters=2)
+    assert result["ok"]
+    want = np.einsum("bmk,bkn->bmn", x.astype(np.float64), y.astype(np.float64))
+    ok, bad, err = refs.allclose_report(arrays["out_511255"].reshape(2, 3, 16), want.astype(np.float32), 1e-3, 1e-3)
+    assert ok, (bad, err)

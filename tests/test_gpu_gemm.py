@@ -241,3 +241,40 @@ def test_gemm_scaled_with_unit_divisor_equals_gemm(ctx, torch_cuda):
     finally:
         ctx.set_gemm_fused_split(1)
     assert torch.equal(c1, c2)
+
+
+@pytest.mark.parametrize("batch,m,n,k,b_layout", [(3, 130, 96, 48, 0), (4, 257, 300, 129, 1), (16, 128, 256, 512, 0)])
+def test_gemm_batched(ctx, torch_cuda, batch, m, n, k, b_layout):
+    """b2k_gemm_tf32x3_batched: each batch entry equals the single GEMM of the
+    same operands bit for bit (same kernel, same split), and float64 normwise."""
+    torch = torch_cuda
+    runtime = pkg("runtime")
+    rng = np.random.default_rng(batch * m + n + k)
+    a = rng.uniform(-1, 1, (batch, m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (batch, k, n) if b_layout == 0 else (batch, n, k)).astype(np.float32)
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    da, db, dbias = dev(torch, a), dev(torch, b), dev(torch, bias)
+    dc = torch.full((batch, m, n), float("nan"), device="cuda")
+    ctx.gemm_batched(da.data_ptr(), db.data_ptr(), dc.data_ptr(), batch, m, n, k, b_layout=b_layout,
+                     bias=dbias.data_ptr(), relu=True)
+    ctx.sync()
+    got = dc.cpu().numpy()
+    ctx.set_gemm_fused_split(0)  # the batched call runs the pre-pass kernel
+    try:
+        for i in range(batch):
+            single = torch.empty((m, n), device="cuda")
+            ctx.gemm(da[i].data_ptr(), db[i].data_ptr(), single.data_ptr(), m, n, k, b_layout=b_layout,
+                     bias=dbias.data_ptr(), relu=True)
+            ctx.sync()
+            assert np.array_equal(got[i], single.cpu().numpy()), i
+    finally:
+        ctx.set_gemm_fused_split(1)
+    bm = b if b_layout == 0 else np.swapaxes(b, 1, 2)
+    exact = np.maximum(np.einsum("bmk,bkn->bmn", a.astype(np.float64), bm.astype(np.float64)) + bias, 0.0)
+    assert tf32.normwise_error(got, exact) <= NORMWISE
+    # a batch stride shorter than one matrix is refused before anything runs
+    status = ctx.lib.b2k_gemm_tf32x3_batched(ctx.handle, da.data_ptr(), db.data_ptr(), dc.data_ptr(), batch, m, n, k,
+                                             k, n if b_layout == 0 else k, n, m * k - 1, n * k, m * n, b_layout, None,
+                                             0, None)
+    with pytest.raises(runtime.B2KError):
+        ctx.check(status, "b2k_gemm_tf32x3_batched")
