@@ -552,26 +552,31 @@ def classify_matmul(node, kernel, args, inputs, outputs):
     last = None
     # B stored [K, N] (b_nk False) or transposed [N, K] (the IR's y^T), each
     # operand order; square shapes fit several and the certificate decides.
+    # Every orientation over the whole shared dimension is tried first; then,
+    # if the IR bounds its K loop below it (a guard ``kk < 63`` over 65
+    # columns), each static integer of the body smaller than K, largest
+    # first, as a prefix contraction A[:, :k] @ B[:k, :] -- the GEMM reads it
+    # through lda / ldb.
+    orientations = []
     for a, b, b_nk in ((mats[0], mats[1], False), (mats[1], mats[0], False),
                        (mats[0], mats[1], True), (mats[1], mats[0], True)):
         sa, sb = _shape(args[a]), _shape(args[b])
         kb, nb = (sb[1], sb[0]) if b_nk else (sb[0], sb[1])
-        if sa[1] != kb or (sa[0], nb) != oshape:
+        if sa[1] == kb and (sa[0], nb) == oshape:
+            orientations.append((a, b, b_nk, sa, sb, nb))
+    literals = sorted(_int_literals(node.body), reverse=True)
+    candidates = [(o, o[3][1], r) for o in orientations for r in relus]
+    candidates += [(o, k, r) for o in orientations
+                   for k in [v for v in literals if 0 < v < o[3][1]][:PREFIX_CANDIDATES] for r in relus]
+    for (a, b, b_nk, sa, sb, nb), k, relu in candidates:
+        try:
+            cert = certify(node, kernel, args, inputs, outputs,
+                           lambda buf, k=k, a=a, b=b, t=b_nk, r=relu: {out: product(buf, a, b, k, t, r)})
+        except Unsupported as exc:
+            last = last or exc
             continue
-        # The whole shared dimension first; then, if the IR bounds its K loop
-        # below it (a guard ``kk < 63`` over 65 columns), each static integer
-        # of the body smaller than K, largest first, as a prefix contraction
-        # A[:, :k] @ B[:k, :] -- the GEMM reads it through lda / ldb.
-        prefixes = sorted((v for v in _int_literals(node.body) if 0 < v < sa[1]), reverse=True)[:PREFIX_CANDIDATES]
-        for k, relu in [(k, r) for k in [sa[1]] + prefixes for r in relus]:
-            try:
-                cert = certify(node, kernel, args, inputs, outputs,
-                               lambda buf, k=k, a=a, b=b, t=b_nk, r=relu: {out: product(buf, a, b, k, t, r)})
-            except Unsupported as exc:
-                last = last or exc
-                continue
-            return {"a": a, "b": b, "out": out, "m": sa[0], "n": nb, "k": k, "lda": sa[1], "ldb": sb[1],
-                    "b_nk": b_nk, "div_buffer": div, "bias": bias, "relu": relu}, cert
+        return {"a": a, "b": b, "out": out, "m": sa[0], "n": nb, "k": k, "lda": sa[1], "ldb": sb[1],
+                "b_nk": b_nk, "div_buffer": div, "bias": bias, "relu": relu}, cert
     raise last or Unsupported("matmul: operand shapes do not contract to the output")
 
 
