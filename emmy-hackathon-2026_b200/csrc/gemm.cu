@@ -939,14 +939,18 @@ int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int6
 // inside the kernel (gemm_fused.cu) and only B is pre-split into `ws`;
 // otherwise both operands are split into `ws` (A_hi, A_lo: m x Kp; B_hi,
 // B_lo: n x Kp) and the kernel above runs.
-// `b_kmajor`: B is stored [n, K] (else [K, n]).
+// `layout`: B2K_B_NK -- B is stored [n, K] (else [K, n]); B2K_A_KM -- A is
+// stored [K, m] (else [m, K]).
 int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
-                         int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu,
+                         int64_t lda, int64_t ldb, int64_t ldc, int layout, const float *bias, int relu,
                          float *ws, cudaStream_t s, const b2k::StreamKScratch *sk, const float *div_ptr,
                          float div_value) {
-  // A divided product runs on the pre-pass kernel, whose epilogue divides.
+  const int b_kmajor = (layout & B2K_B_NK) != 0;
+  const bool a_t = (layout & B2K_A_KM) != 0;
+  // A divided product runs on the pre-pass kernel, whose epilogue divides;
+  // a transposed A is transposed by the pre-pass split.
   const bool divide = div_ptr != nullptr || div_value != 1.0f;
-  const int mode = divide ? 0 : b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count);
+  const int mode = divide || a_t ? 0 : b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count);
   if (mode == 2) return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_kmajor, bias, relu, s);
   const int64_t kp = b2k::gemm_kpad(k);
   int status;
@@ -965,7 +969,13 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
   {
     b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
     const b2k::RowSplit sa{a, m, k, lda, m * lda, 1, ops.a_hi, ops.a_lo};
-    if (b_kmajor) {
+    if (a_t) {
+      // A [K, m] -> hi/lo [m][Kp], the same transform as a [K, n] B
+      status = b2k::split_transpose(ctx, a, k, m, lda, k * lda, 1, kp, ops.a_hi, ops.a_lo, s);
+      if (status == B2K_OK)
+        status = b_kmajor ? b2k::split_rows(ctx, b, n, k, ldb, n * ldb, 1, kp, ops.b_hi, ops.b_lo, s)
+                          : b2k::split_transpose(ctx, b, k, n, ldb, k * ldb, 1, kp, ops.b_hi, ops.b_lo, s);
+    } else if (b_kmajor) {
       // A and a K-major B in one launch
       const b2k::RowSplit sb{b, n, k, ldb, n * ldb, 1, ops.b_hi, ops.b_lo};
       status = b2k::split_rows2(ctx, sa, &sb, kp, s);
@@ -996,10 +1006,11 @@ static int gemm_entry(b2k_ctx *ctx, const float *a, const float *b, float *c, in
                       const float *div_ptr, float div_value, void *stream) {
   B2K_CHECK_CTX(ctx);
   if (m < 0 || n < 0 || k < 0) return b2k::fail(ctx, B2K_EINVAL, "gemm: negative extent");
-  if (b_layout != B2K_B_KN && b_layout != B2K_B_NK) return b2k::fail(ctx, B2K_EINVAL, "gemm: bad b_layout");
+  if ((b_layout & ~(B2K_B_NK | B2K_A_KM)) != 0) return b2k::fail(ctx, B2K_EINVAL, "gemm: bad b_layout");
+  const bool a_t = (b_layout & B2K_A_KM) != 0, b_nk = (b_layout & B2K_B_NK) != 0;
   if (m == 0 || n == 0) return B2K_OK;
   if (!a || !b || !c) return b2k::fail(ctx, B2K_EINVAL, "gemm: null buffer");
-  if (lda < k || ldc < n || ldb < (b_layout == B2K_B_NK ? k : n))
+  if (lda < (a_t ? m : k) || ldc < n || ldb < (b_nk ? k : n))
     return b2k::fail(ctx, B2K_EINVAL, "gemm: leading dimension too small");
   if (m > INT32_MAX - 256 || n > INT32_MAX - 256 || k > INT32_MAX - 64)
     return b2k::fail(ctx, B2K_EINVAL, "gemm: extent exceeds 32-bit TMA coordinates");
@@ -1013,8 +1024,8 @@ static int gemm_entry(b2k_ctx *ctx, const float *a, const float *b, float *c, in
     if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: zero fill");
     return B2K_OK;
   }
-  if (!divide && b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count) == 2)  // needs no scratch
-    return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu, s);
+  if (!divide && !a_t && b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count) == 2)  // needs no scratch
+    return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_nk, bias, relu, s);
   // scratch: split operands, then the stream-K partial slots and flags
   const size_t split_bytes = (b2k_gemm_workspace_bytes(m, n, k) + 255) & ~size_t(255);
   int status = b2k::reserve_workspace(ctx, split_bytes + b2k::streamk_scratch_bytes(ctx->sm_count), s);
@@ -1032,7 +1043,7 @@ static int gemm_entry(b2k_ctx *ctx, const float *a, const float *b, float *c, in
   }
   sk.epoch = ++ctx->flags_epoch;
   if (sk.epoch == 0) sk.epoch = ctx->flags_epoch = 1;
-  return b2k_gemm_tf32x3_impl(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu,
+  return b2k_gemm_tf32x3_impl(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu,
                               static_cast<float *>(ctx->workspace), s, &sk, div_ptr, div_value);
 }
 

@@ -21,7 +21,7 @@
 // The tensor-core GEMM of gemm.cu: splits A and B into `ws` and launches the
 // main kernel on `s`.
 int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
-                         int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu,
+                         int64_t lda, int64_t ldb, int64_t ldc, int layout, const float *bias, int relu,
                          float *ws, cudaStream_t s, const b2k::StreamKScratch *sk, const float *div_ptr,
                          float div_value);
 
@@ -72,10 +72,10 @@ extern "C" int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c,
                                        int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias,
                                        int32_t relu, void *stream) {
   if (m < 0 || n < 0 || k < 0) return B2K_EINVAL;
-  if (b_layout != B2K_B_KN && b_layout != B2K_B_NK) return B2K_EINVAL;
+  if ((b_layout & ~(B2K_B_NK | B2K_A_KM)) != 0) return B2K_EINVAL;
   if (m == 0 || n == 0) return B2K_OK;
   if (!a || !b || !c) return B2K_EINVAL;
-  if (lda < k || ldc < n || ldb < (b_layout == B2K_B_NK ? k : n)) return B2K_EINVAL;
+  if (lda < ((b_layout & B2K_A_KM) ? m : k) || ldc < n || ldb < ((b_layout & B2K_B_NK) ? k : n)) return B2K_EINVAL;
   if (k == 0) return B2K_EUNSUPPORTED;
   const int64_t kp = (k + 31) / 32 * 32;
   if (m > (int64_t)kScratchFloats || n > (int64_t)kScratchFloats ||
@@ -92,6 +92,6 @@ extern "C" int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c,
   local.device = device;
   local.sm_count = symbols.sm_count;
   local.error_flag = symbols.status;
-  return b2k_gemm_tf32x3_impl(&local, a, b, c, m, n, k, lda, ldb, ldc, b_layout == B2K_B_NK, bias, relu,
+  return b2k_gemm_tf32x3_impl(&local, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu,
                               symbols.scratch, (cudaStream_t)stream, nullptr, nullptr, 1.0f);
 }

@@ -90,11 +90,12 @@ class KernelSpec:
                 roles[4] = pos[p["div_buffer"]]
             if p.get("bias"):
                 roles[3] = pos[p["bias"]]
-            b_nk = p.get("b_nk", False)
+            b_nk, a_t = p.get("b_nk", False), p.get("a_t", False)
+            layout = (rt.B_NK if b_nk else rt.B_KN) | (rt.A_KM if a_t else 0)
             return rt.make_desc(rt.KIND_GEMM, roles,
-                                dims=(p["m"], p["n"], p["k"], p.get("lda", p["k"]),
+                                dims=(p["m"], p["n"], p["k"], p.get("lda", p["m"] if a_t else p["k"]),
                                       p.get("ldb", p["k"] if b_nk else p["n"]), p["n"]),
-                                flags=(rt.B_NK if b_nk else rt.B_KN, int(bool(p.get("relu")))))
+                                flags=(layout, int(bool(p.get("relu")))))
         if self.kind == "attention":
             return rt.make_desc(rt.KIND_ATTENTION, {0: pos[p["q"]], 1: pos[p["kt"]], 2: pos[p["v"]],
                                                     3: pos[p["out"]], 4: pos[p["scale"]]},
@@ -542,8 +543,8 @@ def classify_matmul(node, kernel, args, inputs, outputs):
     ops = {s.op.name for s in walk(node.body) if s.kind == "Assign"}
     relus = (False, True) if ops & {"relu", "maximum"} else (False,)
 
-    def product(buf, a, b, k, b_nk, relu):
-        c = buf[a][:, :k] @ (buf[b][:, :k].T if b_nk else buf[b][:k, :])
+    def product(buf, a, b, k, b_nk, relu, a_t=False):
+        c = (buf[a][:k, :].T if a_t else buf[a][:, :k]) @ (buf[b][:, :k].T if b_nk else buf[b][:k, :])
         if div:
             c = c / float(buf[div].reshape(-1)[0])
         if bias:
@@ -557,26 +558,29 @@ def classify_matmul(node, kernel, args, inputs, outputs):
     # columns), each static integer of the body smaller than K, largest
     # first, as a prefix contraction A[:, :k] @ B[:k, :] -- the GEMM reads it
     # through lda / ldb.
+    # A stored [M, K] or transposed [K, M] likewise (a_t).
     orientations = []
-    for a, b, b_nk in ((mats[0], mats[1], False), (mats[1], mats[0], False),
-                       (mats[0], mats[1], True), (mats[1], mats[0], True)):
-        sa, sb = _shape(args[a]), _shape(args[b])
-        kb, nb = (sb[1], sb[0]) if b_nk else (sb[0], sb[1])
-        if sa[1] == kb and (sa[0], nb) == oshape:
-            orientations.append((a, b, b_nk, sa, sb, nb))
+    for a_t in (False, True):
+        for a, b, b_nk in ((mats[0], mats[1], False), (mats[1], mats[0], False),
+                           (mats[0], mats[1], True), (mats[1], mats[0], True)):
+            sa, sb = _shape(args[a]), _shape(args[b])
+            ma, ka = (sa[1], sa[0]) if a_t else (sa[0], sa[1])
+            kb, nb = (sb[1], sb[0]) if b_nk else (sb[0], sb[1])
+            if ka == kb and (ma, nb) == oshape:
+                orientations.append((a, b, a_t, b_nk, ma, ka, nb, sa, sb))
     literals = sorted(_int_literals(node.body), reverse=True)
-    candidates = [(o, o[3][1], r) for o in orientations for r in relus]
+    candidates = [(o, o[5], r) for o in orientations for r in relus]
     candidates += [(o, k, r) for o in orientations
-                   for k in [v for v in literals if 0 < v < o[3][1]][:PREFIX_CANDIDATES] for r in relus]
-    for (a, b, b_nk, sa, sb, nb), k, relu in candidates:
+                   for k in [v for v in literals if 0 < v < o[5]][:PREFIX_CANDIDATES] for r in relus]
+    for (a, b, a_t, b_nk, ma, ka, nb, sa, sb), k, relu in candidates:
         try:
             cert = certify(node, kernel, args, inputs, outputs,
-                           lambda buf, k=k, a=a, b=b, t=b_nk, r=relu: {out: product(buf, a, b, k, t, r)})
+                           lambda buf, k=k, a=a, b=b, t=b_nk, r=relu, at=a_t: {out: product(buf, a, b, k, t, r, at)})
         except Unsupported as exc:
             last = last or exc
             continue
-        return {"a": a, "b": b, "out": out, "m": sa[0], "n": nb, "k": k, "lda": sa[1], "ldb": sb[1],
-                "b_nk": b_nk, "div_buffer": div, "bias": bias, "relu": relu}, cert
+        return {"a": a, "b": b, "out": out, "m": ma, "n": nb, "k": k, "lda": sa[1], "ldb": sb[1],
+                "a_t": a_t, "b_nk": b_nk, "div_buffer": div, "bias": bias, "relu": relu}, cert
     raise last or Unsupported("matmul: operand shapes do not contract to the output")
 
 

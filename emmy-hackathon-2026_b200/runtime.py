@@ -18,7 +18,7 @@ STATUS_NAMES = {B2K_EINVAL: "EINVAL", B2K_EUNSUPPORTED: "EUNSUPPORTED", B2K_ECUD
                 B2K_ETIMEOUT: "ETIMEOUT", B2K_ESCRATCH: "ESCRATCH"}
 
 PW_MAX_INPUTS, PW_MAX_INSNS = 8, 48
-B_KN, B_NK = 0, 1
+B_KN, B_NK, A_KM = 0, 1, 2   # A_KM is a flag or-ed into b_layout: A stored [k, m]
 K_SD, K_DS = 0, 1
 
 OPCODES = {
@@ -263,8 +263,8 @@ class Context:
 
     def _gemm_args(self, a, b, c, m, n, k, b_layout=B_KN, lda=None, ldb=None, ldc=None, bias=0, relu=False,
                    stream=0) -> tuple:
-        lda = k if lda is None else lda
-        ldb = (n if b_layout == B_KN else k) if ldb is None else ldb
+        lda = (m if b_layout & A_KM else k) if lda is None else lda
+        ldb = (k if b_layout & B_NK else n) if ldb is None else ldb
         ldc = n if ldc is None else ldc
         return (self.handle, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias or None, int(relu), stream)
 

@@ -238,11 +238,14 @@ int b2k_selective_exp_f32(b2k_ctx *ctx, const float *x, float *y, int64_t n, voi
  * hi*hi + hi*lo + lo*hi of TF32 halves and FP32 accumulation.
  * A is row-major with leading dimension lda.  b_layout B2K_B_KN: B is
  * row-major [k, n] (ldb >= n); B2K_B_NK: B is stored transposed, row-major
- * [n, k] (ldb >= k).  bias may be NULL; relu is 0 or 1.  C is row-major
- * (ldc >= n).  Uses 2 * (m + n) * round_up(k, 32) * 4 bytes of context
- * scratch for the split operands. */
+ * [n, k] (ldb >= k).  Or-ing B2K_A_KM into b_layout says A is stored
+ * transposed, row-major [k, m] (lda >= m; the pre-pass split transposes it;
+ * not accepted by the host-array and batched calls).  bias may be NULL; relu
+ * is 0 or 1.  C is row-major (ldc >= n).  Uses 2 * (m + n) * round_up(k, 32)
+ * * 4 bytes of context scratch for the split operands. */
 #define B2K_B_KN 0
 #define B2K_B_NK 1
+#define B2K_A_KM 2
 int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                     int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias, int32_t relu,
                     void *stream);

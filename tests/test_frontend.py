@@ -277,6 +277,41 @@ def test_batched_matmul(tmp_path):
     assert desc.kind == rt.KIND_GEMM_BATCHED and tuple(desc.dims[:4]) == (2, 3, 16, 31)
 
 
+def transposed_a_matmul_case(tmp_path):
+    """matmul-2 rewritten to read its left operand transposed: x stored
+    [31, 3] and loaded at (kk, row), so out = x^T @ y."""
+    folder = _copy_case(tmp_path, "matmul-2-cc1c8cef5b4d")
+    path = next(folder.glob("*.ir.json"))
+    graph = json.loads(path.read_text())
+    graph["nodes"]["x_786334"]["outputs"][0]["shape"] = [31, 3]
+    body = graph["nodes"]["out_511255"]["op_fields"]["body"][0]
+    old = "input='x_786334', index=(Var(name='row'), Var(name='kk'))"
+    assert old in body
+    graph["nodes"]["out_511255"]["op_fields"]["body"][0] = body.replace(
+        old, "input='x_786334', index=(Var(name='kk'), Var(name='row'))")
+    path.write_text(json.dumps(graph))
+    meta = json.loads((folder / "meta.json").read_text())
+    for arg in meta["kernels"][0]["args"]:
+        if arg["name"] == "x_786334":
+            arg["shape"] = [31, 3]
+    (folder / "meta.json").write_text(json.dumps(meta))
+    for name in ("inputs.npz", "expected.npz"):
+        (folder / name).unlink()
+    return folder, path
+
+
+def test_matmul_with_transposed_left_operand(tmp_path):
+    fe = pkg("frontend")
+    rt = pkg("runtime")
+    _, path = transposed_a_matmul_case(tmp_path)
+    spec = fe.compile_path(path)
+    p = spec.params
+    assert (spec.kind, p["a"], p["a_t"], p["b_nk"], p["m"], p["n"], p["k"], p["lda"]) == (
+        "matmul", "x_786334", True, False, 3, 16, 31, 3)
+    desc = spec.descriptor()
+    assert desc.flags[0] == rt.A_KM | rt.B_KN and tuple(desc.dims[:6]) == (3, 16, 31, 3, 16, 16)
+
+
 def test_matmul_with_transposed_operand(tmp_path):
     fe = pkg("frontend")
     rt = pkg("runtime")

@@ -103,3 +103,17 @@ def test_batched_matmul_runs(session, tmp_path):
     want = np.einsum("bmk,bkn->bmn", x.astype(np.float64), y.astype(np.float64))
     ok, bad, err = refs.allclose_report(arrays["out_511255"].reshape(2, 3, 16), want.astype(np.float32), 1e-3, 1e-3)
     assert ok, (bad, err)
+
+
+def test_transposed_left_operand_matmul_runs(session, tmp_path):
+    from test_frontend import transposed_a_matmul_case
+    runner = pkg("runner")
+    folder, _ = transposed_a_matmul_case(tmp_path)
+    rng = np.random.default_rng(6)
+    x = rng.standard_normal((31, 3)).astype(np.float32)
+    y = rng.standard_normal((31, 16)).astype(np.float32)
+    result, arrays = runner.Pipeline(folder).run(session, inputs={"x_786334": x, "y_637842": y}, warmup=1, iters=2)
+    assert result["ok"]
+    want = x.astype(np.float64).T @ y.astype(np.float64)
+    ok, bad, err = refs.allclose_report(arrays["out_511255"].reshape(3, 16), want.astype(np.float32), 1e-3, 1e-3)
+    assert ok, (bad, err)

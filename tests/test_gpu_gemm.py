@@ -278,3 +278,35 @@ def test_gemm_batched(ctx, torch_cuda, batch, m, n, k, b_layout):
                                              0, None)
     with pytest.raises(runtime.B2KError):
         ctx.check(status, "b2k_gemm_tf32x3_batched")
+
+
+@pytest.mark.parametrize("m,n,k,b_layout", [(257, 300, 129, 0), (130, 96, 48, 1), (1000, 1000, 776, 0)])
+def test_gemm_transposed_a(ctx, torch_cuda, m, n, k, b_layout):
+    """A stored [k, m] (B2K_A_KM): the same bits as the row-major A through the
+    pre-pass kernel; refused by the host-array call."""
+    torch = torch_cuda
+    runtime = pkg("runtime")
+    rng = np.random.default_rng(m + 2 * n + k)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
+    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    da, dat, db, dbias = dev(torch, a), dev(torch, np.ascontiguousarray(a.T)), dev(torch, b), dev(torch, bias)
+    c_t = torch.empty((m, n), device="cuda")
+    ctx.gemm(dat.data_ptr(), db.data_ptr(), c_t.data_ptr(), m, n, k, b_layout=b_layout | runtime.A_KM,
+             bias=dbias.data_ptr(), relu=True)
+    c = torch.empty((m, n), device="cuda")
+    ctx.set_gemm_fused_split(0)
+    try:
+        ctx.gemm(da.data_ptr(), db.data_ptr(), c.data_ptr(), m, n, k, b_layout=b_layout, bias=dbias.data_ptr(),
+                 relu=True)
+        ctx.sync()
+    finally:
+        ctx.set_gemm_fused_split(1)
+    assert torch.equal(c_t, c)
+    bm = (b if b_layout == 0 else b.T).astype(np.float64)
+    exact = np.maximum(a.astype(np.float64) @ bm + bias, 0.0)
+    assert tf32.normwise_error(c_t.cpu().numpy(), exact) <= NORMWISE
+    host_c = np.empty((m, n), np.float32)
+    at = np.ascontiguousarray(a.T)
+    with pytest.raises(runtime.B2KError):
+        ctx.gemm_host(at.ctypes.data, b.ctypes.data, host_c.ctypes.data, m, n, k, b_layout=b_layout | runtime.A_KM)
