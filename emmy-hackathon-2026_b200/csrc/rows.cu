@@ -183,8 +183,12 @@ __global__ void __launch_bounds__(kThreads) rows_fold(const float *__restrict__ 
 // Fold over the middle axis of [batch][s][cols]: one thread per output
 // column j, folding i = 0 .. s-1 in order (the IR's serial Loop + Accum over
 // that axis).  Consecutive threads hold consecutive columns, so every step of
-// every fold is one coalesced read of a row segment; the loop is unrolled so
-// that several rows' loads are in flight ahead of the dependent fold.
+// every fold is one coalesced read of a row segment.  Each thread loads
+// kAxisAhead rows before folding them in order: with few output columns (a
+// long fold over few cells) the loads in flight, not the threads, carry the
+// bandwidth -- 8 rows ahead ran [8, 8192, 4096] at 1.7 TB/s.
+constexpr int kAxisAhead = 32;
+
 template <int OP>
 __global__ void __launch_bounds__(kThreads) axis_fold(const float *__restrict__ x, float *__restrict__ y,
                                                       int64_t batch, int64_t s_len, int64_t cols,
@@ -196,11 +200,16 @@ __global__ void __launch_bounds__(kThreads) axis_fold(const float *__restrict__ 
   for (int64_t b = blockIdx.y; b < batch; b += gridDim.y) {
     const float *xb = x + b * s_len * cols + j;
     float acc = OP == B2K_ROW_SUM ? 0.0f : fold_identity<OP>();
-#pragma unroll 8
-    for (int64_t i = 0; i < s_len; ++i) {
-      const float v = __ldg(xb + i * cols);
-      acc = OP == B2K_ROW_SUM ? __fadd_rn(acc, v) : fold_op<OP>(acc, v);
+    auto fold = [&](float v) { acc = OP == B2K_ROW_SUM ? __fadd_rn(acc, v) : fold_op<OP>(acc, v); };
+    int64_t i = 0;
+    for (; i + kAxisAhead <= s_len; i += kAxisAhead) {
+      float v[kAxisAhead];
+#pragma unroll
+      for (int u = 0; u < kAxisAhead; ++u) v[u] = __ldg(xb + (i + u) * cols);
+#pragma unroll
+      for (int u = 0; u < kAxisAhead; ++u) fold(v[u]);
     }
+    for (; i < s_len; ++i) fold(__ldg(xb + i * cols));
     if (OP == B2K_ROW_SUM) {
       const float d = div_ptr ? __ldg(div_ptr) : div;
       if (div_ptr || d != 1.0f) acc = __fdiv_rn(acc, d);
