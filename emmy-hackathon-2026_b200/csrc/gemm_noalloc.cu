@@ -1,14 +1,14 @@
 // b2k_gemm_tf32x3_noalloc: the 3xTF32 GEMM for callers that cannot allocate
 // device memory.
 //
-// Some callers may not call cudaMalloc at all: code that runs while a CUDA
-// graph is being captured or replayed from a fixed memory plan, embedders
-// whose device memory is owned by another allocator or pool, and
-// environments that forbid allocation after start-up.  b2k_gemm_tf32x3 needs
-// a context whose scratch arena grows with cudaMalloc; this entry point
-// instead uses a fixed scratch array that is part of the library image
-// itself (a file-scope __device__ array), so it needs no context and calls
-// no allocator.
+// Some callers may not call cudaMalloc at all: embedders whose device memory
+// is owned by another allocator or a pre-sized pool, runtimes that plan every
+// buffer up front and treat an allocation after start-up as an error, and
+// code running inside a host callback or a library hook where a
+// device-synchronising call is not allowed.  b2k_gemm_tf32x3 needs a context
+// whose scratch arena grows with cudaMalloc; this entry point instead uses a
+// fixed scratch array that is part of the library image itself (a file-scope
+// __device__ array), so it needs no context and calls no allocator.
 //
 // The operand split needs 2 * (m + n) * round_up(k, 32) floats of scratch;
 // the array holds B2K_NOALLOC_SCRATCH_BYTES (32 MiB), and larger problems are
@@ -77,10 +77,13 @@ extern "C" int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c,
   if (!a || !b || !c) return B2K_EINVAL;
   if (lda < ((b_layout & B2K_A_KM) ? m : k) || ldc < n || ldb < ((b_layout & B2K_B_NK) ? k : n)) return B2K_EINVAL;
   if (k == 0) return B2K_EUNSUPPORTED;
+  // The extents must fit the kernels' 32-bit TMA coordinates (the limits of
+  // b2k_gemm_tf32x3); this also keeps the scratch arithmetic below far from
+  // int64 overflow.
+  if (m > INT32_MAX - 256 || n > INT32_MAX - 256 || k > INT32_MAX - 64) return B2K_EINVAL;
   const int64_t kp = (k + 31) / 32 * 32;
-  if (m > (int64_t)kScratchFloats || n > (int64_t)kScratchFloats ||
-      2 * (m + n) * kp > (int64_t)kScratchFloats)
-    return B2K_ESCRATCH;
+  // 2 * (m + n) * kp floats, compared without forming the product.
+  if (kp > (int64_t)kScratchFloats / (2 * (m + n))) return B2K_ESCRATCH;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return B2K_ECUDA;
   DeviceSymbols symbols;

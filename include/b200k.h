@@ -343,14 +343,17 @@ typedef struct b2k_kernel_desc {
 } b2k_kernel_desc;
 int b2k_launch(b2k_ctx *ctx, const b2k_kernel_desc *desc, void *const *args, int32_t nargs, void *stream);
 
-/* The same GEMM for callers that cannot allocate device memory (code running
- * under CUDA-graph capture or a fixed memory plan, or memory owned by another
- * allocator).  No counterpart in the reference.  It takes no context and
+/* The same GEMM for callers that cannot allocate device memory: embedders
+ * whose device memory belongs to another allocator or a pre-sized pool,
+ * runtimes that plan every buffer up front, and code in a host callback or
+ * library hook where a synchronising cudaMalloc is not allowed.  No
+ * counterpart in the reference.  It takes no context and
  * allocates nothing: the operand split goes to a fixed scratch array inside
  * the library image (B2K_NOALLOC_SCRATCH_BYTES per device that loads the
  * library, kept until exit).  Problems with 2 * (m + n) * round_up(k, 32) * 4
  * bytes of split operands above that size return B2K_ESCRATCH and launch
- * nothing; K = 0 returns B2K_EUNSUPPORTED.  Runs on the calling thread's
+ * nothing; extents beyond the 32-bit limits of b2k_gemm_tf32x3 return
+ * B2K_EINVAL; K = 0 returns B2K_EUNSUPPORTED.  Runs on the calling thread's
  * current device and the given stream.  The first call on a device looks up
  * the scratch array's device address (cudaGetSymbolAddress); make that first
  * call before any stream capture.  Every call on a device shares the one

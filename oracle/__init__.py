@@ -12,8 +12,6 @@ Contents (each function cites the reference file:line it restates):
   family (tools/research_cases.py:74-103, tests/performance/generators/suite.py:192-234).
 * :mod:`oracle.sexp`   -- the selective subnormal-preserving exponential
   (compile.py:2953-2965) as a CPU model with its error bound.
-* :mod:`oracle.interp` -- a scalar Kernel-IR interpreter
-  (tests/test_research_cases.py:44-231) for small bundled cases.
 
 Parity is pinned: ``tests/test_oracle.py`` checks these functions against the
 bundled expected outputs (``tests/golden/cases/*/expected.npz``) and against

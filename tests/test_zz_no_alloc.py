@@ -1,7 +1,8 @@
 """The allocation-free GEMM entry point, b2k_gemm_tf32x3_noalloc.
 
-Some callers cannot call cudaMalloc (capture-time code, fixed memory plans,
-memory owned by another allocator); for them the library offers a GEMM that
+Some callers cannot call cudaMalloc (embedders whose device memory belongs to
+another allocator or a pre-sized pool, runtimes that plan every buffer up
+front, host callbacks); for them the library offers a GEMM that
 keeps its operand split in a fixed array inside the library image instead of
 a context's growable scratch.  These tests call it through the C ABI twice in
 a row, with different shapes, layouts and data, and check each result
@@ -79,3 +80,8 @@ def test_noalloc_rejects_problems_beyond_its_scratch(ctx, torch_cuda):
     p = dummy.data_ptr()
     status = call_noalloc(lib, p, p, p, m, n, k, k, n, n, 0, None, 0)
     assert status == runtime.B2K_ESCRATCH
+    # A K so large that 2 * (m + n) * round_up(k, 32) would wrap int64 to a
+    # small number: refused before any size arithmetic, nothing launched.
+    status = call_noalloc(lib, p, p, p, 1, 1, 1 << 62, 1 << 62, 1, 1, 0, None, 0)
+    assert status == runtime.B2K_EINVAL
+    torch_cuda.cuda.synchronize()
