@@ -2,27 +2,39 @@
 """Benchmark of the B200 backend's hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|softmax|add|ragged|attention]
-                    [--impl ours|reference]
+                    [--impl ours|reference] [--only]
 
-A step is one pass of the hot path over one batch of synthetic input:
+A step is one pass of the hot path over one batch of synthetic input, the
+BASELINE configurations:
 
-* ``gemm`` (default) -- the 4096^3 FP32 GEMM as 3xTF32 on tcgen05 (split
-  pre-pass + tensor-core kernel), TFLOP/s of useful 2*M*N*K work;
+* ``gemm`` (default, the headline) -- the 4096^3 FP32 GEMM as 3xTF32 on
+  tcgen05 (operand split + tensor-core kernel), TFLOP/s of useful 2*M*N*K work;
 * ``softmax`` -- row softmax of 4096 x 8192 FP32, GB/s of one read + one write;
 * ``add`` -- c = a + b over 2^24 FP32, GB/s of two reads + one write;
 * ``ragged`` -- relu(A B^T + bias), 4097 x 1000 x 777, TFLOP/s;
 * ``attention`` -- softmax(Q K^T / sqrt(128)) V over 4 x 16 heads, S 2048,
   D 128, both contractions 3xTF32, TFLOP/s of useful 4*BH*S*S*D work.
 
-With N > 1 (torchrun, one rank per GPU) every rank processes its own batch of
-the same size (rows of A / rows of the matrix / ranges of the vector: the
-partitioning the work has), so the scaling is weak and no collective is on
-the data path.  ``value`` is all ranks' work over the max-over-ranks device
-time.  ``e2e`` repeats the step through the public host-array API with the
-inputs copied in from page-locked memory and the result copied out, every
-step.  ``--impl reference`` times the reference's CPU evaluation of the same
-workload (its float64 NumPy equations, restated in ``oracle/``) on the
-host cores.
+The line's top-level keys describe the selected workload (``--workload``,
+gemm by default); unless ``--only`` is given, a ``workloads`` object carries
+the same record (value, roofline, CPU baseline, end to end, clocks) for the
+other four configurations, each timed in its own region of the same run,
+and the GEMM and attention records carry a ``sustained`` leg: the same step
+repeated for at least two seconds with its own clock samples.
+
+With N > 1 (torchrun, one rank per GPU) ONE problem of the BASELINE size is
+partitioned over the ranks (rows of A, rows of the softmax, element ranges,
+batch*heads; ``mgpu.partition``) with every rank's shard already in its HBM:
+strong scaling, ``value`` = the whole problem's work over the max-over-ranks
+device time.  ``nccl_e2e`` repeats the partitioned step with its collectives
+(B broadcast from rank 0, all-gather of the output slabs) and ``weak`` gives
+the replica figure (every rank the whole problem).  ``e2e`` is the step
+through the public host-array API (``api.Session``, the ``b2k_*_host``
+calls) with every rank's inputs copied in from page-locked host memory and
+its outputs copied out, every step.  ``--impl reference`` times the
+reference's CPU evaluation of the same workloads -- its float64 NumPy
+equations (tools/research_cases.py:74-103, suite.py:192-234), restated in
+``oracle/refs.py`` -- on the host cores, one full evaluation per step.
 """
 from __future__ import annotations
 
@@ -30,6 +42,7 @@ import argparse
 import contextlib
 import importlib
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -45,10 +58,15 @@ sys.path.insert(0, str(ROOT))
 PKG = "emmy-hackathon-2026_b200"
 METRIC = "3xTF32 FP32-GEMM TFLOP/s & pointwise/softmax GB/s at 1/2/4/8 B200 vs roofline"
 L2_BYTES = 126 * 1024 * 1024
+WORKLOADS = ("gemm", "softmax", "add", "ragged", "attention")
 
 
 def pkg(name):
     return importlib.import_module(f"{PKG}.{name}")
+
+
+def oracle_refs():
+    return importlib.import_module("oracle.refs")
 
 
 def measured_peaks() -> tuple[dict, str]:
@@ -72,8 +90,8 @@ def profile_traffic(name: str) -> float | None:
     return None
 
 
-# --------------------------------------------------------------------------- workloads
-TIMING_EVERY = 8  # steps per sampled launch of the dominant kernel
+def scale(unit: str) -> float:
+    return 1e12 if unit == "TFLOP/s" else 1e9
 
 
 @contextlib.contextmanager
@@ -91,102 +109,174 @@ def stdout_to_stderr():
         os.close(saved)
 
 
+# --------------------------------------------------------------------------- workloads
 class Workload:
-    name = ""
-    unit = ""
-    bound = "hbm"
-    phase = ""          # library timing phase of the dominant kernel
-    kernels_per_step = 2  # the dominant kernel and the operand split before it
-    profile = ""
+    """One BASELINE configuration, partitioned over `world` ranks (this rank's
+    shard = `self.shard`), or whole on every rank when `replica` is set."""
 
-    def __init__(self, rank: int, world: int):
-        self.rank, self.world = rank, world
+    name = unit = bound = phase = profile = ""
+    kernels_per_step = 1      # kernels of the hot path per step
+    align = 1                 # shard granularity (units)
+    steps_default = 2000      # timed steps of a secondary record
+    cpu_seconds = 6.0         # CPU baseline sample length
 
-    # work units per step (flop or bytes), the numerator of `value`
-    def work(self) -> float:
+    def __init__(self, rank: int, world: int, replica: bool = False):
+        self.rank, self.world, self.replica = rank, world, replica
+        mgpu = pkg("mgpu")
+        self.shard = (mgpu.Shard(0, self.units()) if replica or world == 1
+                      else mgpu.partition(self.units(), world, rank, self.align))
+
+    # the partitioned axis: its extent and the work per unit
+    def units(self) -> int:
         raise NotImplementedError
 
+    def work_per_unit(self) -> float:
+        raise NotImplementedError
+
+    def work_total(self) -> float:
+        """Work of all ranks per step: the whole problem, or one whole problem
+        per rank for replicas."""
+        return self.work_per_unit() * self.units() * (self.world if self.replica else 1)
+
+    def work_shard(self) -> float:
+        return self.work_per_unit() * self.shard.count
+
     def dominant_work(self) -> float:
-        """Algorithmic work of one launch of the dominant kernel (roofline numerator)."""
-        return self.work()
+        """Algorithmic work of one launch of the dominant kernel on this rank."""
+        return self.work_shard()
+
+    def operand_bytes(self) -> int:
+        """Bytes of this rank's inputs and outputs (one operand set)."""
+        raise NotImplementedError
+
+    def operand_sets(self) -> int:
+        """Operand copies rotated step by step: enough that the data a step
+        reads was last touched more than an L2's worth of traffic earlier."""
+        size = max(1, self.operand_bytes())
+        return 1 if size > L2_BYTES else min(8, math.ceil(L2_BYTES / size) + 1)
+
+    def l2_note(self) -> str:
+        sets = self.operand_sets()
+        if sets == 1:
+            return "inputs larger than L2"
+        return (f"{sets} operand sets rotated per step ({self.operand_bytes() / 2**20:.0f} MiB each): a step's inputs "
+                f"were last touched {(sets - 1) * self.operand_bytes() / 2**20:.0f} MiB of traffic earlier, more "
+                "than the 126 MB L2")
+
+    # device set-up and one step (kernels only, shard pre-placed)
+    def setup(self, ctx, torch):
+        self.ctx = ctx
+        self.sets = [self.make_set(ctx, torch, i) for i in range(self.operand_sets())]
+        self.i = 0
+
+    def make_set(self, ctx, torch, i):
+        raise NotImplementedError
+
+    def step(self):
+        self.sets[self.i]()
+        self.i = (self.i + 1) % len(self.sets)
+
+    # end to end through the public host-array API
+    def e2e_setup(self, session):
+        raise NotImplementedError
+
+    def e2e_step(self):
+        raise NotImplementedError
+
+    # the partitioned step with its collectives (world > 1)
+    def nccl_setup(self, ctx, torch):
+        raise NotImplementedError
+
+    def nccl_step(self):
+        raise NotImplementedError
+
+    # CPU baseline: the oracle's float64 equations on the whole problem
+    def host_inputs(self):
+        raise NotImplementedError
+
+    def cpu_once(self) -> tuple[float, str]:
+        """One evaluation; returns (work units done, description)."""
+        raise NotImplementedError
+
+    def cpu_sample(self, seconds: float | None = None) -> tuple[float, str]:
+        seconds = self.cpu_seconds if seconds is None else seconds
+        done, work, t0 = 0, 0.0, time.perf_counter()
+        while True:
+            units, what = self.cpu_once()
+            work += units
+            done += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        return work / dt / scale(self.unit), f"{done} x {what}"
+
+    def cpu_extras(self) -> dict:
+        return {}
 
     def config(self) -> dict:
         raise NotImplementedError
 
-    def cpu_once(self, rows: int) -> tuple[float, str]:
-        raise NotImplementedError
-
-    def cpu_extras(self) -> dict:
-        """One-core figure of the same float64 sample (BLAS held to one thread),
-        and, for the GEMMs, the reference's own 3xTF32 model timed on a small
-        shape and extrapolated by flop."""
-        extras = {}
-        try:
-            from threadpoolctl import threadpool_limits
-            with threadpool_limits(limits=1):
-                v, what = self.cpu_sample(max_seconds=2.0, rows=self.reference_rows)
-            extras["single_core"] = {"value": round(v, 5), "unit": self.unit, "sample": what}
-        except ImportError:
-            pass
-        return extras
-
-    def cpu_sample(self, max_seconds: float = 12.0, rows: int | None = None) -> tuple[float, str]:
-        """Repeat the oracle's float64 evaluation of a bounded sample for about
-        `max_seconds`; returns (throughput in the metric's unit, description)."""
-        rows = rows or self.default_rows
-        done, work, t0 = 0, 0.0, time.perf_counter()
-        while True:
-            units, what = self.cpu_once(rows)
-            work += units
-            done += 1
-            if time.perf_counter() - t0 >= max_seconds or done >= 256:
-                break
-        dt = time.perf_counter() - t0
-        return work / dt / scale(self.unit), f"{done} x {what}"
+    def parallelism(self, axis: str) -> str:
+        if self.world == 1:
+            return "1 GPU"
+        if self.replica:
+            return f"{self.world} replicas (every rank the whole problem)"
+        return f"{self.world} GPUs, one problem partitioned by {axis} (rank {self.rank}: {self.shard.count} of {self.units()})"
 
 
 class Gemm(Workload):
     name, unit, bound, phase = "gemm", "TFLOP/s", "tensor", "mma"
     profile = "gemm_tf32x3_4096"
+    kernels_per_step = 2
+    align = 128
+    steps_default = 200
+    cpu_seconds = 8.0
 
-    def __init__(self, rank, world, m=4096, n=4096, k=4096, ragged=False):
-        super().__init__(rank, world)
+    def __init__(self, rank, world, replica=False, m=4096, n=4096, k=4096, ragged=False):
         self.m, self.n, self.k, self.ragged = m, n, k, ragged
+        super().__init__(rank, world, replica)
 
-    def inputs(self):
-        w = pkg("workloads")
-        if self.ragged:
-            return w.ragged_inputs(self.m, self.n, self.k)
-        a, b = w.gemm_inputs(self.m, self.n, self.k)
-        if self.rank:  # each rank owns a different slab of rows of A
-            a = np.random.default_rng(1001 + 7919 * self.rank).uniform(-1, 1, a.shape).astype(np.float32)
-        return a, b, None
+    def units(self):
+        return self.m
 
-    def work(self):
-        return 2.0 * self.m * self.n * self.k
+    def work_per_unit(self):
+        return 2.0 * self.n * self.k
 
     def dominant_work(self):
         # the tensor core executes three TF32 products per useful one
-        return 3.0 * self.work()
+        return 3.0 * self.work_shard()
 
-    def setup(self, ctx, torch):
-        a, b, bias = self.inputs()
-        self.host = (a, b, bias)
-        self.da, self.db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
-        self.dbias = torch.from_numpy(bias).cuda() if bias is not None else None
-        self.dc = torch.empty((self.m, self.n), dtype=torch.float32, device="cuda")
-        self.ctx = ctx
-        # the step's library call with its arguments converted once: every
-        # step still runs the whole GEMM (operand split + tensor-core kernel)
-        self.call = ctx.gemm_call(self.da.data_ptr(), self.db.data_ptr(), self.dc.data_ptr(), self.m, self.n,
-                                  self.k, b_layout=1 if self.ragged else 0,
-                                  bias=self.dbias.data_ptr() if self.dbias is not None else 0, relu=self.ragged)
+    def host_inputs(self):
+        if getattr(self, "_host", None) is None:
+            w = pkg("workloads")
+            if self.ragged:
+                self._host = w.ragged_inputs(self.m, self.n, self.k)
+            else:
+                a, b = w.gemm_inputs(self.m, self.n, self.k)
+                self._host = (a, b, None)
+        return self._host
 
-    def step(self):
-        self.call()
+    def local(self):
+        a, b, bias = self.host_inputs()
+        return a[self.shard.start:self.shard.start + self.shard.count], b, bias
+
+    def operand_bytes(self):
+        a, b, bias = self.local()
+        return a.nbytes + b.nbytes + 4 * a.shape[0] * self.n
+
+    def make_set(self, ctx, torch, i):
+        a, b, bias = self.local()
+        da, db = torch.from_numpy(np.ascontiguousarray(a)).cuda(), torch.from_numpy(b).cuda()
+        dbias = torch.from_numpy(bias).cuda() if bias is not None else None
+        dc = torch.empty((a.shape[0], self.n), dtype=torch.float32, device="cuda")
+        call = ctx.gemm_call(da.data_ptr(), db.data_ptr(), dc.data_ptr(), a.shape[0], self.n, self.k,
+                             b_layout=1 if self.ragged else 0,
+                             bias=dbias.data_ptr() if dbias is not None else 0, relu=self.ragged)
+        call.keep = (da, db, dbias, dc)
+        return call
 
     def e2e_setup(self, session):
-        a, b, bias = self.host
+        a, b, bias = self.local()
         self.session = session
         self.pa, self.pb = session.pinned(a.shape), session.pinned(b.shape)
         self.pa[...] = a
@@ -195,17 +285,62 @@ class Gemm(Workload):
         if bias is not None:
             self.pbias = session.pinned(bias.shape)
             self.pbias[...] = bias
-        self.pc = session.pinned((self.m, self.n))
+        self.pc = session.pinned((a.shape[0], self.n))
         self.e2e_bytes = (a.nbytes + b.nbytes + (bias.nbytes if bias is not None else 0), self.pc.nbytes)
 
     def e2e_step(self):
         self.session.gemm_host(self.pa, self.pb, self.pc, b_layout="nk" if self.ragged else "kn",
                                bias=self.pbias, relu=self.ragged)
 
+    def nccl_setup(self, ctx, torch):
+        a, b, bias = self.local()
+        self.torch, self.ctx = torch, ctx
+        self.n_a = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        self.n_b = torch.from_numpy(b).cuda() if self.rank == 0 else torch.empty(b.shape, device="cuda")
+        self.n_bias = torch.from_numpy(bias).cuda() if bias is not None else None
+        self.n_c = torch.empty((a.shape[0], self.n), device="cuda")
+        self.nccl_note = (f"NCCL broadcast of B ({b.nbytes / 2**20:.0f} MiB) from rank 0, local GEMM, all-gather "
+                          f"of C row slabs ({self.m * self.n * 4 / 2**20:.0f} MiB)")
+
+    def nccl_step(self):
+        mgpu = pkg("mgpu")
+
+        def compute(a_rows, b_full):
+            self.ctx.gemm(a_rows.data_ptr(), b_full.data_ptr(), self.n_c.data_ptr(), a_rows.shape[0], self.n, self.k,
+                          b_layout=1 if self.ragged else 0,
+                          bias=self.n_bias.data_ptr() if self.n_bias is not None else 0, relu=self.ragged)
+            return self.n_c
+        return mgpu.sharded_gemm(self.n_a, self.n_b, self.m, self.rank, self.world, compute, self.torch,
+                                 align=self.align)
+
+    def cpu_once(self):
+        refs = oracle_refs()
+        a, b, bias = self.host_inputs()
+        if self.ragged:
+            refs.matmul_bias_relu(a, b, bias)
+        else:
+            refs.matmul(a, b)
+        return 2.0 * self.m * self.n * self.k, (f"float64 NumPy evaluation of the whole {self.m}x{self.n}x{self.k} "
+                                                "GEMM" + (" + bias + ReLU" if self.ragged else ""))
+
     def cpu_extras(self):
-        extras = super().cpu_extras()
+        extras = {}
+        with contextlib.suppress(ImportError):
+            from threadpoolctl import threadpool_limits
+            refs = oracle_refs()
+            a, b, bias = self.host_inputs()
+            rows = 256
+            b64 = refs._f64(b).T.copy() if self.ragged else refs._f64(b)
+            with threadpool_limits(limits=1):
+                reps, t0 = 0, time.perf_counter()
+                while reps < 2 or time.perf_counter() - t0 < 1.5:
+                    refs._f64(a[:rows]) @ b64
+                    reps += 1
+                dt = (time.perf_counter() - t0) / reps
+            extras["single_core"] = {"value": round(2.0 * rows * self.n * self.k / dt / 1e12, 5), "unit": self.unit,
+                                     "sample": f"{reps} x float64 matmul of a {rows}-row slab of A, BLAS on 1 thread"}
         # tf32_emitter.py:64-96's model (per-8-K atom, three FP32 accumulators),
-        # restated in oracle/tf32.py, on a 256^3 slab: its cost is linear in flop.
+        # restated in oracle/tf32.py, on a 256^3 GEMM: its cost is linear in flop.
         tf32 = importlib.import_module("oracle.tf32")
         rng = np.random.default_rng(5)
         a = rng.uniform(-1, 1, (256, 256)).astype(np.float32)
@@ -220,239 +355,275 @@ class Gemm(Workload):
                                           "3xTF32 model, tf32_emitter.py:64-96), extrapolated by flop"}
         return extras
 
-    def cpu_once(self, rows):
-        # The oracle's float64 equations (refs.matmul / refs.matmul_bias_relu)
-        # on a row slab of A.  B's float64 copy is made once and reused: a
-        # full-size evaluation converts B once, so converting it again for
-        # every slab would understate the reference's throughput.
-        refs = importlib.import_module("oracle.refs")
-        a, b, bias = self.host
-        if getattr(self, "b64", None) is None:
-            self.b64 = refs._f64(b).T.copy() if self.ragged else refs._f64(b)
-        c = refs._f64(a[:rows]) @ self.b64
-        if self.ragged:
-            c = np.maximum(c + refs._f64(bias), 0.0)
-        c.astype(np.float32)
-        return 2.0 * rows * self.n * self.k, f"float64 NumPy matmul of a {rows}-row slab of A ({self.m}x{self.n}x{self.k})"
-
-    default_rows = 1024
-    reference_rows = 256
-
     def config(self):
         return {"workload": "ragged_gemm_bias_relu" if self.ragged else "gemm_3xtf32",
-                "m": self.m * self.world, "m_per_gpu": self.m, "n": self.n, "k": self.k,
+                "m": self.m, "n": self.n, "k": self.k, "m_this_rank": self.shard.count,
                 "b_layout": "n_k (transposed)" if self.ragged else "k_n",
                 "epilogue": "bias+relu" if self.ragged else "copy",
                 "inputs": "A,B ~ N(0,1) seeded" if self.ragged else "A,B ~ U[-1,1] seeded",
-                "l2": "inputs larger than L2" if (self.m * self.k + self.n * self.k) * 4 > L2_BYTES
-                else "inputs smaller than L2 (split scratch 2x inputs)",
-                "parallelism": f"dp{self.world} (rows of A per GPU, B replicated)"}
+                "l2": self.l2_note(), "parallelism": self.parallelism("rows of A (B replicated)")}
 
 
 class Softmax(Workload):
     name, unit, bound, phase = "softmax", "GB/s", "hbm", "softmax"
-    kernels_per_step = 1
     profile = "row_softmax_4096x8192"
+    steps_default = 2000
 
-    def __init__(self, rank, world, rows=4096, cols=8192):
-        super().__init__(rank, world)
+    def __init__(self, rank, world, replica=False, rows=4096, cols=8192):
         self.rows, self.cols = rows, cols
+        super().__init__(rank, world, replica)
 
-    def work(self):
-        return 2.0 * 4 * self.rows * self.cols
+    def units(self):
+        return self.rows
 
-    def setup(self, ctx, torch):
-        x = pkg("workloads").softmax_input(self.rows, self.cols)
-        self.host = x
-        self.ctx = ctx
-        # two operand copies used alternately, as for the add: no step finds
-        # the previous step's data in L2
-        self.sets = []
-        for _ in range(2):
-            dx = torch.from_numpy(x).cuda()
-            dy = torch.empty_like(dx)
-            self.sets.append((dx, dy, ctx.row_softmax_call(dx.data_ptr(), dy.data_ptr(), self.rows, self.cols)))
-        self.i = 0
+    def work_per_unit(self):
+        return 2.0 * 4 * self.cols
 
-    def step(self):
-        self.sets[self.i][2]()
-        self.i ^= 1
+    def host_inputs(self):
+        if getattr(self, "_host", None) is None:
+            self._host = pkg("workloads").softmax_input(self.rows, self.cols)
+        return self._host
+
+    def local(self):
+        return self.host_inputs()[self.shard.start:self.shard.start + self.shard.count]
+
+    def operand_bytes(self):
+        return 2 * self.local().nbytes
+
+    def make_set(self, ctx, torch, i):
+        x = self.local()
+        dx = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        dy = torch.empty_like(dx)
+        call = ctx.row_softmax_call(dx.data_ptr(), dy.data_ptr(), x.shape[0], self.cols)
+        call.keep = (dx, dy)
+        return call
 
     def e2e_setup(self, session):
+        x = self.local()
         self.session = session
-        self.px = session.pinned(self.host.shape)
-        self.px[...] = self.host
-        self.py = session.pinned(self.host.shape)
+        self.px = session.pinned(x.shape)
+        self.px[...] = x
+        self.py = session.pinned(x.shape)
         self.e2e_bytes = (self.px.nbytes, self.py.nbytes)
 
     def e2e_step(self):
         self.session.row_softmax_host(self.px, self.py)
 
-    def cpu_once(self, rows):
-        refs = importlib.import_module("oracle.refs")
-        refs.softmax(self.host[:rows])
-        return 2.0 * 4 * rows * self.cols, f"float64 NumPy stable softmax of {rows} rows x {self.cols}"
+    def nccl_setup(self, ctx, torch):
+        self.torch, self.ctx = torch, ctx
+        self.n_x = torch.from_numpy(np.ascontiguousarray(self.local())).cuda()
+        self.n_y = torch.empty_like(self.n_x)
+        self.nccl_note = f"local softmax, all-gather of the output rows ({self.rows * self.cols * 4 / 2**20:.0f} MiB)"
 
-    default_rows = 512
-    reference_rows = 64
+    def nccl_step(self):
+        mgpu = pkg("mgpu")
+
+        def compute(x):
+            self.ctx.row_softmax(x.data_ptr(), self.n_y.data_ptr(), x.shape[0], self.cols)
+            return self.n_y
+        return mgpu.sharded_slabs((self.n_x,), self.rows, self.rank, self.world, compute, self.torch)
+
+    def cpu_once(self):
+        oracle_refs().softmax(self.host_inputs())
+        return 2.0 * 4 * self.rows * self.cols, f"float64 NumPy stable softmax of the whole {self.rows}x{self.cols} matrix"
 
     def subnormal_exp_args(self) -> int:
         """How many exp arguments x - rowmax of this input give a subnormal
         FP32 result (arguments in [-103.28, -87.34]): the range the selective
         exponential exists for."""
-        if getattr(self, "_subnormal", None) is None:
-            x = getattr(self, "host", None)
-            if x is None:
-                x = pkg("workloads").softmax_input(self.rows, self.cols)
-            t = x - x.max(axis=1, keepdims=True)
-            self._subnormal = int(np.count_nonzero((t >= -103.28) & (t < -87.34)))
-        return self._subnormal
+        x = self.host_inputs()
+        t = x - x.max(axis=1, keepdims=True)
+        return int(np.count_nonzero((t >= -103.28) & (t < -87.34)))
 
     def config(self):
-        return {"workload": "row_softmax", "rows": self.rows * self.world, "rows_per_gpu": self.rows,
-                "cols": self.cols, "inputs": "N(0,16), 1% set to -100, seeded",
-                "operand_sets": "2, alternating per step (nothing carried in L2 between steps)",
-                "exp_args_in_subnormal_range": self.subnormal_exp_args(),
-                "l2": "inputs larger than L2", "parallelism": f"dp{self.world} (rows per GPU)"}
+        return {"workload": "row_softmax", "rows": self.rows, "rows_this_rank": self.shard.count, "cols": self.cols,
+                "inputs": "N(0,16), 1% set to -100, seeded", "exp_args_in_subnormal_range": self.subnormal_exp_args(),
+                "l2": self.l2_note(), "parallelism": self.parallelism("rows")}
 
 
 class Add(Workload):
     name, unit, bound, phase = "add", "GB/s", "hbm", "pointwise"
-    kernels_per_step = 1
     profile = "pointwise_add_2e24"
+    align = 4
+    steps_default = 2000
+    cpu_seconds = 4.0
 
-    def __init__(self, rank, world, n=1 << 24):
-        super().__init__(rank, world)
+    def __init__(self, rank, world, replica=False, n=1 << 24):
         self.n = n
+        super().__init__(rank, world, replica)
 
-    def work(self):
-        return 3.0 * 4 * self.n
+    def units(self):
+        return self.n
 
-    def setup(self, ctx, torch):
-        a, b = pkg("workloads").add_inputs(self.n)
-        self.host = (a, b)
-        self.prog = pkg("runtime").make_program(2, [("add", 0, 1, 0, 0.0)], 2)
-        self.ctx = ctx
-        # Two copies of the operands, used alternately: a step's 201 MB were
-        # last touched two steps earlier, with 201 MB in between, so nothing
-        # of them is left in the 126 MB L2 and every step streams from HBM.
-        self.sets = []
-        for _ in range(2):
-            da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
-            dc = torch.empty_like(da)
-            call = ctx.pointwise_call(self.prog, [da.data_ptr(), db.data_ptr()], dc.data_ptr(), self.n)
-            self.sets.append((da, db, dc, call))
-        self.i = 0
+    def work_per_unit(self):
+        return 3.0 * 4
 
-    def step(self):
-        self.sets[self.i][3]()
-        self.i ^= 1
+    def host_inputs(self):
+        if getattr(self, "_host", None) is None:
+            self._host = pkg("workloads").add_inputs(self.n)
+        return self._host
+
+    def local(self):
+        a, b = self.host_inputs()
+        sl = slice(self.shard.start, self.shard.start + self.shard.count)
+        return a[sl], b[sl]
+
+    def operand_bytes(self):
+        return 3 * self.local()[0].nbytes
+
+    def program(self):
+        if getattr(self, "_prog", None) is None:
+            self._prog = pkg("runtime").make_program(2, [("add", 0, 1, 0, 0.0)], 2)
+        return self._prog
+
+    def make_set(self, ctx, torch, i):
+        a, b = self.local()
+        da, db = torch.from_numpy(np.ascontiguousarray(a)).cuda(), torch.from_numpy(np.ascontiguousarray(b)).cuda()
+        dc = torch.empty_like(da)
+        call = ctx.pointwise_call(self.program(), [da.data_ptr(), db.data_ptr()], dc.data_ptr(), a.size)
+        call.keep_tensors = (da, db, dc)
+        return call
 
     def e2e_setup(self, session):
+        a, b = self.local()
         self.session = session
-        self.pa, self.pb, self.pc = (session.pinned((self.n,)) for _ in range(3))
-        self.pa[...] = self.host[0]
-        self.pb[...] = self.host[1]
+        self.pa, self.pb, self.pc = (session.pinned(a.shape) for _ in range(3))
+        self.pa[...] = a
+        self.pb[...] = b
         self.e2e_bytes = (2 * self.pa.nbytes, self.pc.nbytes)
 
     def e2e_step(self):
-        self.session.pointwise_host(self.prog, [self.pa, self.pb], self.pc)
+        self.session.pointwise_host(self.program(), [self.pa, self.pb], self.pc)
 
-    def cpu_once(self, rows):
-        refs = importlib.import_module("oracle.refs")
-        a, b = self.host
-        refs.pointwise("add", a[:rows], b[:rows])
-        return 3.0 * 4 * rows, f"float64 NumPy a+b over {rows} elements"
+    def nccl_setup(self, ctx, torch):
+        self.torch, self.ctx = torch, ctx
+        a, b = self.local()
+        self.n_a, self.n_b = torch.from_numpy(np.ascontiguousarray(a)).cuda(), torch.from_numpy(np.ascontiguousarray(b)).cuda()
+        self.n_c = torch.empty_like(self.n_a)
+        self.nccl_note = f"local add, all-gather of c's element ranges ({self.n * 4 / 2**20:.0f} MiB)"
 
-    default_rows = 1 << 24
-    reference_rows = 1 << 22
+    def nccl_step(self):
+        mgpu = pkg("mgpu")
+
+        def compute(a, b):
+            self.ctx.pointwise(self.program(), [a.data_ptr(), b.data_ptr()], self.n_c.data_ptr(), a.numel())
+            return self.n_c
+        return mgpu.sharded_slabs((self.n_a, self.n_b), self.n, self.rank, self.world, compute, self.torch,
+                                  align=self.align)
+
+    def cpu_once(self):
+        a, b = self.host_inputs()
+        oracle_refs().pointwise("add", a, b)
+        return 3.0 * 4 * self.n, f"float64 NumPy a + b over all {self.n} elements"
 
     def config(self):
-        return {"workload": "pointwise_add", "n": self.n * self.world, "n_per_gpu": self.n,
-                "operand_sets": "2, alternating per step (nothing carried in L2 between steps)",
-                "inputs": "a,b ~ U[-1,1] seeded", "l2": "inputs larger than L2",
-                "parallelism": f"dp{self.world} (contiguous ranges per GPU)"}
+        return {"workload": "pointwise_add", "n": self.n, "n_this_rank": self.shard.count,
+                "inputs": "a,b ~ U[-1,1] seeded", "l2": self.l2_note(),
+                "parallelism": self.parallelism("contiguous element ranges")}
 
 
 class Attention(Workload):
     name, unit, bound, phase = "attention", "TFLOP/s", "tensor", "flash"
     profile = "attention_tf32x3_64x2048x128"
+    kernels_per_step = 3
+    steps_default = 100
+    cpu_heads = 8           # heads per CPU sample (one head is ~0.3 s of float64 BLAS)
 
-    def __init__(self, rank, world, bh=64, seq=2048, d=128):
-        super().__init__(rank, world)
+    def __init__(self, rank, world, replica=False, bh=64, seq=2048, d=128):
         self.bh, self.seq, self.d = bh, seq, d
+        super().__init__(rank, world, replica)
 
-    def work(self):
-        return 4.0 * self.bh * self.seq * self.seq * self.d
+    def units(self):
+        return self.bh
+
+    def work_per_unit(self):
+        return 4.0 * self.seq * self.seq * self.d
 
     def dominant_work(self):
         # the fused kernel runs both contractions, three TF32 products each
-        return 3.0 * self.work()
+        return 3.0 * self.work_shard()
 
-    def setup(self, ctx, torch):
-        q, k, v = pkg("workloads").attention_inputs(self.bh, self.seq, self.d)
-        if self.rank:
-            q = np.random.default_rng(3001 + 7919 * self.rank).standard_normal(q.shape).astype(np.float32)
-        self.host = (q, k, v)
-        self.dq, self.dk, self.dv = (torch.from_numpy(t).cuda() for t in (q, k, v))
-        self.do = torch.empty_like(self.dq)
-        self.ctx = ctx
-        self.call = ctx.attention_call(self.dq.data_ptr(), self.dk.data_ptr(), self.dv.data_ptr(),
-                                       self.do.data_ptr(), self.bh, self.seq, self.seq, self.d, self.d)
+    def host_inputs(self):
+        if getattr(self, "_host", None) is None:
+            self._host = pkg("workloads").attention_inputs(self.bh, self.seq, self.d)
+        return self._host
 
-    def step(self):
-        self.call()
+    def local(self):
+        sl = slice(self.shard.start, self.shard.start + self.shard.count)
+        return tuple(t[sl] for t in self.host_inputs())
+
+    def operand_bytes(self):
+        return 4 * self.local()[0].nbytes
+
+    def make_set(self, ctx, torch, i):
+        q, k, v = self.local()
+        dq, dk, dv = (torch.from_numpy(np.ascontiguousarray(t)).cuda() for t in (q, k, v))
+        do = torch.empty_like(dq)
+        call = ctx.attention_call(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), do.data_ptr(), q.shape[0], self.seq,
+                                  self.seq, self.d, self.d)
+        call.keep = (dq, dk, dv, do)
+        return call
 
     def e2e_setup(self, session):
+        q, k, v = self.local()
         self.session = session
-        self.pin = [session.pinned(t.shape) for t in self.host]
-        for p, t in zip(self.pin, self.host):
+        self.pin = [session.pinned(t.shape) for t in (q, k, v)]
+        for p, t in zip(self.pin, (q, k, v)):
             p[...] = t
-        self.pout = session.pinned(self.host[0].shape)
-        self.e2e_bytes = (sum(t.nbytes for t in self.host), self.pout.nbytes)
+        self.pout = session.pinned(q.shape)
+        self.e2e_bytes = (3 * q.nbytes, self.pout.nbytes)
 
     def e2e_step(self):
         self.session.attention_host(*self.pin, self.pout)
 
-    def cpu_once(self, rows):
-        refs = importlib.import_module("oracle.refs")
-        q, k, v = self.host
-        heads = max(1, rows)
-        refs.attention_batched(q[:heads], k[:heads], v[:heads])
-        return 4.0 * heads * self.seq * self.seq * self.d, f"float64 NumPy attention of {heads} head(s) (S {self.seq}, D {self.d})"
+    def nccl_setup(self, ctx, torch):
+        self.torch, self.ctx = torch, ctx
+        self.n_in = [torch.from_numpy(np.ascontiguousarray(t)).cuda() for t in self.local()]
+        self.n_o = torch.empty_like(self.n_in[0])
+        self.nccl_note = (f"heads pre-sharded with Q, K and V (nothing broadcast), all-gather of O "
+                          f"({self.bh * self.seq * self.d * 4 / 2**20:.0f} MiB)")
 
-    default_rows = 2
-    reference_rows = 1
+    def nccl_step(self):
+        mgpu = pkg("mgpu")
+
+        def compute(q, k, v):
+            self.ctx.attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), self.n_o.data_ptr(), q.shape[0], self.seq,
+                               self.seq, self.d, self.d)
+            return self.n_o
+        return mgpu.sharded_slabs(tuple(self.n_in), self.bh, self.rank, self.world, compute, self.torch)
+
+    def cpu_once(self):
+        q, k, v = self.host_inputs()
+        h = self.cpu_heads
+        oracle_refs().attention_batched(q[:h], k[:h], v[:h])
+        return 4.0 * h * self.seq * self.seq * self.d, (f"float64 NumPy attention of {h} whole heads (S {self.seq}, "
+                                                        f"D {self.d}) of the 64")
 
     def config(self):
-        return {"workload": "attention_3xtf32", "batch_heads": self.bh * self.world, "batch_heads_per_gpu": self.bh,
+        return {"workload": "attention_3xtf32", "batch_heads": self.bh, "heads_this_rank": self.shard.count,
                 "seq": self.seq, "head_dim": self.d, "scale": "1/sqrt(128)", "inputs": "Q,K,V ~ N(0,1) seeded",
-                "l2": "inputs larger than L2", "parallelism": f"dp{self.world} (batch*heads per GPU)"}
+                "l2": self.l2_note(), "parallelism": self.parallelism("batch*heads")}
 
 
-def make_workload(name, rank, world):
+def make_workload(name, rank, world, replica=False):
     if name == "attention":
-        return Attention(rank, world)
+        return Attention(rank, world, replica)
     if name == "gemm":
-        return Gemm(rank, world)
+        return Gemm(rank, world, replica)
     if name == "ragged":
-        w = Gemm(rank, world, 4097, 1000, 777, ragged=True)
-        w.profile = "gemm_tf32x3_ragged"
+        w = Gemm(rank, world, replica, 4097, 1000, 777, ragged=True)
+        w.name, w.profile, w.steps_default, w.cpu_seconds = "ragged", "gemm_tf32x3_ragged", 2000, 4.0
         return w
     if name == "softmax":
-        return Softmax(rank, world)
+        return Softmax(rank, world, replica)
     if name == "add":
-        return Add(rank, world)
+        return Add(rank, world, replica)
     raise SystemExit(f"unknown workload {name}")
-
-
-def scale(unit: str) -> float:
-    return 1e12 if unit == "TFLOP/s" else 1e9
 
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+    """nvidia-smi clock / throttle-reason samples while a timed region runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -495,11 +666,12 @@ class ClockSampler:
                 return None
         sm = [num(r[1]) for r in rows if num(r[1]) is not None]
         mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        pw = [num(r[3]) for r in rows if num(r[3]) is not None]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
 
 
-# --------------------------------------------------------------------------- arms
+# --------------------------------------------------------------------------- our arm
 def init_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -507,41 +679,194 @@ def init_dist():
     return rank, local, world
 
 
-def strong_scaling_gemm(ctx, torch, dist, rank, world, barrier, max_over_ranks, steps=10, warmup=3) -> dict:
-    """One 4096^3 GEMM split by rows of A over the ranks (mgpu.sharded_gemm):
-    NCCL broadcasts B from rank 0, each rank multiplies its row slab with the
-    C-ABI GEMM, NCCL all-gathers C.  Device-timed with CUDA events around the
-    whole call, max over ranks."""
-    mgpu, workloads = pkg("mgpu"), pkg("workloads")
-    m = n = k = 4096
-    a, b = workloads.gemm_inputs(m, n, k)
-    shard = mgpu.partition(m, world, rank, align=128)
-    a_rows = torch.from_numpy(a[shard.start:shard.start + shard.count]).cuda()
-    b_dev = torch.from_numpy(b).cuda() if rank == 0 else torch.empty((k, n), device="cuda")
+class Runner:
+    """Per-process state of our arm: the context, the process group helpers."""
 
-    def compute(a_part, b_full):
-        c_part = torch.empty((a_part.shape[0], n), device="cuda")
-        ctx.gemm(a_part.data_ptr(), b_full.data_ptr(), c_part.data_ptr(), a_part.shape[0], n, k)
-        return c_part
+    TIMING_EVERY = 8  # steps per sampled launch of a multi-kernel step's dominant kernel
 
-    for _ in range(warmup):
-        mgpu.sharded_gemm(a_rows, b_dev, m, rank, world, compute, torch, device="cuda")
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        c = mgpu.sharded_gemm(a_rows, b_dev, m, rank, world, compute, torch, device="cuda")
-    e1.record()
-    barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1)) / steps
-    # size-independent check of the gathered C: its column sums equal (1^T A) B
-    col = c.double().sum(dim=0).cpu().numpy()
-    want = a.astype(np.float64).sum(axis=0) @ b.astype(np.float64)
-    rel = float(np.max(np.abs(col - want)) / np.max(np.abs(want)))
-    return {"value": round(2.0 * m * n * k / (ms / 1e3) / 1e12, 3), "unit": "TFLOP/s", "ms_per_gemm": round(ms, 4),
-            "n_gpus": world, "steps": steps, "problem": "one 4096x4096x4096 GEMM (strong scaling)",
-            "collectives": "NCCL broadcast of B (64 MiB) from rank 0, all_gather of C row slabs (64 MiB)",
-            "column_sum_rel_err": rel}
+    def __init__(self, torch, dist, rank, local, world):
+        self.torch, self.dist, self.rank, self.local, self.world = torch, dist, rank, local, world
+        self.ctx = pkg("runtime").Context(local)
+        self.peaks, self.peak_basis = measured_peaks()
+
+    def barrier(self):
+        self.torch.cuda.synchronize()
+        if self.dist is not None:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max_over_ranks(self, x: float) -> float:
+        if self.dist is None:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def event_pair(self):
+        return (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
+
+    def timed(self, w: Workload, steps: int, warmup: int, sample_dominant: bool = True) -> dict:
+        """Warm-up, then EXACTLY `steps` steps between barriers; device time with
+        CUDA events (max over ranks), clocks sampled during the region, and the
+        dominant kernel's average launch time."""
+        ctx = self.ctx
+        for _ in range(warmup):
+            w.step()
+        ctx.sync()
+        sampler = ClockSampler(self.local)
+        sampler.start()
+        time.sleep(0.3)
+        ctx.timing_reset()
+        self.barrier()
+        launches_before = ctx.kernel_launches()
+        start, stop = self.event_pair()
+        start.record()
+        for i in range(steps):
+            sampled = sample_dominant and w.kernels_per_step > 1 and i % self.TIMING_EVERY == 0
+            if sampled:
+                ctx.timing(True, phases=[w.phase])
+            w.step()
+            if sampled:
+                ctx.timing(False)
+        stop.record()
+        launches = ctx.kernel_launches() - launches_before
+        self.barrier()
+        clocks = sampler.stop()
+        ctx.sync()  # surfaces a device-side error status
+        ms = self.max_over_ranks(start.elapsed_time(stop))
+        ctx.timing(False)
+        if w.kernels_per_step == 1:
+            # One kernel per step: its average launch duration is the timed
+            # region's event time over its launches (back to back, gaps
+            # included); a bracketed launch would add the events' own latency.
+            dom_ms, dom_launches = ms, max(1, launches)
+            basis = "timed region / launches (one kernel per step)"
+        else:
+            dom_ms, dom_launches = ctx.timing_read(w.phase)
+            dom_ms = self.max_over_ranks(dom_ms)
+            basis = f"CUDA event pair around the kernel on 1 in {self.TIMING_EVERY} steps of the timed region"
+        return {"ms": ms, "steps": steps, "launches": launches, "clocks": clocks,
+                "dom_ms": dom_ms / max(1, dom_launches), "dom_basis": basis}
+
+    def roofline(self, w: Workload, t: dict, sustained: bool = False) -> dict:
+        peaks, basis = self.peaks, self.peak_basis
+        launch_s = t["dom_ms"] / 1e3
+        if w.bound == "tensor":
+            achieved = w.dominant_work() / launch_s / 1e12
+            # a long, power-capped region is compared with the sustained GEMM peak
+            clocks = t["clocks"]
+            capped = sustained or (clocks.get("sm_mhz") or 0) < 0.9 * (clocks.get("sm_max_mhz") or 0)
+            use_sustained = capped and "bf16_tflops_sustained" in peaks
+            peak = (peaks["bf16_tflops_sustained"] if use_sustained else peaks["bf16_tflops"]) / 2.0
+            note = (f"{basis} bf16 dense TF/s / 2 = TF32 dense rate (" + ("sustained" if use_sustained else "burst")
+                    + "); achieved counts the three TF32 products per useful one")
+            unit = "TFLOP/s"
+        else:
+            achieved = w.dominant_work() / launch_s / 1e9
+            peak = peaks["hbm_gbs"]
+            note = f"{basis} HBM copy GB/s"
+            unit = "GB/s"
+        return {"bound": w.bound, "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": unit,
+                "frac": round(achieved / peak, 4), "traffic": profile_traffic(w.profile), "kernel": w.phase,
+                "launch_ms": round(t["dom_ms"], 5), "launch_timing": t["dom_basis"], "peak_basis": note}
+
+    def e2e(self, w: Workload, steps: int) -> dict:
+        api = pkg("api")
+        session = api.Session(self.local)
+        try:
+            w.e2e_setup(session)
+            for _ in range(2):
+                w.e2e_step()
+            session.sync()
+            self.barrier()
+            e0, e1 = self.event_pair()
+            e0.record()
+            for _ in range(steps):
+                w.e2e_step()
+            e1.record()
+            session.sync()
+            self.barrier()
+            ms = self.max_over_ranks(e0.elapsed_time(e1))
+        finally:
+            session.close()
+        return {"value": round(w.work_total() * steps / (ms / 1e3) / scale(w.unit), 3), "unit": w.unit,
+                "h2d_bytes_per_step": int(w.e2e_bytes[0]), "d2h_bytes_per_step": int(w.e2e_bytes[1]),
+                "steps": steps, "ms_per_step": round(ms / steps, 4),
+                "api": "api.Session pipelined host-array calls (b2k_*_host: slabbed copy-in, kernels and copy-out "
+                       "overlapped)" + (", each rank its own shard" if self.world > 1 else "")}
+
+    def nccl_e2e(self, w: Workload, steps: int = 10, warmup: int = 3) -> dict:
+        """The partitioned step with its collectives, device-resident (max over ranks)."""
+        w.nccl_setup(self.ctx, self.torch)
+        for _ in range(warmup):
+            out = w.nccl_step()
+        self.barrier()
+        e0, e1 = self.event_pair()
+        e0.record()
+        for _ in range(steps):
+            out = w.nccl_step()
+        e1.record()
+        self.barrier()
+        ms = self.max_over_ranks(e0.elapsed_time(e1))
+        # size-independent check of the gathered output on every rank
+        checksum = float(out.double().sum().item())
+        return {"value": round(w.work_total() * steps / (ms / 1e3) / scale(w.unit), 3), "unit": w.unit,
+                "ms_per_step": round(ms / steps, 4), "steps": steps, "collectives": w.nccl_note,
+                "gathered_output_sum": checksum}
+
+    def record(self, name: str, args, headline: bool) -> dict:
+        """Every measurement of one workload; rank 0 gets the record."""
+        torch = self.torch
+        w = make_workload(name, self.rank, self.world)
+        w.setup(self.ctx, torch)
+        steps = args.steps if headline else (args.sub_steps or w.steps_default)
+        t = self.timed(w, steps, args.warmup)
+        rec = {"metric": METRIC if headline else f"{w.name} {w.unit}",
+               "value": round(w.work_total() * steps / (t["ms"] / 1e3) / scale(w.unit), 3), "unit": w.unit,
+               "n_gpus": self.world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(t["ms"] / steps, 5),
+               "higher_is_better": True, "scaling": "strong" if self.world > 1 else "weak",
+               "dtype": "f32 (3xtf32 tensor)" if w.bound == "tensor" else "f32",
+               "config": w.config(), "roofline": self.roofline(w, t), "clocks": t["clocks"],
+               "gpu_launches": t["launches"]}
+        if self.world > 1:
+            rec["timing"] = ("kernels only, every rank's shard pre-placed in its HBM; time = max over ranks of each "
+                             "rank's CUDA-event time")
+        # sustained leg: the same step for >= 2 s (tensor-bound workloads, one GPU)
+        if self.world == 1 and w.bound == "tensor" and not args.no_sustained:
+            probe = max(1e-3, t["ms"] / steps / 1e3)
+            s_steps = max(steps, int(math.ceil(2.2 / probe)))
+            ts = self.timed(w, s_steps, 0)
+            rec["sustained"] = {"value": round(w.work_total() * s_steps / (ts["ms"] / 1e3) / scale(w.unit), 3),
+                                "unit": w.unit, "steps": s_steps, "seconds": round(ts["ms"] / 1e3, 3),
+                                "ms_per_step": round(ts["ms"] / s_steps, 5), "clocks": ts["clocks"],
+                                "roofline": self.roofline(w, ts, sustained=True)}
+        w.sets = []
+        torch.cuda.empty_cache()
+        # end to end through the public host-array API
+        rec["e2e"] = self.e2e(w, max(3, min(steps, 20)))
+        torch.cuda.empty_cache()
+        if self.world > 1:
+            rec["nccl_e2e"] = self.nccl_e2e(w)
+            w.n_in = w.n_a = w.n_b = w.n_x = w.n_y = w.n_c = w.n_o = None
+            torch.cuda.empty_cache()
+            # replica figure: every rank the whole problem, no collective
+            wr = make_workload(name, self.rank, self.world, replica=True)
+            wr.setup(self.ctx, torch)
+            tr = self.timed(wr, max(3, min(steps, 50)), args.warmup, sample_dominant=False)
+            rec["weak"] = {"value": round(wr.work_total() * tr["steps"] / (tr["ms"] / 1e3) / scale(w.unit), 3),
+                           "unit": w.unit, "ms_per_step": round(tr["ms"] / tr["steps"], 5), "steps": tr["steps"],
+                           "problem": "every rank the whole BASELINE problem (replicas)"}
+            wr.sets = []
+            torch.cuda.empty_cache()
+        if self.rank == 0 and self.world == 1 and not args.no_cpu:
+            v, sample = w.cpu_sample()
+            cpu = {"value": round(v, 4), "unit": w.unit, "cores": os.cpu_count(), "kind": "port",
+                   "sample": sample + " (oracle/refs.py float64 equations, NumPy/BLAS threads = all cores)"}
+            cpu.update(w.cpu_extras())
+            rec["cpu_baseline"] = cpu
+        else:
+            rec["cpu_baseline"] = None
+        return rec
 
 
 def run_ours(args) -> dict | None:
@@ -556,171 +881,66 @@ def run_ours(args) -> dict | None:
         with stdout_to_stderr():
             pkg("mgpu").init_from_env("nccl", timeout_s=120)
             dist.barrier()
-    runtime, api = pkg("runtime"), pkg("api")
-    ctx = runtime.Context(local)
-    w = make_workload(args.workload, rank, world)
-    w.setup(ctx, torch)
-
-    def barrier():
-        torch.cuda.synchronize()
+    runner = Runner(torch, dist, rank, local, world)
+    try:
+        rec = runner.record(args.workload, args, headline=True)
+        if not args.only:
+            others = {}
+            for name in WORKLOADS:
+                if name != args.workload:
+                    r = runner.record(name, args, headline=False)
+                    r.pop("metric", None)
+                    others[name] = r
+            rec["workloads"] = others
+        rec["vs_baseline"] = None
+        rec["data"] = "synthetic (seeded, distributions of the BASELINE configs)"
+    finally:
+        runner.ctx.close()
         if dist is not None:
             dist.barrier()
-        torch.cuda.synchronize()
+            dist.destroy_process_group()
+    if rank != 0:
+        return None
+    order = ["metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+             "vs_baseline", "dtype", "data", "config"]
+    return {**{k: rec[k] for k in order if k in rec}, **{k: v for k, v in rec.items() if k not in order}}
 
-    def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
-    for _ in range(args.warmup):
-        w.step()
-    ctx.sync()
-    # --- device-resident timed region ------------------------------------------
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    ctx.timing_reset()
-    # The dominant kernel is timed with CUDA events on every TIMING_EVERY-th
-    # step of the timed region: an event pair between two kernels costs a few
-    # microseconds of idle GPU front end, which would inflate a 40-us step.
-    barrier()
-    launches_before = ctx.kernel_launches()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for i in range(args.steps):
-        sampled = i % TIMING_EVERY == 0
-        if sampled:
-            ctx.timing(True, phases=[w.phase])
-        w.step()
-        if sampled:
-            ctx.timing(False)
-    stop.record()
-    launches = ctx.kernel_launches() - launches_before
-    barrier()
-    clocks = sampler.stop()
-    ctx.sync()  # surfaces a device-side error status
-    ms = max_over_ranks(start.elapsed_time(stop))
-    ctx.timing(False)
-    dom_ms, dom_launches = ctx.timing_read(w.phase)
-    dom_ms = max_over_ranks(dom_ms)
-    if w.kernels_per_step == 1:
-        # One kernel per step: its average launch duration is the timed
-        # region's event time over its launches (back to back, gaps included);
-        # a single bracketed launch would also count the event's launch latency.
-        dom_ms, dom_launches = ms, launches
-        launch_basis = "timed region / launches (one kernel per step)"
-    else:
-        launch_basis = f"CUDA event pair around the kernel on 1 in {TIMING_EVERY} steps of the timed region"
-    # --- end-to-end through host arrays ------------------------------------------
-    session = api.Session(local)
-    w.e2e_setup(session)
-    e2e_steps = max(3, min(args.steps, 20))
-    for _ in range(2):
-        w.e2e_step()
-    session.sync()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        w.e2e_step()
-    e1.record()
-    session.sync()
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    # --- strong scaling of one 4096^3 GEMM over NCCL (multi-GPU GEMM runs) ---------
-    strong = None
-    if world > 1 and isinstance(w, Gemm) and not w.ragged:
-        strong = strong_scaling_gemm(ctx, torch, dist, rank, world, barrier, max_over_ranks)
-    # --- report ------------------------------------------------------------------
-    result = None
-    if rank == 0:
-        peaks, basis = measured_peaks()
-        value = world * w.work() * args.steps / (ms / 1e3) / scale(w.unit)
-        avg_launch_s = dom_ms / 1e3 / max(1, dom_launches)
-        if w.bound == "tensor":
-            achieved = w.dominant_work() / avg_launch_s / 1e12
-            # A run whose SM clock the 1 kW power cap held below 90 % of its
-            # maximum is compared with the sustained GEMM peak (measured the
-            # same way, clocks settled under the cap); otherwise the burst peak.
-            capped = (clocks.get("sm_mhz") or 0) < 0.9 * (clocks.get("sm_max_mhz") or 0)
-            sustained = capped and "bf16_tflops_sustained" in peaks
-            peak = (peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]) / 2.0
-            peak_note = (f"{basis} bf16 dense TF/s / 2 = TF32 dense rate ("
-                         + (f"sustained: SM clock {clocks.get('sm_mhz')} of {clocks.get('sm_max_mhz')} MHz under "
-                            f"the power cap" if sustained else "burst") + ")")
-            unit = "TFLOP/s"
-        else:
-            achieved = w.dominant_work() / avg_launch_s / 1e9
-            peak = peaks["hbm_gbs"]
-            peak_note = f"{basis} HBM copy GB/s"
-            unit = "GB/s"
-        cpu = None
-        if world == 1 and not args.no_cpu:
-            v, sample = w.cpu_sample()
-            cpu = {"value": round(v, 4), "unit": w.unit, "cores": os.cpu_count(), "kind": "port",
-                   "sample": sample + " (oracle/refs.py float64 equations, NumPy/BLAS threads = all cores)"}
-            cpu.update(w.cpu_extras())
-        result = {
-            "metric": METRIC, "value": round(value, 3), "unit": w.unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xtf32 tensor)" if w.bound == "tensor" else "f32",
-            "data": "synthetic (seeded, distributions of the BASELINE configs)",
-            "config": w.config(),
-            "e2e": {"value": round(world * w.work() * e2e_steps / (e2e_ms / 1e3) / scale(w.unit), 3), "unit": w.unit,
-                    "h2d_bytes_per_step": int(w.e2e_bytes[0]), "d2h_bytes_per_step": int(w.e2e_bytes[1]),
-                    "steps": e2e_steps, "api": "api.Session pipelined host-array calls (b2k_*_host: slabbed copy-in, kernels and copy-out overlapped)"},
-            "roofline": {"bound": w.bound, "achieved": round(achieved, 2), "peak": round(peak, 2), "unit": unit,
-                         "frac": round(achieved / peak, 4), "traffic": profile_traffic(w.profile),
-                         "kernel": w.phase, "launch_ms": round(avg_launch_s * 1e3, 5), "launch_timing": launch_basis,
-                         "peak_basis": peak_note},
-            "cpu_baseline": cpu,
-            "clocks": clocks,
-            **({"strong_scaling_nccl": strong} if strong else {}),
-            "gpu_launches": launches,
-        }
-    session.close()
-    ctx.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    return result
+# --------------------------------------------------------------------------- reference arm
+def reference_record(name: str, steps: int, warmup: int) -> dict:
+    """The reference's CPU evaluation (float64 NumPy) of one workload, one full
+    evaluation per step (attention: a stated number of whole heads)."""
+    w = make_workload(name, 0, 1)
+    w.host_inputs()
+    for _ in range(warmup):
+        w.cpu_once()
+    t0 = time.perf_counter()
+    work, what = 0.0, ""
+    for _ in range(steps):
+        units, what = w.cpu_once()
+        work += units
+    dt = time.perf_counter() - t0
+    value = work / dt / scale(w.unit)
+    return {"value": round(value, 4), "unit": w.unit, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(dt / steps * 1e3, 3), "config": w.config(),
+            "cpu_baseline": {"value": round(value, 4), "unit": w.unit, "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{what} per step (oracle/refs.py float64 equations of "
+                                       "tools/research_cases.py:74-103 / suite.py:192-234, BLAS threads = all cores)"},
+            "e2e": {"value": round(value, 4), "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def run_reference(args) -> dict | None:
-    rank, local, world = init_dist()
+    rank, _, world = init_dist()
     if rank != 0:
         return None
-    w = make_workload(args.workload, 0, 1)
-    # host inputs only (no device)
-    if isinstance(w, Gemm):
-        w.host = w.inputs()
-    elif isinstance(w, Attention):
-        w.host = pkg("workloads").attention_inputs(w.bh, w.seq, w.d)
-    elif isinstance(w, Softmax):
-        w.host = pkg("workloads").softmax_input(w.rows, w.cols)
-    else:
-        w.host = pkg("workloads").add_inputs(w.n)
-    # one bounded sample per step: a few tens of ms, so even thousands of
-    # steps end within minutes
-    for _ in range(args.warmup):
-        w.cpu_sample(max_seconds=0.0, rows=w.reference_rows)
-    values, samples = [], ""
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        v, samples = w.cpu_sample(max_seconds=0.0, rows=w.reference_rows)
-        values.append(v)
-    dt = time.perf_counter() - t0
-    value = statistics.mean(values)
-    return {"metric": METRIC, "value": round(value, 4), "unit": w.unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
-            "config": w.config(),
-            "cpu_baseline": {"value": round(value, 4), "unit": w.unit, "cores": os.cpu_count(), "kind": "port",
-                             "sample": samples + " per step (oracle/refs.py float64 equations of "
-                                                 "tools/research_cases.py:74-103)", **w.cpu_extras()},
-            "e2e": {"value": round(value, 4), "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    rec = reference_record(args.workload, args.steps, args.warmup)
+    out = {"metric": METRIC, "value": rec["value"], "unit": rec["unit"], "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
+           "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+           "impl": "reference", "config": rec["config"], "cpu_baseline": rec["cpu_baseline"], "e2e": rec["e2e"]}
+    if not args.only:
+        out["workloads"] = {name: reference_record(name, 3, 1) for name in WORKLOADS if name != args.workload}
+    return out
 
 
 def main():
@@ -728,14 +948,15 @@ def main():
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=None)
     parser.add_argument("--warmup", type=int, default=5)
-    parser.add_argument("--workload", default="gemm", choices=["gemm", "softmax", "add", "ragged", "attention"])
+    parser.add_argument("--workload", default="gemm", choices=list(WORKLOADS))
     parser.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    parser.add_argument("--only", action="store_true", help="measure the selected workload only")
+    parser.add_argument("--sub-steps", type=int, default=None, help="timed steps of the other workloads' records")
+    parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline samples")
+    parser.add_argument("--no-sustained", action="store_true", help="skip the >= 2 s sustained legs")
     args = parser.parse_args()
     if args.steps is None:
-        args.steps = {"gemm": 1500, "ragged": 20000, "softmax": 20000, "add": 20000, "attention": 500}[args.workload]
-        if args.impl == "reference":
-            args.steps = 20
+        args.steps = 20 if args.impl == "reference" else make_workload(args.workload, 0, 1).steps_default
     args.warmup = max(3, args.warmup) if args.impl == "ours" else args.warmup
     result = run_reference(args) if args.impl == "reference" else run_ours(args)
     if result is not None:

@@ -17,8 +17,8 @@ namespace {
 
 inline int64_t round32(int64_t x) { return (x + 31) / 32 * 32; }
 
-// 1 = fused kernel, one CTA per query tile (default), 2 = fused kernel on
-// CTA pairs, 0 = three passes (tests and benchmarks compare them).
+// 1 = fused kernel, one CTA per query tile (default), 0 = three passes
+// (tests and benchmarks compare them).
 int g_attention_mode = 1;
 
 }  // namespace
@@ -26,7 +26,7 @@ int g_attention_mode = 1;
 int b2k::attention_mode() { return g_attention_mode; }
 
 extern "C" int b2k_attention_set_fused(int mode) {
-  if (mode < 0 || mode > 2) return B2K_EINVAL;
+  if (mode < 0 || mode > 1) return B2K_EINVAL;
   g_attention_mode = mode;
   return B2K_OK;
 }
@@ -51,7 +51,6 @@ extern "C" int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k
     return b2k::fail(ctx, B2K_EINVAL, "attention: extent exceeds 32-bit TMA coordinates");
   if (!scale_div_ptr && !(scale_div != 0.0f)) return b2k::fail(ctx, B2K_EINVAL, "attention: zero scale divisor");
   cudaStream_t s = (cudaStream_t)stream;
-  ctx->flags_epoch = 0;  // the workspace is reused below: GEMM stream-K flags must be reset next time
   if (b2k::flash_supported(d, dv) && g_attention_mode != 0) {
     int status = b2k::reserve_workspace(ctx, b2k::flash_workspace_floats(bh, s_q, s_kv, d, dv) * sizeof(float), s);
     if (status != B2K_OK) return status;

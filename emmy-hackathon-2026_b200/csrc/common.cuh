@@ -32,9 +32,6 @@ struct b2k_ctx {
   std::vector<cudaEvent_t> sync_events;
   void *staging = nullptr;
   size_t staging_bytes = 0;
-  // Stream-K flag slots in the workspace and the epoch of the last GEMM.
-  unsigned *flags_ptr = nullptr;
-  unsigned flags_epoch = 0;
   // Optional per-phase CUDA-event timing (b2k_timing_*), for the phases
   // whose bit is set in timing_mask.
   bool timing = false;
@@ -130,23 +127,31 @@ struct SplitOperands {
   int64_t kp;
 };
 
-// In-kernel split GEMMs (gemm_fused.cu).  gemm_split_mode returns the
-// path a call takes under the b2k_gemm_set_fused_split switch: 0 = pre-pass
-// split of both operands, 1 = A split into TMEM inside the kernel with B
-// pre-split into `ops` (A must be TMA-readable: 16-byte aligned, row stride a
-// multiple of 4 elements, K >= 16), 2 = both operands split in shared memory
-// (B TMA-readable too; needs no scratch).  Under the default switch the
-// choice between 0 and 1 also weighs their tilings over `sms` SMs.
+// In-kernel split GEMM (gemm_fused.cu).  gemm_split_mode returns the path a
+// call takes under the b2k_gemm_set_fused_split switch: 0 = pre-pass split of
+// both operands; kSplitDirect = A split into TMEM inside the kernel, B
+// pre-split into `ops` (A TMA-readable: 16-byte aligned, row stride a
+// multiple of 4 elements, K >= 16, not stored transposed); kSplitTransposed =
+// C^T = B^T A^T with B split into TMEM inside the kernel and A pre-split (B
+// TMA-readable).  Under the default switch the path with the lowest
+// estimated time over `sms` SMs is taken.
+constexpr int kSplitDirect = 1;
+constexpr int kSplitTransposed = 2;
 int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
-                    int sms);
+                    int layout, int sms);
 // Tile width (columns) of the pre-pass kernel gemm_main picks for n columns.
 int main_tile_width(int64_t n);
 // The tile variant selected with b2k_gemm_set_variant (2 = 128-wide tiles).
 int gemm_variant();
 int gemm_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const SplitOperands &ops, float *c, int64_t m,
                 int64_t n, int64_t ldc, const float *bias, int relu, cudaStream_t s);
-int gemm_smem_split(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
-                    int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, const float *bias, int relu, cudaStream_t s);
+// The transposed orientation: raw B ([k][n] row-major, or [n][k] when b_nk)
+// split inside the kernel, the caller's A pre-split into ops.b_hi / b_lo
+// ([m][kp]); C is the caller's [m][n].  `bn` is the tile width over m (128 or
+// 192; 0 = gemm_transposed_tile_width(m, n, SMs)).
+int gemm_tmem_b(b2k_ctx *ctx, const float *b, int64_t k, int64_t ldb, bool b_nk, const SplitOperands &ops, float *c,
+                int64_t m, int64_t n, int64_t ldc, const float *bias, int relu, cudaStream_t s, int bn = 0);
+int gemm_transposed_tile_width(int64_t m, int64_t n, int sms);
 
 // Row-major [batch][rows, k] -> hi/lo [batch][rows][kp].
 int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t ld, int64_t bs, int64_t batch,
@@ -163,17 +168,6 @@ int split_rows2(b2k_ctx *ctx, const RowSplit &a, const RowSplit *b, int64_t kp, 
 // Row-major [batch][k, n] -> transposed hi/lo [batch][n][kp].
 int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_t ld, int64_t bs, int64_t batch,
                     int64_t kp, float *hi, float *lo, cudaStream_t s);
-// C[z] = epilogue(A[z] * B[z]^T) for z < batch on pre-split operands; the
-// epilogue divides by *div_ptr (or div_value), adds bias[n], applies ReLU.
-// Scratch of the stream-K GEMM: per-CTA partial tiles and publication flags.
-struct StreamKScratch {
-  int grid;
-  float *partials;
-  unsigned *flags;
-  unsigned epoch;
-};
-bool streamk_pays(int64_t m, int64_t n, int64_t kp, int grid);
-size_t streamk_scratch_bytes(int grid);
 
 // Row softmax of x [rows, cols] written as TF32 hi/lo halves [rows][kp] (softmax.cu).
 int softmax_split_rows(b2k_ctx *ctx, const float *x, int64_t rows, int64_t cols, int64_t ld_x, float *hi,
@@ -188,9 +182,11 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
                     int64_t s_kv, int64_t d, int64_t dv, float scale_div, const float *scale_div_ptr, int k_layout,
                     float *ws, cudaStream_t s);
 
+// C[z] = epilogue(A[z] * B[z]^T) for z < batch on pre-split operands; the
+// epilogue divides by *div_ptr (or div_value), adds bias[n], applies ReLU.
 int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
-              cudaStream_t s, const StreamKScratch *sk = nullptr);
+              cudaStream_t s);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -70,19 +70,7 @@ constexpr int kSmem = 2 * kQBytes + kStages * 2 * kSub;
 constexpr uint32_t kColPlo = 256, kColO = 384;
 __host__ __device__ constexpr uint32_t s_col(int j) { return (uint32_t)((j & 1) * 128); }
 
-// Ring geometry.  Single CTA: 3 stages, each a whole K chunk [128 keys x 32
-// dims] or V^T chunk [128 dims x 32 keys], hi and lo (32 KB).  CTA pair
-// (tcgen05 cta_group::2, M = 256): each CTA holds its own 128 query rows and
-// half of every chunk -- 64 keys of a K chunk, 64 dims of a V^T chunk -- so
-// the same 96 KB ring is 6 stages deep and each CTA's tensor core reads half
-// the B operand from its own shared memory.
-template <bool PAIR>
-struct FlashRing {
-  static constexpr int kStages = PAIR ? 6 : 3;
-  static constexpr int kRows = PAIR ? 64 : 128;    // rows of a chunk this CTA holds
-  static constexpr int kChunkBytes = kRows * 32 * 4;  // one half (hi or lo)
-  static_assert(kStages * 2 * kChunkBytes == 3 * 2 * 128 * 32 * 4, "ring size");
-};
+constexpr int kChunkBytes = kSub;  // one half (hi or lo) of a ring stage
 
 struct FlashArgs {
   int tma_o;  // O written by TMA stores from shared memory (16-byte aligned, dv % 4 == 0)
@@ -97,30 +85,22 @@ struct FlashArgs {
   unsigned *err;
 };
 
-template <bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_tf32x3_kernel(const __grid_constant__ CUtensorMap map_qhi, const __grid_constant__ CUtensorMap map_qlo,
                         const __grid_constant__ CUtensorMap map_khi, const __grid_constant__ CUtensorMap map_klo,
                         const __grid_constant__ CUtensorMap map_vhi, const __grid_constant__ CUtensorMap map_vlo,
                         const __grid_constant__ CUtensorMap map_o, const FlashArgs args) {
-  using Ring = FlashRing<PAIR>;
-  constexpr int kStages = Ring::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, q_ready, p_full, pv_done, drain;
   __shared__ __align__(8) uint64_t ring_full[kStages], ring_empty[kStages], s_full[2];
-  // CTA pair: the peer CTA's Q and ring stages landed (forwarded to the even CTA).
-  __shared__ __align__(8) uint64_t peer_q, peer_ready[kStages];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_word;
   __shared__ float part_max[2][BM], part_sum[2][BM];
 
   uint8_t *q_hi = smem_raw, *q_lo = q_hi + kQBytes;
   uint8_t *ring = q_lo + kQBytes;  // stage i: hi at ring + 2i*chunk, lo at ring + (2i+1)*chunk
-  auto st_hi = [&](int i) { return ring + (2 * i) * Ring::kChunkBytes; };
-  auto st_lo = [&](int i) { return ring + (2 * i + 1) * Ring::kChunkBytes; };
-  // The even CTA of a pair issues every MMA; its barriers are the pair's.
-  const uint32_t rank = PAIR ? sm100::cluster_rank() : 0u;
-  const bool leader = rank == 0;
+  auto st_hi = [&](int i) { return ring + (2 * i) * kChunkBytes; };
+  auto st_lo = [&](int i) { return ring + (2 * i + 1) * kChunkBytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y;
@@ -137,26 +117,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (abort_word) atomicOr(args.err, sm100::kSiteAttention);
     sm100::mbar_init(&q_full, 1);
     sm100::mbar_init(&q_ready, 8);             // one arrival per softmax warp (raw Q split)
-    sm100::mbar_init(&p_full, PAIR ? 16 : 8);  // one arrival per softmax warp (of both CTAs)
-    sm100::mbar_init(&peer_q, 1);
+    sm100::mbar_init(&p_full, 8);   // one arrival per softmax warp
     sm100::mbar_init(&pv_done, 1);
     sm100::mbar_init(&drain, 1);
     for (int i = 0; i < kStages; ++i) {
       sm100::mbar_init(&ring_full[i], 1);
       sm100::mbar_init(&ring_empty[i], 1);
-      sm100::mbar_init(&peer_ready[i], 1);
     }
     for (int i = 0; i < 2; ++i) sm100::mbar_init(&s_full[i], 1);
     sm100::fence_barrier_init();
   }
-  // Both CTAs' barriers must exist before either signals the other.
-  if constexpr (PAIR) sm100::cluster_sync();
-  if (warp == 1) {
-    if constexpr (PAIR)
-      sm100::tmem_alloc_pair(&tmem_slot, 512);
-    else
-      sm100::tmem_alloc(&tmem_slot, 512);
-  }
+  if (warp == 1) sm100::tmem_alloc(&tmem_slot, 512);
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -169,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer: Q once, then K_j chunks, V_j chunks, K_{j+1} ...
-      if (!PAIR && args.q_raw) {
+      if (args.q_raw) {
         // raw Q into the hi buffer; the softmax warps split it in place
         sm100::mbar_arrive_expect_tx(&q_full, dblocks * kSub);
         for (int c = 0; c < dblocks; ++c) sm100::tma_load_3d(q_hi + c * kSub, &map_qhi, &q_full, c * 32, (int)m0, head);
@@ -200,17 +171,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto load_chunk = [&](bool is_k, int j, int c) {
         const int i = n % kStages;
         if (n >= kStages &&
-            !sm100::mbar_wait_cluster(&ring_empty[i], ((n / kStages) - 1) & 1, args.err, sm100::kSiteAttention, abort))
+            !sm100::mbar_wait(&ring_empty[i], ((n / kStages) - 1) & 1, args.err, sm100::kSiteAttention, abort))
           return false;
-        sm100::mbar_arrive_expect_tx(&ring_full[i], 2 * Ring::kChunkBytes);
-        const int half = (int)rank * Ring::kRows;  // this CTA's rows of the chunk
-        if (is_k) {  // K chunk: keys j*BN + half.., dims c*32..
-          sm100::tma_load_3d(st_hi(i), &map_khi, &ring_full[i], c * 32, j * BN + half, head);
-          sm100::tma_load_3d(st_lo(i), &map_klo, &ring_full[i], c * 32, j * BN + half, head);
-        } else {     // V^T chunk: dims half.., keys j*BN + 32c..
+        sm100::mbar_arrive_expect_tx(&ring_full[i], 2 * kChunkBytes);
+        if (is_k) {  // K chunk: keys j*BN.., dims c*32..
+          sm100::tma_load_3d(st_hi(i), &map_khi, &ring_full[i], c * 32, j * BN, head);
+          sm100::tma_load_3d(st_lo(i), &map_klo, &ring_full[i], c * 32, j * BN, head);
+        } else {     // V^T chunk: all dims, keys j*BN + 32c..
           const int x = j * BN + 32 * c;
-          sm100::tma_load_3d(st_hi(i), &map_vhi, &ring_full[i], x, half, head);
-          sm100::tma_load_3d(st_lo(i), &map_vlo, &ring_full[i], x, half, head);
+          sm100::tma_load_3d(st_hi(i), &map_vhi, &ring_full[i], x, 0, head);
+          sm100::tma_load_3d(st_lo(i), &map_vlo, &ring_full[i], x, 0, head);
         }
         ++n;
         return true;
@@ -225,50 +195,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int m = n > kStages ? n - kStages : 0; m < n; ++m)
         sm100::mbar_wait(&ring_full[m % kStages], (m / kStages) & 1, args.err, sm100::kSiteDrain, &never);
     }
-  } else if (warp == 1 && !leader) {
-    // ---------------- CTA pair, odd CTA: forward "Q landed" and every "ring
-    // stage landed" to the even CTA, whose MMAs read this CTA's halves.
-    const int total = nblocks * (dblocks + kVChunks);
-    const uint32_t to_peer_q = sm100::map_rank(sm100::smem_addr(&peer_q), 0);
-    bool ok = sm100::mbar_wait_warp(&q_full, 0, args.err, sm100::kSiteAttention, abort);
-    if (ok && lane == 0) sm100::mbar_arrive_cluster(to_peer_q);
-    for (int n = 0; ok && n < total; ++n) {
-      const int i = n % kStages;
-      if (!(ok = sm100::mbar_wait_warp(&ring_full[i], (n / kStages) & 1, args.err, sm100::kSiteAttention, abort)))
-        break;
-      if (lane == 0) sm100::mbar_arrive_cluster(sm100::map_rank(sm100::smem_addr(&peer_ready[i]), 0));
-    }
   } else if (warp == 1) {
     {
       // ---------------- MMA issuer: S_0, then for each block j, S_{j+1}
       // (into the other score buffer, overlapping softmax_j) and O_j = P_j V_j.
       // S_{j+1} reuses the buffer P_{j-1} occupied; O_{j-1}'s MMAs, which read
       // it, were issued earlier and tcgen05 MMAs of one issuer run in order.
-      // CTA pair: M = 256 (each CTA's 128 rows), B split in halves; the O MMA
-      // is 128 wide (columns past dv read zeros and are not stored).
-      const uint32_t id_s = sm100::idesc_tf32(PAIR ? 2 * BM : BM, BN);
-      const uint32_t id_o = sm100::idesc_tf32(PAIR ? 2 * BM : BM, PAIR ? 128 : args.n_pv);
+      const uint32_t id_s = sm100::idesc_tf32(BM, BN);
+      const uint32_t id_o = sm100::idesc_tf32(BM, args.n_pv);
       const uint32_t qh = sm100::smem_addr(q_hi), ql = sm100::smem_addr(q_lo);
       auto mma_ss = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
-        if constexpr (PAIR) sm100::mma_tf32_pair(d, a, b, id, acc); else sm100::mma_tf32(d, a, b, id, acc);
+        sm100::mma_tf32(d, a, b, id, acc);
       };
       auto mma_ts = [&](uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc) {
-        if constexpr (PAIR) sm100::mma_tf32_ts_pair(d, a, b, id, acc); else sm100::mma_tf32_ts(d, a, b, id, acc);
+        sm100::mma_tf32_ts(d, a, b, id, acc);
       };
-      auto commit = [&](uint64_t *bar) {  // to this barrier in every CTA of the group
-        if constexpr (PAIR) sm100::mma_commit_pair_both(bar); else sm100::mma_commit(bar);
-      };
+      auto commit = [&](uint64_t *bar) { sm100::mma_commit(bar); };
       auto stage_ready = [&](int i, int n_) {
-        if (!sm100::mbar_wait_warp(&ring_full[i], (n_ / kStages) & 1, args.err, sm100::kSiteAttention, abort))
-          return false;
-        if constexpr (PAIR)
-          return sm100::mbar_wait_cluster_warp(&peer_ready[i], (n_ / kStages) & 1, args.err, sm100::kSiteAttention,
-                                               abort);
-        return true;
+        return sm100::mbar_wait_warp(&ring_full[i], (n_ / kStages) & 1, args.err, sm100::kSiteAttention, abort);
       };
-      bool ok = !PAIR && args.q_raw ? sm100::mbar_wait_warp(&q_ready, 0, args.err, sm100::kSiteAttention, abort)
-                                    : sm100::mbar_wait_warp(&q_full, 0, args.err, sm100::kSiteAttention, abort);
-      if constexpr (PAIR) ok = ok && sm100::mbar_wait_cluster_warp(&peer_q, 0, args.err, sm100::kSiteAttention, abort);
+      bool ok = args.q_raw ? sm100::mbar_wait_warp(&q_ready, 0, args.err, sm100::kSiteAttention, abort)
+                           : sm100::mbar_wait_warp(&q_full, 0, args.err, sm100::kSiteAttention, abort);
       int n = 0;  // ring chunks consumed
       auto issue_s = [&](int j) {
         for (int c = 0; ok && c < dblocks; ++c, ++n) {
@@ -290,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto issue_pv = [&](int j) {
         // once the softmax has written P_j into TMEM and folded O_{j-1}
-        if (!(ok = sm100::mbar_wait_cluster_warp(&p_full, j & 1, args.err, sm100::kSiteAttention, abort))) return;
+        if (!(ok = sm100::mbar_wait_warp(&p_full, j & 1, args.err, sm100::kSiteAttention, abort))) return;
         sm100::tc_fence_after();
         for (int c = 0; ok && c < kVChunks; ++c, ++n) {
           const int i = n % kStages;
@@ -313,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j + 1 < nblocks) issue_s(j + 1);
         if (ok) issue_pv(j);
       }
-      if constexpr (PAIR) sm100::mma_commit_pair_local(&drain); else sm100::mma_commit(&drain);
+      sm100::mma_commit(&drain);
       int never = 0;
       sm100::mbar_wait(&drain, 0, args.err, sm100::kSiteDrain, &never);
     }
@@ -336,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Fold O_{j-1} = P_{j-1} V_{j-1} (TMEM) into the register accumulator once
     // its MMAs are done; O's TMEM buffer is then free for O_j.
     auto fold_o = [&](int jm1) {
-      ok = ok && sm100::mbar_wait_cluster(&pv_done, jm1 & 1, args.err, sm100::kSiteAttention, abort,
+      ok = ok && sm100::mbar_wait(&pv_done, jm1 & 1, args.err, sm100::kSiteAttention, abort,
                                           3 * sm100::kWaitCycles);
       if (!ok) return;
       sm100::tc_fence_after();
@@ -353,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    if (!PAIR && args.q_raw) {
+    if (args.q_raw) {
       // Split the raw Q tile in place: Q_hi over the raw values, Q_lo in its
       // own buffer, the same 128-byte-swizzled [128 rows x 32] boxes the
       // MMAs read.  Warpgroup wg takes boxes wg, wg + 2, ...; each thread its
@@ -392,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // after a failed wait (ok == false), so the two warpgroups never wait on
     // each other forever; failed waits only skip work.
     for (int j = 0; j < nblocks; ++j) {
-      ok = ok && sm100::mbar_wait_cluster(&s_full[j & 1], (j >> 1) & 1, args.err, sm100::kSiteAttention, abort);
+      ok = ok && sm100::mbar_wait(&s_full[j & 1], (j >> 1) & 1, args.err, sm100::kSiteAttention, abort);
       sm100::tc_fence_after();
       uint32_t sr[SC];
       {
@@ -443,12 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       sm100::tc_fence_before();
       __syncwarp();
-      if (lane == 0 && ok) {
-        if constexpr (PAIR)
-          sm100::mbar_arrive_cluster(sm100::map_rank(sm100::smem_addr(&p_full), 0));
-        else
-          sm100::mbar_arrive(&p_full);
-      }
+      if (lane == 0 && ok) sm100::mbar_arrive(&p_full);
       sm100::named_barrier(2, 256);
       l_run = __fadd_rn(__fmul_rn(l_run, alpha), __fadd_rn(part_sum[0][r], part_sum[1][r]));
       m_run = mx;
@@ -501,15 +443,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   sm100::tc_fence_before();
-  // A pair's MMAs write both CTAs' TMEM and read both CTAs' shared memory:
-  // neither CTA releases TMEM or exits before both are done.
-  if constexpr (PAIR) sm100::cluster_sync(); else __syncthreads();
+  __syncthreads();
   if (warp == 1) {
     sm100::tc_fence_after();
-    if constexpr (PAIR)
-      sm100::tmem_dealloc_pair(tmem, 512);
-    else
-      sm100::tmem_dealloc(tmem, 512);
+    sm100::tmem_dealloc(tmem, 512);
   }
 }
 
@@ -549,18 +486,12 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   float *k_hi = q_lo + bh * s_q * dp, *k_lo = k_hi + bh * s_kv * dp;
   float *v_hi = k_lo + bh * s_kv * dp, *v_lo = v_hi + bh * dv * sp;
   int status;
-  // CTA pairs (mode 2) need at least two query tiles to pair up.  Measured on
-  // B200 (64 heads x 2048 x 2048 x 128): 11.4 k cycles per key block on pairs
-  // against 8.9 k on single CTAs -- the pair MMAs' S and PV phases take
-  // longer although each CTA streams half of K and V -- so single CTAs are
-  // the default.
   const int64_t tiles = (s_q + BM - 1) / BM;
-  const bool pair = attention_mode() == 2 && tiles >= 2;
   // A single CTA loads its Q tile once and can split it in shared memory:
   // that needs raw Q TMA-readable with whole 32-column boxes (d % 32 == 0,
   // 16-byte aligned) and saves the pre-pass writing and the kernel reading
   // Q's hi/lo copies.  Otherwise Q is split by the pre-pass like K.
-  const bool q_raw = !pair && d % 32 == 0 && aligned16(q);
+  const bool q_raw = d % 32 == 0 && aligned16(q);
   const RowSplit sq{q, s_q, d, d, s_q * d, bh, q_hi, q_lo};
   const RowSplit sk{k, s_kv, d, d, s_kv * d, bh, k_hi, k_lo};
   if (k_layout == B2K_K_SD) {
@@ -571,39 +502,25 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
   }
   if (status != B2K_OK) return status;
   if ((status = split_transpose(ctx, v, s_kv, dv, dv, s_kv * dv, bh, sp, v_hi, v_lo, s)) != B2K_OK) return status;
-  const int rows = pair ? FlashRing<true>::kRows : FlashRing<false>::kRows;
   CUtensorMap maps[6];
   if ((status = make_map(ctx, &maps[0], q_raw ? q : q_hi, q_raw ? d : dp, s_q, bh, BM)) != B2K_OK) return status;
   if ((status = make_map(ctx, &maps[1], q_lo, dp, s_q, bh, BM)) != B2K_OK) return status;
-  if ((status = make_map(ctx, &maps[2], k_hi, dp, s_kv, bh, rows)) != B2K_OK) return status;
-  if ((status = make_map(ctx, &maps[3], k_lo, dp, s_kv, bh, rows)) != B2K_OK) return status;
-  if ((status = make_map(ctx, &maps[4], v_hi, sp, dv, bh, rows)) != B2K_OK) return status;
-  if ((status = make_map(ctx, &maps[5], v_lo, sp, dv, bh, rows)) != B2K_OK) return status;
+  if ((status = make_map(ctx, &maps[2], k_hi, dp, s_kv, bh, BN)) != B2K_OK) return status;
+  if ((status = make_map(ctx, &maps[3], k_lo, dp, s_kv, bh, BN)) != B2K_OK) return status;
+  if ((status = make_map(ctx, &maps[4], v_hi, sp, dv, bh, 128)) != B2K_OK) return status;
+  if ((status = make_map(ctx, &maps[5], v_lo, sp, dv, bh, 128)) != B2K_OK) return status;
   // O through TMA stores when it is TMA-writable, else row stores by the threads.
   CUtensorMap map_o{};
   const int tma_o = aligned16(o) && dv % 4 == 0;
   if (tma_o && (status = make_map(ctx, &map_o, o, dv, s_q, bh, BM)) != B2K_OK) return status;
-  FlashArgs args{tma_o, (int)q_raw, pair ? 0 : ctx->sm_count, o, s_q, s_kv, dv, (int)dp, (int)((dv + 15) / 16 * 16),
+  FlashArgs args{tma_o, (int)q_raw, ctx->sm_count, o, s_q, s_kv, dv, (int)dp, (int)((dv + 15) / 16 * 16),
                  1.0f / scale_div, scale_div_ptr, ctx->error_flag};
-  auto kernel = pair ? flash_tf32x3_kernel<true> : flash_tf32x3_kernel<false>;
+  auto kernel = flash_tf32x3_kernel;
   cudaError_t err = set_max_smem(ctx, (const void *)kernel, kSmem);
   if (err != cudaSuccess) return cuda_fail(ctx, err, "flash: set smem");
   PhaseTimer timer(ctx, B2K_PHASE_FLASH, s);
-  cudaLaunchConfig_t config = {};
-  config.gridDim = dim3((unsigned)(pair ? (tiles + 1) / 2 * 2 : tiles), (unsigned)bh);
-  config.blockDim = dim3(kThreads);
-  config.dynamicSmemBytes = kSmem;
-  config.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = pair ? 2 : 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  config.attrs = attr;
-  config.numAttrs = !pair && pdl_enabled() ? 2 : 1;
-  err = cudaLaunchKernelEx(&config, kernel, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], map_o, args);
+  err = launch_kernel(pdl_enabled(), kernel, dim3((unsigned)tiles, (unsigned)bh), dim3(kThreads), kSmem, s, maps[0],
+                      maps[1], maps[2], maps[3], maps[4], maps[5], map_o, args);
   if (err != cudaSuccess) return cuda_fail(ctx, err, "flash: launch");
   return check_launch(ctx, "flash launch");
 }

@@ -452,295 +452,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// --- stream-K persistent variant ----------------------------------------------
-// One CTA per SM (cooperative launch, so all CTAs are resident at once).  The
-// full waves of tiles are processed whole, in the same raster order as the
-// one-tile-per-CTA kernel (tile p + w * grid), which keeps the L2 working set
-// of concurrently active tiles compact; only the remainder tiles -- 68 of 512
-// on 148 SMs, which would otherwise run as a half-empty fourth wave -- are cut
-// into equal contiguous (tile, K block) ranges, one per CTA.  A CTA walks its
-// ranges tile segment by tile segment with the same producer / MMA /
-// epilogue roles and chunked TMEM accumulation as above.  A remainder tile
-// split between CTAs is finished by the CTA holding its first K block: the
-// others (whose remainder range starts inside the tile, so that segment is
-// the first remainder work they do) store their partial sums in a per-CTA
-// slot and publish a launch epoch; the head CTA waits for those slots
-// (bounded), adds them in CTA order (deterministic) and runs the epilogue.
-struct StreamKArgs {
-  GemmArgs g;
-  int tiles_n;          // N tiles per M row of tiles
-  int full_waves;       // whole tiles per CTA, in raster order (tile p + w * grid)
-  int64_t sk_tile0;     // first tile of the split remainder
-  int64_t sk_units;     // remainder tiles * num_kb, cut into equal ranges
-  float *partials;      // [grid][BM * BN]
-  unsigned *flags;      // [grid]: epoch of the last partial published
-  unsigned epoch;
-};
-
-// Work range r of CTA p: r < full_waves is whole tile p + r * grid; the last
-// range is the CTA's share of the remainder's (tile, K block) units.
-__device__ __forceinline__ void work_range(const StreamKArgs &a, int p, int grid, int r, int64_t &u0, int64_t &u1) {
-  const int64_t kb = a.g.num_kb;
-  if (r < a.full_waves) {
-    const int64_t t = p + (int64_t)r * grid;
-    u0 = t * kb;
-    u1 = u0 + kb;
-  } else {
-    u0 = a.sk_tile0 * kb + a.sk_units * p / grid;
-    u1 = a.sk_tile0 * kb + a.sk_units * (p + 1) / grid;
-  }
-}
-
-__device__ __forceinline__ int64_t sk_begin(const StreamKArgs &a, int q, int grid) {
-  return a.sk_tile0 * (int64_t)a.g.num_kb + a.sk_units * q / grid;
-}
-
-template <int BN, int SW, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_streamk_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
-                        const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
-                        const StreamKArgs args) {
-  using Shape = GemmShape<BN, SW, STAGES>;
-  constexpr int CB = Shape::kChunkBlocks;
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[STAGES];
-  __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t tmem_full[2];
-  __shared__ __align__(8) uint64_t tmem_empty[2];
-  __shared__ __align__(8) uint64_t drain_bar;
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_word;
-
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const GemmArgs &g = args.g;
-  const int num_kb = g.num_kb;
-  const int p = blockIdx.x, grid = gridDim.x;
-  const int nranges = args.full_waves + 1;
-  volatile int *abort = &abort_word;
-
-  auto a_hi = [&](int s) { return smem + s * Shape::kStage; };
-  auto a_lo = [&](int s) { return smem + s * Shape::kStage + Shape::kTileA; };
-  auto b_hi = [&](int s) { return smem + s * Shape::kStage + 2 * Shape::kTileA; };
-  auto b_lo = [&](int s) { return smem + s * Shape::kStage + 2 * Shape::kTileA + Shape::kTileB; };
-
-  if (threadIdx.x == 0) {
-    abort_word = 0;
-    for (int s = 0; s < STAGES; ++s) {
-      sm100::mbar_init(&full_bar[s], 1);
-      sm100::mbar_init(&empty_bar[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      sm100::mbar_init(&tmem_full[b], 1);
-      sm100::mbar_init(&tmem_empty[b], kEpilogueWarps);
-    }
-    sm100::mbar_init(&drain_bar, 1);
-    sm100::fence_barrier_init();
-    sm100::prefetch_tensormap(&map_ahi);
-    sm100::prefetch_tensormap(&map_alo);
-    sm100::prefetch_tensormap(&map_bhi);
-    sm100::prefetch_tensormap(&map_blo);
-  }
-  if (warp == 1) sm100::tmem_alloc(&tmem_slot, Shape::kTmemCols);
-  sm100::tc_fence_before();
-  __syncthreads();
-  sm100::tc_fence_after();
-  const uint32_t tmem_base = tmem_slot;
-
-  if (warp == 0) {
-    if (sm100::elect_lane0()) {
-      // TMA producer over the CTA's K blocks, in range order.
-      int n = 0;
-      bool ok = true;
-      for (int r = 0; ok && r < nranges; ++r) {
-      int64_t u0, u1;
-      work_range(args, p, grid, r, u0, u1);
-      for (int64_t u = u0; ok && u < u1; ++u, ++n) {
-        const int64_t t = u / num_kb;
-        const int kb = (int)(u - t * num_kb);
-        const int s = n % STAGES;
-        if (n >= STAGES &&
-            !(ok = sm100::mbar_wait(&empty_bar[s], ((n / STAGES) & 1) ^ 1, args.g.err, sm100::kSiteProducerEmpty,
-                                    abort)))
-          break;
-        sm100::mbar_arrive_expect_tx(&full_bar[s], Shape::kStage);
-        const int m0 = (int)((t / args.tiles_n) * BM), n0 = (int)((t % args.tiles_n) * BN);
-        const int kx = kb * Shape::BK;
-        sm100::tma_load_3d(a_hi(s), &map_ahi, &full_bar[s], kx, m0, 0);
-        sm100::tma_load_3d(a_lo(s), &map_alo, &full_bar[s], kx, m0, 0);
-        sm100::tma_load_3d(b_hi(s), &map_bhi, &full_bar[s], kx, n0, 0);
-        sm100::tma_load_3d(b_lo(s), &map_blo, &full_bar[s], kx, n0, 0);
-      }
-      }
-      int never = 0;
-      for (int k = n > STAGES ? n - STAGES : 0; k < n; ++k)
-        sm100::mbar_wait(&full_bar[k % STAGES], (k / STAGES) & 1, args.g.err, sm100::kSiteDrain, &never);
-    }
-  } else if (warp == 1) {
-    {
-      // MMA issuer: a chunk ends at a multiple of CB K blocks or at the end of a segment.
-      constexpr uint32_t idesc = sm100::idesc_tf32(BM, BN);
-      int n = 0, chunk = 0;
-      bool ok = true, open = false;
-      for (int r = 0; ok && r < nranges; ++r) {
-      int64_t u0, u1;
-      work_range(args, p, grid, r, u0, u1);
-      for (int64_t u = u0; ok && u < u1; ++u, ++n) {
-        const int64_t t = u / num_kb;
-        const int kb = (int)(u - t * num_kb);
-        const bool first = !open;
-        const bool last = ((kb + 1) % CB) == 0 || kb + 1 == num_kb || u + 1 == u1;
-        const int buf = chunk & 1;
-        if (first && chunk >= 2 &&
-            !(ok = sm100::mbar_wait_warp(&tmem_empty[buf], ((chunk >> 1) & 1) ^ 1, args.g.err, sm100::kSiteMmaFull,
-                                    abort)))
-          break;
-        const int s = n % STAGES;
-        if (!(ok = sm100::mbar_wait_warp(&full_bar[s], (n / STAGES) & 1, args.g.err, sm100::kSiteMmaFull, abort))) break;
-        sm100::tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(buf * BN);
-        const uint32_t ahi = sm100::smem_addr(a_hi(s)), alo = sm100::smem_addr(a_lo(s));
-        const uint32_t bhi = sm100::smem_addr(b_hi(s)), blo = sm100::smem_addr(b_lo(s));
-#pragma unroll
-        for (int k = 0; k < Shape::BK / 8; ++k) {
-          const uint32_t off = k * 32;
-          const uint64_t dah = sm100::desc_kmajor<SW>(ahi + off), dal = sm100::desc_kmajor<SW>(alo + off);
-          const uint64_t dbh = sm100::desc_kmajor<SW>(bhi + off), dbl = sm100::desc_kmajor<SW>(blo + off);
-          sm100::mma_tf32(d, dal, dbh, idesc, (first && k == 0) ? 0u : 1u);
-          sm100::mma_tf32(d, dah, dbl, idesc, 1u);
-          sm100::mma_tf32(d, dah, dbh, idesc, 1u);
-        }
-        sm100::mma_commit(&empty_bar[s]);
-        open = true;
-        if (last) {
-          sm100::mma_commit(&tmem_full[buf]);
-          ++chunk;
-          open = false;
-        }
-      }
-      }
-      sm100::mma_commit(&drain_bar);
-      int never = 0;
-      sm100::mbar_wait(&drain_bar, 0, args.g.err, sm100::kSiteDrain, &never);
-    }
-  } else {
-    // Epilogue warps 2..9 (same lane-quarter / column-half mapping as above).
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int epi = threadIdx.x - 64;  // 0..255
-    constexpr int CPT = Shape::kColsPerThread;
-    float acc[CPT];
-#pragma unroll
-    for (int j = 0; j < CPT; ++j) acc[j] = 0.0f;
-    bool ok = true;
-    int chunk = 0;
-    for (int r = 0; r < nranges; ++r) {
-    int64_t u0, u1;
-    work_range(args, p, grid, r, u0, u1);
-    int64_t u = u0;
-    while (u < u1) {
-      const int64_t t = u / num_kb;
-      const int kb0 = (int)(u - t * num_kb);
-      const int64_t seg_end = min(u1, (t + 1) * (int64_t)num_kb);
-      // fold this segment's chunks
-      for (int64_t v = u; v < seg_end;) {
-        const int kb = (int)(v - t * num_kb);
-        const int64_t chunk_end = min(seg_end, t * (int64_t)num_kb + ((kb / CB) + 1) * CB);
-        const int buf = chunk & 1;
-        ok = ok && sm100::mbar_wait(&tmem_full[buf], (chunk >> 1) & 1, args.g.err, sm100::kSiteEpilogueAccum, abort,
-                                    3 * sm100::kWaitCycles);
-        sm100::tc_fence_after();
-        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + half * CPT);
-#pragma unroll
-        for (int j = 0; j < CPT; j += 16) {
-          uint32_t r[16];
-          sm100::tmem_ld_32x32b_x16(taddr + j, r);
-          sm100::tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
-        }
-        sm100::tc_fence_before();
-        __syncwarp();
-        if (lane == 0 && ok) sm100::mbar_arrive(&tmem_empty[buf]);
-        ++chunk;
-        v = chunk_end;
-      }
-      const bool head = kb0 == 0;
-      const bool complete = seg_end == (t + 1) * (int64_t)num_kb;
-      float *slot = args.partials + (int64_t)p * (BM * BN);
-      if (!head) {
-        // publish this CTA's partial of a tile whose head another CTA holds
-#pragma unroll
-        for (int j = 0; j < CPT; ++j) __stcg(slot + (int64_t)j * 256 + epi, acc[j]);
-        __threadfence();
-        sm100::named_barrier(1, 256);
-        if (epi == 0 && ok) atomicExch(args.flags + p, args.epoch);
-      } else {
-        if (!complete) {
-          // add the partials of the following CTAs that cover the rest of the tile, in CTA order
-          for (int q = p + 1; q < grid && sk_begin(args, q, grid) < (t + 1) * (int64_t)num_kb; ++q) {
-            if (epi == 0 && ok) {
-              const long long start = clock64();
-              while (atomicAdd(args.flags + q, 0u) != args.epoch) {
-                if (*abort || clock64() - start > sm100::kWaitCycles) {
-                  atomicOr(args.g.err, sm100::kSiteEpilogueAccum);
-                  *abort = 1;
-                  ok = false;
-                  break;
-                }
-              }
-            }
-            sm100::named_barrier(2, 256);
-            ok = ok && !*abort;
-            __threadfence();
-            const float *other = args.partials + (int64_t)q * (BM * BN);
-#pragma unroll
-            for (int j = 0; j < CPT; ++j) acc[j] = __fadd_rn(acc[j], __ldcg(other + (int64_t)j * 256 + epi));
-          }
-        }
-        // epilogue of the finished tile
-        const int64_t m0 = (t / args.tiles_n) * BM, n0 = (t % args.tiles_n) * BN;
-        const int64_t row = m0 + quarter * 32 + lane;
-        const int64_t col0 = n0 + half * CPT;
-        if (ok && row < g.m && col0 < g.n) {
-          float *crow = g.c + row * g.ldc + col0;
-          const float divisor = g.div_ptr ? __ldg(g.div_ptr) : g.div_value;
-          const bool divide = g.div_ptr != nullptr || g.div_value != 1.0f;
-          const bool vec = ((g.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(g.c) & 15) == 0) && col0 + CPT <= g.n;
-#pragma unroll
-          for (int j = 0; j < CPT; ++j) {
-            float x = acc[j];
-            if (divide) x = __fdiv_rn(x, divisor);
-            if (g.bias) x = __fadd_rn(x, (col0 + j < g.n) ? __ldg(g.bias + col0 + j) : 0.0f);
-            if (g.relu) x = x > 0.0f ? x : 0.0f;
-            acc[j] = x;
-          }
-          if (vec) {
-#pragma unroll
-            for (int j = 0; j < CPT; j += 4)
-              *reinterpret_cast<float4 *>(crow + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < CPT; ++j)
-              if (col0 + j < g.n) crow[j] = acc[j];
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < CPT; ++j) acc[j] = 0.0f;
-      u = seg_end;
-    }
-    }
-  }
-  sm100::tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    sm100::tc_fence_after();
-    sm100::tmem_dealloc(tmem_base, Shape::kTmemCols);
-  }
-}
-
 // --- host side -------------------------------------------------------------
 // K-major FP32 operand [batch][rows][Kp]: box [1, box_rows, SW/4] with the
 // SW-byte swizzle.
@@ -797,69 +508,12 @@ int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, Gemm
   return b2k::check_launch(ctx, "gemm launch");
 }
 
-template <int BN, int SW, int STAGES>
-int launch_streamk(b2k_ctx *ctx, const b2k::SplitOperands &ops, GemmArgs g, const b2k::StreamKScratch &sk,
-                   cudaStream_t s) {
-  using Shape = GemmShape<BN, SW, STAGES>;
-  CUtensorMap maps[4];
-  int status;
-  if ((status = make_operand_map(ctx, &maps[0], ops.a_hi, g.m, ops.kp, 1, BM, SW)) != B2K_OK) return status;
-  if ((status = make_operand_map(ctx, &maps[1], ops.a_lo, g.m, ops.kp, 1, BM, SW)) != B2K_OK) return status;
-  if ((status = make_operand_map(ctx, &maps[2], ops.b_hi, g.n, ops.kp, 1, BN, SW)) != B2K_OK) return status;
-  if ((status = make_operand_map(ctx, &maps[3], ops.b_lo, g.n, ops.kp, 1, BN, SW)) != B2K_OK) return status;
-  g.num_kb = (int)(ops.kp / Shape::BK);
-  StreamKArgs args;
-  args.g = g;
-  args.tiles_n = (int)((g.n + BN - 1) / BN);
-  const int64_t tiles = ((g.m + BM - 1) / BM) * args.tiles_n;
-  args.full_waves = (int)(tiles / sk.grid);
-  args.sk_tile0 = (int64_t)args.full_waves * sk.grid;
-  args.sk_units = (tiles - args.sk_tile0) * g.num_kb;
-  args.partials = sk.partials;
-  args.flags = sk.flags;
-  args.epoch = sk.epoch;
-  auto kernel = gemm_streamk_kernel<BN, SW, STAGES>;
-  cudaError_t err = b2k::set_max_smem(ctx, (const void *)kernel, Shape::kSmem);
-  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm stream-K: set smem");
-  const int grid = sk.grid;
-  void *params[] = {(void *)&maps[0], (void *)&maps[1], (void *)&maps[2], (void *)&maps[3], (void *)&args};
-  err = cudaLaunchCooperativeKernel((const void *)kernel, dim3(grid), dim3(kThreads), params, Shape::kSmem, s);
-  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm stream-K: cooperative launch");
-  return b2k::check_launch(ctx, "gemm stream-K launch");
-}
-
 }  // namespace
 
 // Kernel variant selector (tile width, swizzle, stage count); settable for
 // tuning through b2k_gemm_set_variant.  Outputs at most 128 wide always use
 // the 128-wide tile.
 static int g_gemm_variant = 1;
-// Off by default: measured on B200 (4096^3 and the 4097x1000x777 ragged
-// case) the stream-K kernel was 12-20 % slower than whole tiles per CTA.
-static int g_streamk_enabled = 0;
-
-extern "C" int b2k_gemm_set_streamk(int on) {
-  g_streamk_enabled = on != 0;
-  return B2K_OK;
-}
-
-namespace b2k {
-
-// Stream-K is worth its partial-tile traffic when whole tiles would leave the
-// last wave noticeably under-filled and every CTA still gets >= 8 K blocks.
-bool streamk_pays(int64_t m, int64_t n, int64_t kp, int grid) {
-  if (!g_streamk_enabled || grid <= 0) return false;
-  const int64_t tiles = ((m + 127) / 128) * ((n + 255) / 256);
-  const int64_t units = tiles * (kp / 16);
-  if (units < 8 * (int64_t)grid) return false;
-  const int64_t waves_x100 = tiles * 100 / grid;
-  return (waves_x100 % 100) != 0 && (waves_x100 % 100) < 90;
-}
-
-size_t streamk_scratch_bytes(int grid) { return (size_t)grid * (128 * 256 + 1) * sizeof(float) + 256; }
-
-}  // namespace b2k
-
 namespace b2k {
 
 static void fill_job(RowSplitJob &o, const RowSplit &r) {
@@ -918,12 +572,10 @@ int main_tile_width(int64_t n) {
 
 int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
-              cudaStream_t s, const StreamKScratch *sk) {
+              cudaStream_t s) {
   if (batch > 65535) return fail(ctx, B2K_EINVAL, "gemm: batch exceeds 65535");
   GemmArgs args{c, bias, div_ptr, div_value, m, n, ldc, batch_stride_c, 0, relu, ctx->error_flag, 0};
   PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
-  if (sk && batch == 1 && n > 128 && g_gemm_variant == 1 && streamk_pays(m, n, ops.kp, sk->grid))
-    return launch_streamk<256, 64, 4>(ctx, ops, args, *sk, s);
   if (n <= 128) return launch_main<128, 128, 3>(ctx, ops, batch, args, s);
   switch (g_gemm_variant) {
     case 0: return launch_main<256, 128, 2>(ctx, ops, batch, args, s);
@@ -935,26 +587,25 @@ int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int6
 
 }  // namespace b2k
 
-// Shared by the public entry points.  By default a TMA-readable A is split
-// inside the kernel (gemm_fused.cu) and only B is pre-split into `ws`;
-// otherwise both operands are split into `ws` (A_hi, A_lo: m x Kp; B_hi,
-// B_lo: n x Kp) and the kernel above runs.
+// Shared by the public entry points.  By default the path with the lowest
+// estimated time is taken (gemm_split_mode): a TMA-readable A split inside
+// the kernel with only B pre-split into `ws` (direct orientation), a
+// TMA-readable B split inside the kernel with only A pre-split into `ws`
+// (transposed orientation, for short wide outputs), or both operands split
+// into `ws` (A_hi, A_lo: m x Kp; B_hi, B_lo: n x Kp) for the kernel above.
 // `layout`: B2K_B_NK -- B is stored [n, K] (else [K, n]); B2K_A_KM -- A is
-// stored [K, m] (else [m, K]).
+// stored [K, m] (else [m, K]).  `ws` holds at least 2 (m + n) Kp floats.
 int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                          int64_t lda, int64_t ldb, int64_t ldc, int layout, const float *bias, int relu,
-                         float *ws, cudaStream_t s, const b2k::StreamKScratch *sk, const float *div_ptr,
-                         float div_value) {
+                         float *ws, cudaStream_t s, const float *div_ptr, float div_value) {
   const int b_kmajor = (layout & B2K_B_NK) != 0;
   const bool a_t = (layout & B2K_A_KM) != 0;
-  // A divided product runs on the pre-pass kernel, whose epilogue divides;
-  // a transposed A is transposed by the pre-pass split.
+  // A divided product runs on the pre-pass kernel, whose epilogue divides.
   const bool divide = div_ptr != nullptr || div_value != 1.0f;
-  const int mode = divide || a_t ? 0 : b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count);
-  if (mode == 2) return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_kmajor, bias, relu, s);
+  const int mode = divide ? 0 : b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, layout, ctx->sm_count);
   const int64_t kp = b2k::gemm_kpad(k);
   int status;
-  if (mode == 1) {
+  if (mode == b2k::kSplitDirect) {
     // A is split inside the kernel (into TMEM); only B is pre-split.
     b2k::SplitOperands ops{nullptr, nullptr, ws, ws + n * kp, kp};
     {
@@ -964,6 +615,17 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
     }
     if (status != B2K_OK) return status;
     return b2k::gemm_tmem_a(ctx, a, k, lda, ops, c, m, n, ldc, bias, relu, s);
+  }
+  if (mode == b2k::kSplitTransposed) {
+    // B is split inside the kernel (into TMEM); only A is pre-split, K-major.
+    b2k::SplitOperands ops{nullptr, nullptr, ws, ws + m * kp, kp};
+    {
+      b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
+      status = a_t ? b2k::split_transpose(ctx, a, k, m, lda, k * lda, 1, kp, ops.b_hi, ops.b_lo, s)
+                   : b2k::split_rows(ctx, a, m, k, lda, m * lda, 1, kp, ops.b_hi, ops.b_lo, s);
+    }
+    if (status != B2K_OK) return status;
+    return b2k::gemm_tmem_b(ctx, b, k, ldb, b_kmajor != 0, ops, c, m, n, ldc, bias, relu, s);
   }
   b2k::SplitOperands ops{ws, ws + m * kp, ws + 2 * m * kp, ws + 2 * m * kp + n * kp, kp};
   {
@@ -985,7 +647,7 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
     }
   }
   if (status != B2K_OK) return status;
-  return b2k::gemm_main(ctx, ops, m, n, 1, c, ldc, m * ldc, bias, relu, div_ptr, div_value, s, sk);
+  return b2k::gemm_main(ctx, ops, m, n, 1, c, ldc, m * ldc, bias, relu, div_ptr, div_value, s);
 }
 
 int b2k::gemm_variant() { return g_gemm_variant; }
@@ -1024,27 +686,11 @@ static int gemm_entry(b2k_ctx *ctx, const float *a, const float *b, float *c, in
     if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: zero fill");
     return B2K_OK;
   }
-  if (!divide && !a_t && b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, ctx->sm_count) == 2)  // needs no scratch
-    return b2k::gemm_smem_split(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_nk, bias, relu, s);
-  // scratch: split operands, then the stream-K partial slots and flags
-  const size_t split_bytes = (b2k_gemm_workspace_bytes(m, n, k) + 255) & ~size_t(255);
-  int status = b2k::reserve_workspace(ctx, split_bytes + b2k::streamk_scratch_bytes(ctx->sm_count), s);
+  // scratch: the split operands
+  int status = b2k::reserve_workspace(ctx, b2k_gemm_workspace_bytes(m, n, k), s);
   if (status != B2K_OK) return status;
-  b2k::StreamKScratch sk;
-  sk.grid = ctx->sm_count;
-  sk.partials = reinterpret_cast<float *>(static_cast<char *>(ctx->workspace) + split_bytes);
-  sk.flags = reinterpret_cast<unsigned *>(sk.partials + (size_t)sk.grid * 128 * 256);
-  if (ctx->flags_epoch == 0 || ctx->flags_ptr != sk.flags) {
-    // fresh scratch: no flag may hold a future epoch
-    cudaError_t err = cudaMemsetAsync(sk.flags, 0, (size_t)sk.grid * sizeof(unsigned), s);
-    if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: flag reset");
-    ctx->flags_ptr = sk.flags;
-    ctx->flags_epoch = 0;
-  }
-  sk.epoch = ++ctx->flags_epoch;
-  if (sk.epoch == 0) sk.epoch = ctx->flags_epoch = 1;
   return b2k_gemm_tf32x3_impl(ctx, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu,
-                              static_cast<float *>(ctx->workspace), s, &sk, div_ptr, div_value);
+                              static_cast<float *>(ctx->workspace), s, div_ptr, div_value);
 }
 
 extern "C" int b2k_gemm_tf32x3(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n,
@@ -1077,7 +723,6 @@ extern "C" int b2k_gemm_tf32x3_batched(b2k_ctx *ctx, const float *a, const float
   const int64_t kp = b2k::gemm_kpad(k);
   int status = b2k::reserve_workspace(ctx, (size_t)(2 * (m + n) * kp * batch) * sizeof(float), s);
   if (status != B2K_OK) return status;
-  ctx->flags_epoch = 0;  // the stream-K flags share this scratch: reset them next time
   float *ws = static_cast<float *>(ctx->workspace);
   // [batch][rows][kp] hi/lo halves, the layout the kernel's 3-D tensor maps walk
   b2k::SplitOperands ops{ws, ws + batch * m * kp, ws + 2 * batch * m * kp, ws + 2 * batch * m * kp + batch * n * kp,
@@ -1094,7 +739,7 @@ extern "C" int b2k_gemm_tf32x3_batched(b2k_ctx *ctx, const float *a, const float
     }
   }
   if (status != B2K_OK) return status;
-  return b2k::gemm_main(ctx, ops, m, n, batch, c, ldc, stride_c, bias, relu, nullptr, 1.0f, s, nullptr);
+  return b2k::gemm_main(ctx, ops, m, n, batch, c, ldc, stride_c, bias, relu, nullptr, 1.0f, s);
 }
 
 extern "C" int b2k_gemm_tf32x3_scaled(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n,

@@ -22,8 +22,7 @@
 // main kernel on `s`.
 int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                          int64_t lda, int64_t ldb, int64_t ldc, int layout, const float *bias, int relu,
-                         float *ws, cudaStream_t s, const b2k::StreamKScratch *sk, const float *div_ptr,
-                         float div_value);
+                         float *ws, cudaStream_t s, const float *div_ptr, float div_value);
 
 namespace {
 
@@ -96,5 +95,5 @@ extern "C" int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c,
   local.sm_count = symbols.sm_count;
   local.error_flag = symbols.status;
   return b2k_gemm_tf32x3_impl(&local, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu,
-                              symbols.scratch, (cudaStream_t)stream, nullptr, nullptr, 1.0f);
+                              symbols.scratch, (cudaStream_t)stream, nullptr, 1.0f);
 }

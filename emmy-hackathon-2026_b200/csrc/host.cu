@@ -297,8 +297,8 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
   b2k::Pipe pipe(ctx, s);
   // The kernel is chosen for the whole call's m, as b2k_gemm_tf32x3 chooses
   // it, so that the result equals the device entry point's bit for bit.
-  const int mode = k == 0 ? 0 : b2k::gemm_split_mode(da, db, m, n, k, k, b_cols, ctx->sm_count);
-  if (k == 0 || mode == 2) {
+  const int mode = k == 0 ? 0 : b2k::gemm_split_mode(da, db, m, n, k, k, b_cols, b_layout, ctx->sm_count);
+  if (k == 0) {
     // No split operands to share between slabs: each slab is a whole GEMM.
     B2K_TRY(pipe.begin());
     B2K_TRY(pipe.in(db, (size_t)b_cols * 4, b, (size_t)ldb * 4, (size_t)b_cols * 4, b_rows));
@@ -313,12 +313,35 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
     }
     return pipe.end();
   }
+  const int64_t kp = b2k::gemm_kpad(k);
+  if (mode == b2k::kSplitTransposed) {
+    // B is read raw by the kernel (split into TMEM); each slab splits its rows
+    // of A into the workspace.  The tile width is the whole call's.
+    const int bn = b2k::gemm_transposed_tile_width(m, n, ctx->sm_count);
+    B2K_TRY(b2k::reserve_workspace(ctx, (size_t)(2 * per * kp) * 4, s));
+    float *ws = static_cast<float *>(ctx->workspace);
+    b2k::SplitOperands ops{nullptr, nullptr, ws, ws + per * kp, kp};
+    B2K_TRY(pipe.begin());
+    B2K_TRY(pipe.in(db, (size_t)b_cols * 4, b, (size_t)ldb * 4, (size_t)b_cols * 4, b_rows));
+    if (bias) B2K_TRY(pipe.in(const_cast<float *>(dbias), 4, bias, 4, (size_t)n * 4, 1));
+    for (int64_t r0 = 0; r0 < m; r0 += per) {
+      const int64_t nr = std::min(per, m - r0);
+      B2K_TRY(pipe.in(da + r0 * k, (size_t)k * 4, a + r0 * lda, (size_t)lda * 4, (size_t)k * 4, nr));
+      B2K_TRY(pipe.landed());
+      {
+        b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
+        B2K_TRY(b2k::split_rows(ctx, da + r0 * k, nr, k, k, nr * k, 1, kp, ops.b_hi, ops.b_lo, s));
+      }
+      B2K_TRY(b2k::gemm_tmem_b(ctx, db, k, b_cols, b_nk, ops, dc + r0 * n, nr, n, n, dbias, relu, s, bn));
+      B2K_TRY(pipe.computed());
+      B2K_TRY(pipe.out(c + r0 * ldc, (size_t)ldc * 4, dc + r0 * n, (size_t)n * 4, (size_t)n * 4, nr));
+    }
+    return pipe.end();
+  }
   // B is split once into the workspace; each slab then splits its rows of A
   // (pre-pass path) or reads them raw (A split into TMEM inside the kernel).
-  const int64_t kp = b2k::gemm_kpad(k);
-  const bool tmem_a = mode == 1;
+  const bool tmem_a = mode == b2k::kSplitDirect;
   B2K_TRY(b2k::reserve_workspace(ctx, (size_t)(2 * n * kp + (tmem_a ? 0 : 2 * per * kp)) * 4, s));
-  ctx->flags_epoch = 0;  // the workspace is reused: stream-K flags must be reset by the next device GEMM
   float *ws = static_cast<float *>(ctx->workspace);
   b2k::SplitOperands ops{ws + 2 * n * kp, ws + 2 * n * kp + per * kp, ws, ws + n * kp, kp};
   B2K_TRY(pipe.begin());

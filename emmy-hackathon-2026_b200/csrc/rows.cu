@@ -275,7 +275,6 @@ extern "C" int b2k_row_op_f32(b2k_ctx *ctx, const b2k_row_params *params, const 
     const int parts = ctx->sm_count * 4;
     int status = b2k::reserve_workspace(ctx, (size_t)parts * sizeof(float), s);
     if (status != B2K_OK) return status;
-    ctx->flags_epoch = 0;  // GEMM stream-K flags share this scratch: reset them next time
     float *partials = static_cast<float *>(ctx->workspace);
     b2k::launch_kernel(b2k::pdl_enabled(), sum_partials, dim3(parts), dim3(kThreads), 0, s, x, cols, partials);
     b2k::launch_kernel(b2k::pdl_enabled(), sum_finish, dim3(1), dim3(kThreads), 0, s, a, (const float *)partials,

@@ -367,127 +367,4 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 
 __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; }
 
-// --- CTA pairs (clusters of 2, tcgen05 cta_group::2) -------------------------
-// The pair's two CTAs run the same kernel with the same shared-memory layout,
-// so an object sits at the same offset in both; mapa gives its address in
-// the other CTA's window of the cluster's shared memory.
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Shared::cluster address of the object at shared address `addr` in CTA `rank`.
-__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-// Every thread of both CTAs: release own writes, wait for the other CTA.
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Arrive (release at cluster scope) on a barrier given by its shared::cluster address.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// mbar_wait with acquire at cluster scope, for barriers the other CTA of the
-// pair arrives on (bounded like mbar_wait).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *err, unsigned site,
-                                                  volatile int *abort, long long budget = kWaitCycles) {
-  const uint32_t addr = smem_addr(bar);
-  if (mbar_try_wait_cluster(addr, parity)) return true;
-  const long long start = clock64();
-  while (!mbar_try_wait_cluster(addr, parity)) {
-    if (*abort) return false;
-    if (clock64() - start > budget) {
-      atomicOr(err, site);
-      *abort = 1;
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t *bar, uint32_t parity, unsigned *err, unsigned site,
-                                                       volatile int *abort, long long budget = kWaitCycles) {
-  const bool ok = mbar_wait_cluster(bar, parity, err, site, abort, budget);
-  return __all_sync(0xffffffffu, ok);
-}
-
-// Pair-wide TMEM allocation: one warp with the same warp index in each CTA;
-// both receive the same address at the same shared-memory slot.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t base, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols) : "memory");
-}
-
-// Pair MMAs (issued by the even CTA; warp-wide with elect.sync like mma_tf32):
-// M = 256, the A rows and the D rows split between the CTAs (128 each, same
-// shared-memory / TMEM offsets), the B operand's N rows split in halves.
-__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred e, p;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_tf32_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred e, p;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive on the barrier at shared address `bar` in BOTH CTAs of the pair once
-// every pair MMA issued so far by this warp completes (tcgen05.commit with a
-// CTA mask; this is not a TMA load and moves no data).
-__device__ __forceinline__ void mma_commit_pair_both(uint64_t *bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(
-          smem_addr(bar)),
-      "h"((unsigned short)0x3)
-      : "memory");
-}
-
-// Arrive on this CTA's barrier `bar` once every pair MMA issued so far completes.
-__device__ __forceinline__ void mma_commit_pair_local(uint64_t *bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_addr(bar))
-      : "memory");
-}
-
 }  // namespace sm100

@@ -1,19 +1,27 @@
 """Multi-GPU sharding of the hot path: one process per GPU, torch.distributed.
 
-The reference is single-GPU.  Every workload of the hot path partitions into
-independent units -- rows of A (B replicated), rows of the softmax matrix,
-ranges of a pointwise vector, batch*head of attention -- so the data path
-needs no collective.  Two drivers are provided:
+The reference is single-GPU (its runner drives one device,
+tools/local_runner.py:246-342).  Every workload of the hot path partitions
+into independent units, so one problem is split over the ranks with no
+collective inside the computation:
 
-* weak scaling (``bench.py --gpus N``): every rank processes its own batch;
-  only a barrier and a max-over-ranks time use the process group;
-* strong scaling of one problem (:func:`sharded_gemm`): rank 0's B is
-  broadcast, each rank computes its row slab of C = A B on its own GPU, and
-  the slabs are all-gathered -- NCCL over NVLink only for the broadcast and
-  the gather, as the hot-path plan prescribes.
+* GEMM (and the ragged GEMM): rows of A, B replicated -- each rank computes
+  its row slab of C;
+* row softmax: rows of the matrix;
+* pointwise add: contiguous element ranges (multiples of 4 elements, so every
+  shard keeps 16-byte vector accesses);
+* attention: batch * heads.
 
-The compute step is a callback so the collective plumbing can be exercised
-with the ``gloo`` backend on CPU; on GPUs the callback is the C-ABI GEMM.
+NCCL over NVLink moves data only where the problem needs it: the broadcast of
+B from rank 0 (:func:`sharded_gemm`) and the all-gather of the output slabs
+(:func:`all_gather_slabs`); attention's K and V are sharded by head along
+with Q, so they need no broadcast.  ``bench.py --gpus N`` times the
+partitioned problem twice: kernels only, with every rank's shard already in
+its HBM (strong scaling, max over ranks), and end to end through these
+functions with the collectives included.
+
+The compute step is a callback so the collective plumbing runs with the
+``gloo`` backend on CPU in the tests; on GPUs the callback is a C-ABI call.
 """
 from __future__ import annotations
 
@@ -55,23 +63,50 @@ def init_from_env(backend: str, timeout_s: float = 120.0):
     return rank, world
 
 
-def sharded_gemm(a_rows, b, m: int, rank: int, world: int, compute, torch, device=None):
+def all_gather_slabs(local, units: int, rank: int, world: int, torch, align: int = 1):
+    """Concatenate every rank's slab (dim 0; rank r holds ``partition(units,
+    world, r, align)``) into the full tensor on every rank.  Slabs are padded
+    to the largest one so the gather is one equal-sized collective."""
+    import torch.distributed as dist
+    if world == 1:
+        return local
+    shards = [partition(units, world, r, align) for r in range(world)]
+    if local.shape[0] != shards[rank].count:
+        raise ValueError("local slab does not match this rank's shard")
+    width = max(s.count for s in shards)
+    tail = tuple(local.shape[1:])
+    if local.shape[0] == width:
+        padded = local.contiguous()
+    else:
+        padded = torch.zeros((width,) + tail, dtype=local.dtype, device=local.device)
+        padded[: local.shape[0]] = local
+    out = torch.empty((world * width,) + tail, dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, padded)
+    if all(s.count == width for s in shards):
+        return out
+    return torch.cat([out[r * width: r * width + s.count] for r, s in enumerate(shards)], dim=0)
+
+
+def sharded_gemm(a_rows, b, m: int, rank: int, world: int, compute, torch, device=None, align: int = 1):
     """Strong-scaling C = A B over the process group.
 
-    ``a_rows`` is this rank's row slab of A (``partition(m, world, rank)``),
-    ``b`` is B on rank 0 and an allocated tensor of the same shape elsewhere
-    (it is overwritten by the broadcast).  ``compute(a_rows, b) -> c_rows``
-    runs the local GEMM.  Returns the full C on every rank."""
+    ``a_rows`` is this rank's row slab of A (``partition(m, world, rank,
+    align)``), ``b`` is B on rank 0 and an allocated tensor of the same shape
+    elsewhere (it is overwritten by the broadcast).  ``compute(a_rows, b) ->
+    c_rows`` runs the local GEMM.  Returns the full C on every rank."""
     import torch.distributed as dist
     if world > 1:
         dist.broadcast(b, src=0)
     c_rows = compute(a_rows, b)
-    if world == 1:
-        return c_rows
-    shards = [partition(m, world, r) for r in range(world)]
-    width = max(s.count for s in shards)
-    padded = torch.zeros((width, c_rows.shape[1]), dtype=c_rows.dtype, device=device)
-    padded[: c_rows.shape[0]] = c_rows
-    gathered = [torch.empty_like(padded) for _ in range(world)]
-    dist.all_gather(gathered, padded)
-    return torch.cat([g[: s.count] for g, s in zip(gathered, shards)], dim=0)
+    return all_gather_slabs(c_rows, m, rank, world, torch, align)
+
+
+def sharded_slabs(inputs, units: int, rank: int, world: int, compute, torch, align: int = 1):
+    """Strong scaling of a row-independent operation: ``inputs`` are this
+    rank's slabs (dim 0 = its ``partition(units, world, rank, align)``) --
+    rows of the softmax matrix, element ranges of the pointwise operands,
+    heads of Q, K and V -- ``compute(*inputs) -> out_slab`` runs the local
+    kernel, and the output slabs are all-gathered.  Returns the full output
+    on every rank."""
+    out = compute(*inputs)
+    return all_gather_slabs(out, units, rank, world, torch, align)

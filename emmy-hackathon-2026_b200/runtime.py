@@ -113,7 +113,6 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_gemm_tf32x3_batched": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I32,
                                  _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
-    "b2k_gemm_set_streamk": ([C.c_int], C.c_int),
     "b2k_gemm_set_fused_split": ([C.c_int], C.c_int),
     "b2k_attention_set_fused": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
@@ -382,13 +381,10 @@ class Context:
         return int(count.value)
 
     def set_gemm_fused_split(self, mode: int) -> None:
-        """0 = pre-pass split of A and B; 3 = A split in-kernel into TMEM; 1 (default)
-        = 3 unless the pre-pass kernel's wider tiles need fewer waves; 2 = A and
-        B split in shared memory inside the kernel."""
+        """0 = pre-pass split of A and B; 3 = A split in-kernel into TMEM (direct);
+        2 = B split in-kernel into TMEM, C^T = B^T A^T (transposed); 1 (default)
+        = whichever of the three the estimate says is fastest."""
         self.check(self.lib.b2k_gemm_set_fused_split(int(mode)), "b2k_gemm_set_fused_split")
-
-    def set_gemm_streamk(self, on: bool) -> None:
-        self.check(self.lib.b2k_gemm_set_streamk(int(bool(on))), "b2k_gemm_set_streamk")
 
     def set_pdl(self, on: bool) -> None:
         """Programmatic dependent launch between a call's kernels (process-wide, default on)."""

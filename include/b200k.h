@@ -290,11 +290,8 @@ int b2k_attention_tf32x3(b2k_ctx *ctx, const float *q, const float *k, const flo
                          int64_t s_q, int64_t s_kv, int64_t d, int64_t dv, float scale_div,
                          const float *scale_div_ptr, int32_t k_layout, void *stream);
 /* Process-wide choice of attention path where head dims allow the fused
- * kernel: 1 (default) the fused kernel with one CTA per query tile; 2 the
- * fused kernel on CTA pairs (tcgen05 cta_group::2, M = 256: two query tiles
- * of a head share every K / V chunk, each CTA loading half -- measured slower
- * on B200 than 1); 0 the three-pass path (for comparisons).  Other values
- * return B2K_EINVAL. */
+ * kernel: 1 (default) the fused kernel with one CTA per query tile; 0 the
+ * three-pass path (for comparisons).  Other values return B2K_EINVAL. */
 int b2k_attention_set_fused(int mode);
 
 /* --- launch by descriptor ----------------------------------------------------
@@ -376,32 +373,31 @@ int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c, int64_t m,
  * other variant 192-wide ones.  No counterpart in the reference, whose plan
  * geometry comes from the IR. */
 int b2k_gemm_set_variant(int variant);
-/* Process-wide switch for the persistent stream-K schedule of the default
- * variant (0 = off, the default; 1 = on): one CTA per SM takes an equal share
- * of the (tile, K block) work instead of whole tiles, so a partial last wave
- * of tiles does not idle SMs.  Off by default because it measured slower on
- * B200 than one tile per CTA.  No counterpart in the reference. */
-int b2k_gemm_set_streamk(int on);
 /* Process-wide choice of where b2k_gemm_tf32x3 (and the no-alloc variant)
  * split operands into TF32 hi/lo halves:
- *   3            A is staged raw by TMA and split inside the tensor-core
- *                kernel into tensor memory, which the MMAs read A from (128 x
- *                192 tiles); B is split once by a pre-pass.  Needs A 16-byte
- *                aligned with a row stride that is a multiple of 4 elements and
- *                K >= 16.
- *   1 (default)  3 where A qualifies, unless the pre-pass kernel's 128 x 256
- *                tiles cover the output in enough fewer waves over the SMs
- *                that (waves x tile width) drops by more than 10 %: then 0.
- *                (4097 x 1000 tiles as 198 tiles of 192 -- two waves on 148
- *                SMs -- or 132 tiles of 256 -- one wave.)
- *   2            both operands staged raw and split in shared memory inside
- *                the kernel (no pre-pass, no scratch; both operands must be
- *                TMA-readable as above).  Measured slower on B200: the split
- *                doubles the shared-memory traffic the tensor core competes for.
- *   0            both operands split by the pre-pass.
- * Calls whose operands do not meet a mode's conditions take the pre-pass path
- * (2 falls back to 3 when only B is not TMA-readable).  Returns B2K_EINVAL
- * for other values.  No counterpart in the reference. */
+ *   3            direct: A is staged raw by TMA and split inside the
+ *                tensor-core kernel into tensor memory, which the MMAs read A
+ *                from (128 x 192 tiles, 128 x 128 for n <= 128); B is split
+ *                once by a pre-pass.  Needs A 16-byte aligned, not stored
+ *                transposed, with a row stride that is a multiple of 4
+ *                elements, and K >= 16.
+ *   2            transposed: the kernel computes C^T = B^T A^T, so B is staged
+ *                raw and split inside the kernel into tensor memory (a [K, N]
+ *                B read in 128-column boxes, a [N, K] B by rows) and only A is
+ *                split by the pre-pass; the epilogue writes C transposed back
+ *                into row-major C.  For short, wide outputs (a row shard of a
+ *                large GEMM) it splits the small operand and tiles the output
+ *                128 columns by 128 or 192 rows.  Needs B 16-byte aligned with
+ *                a row stride that is a multiple of 4 elements, K >= 16 and,
+ *                for a [K, N] B, N >= 128.
+ *   1 (default)  whichever of 0, 2 and 3 the operands allow and an estimate
+ *                of (waves of tiles over the SMs) x (tile time) + (pre-pass
+ *                bytes) says is fastest.
+ *   0            both operands split by the pre-pass (128 x 256 tiles).
+ * Calls whose operands do not meet a mode's conditions take the pre-pass
+ * path.  Every path runs the same three TF32 products per 8-wide K step with
+ * the same 256-wide chunked FP32 accumulation.  Returns B2K_EINVAL for other
+ * values.  No counterpart in the reference. */
 int b2k_gemm_set_fused_split(int mode);
 
 /* --- pipelined host-array calls ----------------------------------------------

@@ -65,12 +65,18 @@ def attention(q, kt, v, scale) -> np.ndarray:
     return (stable_softmax(scores) @ _f64(v)).astype(np.float32)
 
 
-def attention_batched(q, k, v, scale: float | None = None) -> np.ndarray:
-    """Per-(batch, head) :func:`attention` with K stored like Q (``[BH, S, D]``)."""
-    q, k, v = _f64(q), _f64(k), _f64(v)
+def attention_batched(q, k, v, scale: float | None = None, heads_per_pass: int = 8) -> np.ndarray:
+    """Per-(batch, head) :func:`attention` with K stored like Q (``[BH, S, D]``),
+    evaluated a few heads at a time (batched float64 BLAS matmuls) so that the
+    float64 score tensor stays a few hundred MB at S = 2048."""
+    q = np.asarray(q, dtype=np.float32)
     scale = math.sqrt(q.shape[-1]) if scale is None else scale
-    scores = np.einsum("hsd,htd->hst", q, k) / float(scale)
-    return np.einsum("hst,htd->hsd", stable_softmax(scores), v).astype(np.float32)
+    out = np.empty(q.shape[:-1] + (np.shape(v)[-1],), dtype=np.float32)
+    for h in range(0, q.shape[0], heads_per_pass):
+        qh, kh, vh = _f64(q[h:h + heads_per_pass]), _f64(k[h:h + heads_per_pass]), _f64(v[h:h + heads_per_pass])
+        scores = np.matmul(qh, np.swapaxes(kh, 1, 2)) / float(scale)
+        out[h:h + heads_per_pass] = np.matmul(stable_softmax(scores), vh).astype(np.float32)
+    return out
 
 
 def rmsnorm(x, w=None, eps: float = 1e-5) -> np.ndarray:

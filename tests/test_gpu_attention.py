@@ -46,10 +46,8 @@ def test_attention_matches_float64(ctx, torch_cuda, bh, s_q, s_kv, d, dv, k_layo
 @pytest.mark.parametrize("bh,s_q,s_kv,d,dv", [(2, 300, 257, 128, 128), (1, 64, 64, 64, 64), (3, 129, 33, 100, 24),
                                          (2, 256, 200, 128, 64), (1, 640, 384, 32, 128)])
 def test_attention_paths_agree(ctx, torch_cuda, bh, s_q, s_kv, d, dv):
-    """Fused kernel on CTA pairs (mode 2: odd tile counts leave a CTA with no
-    rows; dv <= 64 leaves the odd CTA's V half all zero), fused with one CTA
-    per tile (1, the default) and three passes (0) against float64 and each
-    other."""
+    """The fused kernel (1, the default) and the three passes (0) against
+    float64 and each other."""
     runtime = pkg("runtime")
     lib = runtime.library()
     rng = np.random.default_rng(17 + s_q)
@@ -59,7 +57,7 @@ def test_attention_paths_agree(ctx, torch_cuda, bh, s_q, s_kv, d, dv):
     want = refs.attention_batched(q, k, v, math.sqrt(d))
     outs = []
     try:
-        for mode in (2, 1, 0):
+        for mode in (1, 0):
             assert lib.b2k_attention_set_fused(mode) == runtime.B2K_OK
             outs.append(run(ctx, torch_cuda, q, k, v))
     finally:
@@ -68,7 +66,7 @@ def test_attention_paths_agree(ctx, torch_cuda, bh, s_q, s_kv, d, dv):
         ok, bad, err = refs.allclose_report(got, want, RTOL, ATOL)
         assert ok, (bad, err)
     np.testing.assert_allclose(outs[0], outs[1], rtol=1e-5, atol=1e-6)
-    assert lib.b2k_attention_set_fused(3) == runtime.B2K_EINVAL
+    assert lib.b2k_attention_set_fused(2) == runtime.B2K_EINVAL
 
 
 def test_attention_scale_from_device_buffer(ctx, torch_cuda):
@@ -81,13 +79,12 @@ def test_attention_scale_from_device_buffer(ctx, torch_cuda):
     assert ok, (bad, err)
 
 
-def test_attention_baseline_config_sampled_heads(ctx, torch_cuda):
-    """4 x 16 heads, S 2048, D 128: two heads checked in full against float64."""
+def test_attention_baseline_config_every_head(ctx, torch_cuda):
+    """4 x 16 heads, S 2048, D 128: every output of all 64 heads against
+    float64 at the attention family's tolerance."""
     workloads = pkg("workloads")
     q, k, v = workloads.attention_inputs()
     got = run(ctx, torch_cuda, q, k, v)
-    for h in (0, 37):
-        want = refs.attention_batched(q[h:h + 1], k[h:h + 1], v[h:h + 1], math.sqrt(128))
-        ok, bad, err = refs.allclose_report(got[h:h + 1], want, RTOL, ATOL)
-        assert ok, (h, bad, err)
-    assert np.isfinite(got).all()
+    want = refs.attention_batched(q, k, v, math.sqrt(128))
+    ok, bad, err = refs.allclose_report(got, want, RTOL, ATOL)
+    assert ok, (bad, err)

@@ -80,14 +80,15 @@ def test_gemm_maxfinite_times_zero(ctx, torch_cuda):
 
 
 def test_gemm_4096_cubed(ctx, torch_cuda):
-    """The benchmark configuration, checked on sampled rows against float64."""
+    """The benchmark configuration: every one of the 4096 x 4096 outputs
+    against float64 (the host BLAS does the whole product in well under a
+    second), normwise and at the matmul tolerance."""
     workloads = pkg("workloads")
     a, b = workloads.gemm_inputs()
     got = run_gemm(ctx, torch_cuda, a, b)
-    rows = np.random.default_rng(11).choice(a.shape[0], 64, replace=False)
-    exact = a[rows].astype(np.float64) @ b.astype(np.float64)
-    assert tf32.normwise_error(got[rows], exact) <= NORMWISE
-    ok, bad, err = refs.allclose_report(got[rows], exact.astype(np.float32), 1e-3, 1e-3)
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    assert tf32.normwise_error(got, exact) <= NORMWISE
+    ok, bad, err = refs.allclose_report(got, exact.astype(np.float32), 1e-3, 1e-3)
     assert ok, (bad, err)
     # size-independent checksum: column sums of C equal (1^T A) B
     colsum = (a.astype(np.float64).sum(axis=0) @ b.astype(np.float64))
@@ -111,44 +112,25 @@ def test_gemm_every_variant(ctx, torch_cuda, variant, m, n, k):
     assert tf32.normwise_error(got, a.astype(np.float64) @ b.astype(np.float64)) <= NORMWISE
 
 
-@pytest.mark.parametrize("m,n,k,b_layout", [(4096, 4096, 4096, 0), (4097, 1000, 777, 1), (1024, 2048, 512, 0),
-                                            (1000, 2000, 1000, 1)])
-def test_gemm_streamk_opt_in(ctx, torch_cuda, m, n, k, b_layout):
-    """The opt-in stream-K schedule (partial tiles combined through scratch)
-    matches whole-tile results to the 3xTF32 bound."""
-    rng = np.random.default_rng(m + 3 * n + 7 * k)
-    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
-    b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
-    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
-    ctx.set_gemm_streamk(True)
-    ctx.set_gemm_fused_split(0)  # stream-K is a schedule of the pre-pass kernel
-    try:
-        got = run_gemm(ctx, torch_cuda, a, b, b_layout=b_layout, bias=bias, relu=True)
-        again = run_gemm(ctx, torch_cuda, a, b, b_layout=b_layout, bias=bias, relu=True)
-    finally:
-        ctx.set_gemm_streamk(False)
-        ctx.set_gemm_fused_split(1)
-    bm = b if b_layout == 0 else b.T
-    rows = np.random.default_rng(5).choice(m, min(m, 128), replace=False)
-    exact = np.maximum(a[rows].astype(np.float64) @ bm.astype(np.float64) + bias, 0.0)
-    assert tf32.normwise_error(got[rows], exact) <= NORMWISE
-    np.testing.assert_array_equal(got, again)  # fixed combination order
-
-
 FUSED_CASES = [
     (4096, 4096, 4096, 0), (1000, 1000, 776, 1), (300, 520, 200, 0), (257, 384, 1000, 0), (130, 96, 48, 1),
     (130, 96, 48, 0), (64, 128, 16, 0), (33, 200, 20, 1), (512, 200, 36, 0), (2048, 4000, 300, 1),
     (4097, 1000, 776, 1),  # mode 1 takes the pre-pass kernel: one wave of 256-wide tiles
+    # short, wide outputs (row shards of a multi-GPU GEMM): mode 1 takes the
+    # transposed orientation (B split in the kernel, A pre-split)
+    (512, 4096, 4096, 0), (1024, 4096, 1024, 0), (300, 2000, 1000, 1), (200, 1000, 64, 0), (130, 128, 48, 0),
 ]
 
 
 @pytest.mark.parametrize("m,n,k,b_layout", FUSED_CASES)
 def test_gemm_split_modes_match_float64_and_each_other(ctx, torch_cuda, m, n, k, b_layout):
     """The three split placements (0: pre-pass for A and B; 3: A split into
-    TMEM inside the kernel, B pre-split; 2: A and B split in shared memory,
-    B read K-major or MN-major) and the default choice between 0 and 3 (1)
-    against float64, the 3xTF32 model and each other on the same inputs.
-    Shapes cover ragged M, N and K, N <= 128 and K = 16."""
+    TMEM inside the kernel, B pre-split; 2: the transposed orientation, B split
+    into TMEM inside the kernel -- read MN-major from a [K, N] B or K-major
+    from an [N, K] B -- A pre-split, C written transposed) and the default
+    choice among them (1) against float64, the 3xTF32 model and each other on
+    the same inputs.  Shapes cover ragged M, N and K, N <= 128, K = 16 and
+    short wide outputs."""
     rng = np.random.default_rng(m * 31 + n * 7 + k + b_layout)
     a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
     b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
@@ -166,7 +148,10 @@ def test_gemm_split_modes_match_float64_and_each_other(ctx, torch_cuda, m, n, k,
     model = np.maximum(tf32.gemm_3xtf32(a, bm) + bias, 0.0) if m * n * k <= 1 << 24 else None
     for mode in (1, 2, 3):
         assert tf32.normwise_error(got[mode][rows], exact) <= NORMWISE, mode
-        assert tf32.normwise_error(got[mode], got[0]) <= 1e-7, mode
+        # the same products and chunked folds on every path; the transposed
+        # orientation swaps the MMA operand roles, which may reorder the
+        # in-instruction sum of each 8-wide step (measured 1.3e-7 at 4096^3)
+        assert tf32.normwise_error(got[mode], got[0]) <= 5e-7, mode
         if model is not None:
             assert tf32.normwise_error(got[mode], model) <= 2e-6, mode
 
@@ -291,21 +276,23 @@ def test_gemm_transposed_a(ctx, torch_cuda, m, n, k, b_layout):
     b = rng.uniform(-1, 1, (k, n) if b_layout == 0 else (n, k)).astype(np.float32)
     bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
     da, dat, db, dbias = dev(torch, a), dev(torch, np.ascontiguousarray(a.T)), dev(torch, b), dev(torch, bias)
-    c_t = torch.empty((m, n), device="cuda")
-    ctx.gemm(dat.data_ptr(), db.data_ptr(), c_t.data_ptr(), m, n, k, b_layout=b_layout | runtime.A_KM,
-             bias=dbias.data_ptr(), relu=True)
-    c = torch.empty((m, n), device="cuda")
-    ctx.set_gemm_fused_split(0)
-    try:
-        ctx.gemm(da.data_ptr(), db.data_ptr(), c.data_ptr(), m, n, k, b_layout=b_layout, bias=dbias.data_ptr(),
-                 relu=True)
-        ctx.sync()
-    finally:
-        ctx.set_gemm_fused_split(1)
-    assert torch.equal(c_t, c)
     bm = (b if b_layout == 0 else b.T).astype(np.float64)
     exact = np.maximum(a.astype(np.float64) @ bm + bias, 0.0)
-    assert tf32.normwise_error(c_t.cpu().numpy(), exact) <= NORMWISE
+    try:
+        for mode in (0, 1, 2):
+            ctx.set_gemm_fused_split(mode)
+            c_t = torch.empty((m, n), device="cuda")
+            ctx.gemm(dat.data_ptr(), db.data_ptr(), c_t.data_ptr(), m, n, k, b_layout=b_layout | runtime.A_KM,
+                     bias=dbias.data_ptr(), relu=True)
+            c = torch.empty((m, n), device="cuda")
+            ctx.gemm(da.data_ptr(), db.data_ptr(), c.data_ptr(), m, n, k, b_layout=b_layout, bias=dbias.data_ptr(),
+                     relu=True)
+            ctx.sync()
+            if mode != 1:  # same path for both storage orders: same bits
+                assert torch.equal(c_t, c), mode
+            assert tf32.normwise_error(c_t.cpu().numpy(), exact) <= NORMWISE, mode
+    finally:
+        ctx.set_gemm_fused_split(1)
     host_c = np.empty((m, n), np.float32)
     at = np.ascontiguousarray(a.T)
     with pytest.raises(runtime.B2KError):

@@ -87,7 +87,9 @@ GEMM_CASES = [
     (1000, 520, 300, "nk", True, 1),
     (2300, 700, 777, "nk", True, 1),      # lda 777: pre-pass split of each slab
     (640, 384, 256, "kn", False, 0),
-    (640, 384, 256, "kn", True, 2),       # whole GEMM per slab
+    (640, 384, 256, "kn", True, 2),       # transposed orientation: each slab splits its rows of A
+    (700, 4096, 512, "kn", True, 1),      # short and wide: the default takes the transposed orientation
+    (300, 1000, 640, "nk", False, 2),
     (5, 7, 3, "kn", False, 1),
     (2304, 1024, 1024, "kn", False, 3),   # A split into TMEM, forced
     (4097, 1000, 776, "nk", True, 1),     # aligned A, but the pre-pass kernel tiles in fewer waves

@@ -1,6 +1,7 @@
 """Multi-rank host logic on CPU with the gloo backend (world_size 2): shard
-plans, the broadcast / all-gather plumbing of the strong-scaling GEMM, and a
-rank that fails -- all without a GPU."""
+plans, the broadcast / all-gather plumbing of every partitioned workload
+(GEMM, ragged GEMM, softmax, add, attention), and a rank that fails -- all
+without a GPU."""
 from __future__ import annotations
 
 import os
@@ -40,20 +41,50 @@ def _worker(rank, world, port, mode, results):
     import torch.distributed as dist
     mgpu.init_from_env("gloo", timeout_s=20)
     try:
-        m, k, n = 37, 16, 9
         rng = np.random.default_rng(0)
-        a = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32))
-        b_full = torch.from_numpy(rng.standard_normal((k, n)).astype(np.float32))
-        shard = mgpu.partition(m, world, rank)
-        b = b_full.clone() if rank == 0 else torch.zeros_like(b_full)
-        if mode == "fail" and rank == 1:
-            raise RuntimeError("rank 1 fails before its collective")
+        if mode in ("ok", "fail", "ragged"):
+            # rows of A over the ranks, B broadcast from rank 0 (4097-like ragged
+            # shards with mode "ragged": the last rank takes the remainder)
+            m, k, n = (37, 16, 9) if mode != "ragged" else (131, 12, 10)
+            align = 1 if mode != "ragged" else 32
+            a = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32))
+            b_full = torch.from_numpy(rng.standard_normal((k, n)).astype(np.float32))
+            shard = mgpu.partition(m, world, rank, align)
+            b = b_full.clone() if rank == 0 else torch.zeros_like(b_full)
+            if mode == "fail" and rank == 1:
+                raise RuntimeError("rank 1 fails before its collective")
 
-        # test-only compute callback standing in for the GPU GEMM
-        def compute(ar, bb):
-            return ar @ bb
-        c = mgpu.sharded_gemm(a[shard.start:shard.start + shard.count].clone(), b, m, rank, world, compute, torch)
-        results[rank] = float((c - a @ b_full).abs().max())
+            # test-only compute callback standing in for the GPU GEMM
+            def compute(ar, bb):
+                return ar @ bb
+            c = mgpu.sharded_gemm(a[shard.start:shard.start + shard.count].clone(), b, m, rank, world, compute, torch,
+                                  align=align)
+            results[rank] = float((c - a @ b_full).abs().max())
+        elif mode == "softmax":
+            rows, cols = 10, 33  # rows per rank 5 / 5
+            x = torch.from_numpy(rng.standard_normal((rows, cols)).astype(np.float32))
+            sh = mgpu.partition(rows, world, rank)
+            y = mgpu.sharded_slabs((x[sh.start:sh.start + sh.count],), rows, rank, world,
+                                   lambda xs: torch.softmax(xs, dim=-1), torch)
+            results[rank] = float((y - torch.softmax(x, dim=-1)).abs().max())
+        elif mode == "add":
+            n = 1003  # shards of 500 and 503 elements (align 4)
+            a = torch.from_numpy(rng.standard_normal(n).astype(np.float32))
+            b = torch.from_numpy(rng.standard_normal(n).astype(np.float32))
+            sh = mgpu.partition(n, world, rank, 4)
+            c = mgpu.sharded_slabs((a[sh.start:sh.start + sh.count], b[sh.start:sh.start + sh.count]), n, rank,
+                                   world, lambda x, y: x + y, torch, align=4)
+            results[rank] = float((c - (a + b)).abs().max())
+        elif mode == "attention":
+            bh, s, d = 6, 16, 8  # heads 3 / 3; K and V sharded with Q, nothing broadcast
+            q, k, v = (torch.from_numpy(rng.standard_normal((bh, s, d)).astype(np.float32)) for _ in range(3))
+            sh = mgpu.partition(bh, world, rank)
+            sl = slice(sh.start, sh.start + sh.count)
+
+            def attend(qq, kk, vv):
+                return torch.softmax(qq @ kk.transpose(1, 2) / d ** 0.5, dim=-1) @ vv
+            o = mgpu.sharded_slabs((q[sl], k[sl], v[sl]), bh, rank, world, attend, torch)
+            results[rank] = float((o - attend(q, k, v)).abs().max())
     except Exception as exc:  # reported to the parent
         results[rank] = f"error: {type(exc).__name__}: {exc}"
     finally:
@@ -77,8 +108,12 @@ def _run(world, mode):
     return dict(results)
 
 
-def test_sharded_gemm_gloo_world2():
-    results = _run(2, "ok")
+@pytest.mark.parametrize("mode", ["ok", "ragged", "softmax", "add", "attention"])
+def test_sharded_gloo_world2(mode):
+    """Each partitioned workload (GEMM rows of A with B broadcast -- even and
+    ragged shards --, softmax rows, add element ranges, attention heads)
+    gathers to the unsharded result on every rank."""
+    results = _run(2, mode)
     assert set(results) == {0, 1}, results
     assert all(isinstance(v, float) and v < 1e-4 for v in results.values()), results
 

@@ -35,6 +35,17 @@ def test_simulate_matmul_bit_exact(vectors, name):
     np.testing.assert_array_equal(got, vectors[f"{name}_c"])
 
 
+def test_reference_atom_ptx_fixture_is_pinned():
+    """The reference's one-atom PTX (tf32_emitter.synthetic_ptx output, run on
+    the GPU by test_gpu_reference_ptx.py) is the file its generator recorded:
+    checked by hash only, the text is not inspected."""
+    import hashlib
+    record = json.loads((GOLDEN / "manifest.json").read_text())["reference_ptx"]
+    data = (GOLDEN / record["file"]).read_bytes()
+    assert hashlib.sha256(data).hexdigest() == record["sha256"]
+    assert record["entry"] == "synthetic_mma"
+
+
 def test_maxfinite_witness_model_is_nan(vectors):
     """The reference model turns max-finite x 0 into NaN (rna overflows to inf);
     the device split clamps instead, matching the bundled expected 0."""

@@ -148,9 +148,14 @@ def test_run_given_and_seeded_inputs(server):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("name", ["m02_matmul_rect-aeb1568894b7", "f02_row_softmax-89d56c168a0b",
+@pytest.mark.parametrize("name", ["p01_vector_add-5e973341ada3", "m01_matmul_512-cd9a29496fcc",
+                                  "m02_matmul_rect-aeb1568894b7", "f02_row_softmax-89d56c168a0b",
                                   "a01_attention-c10866af73f8", "attention-0-9170e7b0641d"])
-def test_run_matches_expected(server, name):
+def test_compile_then_run_matches_expected(server, name):
+    """The runner's success path (tools/local_runner.py:345-375): POST
+    /compile, then /run with the case's inputs.npz by kernel_id; the returned
+    values equal expected.npz at the case's tolerance and the returned sum is
+    the sum of those values (the output summary of local_runner.py:333-342)."""
     oracle = pytest.importorskip("oracle.refs")
     folder = CASES / name
     meta = json.loads((folder / "meta.json").read_text())
@@ -158,10 +163,15 @@ def test_run_matches_expected(server, name):
         inputs = {k: {"data": data[k].reshape(-1).tolist()} for k in data.files}
     with np.load(folder / "expected.npz") as data:
         expected = {k: data[k] for k in data.files}
-    status, reply = _call(server, "/run", {**_case_body(name), "inputs": inputs, "warmup": 1, "iters": 2,
-                                           "max_return": 1 << 20})
+    status, compiled = _call(server, "/compile", _case_body(name))
+    assert status == 200 and compiled["ok"], compiled
+    status, reply = _call(server, "/run", {"kernel_id": compiled["kernel_id"], "inputs": inputs, "warmup": 1,
+                                           "iters": 2, "max_return": 1 << 20})
     assert status == 200 and reply["ok"], reply
     for out, want in expected.items():
-        got = np.asarray(reply["outputs"][out]["values"], np.float32).reshape(want.shape)
+        summary = reply["outputs"][out]
+        got = np.asarray(summary["values"], np.float32).reshape(want.shape)
+        assert not summary["truncated"] and summary["shape"] == list(want.shape)
         ok, bad, err = oracle.allclose_report(got, want, meta["rtol"], meta["atol"])
         assert ok, (out, bad, err)
+        assert np.isclose(summary["sum"], float(got.astype(np.float64).sum()), rtol=1e-5, atol=1e-3)
