@@ -833,8 +833,9 @@ class Runner:
                              "rank's CUDA-event time")
         # sustained leg: the same step for >= 2 s (tensor-bound workloads, one GPU)
         if self.world == 1 and w.bound == "tensor" and not args.no_sustained:
-            probe = max(1e-3, t["ms"] / steps / 1e3)
-            s_steps = max(steps, int(math.ceil(2.2 / probe)))
+            per_step_s = max(1e-6, t["ms"] / steps / 1e3)
+            # the power cap slows a long region by up to ~20 %: aim well past 2 s
+            s_steps = max(steps, int(math.ceil(2.5 / per_step_s)))
             ts = self.timed(w, s_steps, 0)
             rec["sustained"] = {"value": round(w.work_total() * s_steps / (ts["ms"] / 1e3) / scale(w.unit), 3),
                                 "unit": w.unit, "steps": s_steps, "seconds": round(ts["ms"] / 1e3, 3),

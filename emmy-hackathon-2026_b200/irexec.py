@@ -288,6 +288,9 @@ class CTAExecutor:
         elif k == "Loop":
             if s.get("seed"):
                 self._seed(s.body, env, mask)
+            if _fold_loop(s):
+                self._run_fold_loop(s, env, mask)
+                return
             for v in range(static_int(s.axis.extent)):
                 env[s.axis.name] = np.full(self.nlanes, v, dtype=np.int64)
                 self.run(s.body, env, mask)
@@ -363,6 +366,77 @@ class CTAExecutor:
         else:
             raise ExecError(f"statement {k!r} is outside the hot path")
 
+    # --- fold loops, all iterations at once -----------------------------------------
+    def _run_fold_loop(self, s, env, mask):
+        """A Loop whose body only loads, computes and folds into accumulators
+        (a dot product over K, a sum over keys): every iteration of a chunk is
+        evaluated at once as a second array axis, and each accumulator takes
+        its chunk's fold in iteration order -- the same mathematics as the
+        serial loop, with the folds of one chunk reassociated (float64, far
+        inside the certificate's tolerance).  Names the body defines keep the
+        last iteration's value, as after the serial loop."""
+        extent = static_int(s.axis.extent)
+        if extent <= 0:
+            return
+        n = self.nlanes
+        chunk = max(1, min(extent, 4_000_000 // max(1, n)))
+        saved = (self.tid, self.bid, self.gid)
+        self.tid, self.bid, self.gid = self.tid[:, None], self.bid[:, None], self.gid[:, None]
+        m2 = mask[:, None]
+        last: dict = {}
+        try:
+            for c0 in range(0, extent, chunk):
+                c1 = min(extent, c0 + chunk)
+                self.budget -= len(s.body)
+                if self.budget < 0:
+                    raise ExecError("execution budget exhausted")
+                venv = _ColumnView(env, n)
+                venv[s.axis.name] = np.arange(c0, c1, dtype=np.int64)[None, :]
+                shape2 = (n, c1 - c0)
+                for st in s.body:
+                    if st.kind == "Load":
+                        buf, bshape, shared = self._buffer(st.input)
+                        size = int(np.prod(bshape)) if len(bshape) else 1
+                        if len(st.index) == 0 and size == 1:
+                            flat = np.zeros(shape2, dtype=np.int64)
+                        else:
+                            if len(st.index) != len(bshape):
+                                raise ExecError("index rank differs from buffer rank")
+                            flat = 0
+                            for dim, e in zip(bshape, st.index):
+                                flat = flat * int(dim) + np.asarray(self.expr(e, venv), dtype=np.int64)
+                            flat = np.broadcast_to(np.asarray(flat, dtype=np.int64), shape2)
+                        for off, name in enumerate(st.names):
+                            f = flat + off
+                            if np.any(m2 & ((f < 0) | (f >= size))):
+                                raise ExecError(f"out-of-bounds read of {st.input!r}")
+                            f = np.where(m2, f, 0)
+                            venv[name] = buf[self.cta_slot[:, None], f] if shared else buf.reshape(-1)[f]
+                            last[name] = True
+                    elif st.kind == "Assign":
+                        venv[st.name] = _elementwise(st.op.name, [venv[a] for a in st.args])
+                        last[st.name] = True
+                    elif st.kind == "Let":
+                        venv[st.name] = self.expr(st.value, venv)
+                        last[st.name] = True
+                    else:  # Accum: fold this chunk's values in order into the accumulator
+                        base = st.base or st.name
+                        if base not in env:
+                            raise ExecError(f"accumulator {base!r} read before it is seeded")
+                        vals = np.broadcast_to(np.asarray(venv[st.value], dtype=np.float64), shape2)
+                        op = st.op.name
+                        with np.errstate(all="ignore"):
+                            part = {"add": np.sum, "multiply": np.prod, "maximum": np.max,
+                                    "minimum": np.min}[op](vals, axis=1)
+                        self._assign(env, st.name, _elementwise(op, [np.asarray(env[base]), part]), mask)
+                        venv[st.name] = np.asarray(env[st.name])[:, None]
+                for name in last:
+                    value = np.broadcast_to(np.asarray(venv[name]), shape2)[:, -1]
+                    self._assign(env, name, value, mask)
+            env[s.axis.name] = np.full(n, extent - 1, dtype=np.int64)
+        finally:
+            self.tid, self.bid, self.gid = saved
+
     def _tree_halve(self, s, env):
         length = int(s.length)
         nct = len(self.L.ctas)
@@ -395,6 +469,83 @@ class _SubExecutor:
             env[s.name] = _elementwise(s.op.name, [env[a] for a in s.args])
 
 
+class _ColumnView(dict):
+    """The environment seen by a fold loop's iterations: names the body sets
+    live here; anything else is read from the enclosing environment, a
+    per-lane value turned into a column so it broadcasts against the
+    iteration axis."""
+
+    def __init__(self, base: dict, lanes: int):
+        super().__init__()
+        self.base, self.lanes = base, lanes
+
+    def __missing__(self, key):
+        value = self.base[key]
+        if isinstance(value, np.ndarray) and value.shape == (self.lanes,):
+            value = value[:, None]
+        self[key] = value
+        return value
+
+    def __contains__(self, key) -> bool:
+        return dict.__contains__(self, key) or key in self.base
+
+
+_FOLD_OPS = frozenset({"add", "multiply", "maximum", "minimum"})
+
+
+def expr_vars(e) -> set:
+    """Variable names an index / value expression reads."""
+    found: set = set()
+
+    def visit(v):
+        if isinstance(v, Node):
+            if v.kind == "Var":
+                found.add(v.name)
+            for x in v.positional:
+                visit(x)
+            for x in v.fields.values():
+                visit(x)
+        elif isinstance(v, (tuple, list)):
+            for x in v:
+                visit(x)
+    visit(e)
+    return found
+
+
+def _fold_loop(s: Node) -> bool:
+    """Whether a Loop body is a pure fold: Loads, Lets and Assigns that feed
+    Accums of add / multiply / maximum / minimum into accumulators that no
+    other statement of the body reads (a dot product, a sum over keys)."""
+    accs, local = set(), set()
+    for st in s.body:
+        if not isinstance(st, Node):
+            return False
+        if st.kind == "Load":
+            local.update(st.names)
+        elif st.kind in ("Assign", "Let"):
+            local.add(st.name)
+        elif st.kind == "Accum":
+            if st.op.name not in _FOLD_OPS or st.get("base") not in (None, st.name):
+                return False
+            accs.add(st.name)
+        else:
+            return False
+    if accs & local or not accs:
+        return False
+    for st in s.body:
+        if st.kind == "Assign":
+            used = set(st.args)
+        elif st.kind == "Accum":
+            used = {st.value}
+        elif st.kind == "Load":
+            used = expr_vars(st.index)
+        else:
+            used = expr_vars(st.value)
+        if used & accs:
+            return False
+    return True
+
+
 def _is_int(v) -> bool:
     return isinstance(v, (int, np.integer)) or (isinstance(v, np.ndarray) and v.dtype.kind in "iu")
 
@@ -404,6 +555,153 @@ def _trunc_div(a, b):
     b = np.asarray(b, dtype=np.int64)
     q = np.abs(a) // np.where(b == 0, 1, np.abs(b))
     return np.where((a < 0) ^ (b < 0), -q, q)
+
+
+# --------------------------------------------------------------------------- output placement
+class NotProvable(ExecError):
+    """Where a kernel writes depends on data, so its coverage has no index-only proof."""
+
+
+def placement_slice(body, outputs) -> set:
+    """The statements that decide WHERE a kernel writes its outputs: every
+    Write to an output buffer, the Tile / Loop / Cond statements around them,
+    and the Let statements (and loops) defining the names their indices,
+    conditions and loop bounds read, transitively.  Returns their ids.  A
+    name defined by a Load, Assign, Accum, Init or warp exchange -- a value
+    computed from data -- raises NotProvable."""
+    parent: dict = {}
+    lets: dict = {}
+    axes: dict = {}
+    data: set = set()
+    writes = []
+
+    def visit(stmts, par):
+        for st in stmts:
+            if not isinstance(st, Node):
+                continue
+            parent[id(st)] = par
+            k = st.kind
+            if k == "Let":
+                lets.setdefault(st.name, []).append(st)
+            elif k == "Load":
+                data.update(st.names)
+            elif k in ("Assign", "Accum", "Init"):
+                data.add(st.name)
+            elif k == "WarpShuffle":
+                data.update(st.state)
+                data.update(st.state_b)
+            elif k == "TreeHalve":
+                data.update(st.state)
+            elif k in ("Loop", "StridedLoop"):
+                axes.setdefault(st.axis.name, []).append(st)
+            elif k == "Tile":
+                for a in st.axes:
+                    axes.setdefault(a.name, []).append(st)
+            elif k == "Write" and st.output in outputs:
+                writes.append(st)
+            for sub in (st.fields.get("body"), st.fields.get("else_body")):
+                if isinstance(sub, tuple):
+                    visit(sub, st)
+            if k == "Select":
+                raise NotProvable("Select statements")
+
+    visit(body, None)
+    keep: set = set()
+    needed: set = set()
+
+    def mark(st):
+        while st is not None and id(st) not in keep:
+            keep.add(id(st))
+            k = st.kind
+            if k == "Cond":
+                needed.update(expr_vars(st.cond))
+            elif k == "StridedLoop":
+                needed.update(expr_vars(st.start) | expr_vars(st.step) | expr_vars(st.get("end")))
+            elif k == "Write":
+                needed.update(expr_vars(st.index))
+            elif k == "Let":
+                needed.update(expr_vars(st.value))
+            st = parent[id(st)]
+
+    for w in writes:
+        mark(w)
+    done: set = set()
+    while needed - done:
+        name = next(iter(needed - done))
+        done.add(name)
+        if name in data:
+            raise NotProvable(f"output placement depends on {name!r}, a value computed from data")
+        if name in lets or name in axes:
+            for st in lets.get(name, []) + axes.get(name, []):
+                mark(st)
+        elif name not in ("tid", "lane", "warp"):
+            raise NotProvable(f"output placement reads the unbound name {name!r}")
+    return keep
+
+
+@dataclass
+class Coverage:
+    counts: dict                 # output name -> writes per element over the whole launch
+    writes_per_cta: np.ndarray   # element writes each CTA performs
+
+
+class _PlacementExecutor(CTAExecutor):
+    """Runs only the placement slice of a kernel and counts output writes."""
+
+    def __init__(self, launch, keep, coverage):
+        super().__init__(launch)
+        self.keep, self.coverage = keep, coverage
+
+    def _buffer(self, name):
+        if name in self.coverage.counts:
+            return None, self.L.shapes[name], False
+        return super()._buffer(name)
+
+    def run(self, body, env, mask):
+        for stmt in body:
+            if isinstance(stmt, Node) and id(stmt) in self.keep:
+                self.stmt(stmt, env, mask)
+
+    def stmt(self, s: Node, env, mask):
+        if s.kind != "Write":
+            return super().stmt(s, env, mask)
+        self.budget -= 1
+        if self.budget < 0:
+            raise ExecError("execution budget exhausted")
+        counts = self.coverage.counts[s.output]
+        flat = self._flat(self.L.shapes[s.output], s.index, env)
+        idx = np.nonzero(mask)[0]
+        for off in range(len(s.values)):
+            f = flat[idx] + off
+            if np.any((f < 0) | (f >= counts.size)):
+                raise ExecError(f"out-of-bounds write of {s.output!r}")
+            np.add.at(counts, f, 1)
+        per_cta = np.bincount(self.cta_slot[idx], minlength=len(self.L.ctas)) * len(s.values)
+        self.coverage.writes_per_cta[self.L.ctas] += per_cta
+
+
+def write_coverage(body, grid: int, block: int, shapes: dict, outputs, max_lanes: int = 1 << 21,
+                   max_statements: int = 2_000_000) -> Coverage:
+    """Exact write counts of every output element over the WHOLE launch (every
+    CTA of `grid`), from the placement slice alone -- the closed-form
+    counterpart of the reference's launch enumeration (tensor_core.py:1577-1612)
+    that costs a few index evaluations per lane whatever the contraction or
+    row length.  CTAs run in chunks of at most `max_lanes` lanes."""
+    keep = placement_slice(body, set(outputs))
+    coverage = Coverage({name: np.zeros(max(1, int(np.prod(shapes[name]))), dtype=np.int64) for name in outputs},
+                        np.zeros(grid, dtype=np.int64))
+    per_chunk = max(1, max_lanes // max(1, block))
+    budget = max_statements
+    for c0 in range(0, grid, per_chunk):
+        ctas = np.arange(c0, min(grid, c0 + per_chunk), dtype=np.int64)
+        launch = Launch(grid=grid, block=block, ctas=ctas, buffers={}, shapes=shapes, max_statements=budget)
+        ex = _PlacementExecutor(launch, keep, coverage)
+        try:
+            ex.run(body, {}, np.ones(ex.nlanes, dtype=bool))
+        except (IRError, KeyError, IndexError, TypeError, AttributeError) as exc:
+            raise ExecError(f"{type(exc).__name__}: {exc}") from exc
+        budget = ex.budget
+    return coverage
 
 
 def execute(body, grid: int, block: int, ctas, buffers: dict, shapes: dict,

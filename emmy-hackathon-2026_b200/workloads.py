@@ -92,7 +92,12 @@ def attention_flop(bh: int, seq: int, d: int) -> int:
 #   add        template p01_vector_add   shape (n,)        a0 = n / vector width, grid = a0 / block
 #   softmax    template f02_row_softmax  shape (rows, cols) a0 = rows, a1..a3 = cols, grid = rows
 #   gemm       template m01_matmul_512   shape (m, n, k)   a0_b = m / 32, a1_b = n / 64, _ks = k,
-#                                                          windows a0 = m, a1 = n, grid = m/32 * n/64
+#                                                          windows a0 = m, a1 = n, grid = m/32 * n/64;
+#                                                          the reference scales only M and N of this
+#                                                          schedule (its perf cases keep K = 512), whose
+#                                                          cp.async prefetch guard holds K as literals
+#                                                          (_ks + 128 < K ? _ks + 128 : K - 64): those two
+#                                                          literals are rewritten for the new K as well
 #   attention  template a01_attention    shape (seq, width) a0_b = seq / 32, a5_b = width / 32, a1 = seq,
 #                                                          a2 = width (the reference keeps width 64 and
 #                                                          does not list a2; here the head dim changes
@@ -123,7 +128,47 @@ def _rescale_stmt(node, extents: dict, windows: dict):
     return node.replace(**changes) if changes else node
 
 
-def rescale_graph(graph: dict, shapes: dict, extents: dict, windows: dict | None = None) -> dict:
+def _rewrite_guard_literals(value, axis: str, literals: dict):
+    """Replace the integer literals in `literals` inside every TernaryExpr whose
+    condition reads `axis` (a loop-bound guard), anywhere under `value`."""
+    from .ir import Node
+
+    def reads(e):
+        if isinstance(e, Node):
+            if e.kind == "Var" and e.name == axis:
+                return True
+            return any(reads(v) for v in e.positional) or any(reads(v) for v in e.fields.values())
+        if isinstance(e, (tuple, list)):
+            return any(reads(v) for v in e)
+        return False
+
+    def swap(e):
+        if isinstance(e, Node):
+            if e.kind == "Literal" and isinstance(e.value, int) and not isinstance(e.value, bool) \
+                    and e.value in literals:
+                return e.replace(value=literals[e.value])
+            return Node(e.kind, tuple(swap(v) for v in e.positional), {k: swap(v) for k, v in e.fields.items()})
+        if isinstance(e, tuple):
+            return tuple(swap(v) for v in e)
+        if isinstance(e, list):
+            return [swap(v) for v in e]
+        return e
+
+    def visit(e):
+        if isinstance(e, Node):
+            if e.kind == "TernaryExpr" and reads(e.cond):
+                return swap(e)
+            return Node(e.kind, tuple(visit(v) for v in e.positional), {k: visit(v) for k, v in e.fields.items()})
+        if isinstance(e, tuple):
+            return tuple(visit(v) for v in e)
+        if isinstance(e, list):
+            return [visit(v) for v in e]
+        return e
+    return visit(value)
+
+
+def rescale_graph(graph: dict, shapes: dict, extents: dict, windows: dict | None = None,
+                  guards: tuple | None = None) -> dict:
     """A copy of an IR graph (JSON dict) with tensor shapes, axis extents and
     window parents rewritten; statements are otherwise unchanged."""
     import copy
@@ -136,7 +181,10 @@ def rescale_graph(graph: dict, shapes: dict, extents: dict, windows: dict | None
                 out["shape"] = [int(s) for s in shapes[out["name"]]]
         if node.get("op") == "KernelOp":
             body = node["op_fields"]["body"]
-            node["op_fields"]["body"] = [render(_rescale_stmt(parse(s), extents, windows or {})) for s in body]
+            stmts = [_rescale_stmt(parse(s), extents, windows or {}) for s in body]
+            if guards:
+                stmts = [_rewrite_guard_literals(st, guards[0], guards[1]) for st in stmts]
+            node["op_fields"]["body"] = [render(st) for st in stmts]
     return graph
 
 
@@ -154,6 +202,7 @@ def scaled_case(template, out, family: str, shape, seed: int = 20260101) -> Path
     kernel = meta["kernels"][0]
     args = {a["name"]: a for a in kernel["args"]}
     windows: dict = {}
+    guards = None
     if family == "add":
         (n,) = shape
         shapes = {name: (n,) for name in args}
@@ -175,6 +224,8 @@ def scaled_case(template, out, family: str, shape, seed: int = 20260101) -> Path
         extents = {"a0_b": m // 32, "a1_b": n // 64, "_ks": k}
         windows = {"a0": m, "a1": n}
         grid = (m // 32) * (n // 64)
+        k_old = args["x0"]["shape"][1]
+        guards = ("_ks", {k_old: k, k_old - 64: k - 64})
     elif family == "attention":
         seq, width = shape
         shapes = {"q": (seq, width), "kt": (width, seq), "v": (seq, width), "matmul_1": (seq, width)}
@@ -183,7 +234,7 @@ def scaled_case(template, out, family: str, shape, seed: int = 20260101) -> Path
         args["div_c1"]["data"] = [math.sqrt(width)]
     else:
         raise ValueError(f"unknown family {family!r}")
-    graph = rescale_graph(graph, shapes, extents, windows)
+    graph = rescale_graph(graph, shapes, extents, windows, guards)
     index = 0
     for name in kernel["arg_order"]:
         arg = args[name]
