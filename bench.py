@@ -135,7 +135,9 @@ class Workload:
 
     def work_total(self) -> float:
         """Work of all ranks per step: the whole problem, or one whole problem
-        per rank for replicas."""
+        per rank for replicas (an emulated shard: that shard's work)."""
+        if getattr(self, "emulated", False):
+            return self.work_shard()
         return self.work_per_unit() * self.units() * (self.world if self.replica else 1)
 
     def work_shard(self) -> float:
@@ -217,6 +219,9 @@ class Workload:
         raise NotImplementedError
 
     def parallelism(self, axis: str) -> str:
+        if getattr(self, "emulated", False):
+            return (f"1 GPU running rank 0's shard of a {self.world}-way partition by {axis} "
+                    f"({self.shard.count} of {self.units()}); value = that shard's work")
         if self.world == 1:
             return "1 GPU"
         if self.replica:
@@ -817,7 +822,11 @@ class Runner:
     def record(self, name: str, args, headline: bool) -> dict:
         """Every measurement of one workload; rank 0 gets the record."""
         torch = self.torch
-        w = make_workload(name, self.rank, self.world)
+        if self.world == 1 and args.shard_of > 1:
+            w = make_workload(name, 0, args.shard_of)
+            w.emulated = True
+        else:
+            w = make_workload(name, self.rank, self.world)
         w.setup(self.ctx, torch)
         steps = args.steps if headline else (args.sub_steps or w.steps_default)
         t = self.timed(w, steps, args.warmup)
@@ -859,7 +868,7 @@ class Runner:
                            "problem": "every rank the whole BASELINE problem (replicas)"}
             wr.sets = []
             torch.cuda.empty_cache()
-        if self.rank == 0 and self.world == 1 and not args.no_cpu:
+        if self.rank == 0 and self.world == 1 and not args.no_cpu and not getattr(w, "emulated", False):
             v, sample = w.cpu_sample()
             cpu = {"value": round(v, 4), "unit": w.unit, "cores": os.cpu_count(), "kind": "port",
                    "sample": sample + " (oracle/refs.py float64 equations, NumPy/BLAS threads = all cores)"}
@@ -955,6 +964,8 @@ def main():
     parser.add_argument("--sub-steps", type=int, default=None, help="timed steps of the other workloads' records")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline samples")
     parser.add_argument("--no-sustained", action="store_true", help="skip the >= 2 s sustained legs")
+    parser.add_argument("--shard-of", type=int, default=1,
+                        help="on one GPU, time rank 0's shard of an N-way partition (profiling the multi-GPU shapes)")
     args = parser.parse_args()
     if args.steps is None:
         args.steps = 20 if args.impl == "reference" else make_workload(args.workload, 0, 1).steps_default
