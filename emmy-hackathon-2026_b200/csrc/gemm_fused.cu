@@ -395,14 +395,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int folded = 0;
     for (int kb = group; kb < num_kb && ok; kb += G) {
-      const int s = kb % Shape::kStages;
-      if (!sm100::mbar_wait(&full_bar[s], (kb / Shape::kStages) & 1, args.err, sm100::kSiteConvert, abort)) {
-        ok = false;
-        break;
-      }
       // TMEM A stage t is free once the MMAs of block kb - kAStages are done.
       // That block's empty_bar phase cannot complete again before this
       // group's block kb has been consumed, so the parity is unambiguous.
+      // It is waited first: with those MMAs done, the load of block
+      // kb - kStages into stage s (kStages >= kAStages) has landed and been
+      // consumed, so the full_bar wait below cannot meet the stage a phase
+      // behind.  (Stage s alternates between groups when kStages is not a
+      // multiple of the group count; waited the other way round, a group
+      // could see another group's load still in flight as its own.)
+      const int s = kb % Shape::kStages;
       const int t = kb % Shape::kAStages;
       if (kb >= Shape::kAStages) {
         const int prev = kb - Shape::kAStages;
@@ -411,6 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+      }
+      if (!sm100::mbar_wait(&full_bar[s], (kb / Shape::kStages) & 1, args.err, sm100::kSiteConvert, abort)) {
+        ok = false;
+        break;
       }
       sm100::tc_fence_after();
       const uint32_t src = sm100::smem_addr(a_raw(s)) + row_off;
