@@ -187,6 +187,15 @@ class Workload:
         raise NotImplementedError
 
     # the partitioned step with its collectives (world > 1)
+    def overlap_splits(self) -> int:
+        """Pieces (row pieces, or B column panels for the GEMM) per rank in the
+        collective step, each gathered while the next computes.  Two at 2 and
+        4 GPUs: each piece still fills the GPU in as many waves as the whole
+        shard (2048 x 2048 GEMM panels and 1024 x 2048 ones in the transposed
+        orientation are 128 tiles; 16 and 8 attention heads are 256 and 128
+        query tiles).  One at 8, where a piece would leave SMs idle."""
+        return 2 if self.world in (2, 4) else 1
+
     def nccl_setup(self, ctx, torch):
         raise NotImplementedError
 
@@ -298,23 +307,35 @@ class Gemm(Workload):
                                bias=self.pbias, relu=self.ragged)
 
     def nccl_setup(self, ctx, torch):
+        mgpu = pkg("mgpu")
         a, b, bias = self.local()
         self.torch, self.ctx = torch, ctx
         self.n_a = torch.from_numpy(np.ascontiguousarray(a)).cuda()
-        self.n_b = torch.from_numpy(b).cuda() if self.rank == 0 else torch.empty(b.shape, device="cuda")
+        # B as column panels, each its own contiguous tensor (rows of the
+        # [N, K] B of the ragged config); the ragged GEMM's 1000 columns stay
+        # one panel (500-column panels would not fill the GPU)
+        self.panels = mgpu.column_panels(self.n, 1 if self.ragged else self.overlap_splits())
+        self.n_b = []
+        for pan in self.panels:
+            cols = slice(pan.start, pan.start + pan.count)
+            part = np.ascontiguousarray(b[cols] if self.ragged else b[:, cols])
+            self.n_b.append(torch.from_numpy(part).cuda() if self.rank == 0
+                            else torch.empty(part.shape, device="cuda"))
         self.n_bias = torch.from_numpy(bias).cuda() if bias is not None else None
-        self.n_c = torch.empty((a.shape[0], self.n), device="cuda")
-        self.nccl_note = (f"NCCL broadcast of B ({b.nbytes / 2**20:.0f} MiB) from rank 0, local GEMM, all-gather "
-                          f"of C row slabs ({self.m * self.n * 4 / 2**20:.0f} MiB)")
+        self.n_c = [torch.empty((a.shape[0], pan.count), device="cuda") for pan in self.panels]
+        self.nccl_note = (f"NCCL broadcast of B ({b.nbytes / 2**20:.0f} MiB, {len(self.panels)} column panel(s)) "
+                          f"from rank 0, local GEMM per panel, all-gather of C ({self.m * self.n * 4 / 2**20:.0f} "
+                          "MiB); panel p+1's broadcast and panel p's gather overlap the GEMMs")
 
     def nccl_step(self):
         mgpu = pkg("mgpu")
 
-        def compute(a_rows, b_full):
-            self.ctx.gemm(a_rows.data_ptr(), b_full.data_ptr(), self.n_c.data_ptr(), a_rows.shape[0], self.n, self.k,
-                          b_layout=1 if self.ragged else 0,
-                          bias=self.n_bias.data_ptr() if self.n_bias is not None else 0, relu=self.ragged)
-            return self.n_c
+        def compute(a_rows, b_panel, i):
+            pan, out = self.panels[i], self.n_c[i]
+            bias = self.n_bias[pan.start:pan.start + pan.count].data_ptr() if self.n_bias is not None else 0
+            self.ctx.gemm(a_rows.data_ptr(), b_panel.data_ptr(), out.data_ptr(), a_rows.shape[0], pan.count, self.k,
+                          b_layout=1 if self.ragged else 0, bias=bias, relu=self.ragged)
+            return out
         return mgpu.sharded_gemm(self.n_a, self.n_b, self.m, self.rank, self.world, compute, self.torch,
                                  align=self.align)
 
@@ -425,15 +446,18 @@ class Softmax(Workload):
         self.torch, self.ctx = torch, ctx
         self.n_x = torch.from_numpy(np.ascontiguousarray(self.local())).cuda()
         self.n_y = torch.empty_like(self.n_x)
-        self.nccl_note = f"local softmax, all-gather of the output rows ({self.rows * self.cols * 4 / 2**20:.0f} MiB)"
+        self.nccl_note = (f"local softmax, all-gather of the output rows ({self.rows * self.cols * 4 / 2**20:.0f} MiB) "
+                          f"in {self.overlap_splits()} piece(s) per rank, each gathered while the next computes")
 
     def nccl_step(self):
         mgpu = pkg("mgpu")
 
-        def compute(x):
-            self.ctx.row_softmax(x.data_ptr(), self.n_y.data_ptr(), x.shape[0], self.cols)
-            return self.n_y
-        return mgpu.sharded_slabs((self.n_x,), self.rows, self.rank, self.world, compute, self.torch)
+        def compute(x, piece):
+            out = self.n_y[piece.start:piece.start + piece.count]
+            self.ctx.row_softmax(x.data_ptr(), out.data_ptr(), x.shape[0], self.cols)
+            return out
+        return mgpu.sharded_slabs((self.n_x,), self.rows, self.rank, self.world, compute, self.torch,
+                                  pieces=self.overlap_splits())
 
     def cpu_once(self):
         oracle_refs().softmax(self.host_inputs())
@@ -512,16 +536,18 @@ class Add(Workload):
         a, b = self.local()
         self.n_a, self.n_b = torch.from_numpy(np.ascontiguousarray(a)).cuda(), torch.from_numpy(np.ascontiguousarray(b)).cuda()
         self.n_c = torch.empty_like(self.n_a)
-        self.nccl_note = f"local add, all-gather of c's element ranges ({self.n * 4 / 2**20:.0f} MiB)"
+        self.nccl_note = (f"local add, all-gather of c's element ranges ({self.n * 4 / 2**20:.0f} MiB) in "
+                          f"{self.overlap_splits()} piece(s) per rank, each gathered while the next computes")
 
     def nccl_step(self):
         mgpu = pkg("mgpu")
 
-        def compute(a, b):
-            self.ctx.pointwise(self.program(), [a.data_ptr(), b.data_ptr()], self.n_c.data_ptr(), a.numel())
-            return self.n_c
+        def compute(a, b, piece):
+            out = self.n_c[piece.start:piece.start + piece.count]
+            self.ctx.pointwise(self.program(), [a.data_ptr(), b.data_ptr()], out.data_ptr(), a.numel())
+            return out
         return mgpu.sharded_slabs((self.n_a, self.n_b), self.n, self.rank, self.world, compute, self.torch,
-                                  align=self.align)
+                                  align=self.align, pieces=self.overlap_splits())
 
     def cpu_once(self):
         a, b = self.host_inputs()
@@ -593,16 +619,19 @@ class Attention(Workload):
         self.n_in = [torch.from_numpy(np.ascontiguousarray(t)).cuda() for t in self.local()]
         self.n_o = torch.empty_like(self.n_in[0])
         self.nccl_note = (f"heads pre-sharded with Q, K and V (nothing broadcast), all-gather of O "
-                          f"({self.bh * self.seq * self.d * 4 / 2**20:.0f} MiB)")
+                          f"({self.bh * self.seq * self.d * 4 / 2**20:.0f} MiB) in {self.overlap_splits()} piece(s) per "
+                          "rank, each gathered while the next computes")
 
     def nccl_step(self):
         mgpu = pkg("mgpu")
 
-        def compute(q, k, v):
-            self.ctx.attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), self.n_o.data_ptr(), q.shape[0], self.seq,
+        def compute(q, k, v, piece):
+            out = self.n_o[piece.start:piece.start + piece.count]
+            self.ctx.attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), q.shape[0], self.seq,
                                self.seq, self.d, self.d)
-            return self.n_o
-        return mgpu.sharded_slabs(tuple(self.n_in), self.bh, self.rank, self.world, compute, self.torch)
+            return out
+        return mgpu.sharded_slabs(tuple(self.n_in), self.bh, self.rank, self.world, compute, self.torch,
+                                  pieces=self.overlap_splits())
 
     def cpu_once(self):
         q, k, v = self.host_inputs()

@@ -63,16 +63,19 @@ def init_from_env(backend: str, timeout_s: float = 120.0):
     return rank, world
 
 
-def all_gather_slabs(local, units: int, rank: int, world: int, torch, align: int = 1):
-    """Concatenate every rank's slab (dim 0; rank r holds ``partition(units,
-    world, r, align)``) into the full tensor on every rank.  Slabs are padded
-    to the largest one so the gather is one equal-sized collective."""
+def gather_start(local, units: int, rank: int, world: int, torch, align: int = 1):
+    """Start the all-gather of this rank's slab (dim 0; rank r holds
+    ``partition(units, world, r, align)``) without waiting for it.  Returns a
+    function that waits and returns the full tensor.  Slabs are padded to the
+    largest one so the gather is one equal-sized collective; on GPUs it runs
+    on the process group's own stream, so kernels issued after this call
+    overlap it."""
     import torch.distributed as dist
-    if world == 1:
-        return local
     shards = [partition(units, world, r, align) for r in range(world)]
     if local.shape[0] != shards[rank].count:
         raise ValueError("local slab does not match this rank's shard")
+    if world == 1:
+        return lambda: local
     width = max(s.count for s in shards)
     tail = tuple(local.shape[1:])
     if local.shape[0] == width:
@@ -81,32 +84,92 @@ def all_gather_slabs(local, units: int, rank: int, world: int, torch, align: int
         padded = torch.zeros((width,) + tail, dtype=local.dtype, device=local.device)
         padded[: local.shape[0]] = local
     out = torch.empty((world * width,) + tail, dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(out, padded)
-    if all(s.count == width for s in shards):
-        return out
-    return torch.cat([out[r * width: r * width + s.count] for r, s in enumerate(shards)], dim=0)
+    work = dist.all_gather_into_tensor(out, padded, async_op=True)
+
+    def finish():
+        work.wait()
+        if all(s.count == width for s in shards):
+            return out
+        return torch.cat([out[r * width: r * width + s.count] for r, s in enumerate(shards)], dim=0)
+    return finish
 
 
-def sharded_gemm(a_rows, b, m: int, rank: int, world: int, compute, torch, device=None, align: int = 1):
+def all_gather_slabs(local, units: int, rank: int, world: int, torch, align: int = 1):
+    """Concatenate every rank's slab (dim 0; rank r holds ``partition(units,
+    world, r, align)``) into the full tensor on every rank."""
+    return gather_start(local, units, rank, world, torch, align)()
+
+
+def column_panels(n: int, panels: int):
+    """``panels`` contiguous column ranges of an n-wide B (the last one takes
+    the remainder)."""
+    return [partition(n, panels, p) for p in range(panels)]
+
+
+def sharded_gemm(a_rows, b, m: int, rank: int, world: int, compute, torch, align: int = 1):
     """Strong-scaling C = A B over the process group.
 
     ``a_rows`` is this rank's row slab of A (``partition(m, world, rank,
-    align)``), ``b`` is B on rank 0 and an allocated tensor of the same shape
-    elsewhere (it is overwritten by the broadcast).  ``compute(a_rows, b) ->
-    c_rows`` runs the local GEMM.  Returns the full C on every rank."""
+    align)``).  ``b`` is B on rank 0 and an allocated tensor of the same
+    shape elsewhere (overwritten by the broadcast), or a list of B's column
+    panels in that form (each its own contiguous tensor: [K, width], or
+    [width, K] for a transposed B; :func:`column_panels` gives the ranges).
+    ``compute(a_rows, b_panel, index) -> c_panel`` runs the local GEMM of
+    panel ``index`` and returns its [rows, width] result, which must stay
+    valid until this call returns.  Returns the full C on every rank.
+
+    With several panels the steps overlap: every panel's broadcast is issued
+    at once and runs in order on the process group's stream; the GEMM of
+    panel p waits only for panel p, and the all-gather of panel p's C runs
+    while panel p + 1 computes.  Panels pay off when each panel's GEMM still
+    fills the GPU (2048 x 2048 x 4096 per rank at 2 GPUs: 128 tiles, as many
+    waves as the unsplit 2048 x 4096)."""
     import torch.distributed as dist
-    if world > 1:
-        dist.broadcast(b, src=0)
-    c_rows = compute(a_rows, b)
-    return all_gather_slabs(c_rows, m, rank, world, torch, align)
+    panels = list(b) if isinstance(b, (list, tuple)) else [b]
+    bcast = [dist.broadcast(p, src=0, async_op=True) for p in panels] if world > 1 else []
+    finishers = []
+    for i, panel in enumerate(panels):
+        if bcast:
+            bcast[i].wait()
+        finishers.append(gather_start(compute(a_rows, panel, i), m, rank, world, torch, align))
+    parts = [f() for f in finishers]
+    return parts[0] if len(parts) == 1 else torch.cat(parts, dim=1)
 
 
-def sharded_slabs(inputs, units: int, rank: int, world: int, compute, torch, align: int = 1):
+def sharded_slabs(inputs, units: int, rank: int, world: int, compute, torch, align: int = 1, pieces: int = 1):
     """Strong scaling of a row-independent operation: ``inputs`` are this
     rank's slabs (dim 0 = its ``partition(units, world, rank, align)``) --
     rows of the softmax matrix, element ranges of the pointwise operands,
-    heads of Q, K and V -- ``compute(*inputs) -> out_slab`` runs the local
-    kernel, and the output slabs are all-gathered.  Returns the full output
-    on every rank."""
-    out = compute(*inputs)
-    return all_gather_slabs(out, units, rank, world, torch, align)
+    heads of Q, K and V.  ``compute(*input_pieces, piece) -> out_piece`` runs
+    the local kernel on rows ``piece`` (a :class:`Shard` within this rank's
+    slab) and returns that piece's output, which must stay valid until this
+    call returns.  The output is all-gathered; returns the full output on
+    every rank.
+
+    With ``pieces`` > 1 the slab is cut into that many row pieces and the
+    all-gather of piece i runs while piece i + 1 computes.  That needs equal
+    shards on every rank, cut into equal pieces (multiples of ``align``);
+    otherwise the slab runs as one piece."""
+    shards = [partition(units, world, r, align) for r in range(world)]
+    count = shards[rank].count
+    if (pieces > 1 and all(s.count == count for s in shards) and count % pieces == 0
+            and (count // pieces) % align == 0):
+        step = count // pieces
+    else:
+        pieces, step = 1, count
+    if pieces == 1:
+        return all_gather_slabs(compute(*inputs, Shard(0, count)), units, rank, world, torch, align)
+    finishers = []
+    for i in range(pieces):
+        piece = Shard(i * step, step)
+        out = compute(*(x[piece.start:piece.start + step] for x in inputs), piece)
+        finishers.append(gather_start(out, step * world, rank, world, torch))
+    # gathered piece i is [world * step] rows, rank-major; rank r's piece i
+    # belongs at rows r * count + i * step of the full output
+    parts = [f() for f in finishers]
+    tail = tuple(parts[0].shape[1:])
+    full = torch.empty((world * count,) + tail, dtype=parts[0].dtype, device=parts[0].device)
+    view = full.view((world, pieces, step) + tail)
+    for i, g in enumerate(parts):
+        view[:, i].copy_(g.view((world, step) + tail))
+    return full

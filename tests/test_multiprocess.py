@@ -42,7 +42,7 @@ def _worker(rank, world, port, mode, results):
     mgpu.init_from_env("gloo", timeout_s=20)
     try:
         rng = np.random.default_rng(0)
-        if mode in ("ok", "fail", "ragged"):
+        if mode in ("ok", "fail", "ragged", "panels"):
             # rows of A over the ranks, B broadcast from rank 0 (4097-like ragged
             # shards with mode "ragged": the last rank takes the remainder)
             m, k, n = (37, 16, 9) if mode != "ragged" else (131, 12, 10)
@@ -54,26 +54,37 @@ def _worker(rank, world, port, mode, results):
             if mode == "fail" and rank == 1:
                 raise RuntimeError("rank 1 fails before its collective")
 
+            if mode == "panels":
+                # B broadcast as three column panels (widths 3, 3, 3), one GEMM per panel
+                pans = mgpu.column_panels(n, 3)
+                b = [b[:, p.start:p.start + p.count].contiguous() for p in pans]
+
             # test-only compute callback standing in for the GPU GEMM
-            def compute(ar, bb):
+            def compute(ar, bb, i):
                 return ar @ bb
             c = mgpu.sharded_gemm(a[shard.start:shard.start + shard.count].clone(), b, m, rank, world, compute, torch,
                                   align=align)
             results[rank] = float((c - a @ b_full).abs().max())
         elif mode == "softmax":
-            rows, cols = 10, 33  # rows per rank 5 / 5
+            rows, cols = 12, 33  # rows per rank 6 / 6, in three pieces of 2 rows
             x = torch.from_numpy(rng.standard_normal((rows, cols)).astype(np.float32))
             sh = mgpu.partition(rows, world, rank)
-            y = mgpu.sharded_slabs((x[sh.start:sh.start + sh.count],), rows, rank, world,
-                                   lambda xs: torch.softmax(xs, dim=-1), torch)
+            seen = []
+
+            def soft(xs, piece):
+                seen.append((piece.start, piece.count))
+                return torch.softmax(xs, dim=-1)
+            y = mgpu.sharded_slabs((x[sh.start:sh.start + sh.count],), rows, rank, world, soft, torch, pieces=3)
+            assert seen == [(0, 2), (2, 2), (4, 2)], seen
             results[rank] = float((y - torch.softmax(x, dim=-1)).abs().max())
         elif mode == "add":
             n = 1003  # shards of 500 and 503 elements (align 4)
             a = torch.from_numpy(rng.standard_normal(n).astype(np.float32))
             b = torch.from_numpy(rng.standard_normal(n).astype(np.float32))
             sh = mgpu.partition(n, world, rank, 4)
+            # unequal shards: the pieces request falls back to one piece
             c = mgpu.sharded_slabs((a[sh.start:sh.start + sh.count], b[sh.start:sh.start + sh.count]), n, rank,
-                                   world, lambda x, y: x + y, torch, align=4)
+                                   world, lambda x, y, piece: x + y, torch, align=4, pieces=2)
             results[rank] = float((c - (a + b)).abs().max())
         elif mode == "attention":
             bh, s, d = 6, 16, 8  # heads 3 / 3; K and V sharded with Q, nothing broadcast
@@ -81,9 +92,9 @@ def _worker(rank, world, port, mode, results):
             sh = mgpu.partition(bh, world, rank)
             sl = slice(sh.start, sh.start + sh.count)
 
-            def attend(qq, kk, vv):
+            def attend(qq, kk, vv, piece=None):
                 return torch.softmax(qq @ kk.transpose(1, 2) / d ** 0.5, dim=-1) @ vv
-            o = mgpu.sharded_slabs((q[sl], k[sl], v[sl]), bh, rank, world, attend, torch)
+            o = mgpu.sharded_slabs((q[sl], k[sl], v[sl]), bh, rank, world, attend, torch, pieces=3)
             results[rank] = float((o - attend(q, k, v)).abs().max())
     except Exception as exc:  # reported to the parent
         results[rank] = f"error: {type(exc).__name__}: {exc}"
@@ -108,10 +119,11 @@ def _run(world, mode):
     return dict(results)
 
 
-@pytest.mark.parametrize("mode", ["ok", "ragged", "softmax", "add", "attention"])
+@pytest.mark.parametrize("mode", ["ok", "ragged", "panels", "softmax", "add", "attention"])
 def test_sharded_gloo_world2(mode):
     """Each partitioned workload (GEMM rows of A with B broadcast -- even and
-    ragged shards --, softmax rows, add element ranges, attention heads)
+    ragged shards, whole or as column panels --, softmax rows and attention
+    heads in pieces gathered while the next computes, add element ranges)
     gathers to the unsharded result on every rank."""
     results = _run(2, mode)
     assert set(results) == {0, 1}, results
