@@ -352,8 +352,8 @@ int b2k_launch(b2k_ctx *ctx, const b2k_kernel_desc *desc, void *const *args, int
  * nothing; extents beyond the 32-bit limits of b2k_gemm_tf32x3 return
  * B2K_EINVAL; K = 0 returns B2K_EUNSUPPORTED.  Runs on the calling thread's
  * current device and the given stream.  The first call on a device looks up
- * the scratch array's device address (cudaGetSymbolAddress); make that first
- * call before any stream capture.  Every call on a device shares the one
+ * the scratch array's device address (cudaGetSymbolAddress) and keeps it.
+ * Every call on a device shares the one
  * array, so calls that overlap on the GPU (different streams, no ordering)
  * race and corrupt each other's results; calls on one stream are safe.  Each
  * call rewrites all the scratch it reads, so nothing needs clearing.  A
