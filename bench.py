@@ -27,7 +27,8 @@ partitioned over the ranks (rows of A, rows of the softmax, element ranges,
 batch*heads; ``mgpu.partition``) with every rank's shard already in its HBM:
 strong scaling, ``value`` = the whole problem's work over the max-over-ranks
 device time.  ``nccl_e2e`` repeats the partitioned step with its collectives
-(B broadcast from rank 0, all-gather of the output slabs) and ``weak`` gives
+(B broadcast from rank 0, all-gather of the output slabs) through the
+library's multi-GPU driver (``b2k_mgpu_*``, its own NCCL communicator), and ``weak`` gives
 the replica figure (every rank the whole problem).  ``e2e`` is the step
 through the public host-array API (``api.Session``, the ``b2k_*_host``
 calls) with every rank's inputs copied in from page-locked host memory and
@@ -196,7 +197,7 @@ class Workload:
         query tiles).  One at 8, where a piece would leave SMs idle."""
         return 2 if self.world in (2, 4) else 1
 
-    def nccl_setup(self, ctx, torch):
+    def nccl_setup(self, ctx, torch, group):
         raise NotImplementedError
 
     def nccl_step(self):
@@ -306,38 +307,28 @@ class Gemm(Workload):
         self.session.gemm_host(self.pa, self.pb, self.pc, b_layout="nk" if self.ragged else "kn",
                                bias=self.pbias, relu=self.ragged)
 
-    def nccl_setup(self, ctx, torch):
-        mgpu = pkg("mgpu")
+    def nccl_setup(self, ctx, torch, group):
         a, b, bias = self.local()
-        self.torch, self.ctx = torch, ctx
+        self.torch, self.group = torch, group
         self.n_a = torch.from_numpy(np.ascontiguousarray(a)).cuda()
-        # B as column panels, each its own contiguous tensor (rows of the
-        # [N, K] B of the ragged config); the ragged GEMM's 1000 columns stay
-        # one panel (500-column panels would not fill the GPU)
-        self.panels = mgpu.column_panels(self.n, 1 if self.ragged else self.overlap_splits())
-        self.n_b = []
-        for pan in self.panels:
-            cols = slice(pan.start, pan.start + pan.count)
-            part = np.ascontiguousarray(b[cols] if self.ragged else b[:, cols])
-            self.n_b.append(torch.from_numpy(part).cuda() if self.rank == 0
-                            else torch.empty(part.shape, device="cuda"))
+        self.n_b = torch.from_numpy(np.ascontiguousarray(b)).cuda() if self.rank == 0 else None
         self.n_bias = torch.from_numpy(bias).cuda() if bias is not None else None
-        self.n_c = [torch.empty((a.shape[0], pan.count), device="cuda") for pan in self.panels]
-        self.nccl_note = (f"NCCL broadcast of B ({b.nbytes / 2**20:.0f} MiB, {len(self.panels)} column panel(s)) "
-                          f"from rank 0, local GEMM per panel, all-gather of C ({self.m * self.n * 4 / 2**20:.0f} "
-                          "MiB); panel p+1's broadcast and panel p's gather overlap the GEMMs")
+        self.n_c = torch.empty((self.m, self.n), device="cuda")
+        # the ragged GEMM's 1000 columns stay one panel (500-column panels
+        # would not fill the GPU)
+        self.panels = 1 if self.ragged else self.overlap_splits()
+        self.nccl_note = (f"b2k_mgpu_gemm_tf32x3: NCCL broadcast of B ({b.nbytes / 2**20:.0f} MiB) from rank 0 in "
+                          f"{self.panels} column panel(s), local GEMM per panel, all-gather of C "
+                          f"({self.m * self.n * 4 / 2**20:.0f} MiB); panel p+1's broadcast and panel p's gather "
+                          "overlap the GEMMs")
 
     def nccl_step(self):
-        mgpu = pkg("mgpu")
-
-        def compute(a_rows, b_panel, i):
-            pan, out = self.panels[i], self.n_c[i]
-            bias = self.n_bias[pan.start:pan.start + pan.count].data_ptr() if self.n_bias is not None else 0
-            self.ctx.gemm(a_rows.data_ptr(), b_panel.data_ptr(), out.data_ptr(), a_rows.shape[0], pan.count, self.k,
-                          b_layout=1 if self.ragged else 0, bias=bias, relu=self.ragged)
-            return out
-        return mgpu.sharded_gemm(self.n_a, self.n_b, self.m, self.rank, self.world, compute, self.torch,
-                                 align=self.align)
+        self.group.gemm(self.n_a.data_ptr(), self.n_b.data_ptr() if self.n_b is not None else 0,
+                        self.n_c.data_ptr(), self.m, self.n, self.k, align=self.align,
+                        b_layout=1 if self.ragged else 0,
+                        bias=self.n_bias.data_ptr() if self.n_bias is not None else 0, relu=self.ragged,
+                        panels=self.panels)
+        return self.n_c
 
     def cpu_once(self):
         refs = oracle_refs()
@@ -442,22 +433,17 @@ class Softmax(Workload):
     def e2e_step(self):
         self.session.row_softmax_host(self.px, self.py)
 
-    def nccl_setup(self, ctx, torch):
-        self.torch, self.ctx = torch, ctx
+    def nccl_setup(self, ctx, torch, group):
+        self.torch, self.group = torch, group
         self.n_x = torch.from_numpy(np.ascontiguousarray(self.local())).cuda()
-        self.n_y = torch.empty_like(self.n_x)
-        self.nccl_note = (f"local softmax, all-gather of the output rows ({self.rows * self.cols * 4 / 2**20:.0f} MiB) "
+        self.n_y = torch.empty((self.rows, self.cols), device="cuda")
+        self.nccl_note = (f"b2k_mgpu_row_softmax_f32: local softmax, all-gather of the output rows ({self.rows * self.cols * 4 / 2**20:.0f} MiB) "
                           f"in {self.overlap_splits()} piece(s) per rank, each gathered while the next computes")
 
     def nccl_step(self):
-        mgpu = pkg("mgpu")
-
-        def compute(x, piece):
-            out = self.n_y[piece.start:piece.start + piece.count]
-            self.ctx.row_softmax(x.data_ptr(), out.data_ptr(), x.shape[0], self.cols)
-            return out
-        return mgpu.sharded_slabs((self.n_x,), self.rows, self.rank, self.world, compute, self.torch,
-                                  pieces=self.overlap_splits())
+        self.group.row_softmax(self.n_x.data_ptr(), self.n_y.data_ptr(), self.rows, self.cols,
+                               pieces=self.overlap_splits())
+        return self.n_y
 
     def cpu_once(self):
         oracle_refs().softmax(self.host_inputs())
@@ -531,23 +517,18 @@ class Add(Workload):
     def e2e_step(self):
         self.session.pointwise_host(self.program(), [self.pa, self.pb], self.pc)
 
-    def nccl_setup(self, ctx, torch):
-        self.torch, self.ctx = torch, ctx
+    def nccl_setup(self, ctx, torch, group):
+        self.torch, self.group = torch, group
         a, b = self.local()
         self.n_a, self.n_b = torch.from_numpy(np.ascontiguousarray(a)).cuda(), torch.from_numpy(np.ascontiguousarray(b)).cuda()
-        self.n_c = torch.empty_like(self.n_a)
-        self.nccl_note = (f"local add, all-gather of c's element ranges ({self.n * 4 / 2**20:.0f} MiB) in "
+        self.n_c = torch.empty(self.n, device="cuda")
+        self.nccl_note = (f"b2k_mgpu_pointwise_f32: local add, all-gather of c's element ranges ({self.n * 4 / 2**20:.0f} MiB) in "
                           f"{self.overlap_splits()} piece(s) per rank, each gathered while the next computes")
 
     def nccl_step(self):
-        mgpu = pkg("mgpu")
-
-        def compute(a, b, piece):
-            out = self.n_c[piece.start:piece.start + piece.count]
-            self.ctx.pointwise(self.program(), [a.data_ptr(), b.data_ptr()], out.data_ptr(), a.numel())
-            return out
-        return mgpu.sharded_slabs((self.n_a, self.n_b), self.n, self.rank, self.world, compute, self.torch,
-                                  align=self.align, pieces=self.overlap_splits())
+        self.group.pointwise(self.program(), [self.n_a.data_ptr(), self.n_b.data_ptr()], self.n_c.data_ptr(),
+                             self.n, align=self.align, pieces=self.overlap_splits())
+        return self.n_c
 
     def cpu_once(self):
         a, b = self.host_inputs()
@@ -614,24 +595,19 @@ class Attention(Workload):
     def e2e_step(self):
         self.session.attention_host(*self.pin, self.pout)
 
-    def nccl_setup(self, ctx, torch):
-        self.torch, self.ctx = torch, ctx
+    def nccl_setup(self, ctx, torch, group):
+        self.torch, self.group = torch, group
         self.n_in = [torch.from_numpy(np.ascontiguousarray(t)).cuda() for t in self.local()]
-        self.n_o = torch.empty_like(self.n_in[0])
-        self.nccl_note = (f"heads pre-sharded with Q, K and V (nothing broadcast), all-gather of O "
+        self.n_o = torch.empty((self.bh, self.seq, self.d), device="cuda")
+        self.nccl_note = (f"b2k_mgpu_attention_tf32x3: heads pre-sharded with Q, K and V (nothing broadcast), all-gather of O "
                           f"({self.bh * self.seq * self.d * 4 / 2**20:.0f} MiB) in {self.overlap_splits()} piece(s) per "
                           "rank, each gathered while the next computes")
 
     def nccl_step(self):
-        mgpu = pkg("mgpu")
-
-        def compute(q, k, v, piece):
-            out = self.n_o[piece.start:piece.start + piece.count]
-            self.ctx.attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), q.shape[0], self.seq,
-                               self.seq, self.d, self.d)
-            return out
-        return mgpu.sharded_slabs(tuple(self.n_in), self.bh, self.rank, self.world, compute, self.torch,
-                                  pieces=self.overlap_splits())
+        q, k, v = self.n_in
+        self.group.attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), self.n_o.data_ptr(), self.bh, self.seq,
+                             self.seq, self.d, self.d, pieces=self.overlap_splits())
+        return self.n_o
 
     def cpu_once(self):
         q, k, v = self.host_inputs()
@@ -729,6 +705,21 @@ class Runner:
         self.torch, self.dist, self.rank, self.local, self.world = torch, dist, rank, local, world
         self.ctx = pkg("runtime").Context(local)
         self.peaks, self.peak_basis = measured_peaks()
+        self.group = None
+
+    def native_group(self):
+        """The library's own NCCL communicator (b2k_mgpu_*): rank 0 makes the
+        rendezvous id, the process group hands it to every rank."""
+        if self.group is None:
+            rt, torch = pkg("runtime"), self.torch
+            uid = torch.zeros(rt.MGPU_ID_BYTES, dtype=torch.uint8, device="cuda")
+            if self.rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(rt.mgpu_unique_id()), dtype=torch.uint8))
+            if self.dist is not None:
+                self.dist.broadcast(uid, src=0)
+            with stdout_to_stderr():  # NCCL may print its version while the communicator comes up
+                self.group = rt.MultiGpu(self.ctx, self.world, self.rank, bytes(uid.cpu().numpy().tobytes()))
+        return self.group
 
     def barrier(self):
         self.torch.cuda.synchronize()
@@ -837,16 +828,20 @@ class Runner:
                        "overlapped)" + (", each rank its own shard" if self.world > 1 else "")}
 
     def nccl_e2e(self, w: Workload, steps: int = 10, warmup: int = 3) -> dict:
-        """The partitioned step with its collectives, device-resident (max over ranks)."""
-        w.nccl_setup(self.ctx, self.torch)
+        """The partitioned step with its collectives, device-resident (max over
+        ranks), through the library's multi-GPU driver (b2k_mgpu_*)."""
+        group = self.native_group()
+        w.nccl_setup(self.ctx, self.torch, group)
         for _ in range(warmup):
             out = w.nccl_step()
+        group.sync(timeout_ms=120000)
         self.barrier()
         e0, e1 = self.event_pair()
         e0.record()
         for _ in range(steps):
             out = w.nccl_step()
         e1.record()
+        group.sync(timeout_ms=120000)
         self.barrier()
         ms = self.max_over_ranks(e0.elapsed_time(e1))
         # size-independent check of the gathered output on every rank
@@ -941,6 +936,8 @@ def run_ours(args) -> dict | None:
         rec["vs_baseline"] = None
         rec["data"] = "synthetic (seeded, distributions of the BASELINE configs)"
     finally:
+        if runner.group is not None:
+            runner.group.close()
         runner.ctx.close()
         if dist is not None:
             dist.barrier()

@@ -13,9 +13,11 @@ from pathlib import Path
 LIBRARY_PATH = Path(__file__).resolve().parent / "libb200k.so"
 
 B2K_OK, B2K_EINVAL, B2K_EUNSUPPORTED, B2K_ECUDA, B2K_ETIMEOUT, B2K_ESCRATCH = 0, 1, 2, -1, -2, 3
+B2K_ENCCL = -3
 NOALLOC_SCRATCH_BYTES = 32 << 20
+MGPU_ID_BYTES = 128
 STATUS_NAMES = {B2K_EINVAL: "EINVAL", B2K_EUNSUPPORTED: "EUNSUPPORTED", B2K_ECUDA: "ECUDA",
-                B2K_ETIMEOUT: "ETIMEOUT", B2K_ESCRATCH: "ESCRATCH"}
+                B2K_ETIMEOUT: "ETIMEOUT", B2K_ESCRATCH: "ESCRATCH", B2K_ENCCL: "ENCCL"}
 
 PW_MAX_INPUTS, PW_MAX_INSNS = 8, 48
 B_KN, B_NK, A_KM = 0, 1, 2   # A_KM is a flag or-ed into b_layout: A stored [k, m]
@@ -129,6 +131,15 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_kernel_launches": ([C.c_void_p, C.POINTER(_I64)], C.c_int),
     "b2k_selftest_wait_timeout": ([C.c_void_p, _I64, C.c_void_p], C.c_int),
     "b2k_launch": ([C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p), C.c_int32, C.c_void_p], C.c_int),
+    "b2k_mgpu_partition": ([_I64, _I32, _I32, _I64, C.POINTER(_I64), C.POINTER(_I64)], C.c_int),
+    "b2k_mgpu_unique_id": ([_P], C.c_int),
+    "b2k_mgpu_init": ([_P, _I32, _I32, _P, _I64, C.POINTER(_P)], C.c_int),
+    "b2k_mgpu_destroy": ([_P], C.c_int),
+    "b2k_mgpu_sync": ([_P, _P, _I64], C.c_int),
+    "b2k_mgpu_gemm_tf32x3": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P, _I32, _I32, _P], C.c_int),
+    "b2k_mgpu_row_softmax_f32": ([_P, _P, _P, _I64, _I64, _I32, _P], C.c_int),
+    "b2k_mgpu_pointwise_f32": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _I64, _I32, _P], C.c_int),
+    "b2k_mgpu_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I32, _P], C.c_int),
 }
 
 PHASES = {"split": 0, "mma": 1, "pointwise": 2, "softmax": 3, "attention": 4, "rows": 5, "flash": 6}
@@ -418,3 +429,76 @@ class Context:
 
     def memset(self, dst: int, value: int, nbytes: int, stream: int = 0) -> None:
         self.check(self.lib.b2k_memset(self.handle, dst, value, nbytes, stream), "b2k_memset")
+
+
+# --- multi-GPU (b2k_mgpu_*) ---------------------------------------------------
+def mgpu_partition(units: int, world: int, rank: int, align: int = 1) -> tuple[int, int]:
+    """(start, count) of ``rank``'s shard, computed by the library
+    (``b2k_mgpu_partition``; host arithmetic, no device needed)."""
+    start, count = _I64(), _I64()
+    status = library().b2k_mgpu_partition(units, world, rank, align, C.byref(start), C.byref(count))
+    if status != B2K_OK:
+        raise B2KError(status, "bad partition request", "b2k_mgpu_partition")
+    return start.value, count.value
+
+
+def mgpu_unique_id() -> bytes:
+    """The communicator's rendezvous token (made on one rank, given to all)."""
+    buf = C.create_string_buffer(MGPU_ID_BYTES)
+    status = library().b2k_mgpu_unique_id(buf)
+    if status != B2K_OK:
+        raise B2KError(status, "NCCL unavailable or failed to make an id", "b2k_mgpu_unique_id")
+    return buf.raw
+
+
+class MultiGpu:
+    """One rank of a ``b2k_mgpu`` communicator, bound to a :class:`Context`.
+
+    Every method takes this rank's shard of the inputs (device addresses) and
+    leaves the whole output on every rank; see include/b200k.h."""
+
+    def __init__(self, ctx: Context, world: int, rank: int, uid: bytes, timeout_ms: int = 60000):
+        if len(uid) != MGPU_ID_BYTES:
+            raise ValueError("the unique id is 128 bytes")
+        self.ctx, self.world, self.rank = ctx, world, rank
+        self._uid = C.create_string_buffer(uid, MGPU_ID_BYTES)
+        handle = _P()
+        ctx.check(ctx.lib.b2k_mgpu_init(ctx.handle, world, rank, self._uid, timeout_ms, C.byref(handle)),
+                  "b2k_mgpu_init")
+        self.handle = handle
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.ctx.lib.b2k_mgpu_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self) -> "MultiGpu":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def _call(self, name: str, *args) -> None:
+        self.ctx.check(getattr(self.ctx.lib, name)(self.handle, *args), name)
+
+    def sync(self, stream: int = 0, timeout_ms: int = 60000) -> None:
+        self._call("b2k_mgpu_sync", stream, timeout_ms)
+
+    def gemm(self, a_rows: int, b: int, c: int, m: int, n: int, k: int, *, align: int = 1, b_layout: int = B_KN,
+             bias: int = 0, relu: bool = False, panels: int = 1, stream: int = 0) -> None:
+        self._call("b2k_mgpu_gemm_tf32x3", a_rows, b or None, c, m, n, k, align, b_layout, bias or None, int(relu),
+                   panels, stream)
+
+    def row_softmax(self, x_rows: int, y: int, rows: int, cols: int, *, pieces: int = 1, stream: int = 0) -> None:
+        self._call("b2k_mgpu_row_softmax_f32", x_rows or None, y, rows, cols, pieces, stream)
+
+    def pointwise(self, program: PwProgram, inputs: list[int], out: int, n: int, *, align: int = 1,
+                  pieces: int = 1, stream: int = 0) -> None:
+        ptrs = (_P * max(1, len(inputs)))(*inputs)
+        self._call("b2k_mgpu_pointwise_f32", C.byref(program), ptrs, out, n, align, pieces, stream)
+
+    def attention(self, q: int, k: int, v: int, o: int, bh: int, s_q: int, s_kv: int, d: int, dv: int, *,
+                  scale_div: float | None = None, pieces: int = 1, stream: int = 0) -> None:
+        scale = float(d) ** 0.5 if scale_div is None else float(scale_div)
+        self._call("b2k_mgpu_attention_tf32x3", q or None, k or None, v or None, o, bh, s_q, s_kv, d, dv, scale,
+                   pieces, stream)

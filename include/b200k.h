@@ -35,6 +35,7 @@ extern "C" {
 #define B2K_ECUDA (-1)     /* CUDA runtime/driver error */
 #define B2K_ETIMEOUT (-2)  /* a device-side bounded wait expired (kernel error flag) */
 #define B2K_ESCRATCH 3     /* problem needs more than the fixed no-alloc scratch array */
+#define B2K_ENCCL (-3)     /* NCCL error; the multi-GPU handle is aborted and must be destroyed */
 
 typedef struct b2k_ctx b2k_ctx;
 
@@ -363,6 +364,65 @@ int b2k_launch(b2k_ctx *ctx, const b2k_kernel_desc *desc, void *const *args, int
 int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                             int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias,
                             int32_t relu, void *stream);
+
+/* --- multi-GPU: one problem over the GPUs of a node -------------------------
+ * One process per GPU, each with its own b2k_ctx and one NCCL communicator
+ * (NCCL is opened at run time; without it these calls return
+ * B2K_EUNSUPPORTED and everything else works).  The reference is single-GPU
+ * (tools/local_runner.py:246-342 drives one device); each workload of its hot
+ * path splits into independent units, so a call takes this rank's shard of
+ * the inputs and returns the whole output on every rank:
+ *   shard of `units` for rank r = b2k_mgpu_partition(units, world, r, align):
+ *   contiguous, every shard but the last a multiple of `align`, the last
+ *   taking the remainder (4097 rows over 8 ranks: seven of 512, one of 513).
+ * Collectives run on a stream of the handle's own and overlap the compute on
+ * the caller's stream; the caller's stream waits for them at the end of each
+ * call.  Calls on one handle are ordered like any other stream work.  Every
+ * rank must make the same calls in the same order.  Returns B2K_ENCCL after
+ * an NCCL error and B2K_ETIMEOUT when a bounded wait expires; the handle is
+ * then aborted and only b2k_mgpu_destroy remains valid. */
+typedef struct b2k_mgpu b2k_mgpu;
+#define B2K_MGPU_ID_BYTES 128
+int b2k_mgpu_partition(int64_t units, int32_t world, int32_t rank, int64_t align, int64_t *start, int64_t *count);
+/* Rendezvous token: one rank makes it; the caller hands the 128 bytes to
+ * every rank by its own channel (a file, a socket, a process-group broadcast). */
+int b2k_mgpu_unique_id(void *id);
+/* Join the communicator of `world` ranks as `rank` on ctx's device.  Returns
+ * B2K_ETIMEOUT (nothing left behind) if the ranks have not all joined within
+ * timeout_ms. */
+int b2k_mgpu_init(b2k_ctx *ctx, int32_t world, int32_t rank, const void *id, int64_t timeout_ms, b2k_mgpu **out);
+int b2k_mgpu_destroy(b2k_mgpu *mg);
+/* Wait for the work issued on `stream` (the calls' collectives included),
+ * at most timeout_ms: a collective whose peer has gone (a rank that exited
+ * or stopped calling) ends in B2K_ETIMEOUT or B2K_ENCCL, not a hang. */
+int b2k_mgpu_sync(b2k_mgpu *mg, void *stream, int64_t timeout_ms);
+/* C = relu?(A B + bias) for C [m][n] (row-major, complete on every rank).
+ * a_rows: this rank's rows of A, partition(m, world, rank, align), row-major
+ * [rows][k] contiguous.  b: B on rank 0 only (other ranks may pass NULL),
+ * [k][n] (B2K_B_KN) or [n][k] (B2K_B_NK), contiguous.  bias: [n] on every
+ * rank, or NULL.  B is broadcast in `panels` column panels (1..16): panel
+ * p's GEMM waits only for panel p, and panel p's C is gathered while panel
+ * p + 1 computes.  Replaces a launch of the reference's GEMM plan
+ * (tensor_core.py:232-330) by its row-partitioned form. */
+int b2k_mgpu_gemm_tf32x3(b2k_mgpu *mg, const float *a_rows, const float *b, float *c, int64_t m, int64_t n,
+                         int64_t k, int64_t align, int32_t b_layout, const float *bias, int32_t relu, int32_t panels,
+                         void *stream);
+/* Row softmax of a [rows][cols] matrix: x_rows is this rank's rows
+ * (partition(rows, world, rank, 1)), y the whole output.  The gathers run
+ * per piece (1..16; equal shards only, else one piece), piece i while piece
+ * i + 1 computes. */
+int b2k_mgpu_row_softmax_f32(b2k_mgpu *mg, const float *x_rows, float *y, int64_t rows, int64_t cols,
+                             int32_t pieces, void *stream);
+/* A pointwise program over n elements: non-broadcast input r holds this
+ * rank's elements, partition(n, world, rank, align) (plus offset[r] elements
+ * of window), broadcast inputs their one element; out is the whole output. */
+int b2k_mgpu_pointwise_f32(b2k_mgpu *mg, const b2k_pw_program *program, const float *const *inputs, float *out,
+                           int64_t n, int64_t align, int32_t pieces, void *stream);
+/* Attention over bh heads: q, k ([heads][s_kv][d]) and v are this rank's
+ * heads, partition(bh, world, rank, 1); o [bh][s_q][dv] the whole output. */
+int b2k_mgpu_attention_tf32x3(b2k_mgpu *mg, const float *q, const float *k, const float *v, float *o, int64_t bh,
+                              int64_t s_q, int64_t s_kv, int64_t d, int64_t dv, float scale_div, int32_t pieces,
+                              void *stream);
 
 /* Select the GEMM kernel variant for subsequent calls (process-wide; for
  * tuning and benchmarking): 0 = 128x256 tile, 128-byte swizzle, 2 stages;

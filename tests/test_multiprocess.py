@@ -33,6 +33,18 @@ def test_partition_covers_exactly_once(units, world, align):
     assert all(s.count % align == 0 for s in shards[:-1])
 
 
+def test_library_partition_matches_python():
+    """b2k_mgpu_partition (host arithmetic in the C library) gives the shards
+    mgpu.partition gives."""
+    rt, mgpu = pkg("runtime"), pkg("mgpu")
+    for units, world, align in [(4097, 8, 1), (1 << 24, 8, 4), (5, 8, 1), (4096, 3, 128), (64, 2, 1), (0, 4, 1)]:
+        for r in range(world):
+            s = mgpu.partition(units, world, r, align)
+            assert rt.mgpu_partition(units, world, r, align) == (s.start, s.count)
+    with pytest.raises(rt.B2KError):
+        rt.mgpu_partition(10, 2, 2, 1)
+
+
 def _worker(rank, world, port, mode, results):
     sys.path.insert(0, str(ROOT))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
