@@ -107,7 +107,7 @@ int settle(b2k_mgpu *mg, ncclResult_t r, const char *what, int64_t timeout_ms = 
       return fail(mg->ctx, B2K_ETIMEOUT, "%s: no progress within %lld ms (communicator aborted)", what,
                   (long long)timeout_ms);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    std::this_thread::sleep_for(std::chrono::microseconds(5));
     nccl().async_error(mg->comm, &r);
   }
   if (r != ncclSuccess) {
