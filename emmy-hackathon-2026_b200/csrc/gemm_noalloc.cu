@@ -46,7 +46,9 @@ std::mutex g_mutex;
 
 // Host code cannot pass g_scratch itself to a kernel: on the host that name
 // is only a stand-in for the device array.  Look up the device addresses once
-// per device, with that device current.
+// per device, with that device current.  The first call of the entry point on
+// a device does this set-up, so that first call should come before any
+// stream capture begins.
 int device_symbols(int device, DeviceSymbols *out) {
   std::lock_guard<std::mutex> lock(g_mutex);
   DeviceSymbols &entry = g_devices[device];

@@ -353,7 +353,8 @@ int b2k_launch(b2k_ctx *ctx, const b2k_kernel_desc *desc, void *const *args, int
  * nothing; extents beyond the 32-bit limits of b2k_gemm_tf32x3 return
  * B2K_EINVAL; K = 0 returns B2K_EUNSUPPORTED.  Runs on the calling thread's
  * current device and the given stream.  The first call on a device looks up
- * the scratch array's device address (cudaGetSymbolAddress) and keeps it.
+ * the scratch array's device address (cudaGetSymbolAddress) and keeps it;
+ * make that first call on each device before any stream capture begins.
  * Every call on a device shares the one
  * array, so calls that overlap on the GPU (different streams, no ordering)
  * race and corrupt each other's results; calls on one stream are safe.  Each
