@@ -137,9 +137,6 @@ struct SplitOperands {
 // estimated time over `sms` SMs is taken.
 constexpr int kSplitDirect = 1;
 constexpr int kSplitTransposed = 2;
-// kSplitWide = A split into TMEM inside the 128 x 256 tile kernel of
-// gemm_wide.cu (any row stride of A; one accumulator buffer), B pre-split.
-constexpr int kSplitWide = 3;
 int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
                     int layout, int sms);
 // Tile width (columns) of the pre-pass kernel gemm_main picks for n columns.
@@ -155,13 +152,6 @@ int gemm_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const Spli
 int gemm_tmem_b(b2k_ctx *ctx, const float *b, int64_t k, int64_t ldb, bool b_nk, const SplitOperands &ops, float *c,
                 int64_t m, int64_t n, int64_t ldc, const float *bias, int relu, cudaStream_t s, int bn = 0);
 int gemm_transposed_tile_width(int64_t m, int64_t n, int sms);
-// The 128 x 256 tile kernel (gemm_wide.cu): raw A [m][k] (row stride lda, any
-// stride, 16-byte aligned base) split inside the kernel, B pre-split into
-// ops.b_hi / b_lo ([n][kp]).
-int gemm_wide(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const SplitOperands &ops, float *c, int64_t m,
-              int64_t n, int64_t ldc, const float *bias, int relu, cudaStream_t s);
-// Rows grouped per TMA box row of the wide kernel's A map: 1, 2 or 4.
-int wide_row_group(int64_t lda);
 
 // Row-major [batch][rows, k] -> hi/lo [batch][rows][kp].
 int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t ld, int64_t bs, int64_t batch,

@@ -605,7 +605,7 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
   const int mode = divide ? 0 : b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, layout, ctx->sm_count);
   const int64_t kp = b2k::gemm_kpad(k);
   int status;
-  if (mode == b2k::kSplitDirect || mode == b2k::kSplitWide) {
+  if (mode == b2k::kSplitDirect) {
     // A is split inside the kernel (into TMEM); only B is pre-split.
     b2k::SplitOperands ops{nullptr, nullptr, ws, ws + n * kp, kp};
     {
@@ -614,7 +614,6 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
                         : b2k::split_transpose(ctx, b, k, n, ldb, k * ldb, 1, kp, ops.b_hi, ops.b_lo, s);
     }
     if (status != B2K_OK) return status;
-    if (mode == b2k::kSplitWide) return b2k::gemm_wide(ctx, a, k, lda, ops, c, m, n, ldc, bias, relu, s);
     return b2k::gemm_tmem_a(ctx, a, k, lda, ops, c, m, n, ldc, bias, relu, s);
   }
   if (mode == b2k::kSplitTransposed) {

@@ -557,12 +557,11 @@ int launch_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const b2
 
 // b2k_gemm_set_fused_split: 0 = pre-pass split of both operands, 1 = choose
 // by the cost estimate below (default), 2 = the transposed orientation
-// wherever TMA can read B, 3 = the direct orientation wherever TMA can read A,
-// 4 = the wide kernel (gemm_wide.cu) wherever its A map can be built.
+// wherever TMA can read B, 3 = the direct orientation wherever TMA can read A.
 static int g_split_mode = 1;
 
 extern "C" int b2k_gemm_set_fused_split(int mode) {
-  if (mode < 0 || mode > 4) return B2K_EINVAL;
+  if (mode < 0 || mode > 3) return B2K_EINVAL;
   g_split_mode = mode;
   return B2K_OK;
 }
@@ -612,10 +611,6 @@ int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_
   // or [k][n] MN-major (whole 128-column boxes: n >= 128)
   const bool direct_ok = !a_t && tma_readable(a, lda);
   const bool transposed_ok = tma_readable(b, ldb) && (b_nk || n >= BM);
-  // wide: A [m][k] by TMA in groups of wide_row_group(lda) rows (x
-  // coordinates within 32 bits)
-  const bool wide_ok = !a_t && aligned16(a) && m >= BM && wide_row_group(lda) * lda <= INT32_MAX - 1024;
-  if (g_split_mode == 4) return wide_ok ? kSplitWide : 0;
   if (g_split_mode == 3) return direct_ok ? kSplitDirect : 0;
   if (g_split_mode == 2) return transposed_ok ? kSplitTransposed : 0;
   if (sms <= 0) return direct_ok ? kSplitDirect : 0;

@@ -340,7 +340,7 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
   }
   // B is split once into the workspace; each slab then splits its rows of A
   // (pre-pass path) or reads them raw (A split into TMEM inside the kernel).
-  const bool tmem_a = mode == b2k::kSplitDirect || mode == b2k::kSplitWide;
+  const bool tmem_a = mode == b2k::kSplitDirect;
   B2K_TRY(b2k::reserve_workspace(ctx, (size_t)(2 * n * kp + (tmem_a ? 0 : 2 * per * kp)) * 4, s));
   float *ws = static_cast<float *>(ctx->workspace);
   b2k::SplitOperands ops{ws + 2 * n * kp, ws + 2 * n * kp + per * kp, ws, ws + n * kp, kp};
@@ -357,9 +357,7 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
     const int64_t nr = std::min(per, m - r0);
     B2K_TRY(pipe.in(da + r0 * k, (size_t)k * 4, a + r0 * lda, (size_t)lda * 4, (size_t)k * 4, nr));
     B2K_TRY(pipe.landed());
-    if (mode == b2k::kSplitWide) {
-      B2K_TRY(b2k::gemm_wide(ctx, da + r0 * k, k, k, ops, dc + r0 * n, nr, n, n, dbias, relu, s));
-    } else if (tmem_a) {
+    if (tmem_a) {
       B2K_TRY(b2k::gemm_tmem_a(ctx, da + r0 * k, k, k, ops, dc + r0 * n, nr, n, n, dbias, relu, s));
     } else {
       {

@@ -116,7 +116,6 @@ SIGNATURES: dict[str, tuple] = {
                                  _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
     "b2k_gemm_set_fused_split": ([C.c_int], C.c_int),
-    "b2k_gemm_set_wide_chunk": ([C.c_int], C.c_int),
     "b2k_attention_set_fused": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
@@ -394,14 +393,9 @@ class Context:
 
     def set_gemm_fused_split(self, mode: int) -> None:
         """0 = pre-pass split of A and B; 3 = A split in-kernel into TMEM (direct);
-        2 = B split in-kernel into TMEM, C^T = B^T A^T (transposed); 4 = A split
-        in-kernel on 128 x 256 tiles with one accumulator, any row stride of A
-        (wide); 1 (default) = whichever of them the estimate says is fastest."""
+        2 = B split in-kernel into TMEM, C^T = B^T A^T (transposed); 1 (default)
+        = whichever of the three the estimate says is fastest."""
         self.check(self.lib.b2k_gemm_set_fused_split(int(mode)), "b2k_gemm_set_fused_split")
-
-    def set_gemm_wide_chunk(self, k: int) -> None:
-        """K elements per accumulation chunk of the wide kernel (16..384, multiple of 16; default 256)."""
-        self.check(self.lib.b2k_gemm_set_wide_chunk(int(k)), "b2k_gemm_set_wide_chunk")
 
     def set_pdl(self, on: bool) -> None:
         """Programmatic dependent launch between a call's kernels (process-wide, default on)."""

@@ -436,13 +436,6 @@ int b2k_mgpu_attention_tf32x3(b2k_mgpu *mg, const float *q, const float *k, cons
 int b2k_gemm_set_variant(int variant);
 /* Process-wide choice of where b2k_gemm_tf32x3 (and the no-alloc variant)
  * split operands into TF32 hi/lo halves:
- *   4            wide: A is staged raw by TMA and split inside a tensor-core
- *                kernel with 128 x 256 tiles and one accumulator buffer (the
- *                tensor core waits while each 256-wide K chunk is folded);
- *                any row stride of A: a stride that is not a multiple of 4
- *                elements is read as groups of 2 or 4 rows whose stride is.
- *                B is split once by a pre-pass.  Needs A 16-byte aligned,
- *                not stored transposed, and M >= 128.
  *   3            direct: A is staged raw by TMA and split inside the
  *                tensor-core kernel into tensor memory, which the MMAs read A
  *                from (128 x 192 tiles, 128 x 128 for n <= 128); B is split
@@ -458,7 +451,7 @@ int b2k_gemm_set_variant(int variant);
  *                128 columns by 128 or 192 rows.  Needs B 16-byte aligned with
  *                a row stride that is a multiple of 4 elements, K >= 16 and,
  *                for a [K, N] B, N >= 128.
- *   1 (default)  whichever of 0, 2, 3 and 4 the operands allow and an estimate
+ *   1 (default)  whichever of 0, 2 and 3 the operands allow and an estimate
  *                of (waves of tiles over the SMs) x (tile time) + (pre-pass
  *                bytes) says is fastest.
  *   0            both operands split by the pre-pass (128 x 256 tiles).
@@ -467,12 +460,6 @@ int b2k_gemm_set_variant(int variant);
  * the same 256-wide chunked FP32 accumulation.  Returns B2K_EINVAL for other
  * values.  No counterpart in the reference. */
 int b2k_gemm_set_fused_split(int mode);
-/* K elements per accumulation chunk of the wide kernel (mode 4): a multiple
- * of 16 from 16 to 384, default 256 (the chunk of the other kernels).  Longer
- * chunks mean fewer folds the tensor core waits for and a larger rounding
- * error per chunk.  Process-wide; returns B2K_EINVAL for other values.  No
- * counterpart in the reference. */
-int b2k_gemm_set_wide_chunk(int k);
 
 /* --- pipelined host-array calls ----------------------------------------------
  * The runner's per-request host flow -- copy every input in, launch, copy

@@ -156,81 +156,6 @@ def test_gemm_split_modes_match_float64_and_each_other(ctx, torch_cuda, m, n, k,
             assert tf32.normwise_error(got[mode], model) <= 2e-6, mode
 
 
-WIDE_CASES = [
-    # (m, n, k, b_layout, lda): lda % 4 selects the row grouping of A's map
-    (4097, 1000, 777, 1, 777),  # the ragged configuration, groups of 4 rows
-    (300, 520, 200, 0, 200),    # lda % 4 == 0: one row per box row (swizzled tile)
-    (257, 300, 77, 0, 77),      # groups of 4, a tail row outside the map
-    (130, 256, 50, 1, 50),      # lda = 2 mod 4: groups of 2
-    (129, 64, 33, 0, 35),       # lda > k: the last group's rows read directly
-    (512, 700, 1000, 1, 1003),  # four chunks of 256 K, padded rows
-    (128, 8, 16, 0, 17),        # one K block, a narrow output
-]
-
-
-@pytest.mark.parametrize("m,n,k,b_layout,lda", WIDE_CASES)
-def test_gemm_wide_kernel_matches_prepass_and_float64(ctx, torch_cuda, m, n, k, b_layout, lda):
-    """Split mode 4 (A split into TMEM on 128 x 256 tiles, one accumulator
-    buffer, A read through a grouped-row map when its row stride is not a
-    multiple of 16 bytes) against float64, the 3xTF32 model and the pre-pass
-    kernel on the same inputs, with bias and ReLU; C written both by TMA
-    stores (aligned) and by row stores (C at an odd offset)."""
-    torch = torch_cuda
-    rng = np.random.default_rng(m * 13 + n * 5 + k + lda)
-    a_full = rng.standard_normal((m, lda)).astype(np.float32)
-    a = np.ascontiguousarray(a_full[:, :k])
-    b = rng.standard_normal((k, n) if b_layout == 0 else (n, k)).astype(np.float32)
-    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
-    da, db, dbias = dev(torch, a_full), dev(torch, b), dev(torch, bias)
-    outs = {}
-    try:
-        for mode in (0, 4):
-            ctx.set_gemm_fused_split(mode)
-            for shift in (0, 1):
-                buf = torch.full((m * n + 4,), float("nan"), dtype=torch.float32, device="cuda")
-                c = buf[shift:shift + m * n]
-                ctx.gemm(da.data_ptr(), db.data_ptr(), c.data_ptr(), m, n, k, b_layout=b_layout, lda=lda,
-                         bias=dbias.data_ptr(), relu=True)
-                ctx.sync()
-                outs[(mode, shift)] = c.cpu().numpy().reshape(m, n)
-    finally:
-        ctx.set_gemm_fused_split(1)
-    bm = (b if b_layout == 0 else b.T).astype(np.float64)
-    exact = np.maximum(a.astype(np.float64) @ bm + bias, 0.0)
-    wide = outs[(4, 0)]
-    assert np.array_equal(wide, outs[(4, 1)])  # both C write paths, same bits
-    assert tf32.normwise_error(wide, exact) <= NORMWISE
-    ok, bad, err = refs.allclose_report(wide, exact.astype(np.float32), 1e-3, 1e-3)
-    assert ok, (bad, err)
-    # same products and chunk folds as the pre-pass kernel; the MMA reads A
-    # from TMEM instead of shared memory
-    assert tf32.normwise_error(wide, outs[(0, 0)]) <= 5e-7
-    if m * n * k <= 1 << 24:
-        assert tf32.normwise_error(wide, np.maximum(tf32.gemm_3xtf32(a, bm.astype(np.float32)) + bias, 0.0)) <= 2e-6
-
-
-@pytest.mark.parametrize("chunk", [16, 128, 384])
-def test_gemm_wide_kernel_chunk_lengths(ctx, torch_cuda, chunk):
-    """Every accumulation chunk length of the wide kernel stays within the
-    3xTF32 error bound on the ragged shape; outside 16..384 (or off a
-    multiple of 16) the setter refuses."""
-    runtime = pkg("runtime")
-    workloads = pkg("workloads")
-    a, bt, bias = workloads.ragged_inputs()
-    try:
-        ctx.set_gemm_fused_split(4)
-        ctx.set_gemm_wide_chunk(chunk)
-        got = run_gemm(ctx, torch_cuda, a, bt, b_layout=1, bias=bias, relu=True)
-    finally:
-        ctx.set_gemm_wide_chunk(256)
-        ctx.set_gemm_fused_split(1)
-    exact = np.maximum(a.astype(np.float64) @ bt.astype(np.float64).T + bias, 0.0)
-    assert tf32.normwise_error(got, exact) <= NORMWISE
-    for bad in (0, 8, 400, 24):
-        with pytest.raises(runtime.B2KError):
-            ctx.set_gemm_wide_chunk(bad)
-
-
 def test_gemm_fused_split_special_values(ctx, torch_cuda):
     """Max-finite times zero stays 0 and infinities propagate through the
     in-kernel split as through the pre-pass split."""
