@@ -196,7 +196,7 @@ def test_gemm_inline_split_same_bits(ctx, torch_cuda, m, n, k, lda, ldb, c_shift
     finally:
         ctx.set_gemm_inline_split(INLINE_DEFAULT)
         ctx.set_gemm_fused_split(1)
-    fits = ((m + 127) // 128) * ((n + 255) // 256) <= ctx.sm_count()
+    fits = ((m + 127) // 128) * ((n + 255) // 256) <= ctx.sm_count
     assert launches[True] == (1 if fits else 2) and launches[False] == 2
     for got in outs[True]:
         assert np.array_equal(got, outs[False][0])
