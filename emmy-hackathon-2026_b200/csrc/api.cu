@@ -165,7 +165,6 @@ int b2k_destroy(b2k_ctx *ctx) {
   if (ctx->staging) cudaFree(ctx->staging);
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->error_flag) cudaFree(ctx->error_flag);
-  if (ctx->split_flags) cudaFree(ctx->split_flags);
   delete ctx;
   return B2K_OK;
 }

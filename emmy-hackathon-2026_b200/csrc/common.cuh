@@ -24,13 +24,6 @@ struct b2k_ctx {
   size_t workspace_bytes = 0;
   // Device-side error word written by kernels whose bounded waits expire.
   unsigned int *error_flag = nullptr;
-  // Ready flags of the GEMM's in-kernel operand split (gemm.cu): one word per
-  // split K block, holding the epoch of the call that last wrote the block.
-  unsigned int *split_flags = nullptr;
-  unsigned int split_epoch = 0;
-  // Scratch is a fixed array that must not grow (the allocation-free entry
-  // point): paths that would allocate are not taken.
-  bool fixed_scratch = false;
   // Kernels enqueued through this context (b2k_kernel_launches).
   int64_t kernel_launches = 0;
   // Pipelined host-array calls (host.cu): copy streams, dependency events

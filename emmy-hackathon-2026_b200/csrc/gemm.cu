@@ -26,7 +26,6 @@
 
 #include <algorithm>
 #include <mutex>
-#include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -186,21 +185,6 @@ constexpr int kChunkK = 256;
 constexpr int kEpilogueWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpilogueWarps;  // producer, MMA, epilogue
 
-// The operand split done inside the tensor-core kernel (FUSE, see
-// gemm_tf32x3_kernel): raw A [m][k] and B [n][k] (row strides lda, ldb) are
-// written K-major as hi/lo [rows][kp] by the CTAs' epilogue warps, K block by
-// K block; `flags` holds one word per (operand tile, K block) -- [m tiles]
-// [num_kb] for A, then [n tiles][num_kb] for B -- set to `epoch` once the
-// block is written.
-struct InlineSplit {
-  const float *a, *b;
-  float *a_hi, *a_lo, *b_hi, *b_lo;
-  int64_t lda, ldb, k, kp;
-  unsigned *flags;
-  unsigned epoch;
-  int a_vec, b_vec;  // rows 16-byte aligned: float4 loads
-};
-
 struct GemmArgs {
   float *c;
   const float *bias;
@@ -211,55 +195,7 @@ struct GemmArgs {
   int relu;
   unsigned *err;
   int tma_c;  // C written by TMA stores from shared memory (main kernel only)
-  InlineSplit split;  // FUSE kernels only
 };
-
-// COUNT consecutive values of row `row` from column k0 (zeros at k0 + e >= k).
-template <int COUNT>
-__device__ __forceinline__ void load_row_chunk(const float *src, int64_t ld, int64_t row, int64_t k0, int64_t k,
-                                               bool vec, float (&v)[COUNT]) {
-  const float *p = src + row * ld + k0;
-  if (vec && k0 + COUNT <= k) {
-#pragma unroll
-    for (int q = 0; q < COUNT / 4; ++q) {
-      const float4 t = __ldg(reinterpret_cast<const float4 *>(p) + q);
-      v[4 * q] = t.x, v[4 * q + 1] = t.y, v[4 * q + 2] = t.z, v[4 * q + 3] = t.w;
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < COUNT; ++e) v[e] = k0 + e < k ? __ldg(p + e) : 0.0f;
-  }
-}
-
-// Split them into the hi/lo copies [row][kp] at column k0 (16-byte aligned).
-template <int COUNT>
-__device__ __forceinline__ void store_row_chunk(float *hi, float *lo, int64_t kp, int64_t row, int64_t k0,
-                                                const float (&v)[COUNT]) {
-#pragma unroll
-  for (int q = 0; q < COUNT / 4; ++q) {
-    float4 h, l;
-    split_tf32x4(make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]), h, l);
-    *reinterpret_cast<float4 *>(hi + row * kp + k0 + 4 * q) = h;
-    *reinterpret_cast<float4 *>(lo + row * kp + k0 + 4 * q) = l;
-  }
-}
-
-// Bounded wait until another CTA has published a split block of this call.
-__device__ __forceinline__ bool wait_split_flag(const unsigned *flag, unsigned epoch, unsigned *err,
-                                                volatile int *abort) {
-  if (sm100::ld_acquire_gpu(flag) == epoch) return true;
-  const long long start = clock64();
-  while (sm100::ld_acquire_gpu(flag) != epoch) {
-    if (*abort) return false;
-    if (clock64() - start > sm100::kWaitCycles) {
-      atomicOr(err, sm100::kSiteSplitFlag);
-      *abort = 1;
-      return false;
-    }
-    __nanosleep(32);
-  }
-  return true;
-}
 
 // C staging for the TMA store: BN / 32 boxes of 128 rows x 32 FP32 (16 KB)
 // with the 128-byte swizzle; a warp's row-per-thread 16-byte writes then hit
@@ -284,19 +220,7 @@ struct GemmShape {
 // TMA_C selects the C write path at compile time: one kernel holding both
 // paths needs more registers than the 168 a 320-thread CTA may use, and its
 // spills cost more than the whole epilogue.
-//
-// FUSE: the operand split runs inside this kernel instead of a pre-pass
-// launch.  The grid is launched cooperatively (every CTA resident at once;
-// at most one CTA per SM).  Before their first fold the epilogue warps of
-// CTA (n tile nt, m tile mt) split the A K blocks nt, nt + n_tiles, ... of
-// their M tile and the B K blocks mt, mt + m_tiles, ... of their N tile --
-// every block has exactly one writer -- two A blocks and one B block per
-// round with all loads issued before any store, and publish each finished
-// block by a release store of the call's epoch into its flag.  The TMA
-// producer acquires the flags of the A and B blocks of K block kb before
-// loading them.  Nothing in the split phase waits, so every flag is set
-// whatever the producers do; their waits are bounded all the same.
-template <int BN, int SW, int STAGES, bool TMA_C, bool FUSE = false>
+template <int BN, int SW, int STAGES, bool TMA_C>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                        const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
@@ -363,16 +287,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kb >= STAGES &&
             !sm100::mbar_wait(&empty_bar[s], (round & 1) ^ 1, args.err, sm100::kSiteProducerEmpty, abort))
           break;
-        if constexpr (FUSE) {
-          const unsigned *flags = args.split.flags;
-          if (!wait_split_flag(flags + (int64_t)blockIdx.y * num_kb + kb, args.split.epoch, args.err, abort) ||
-              !wait_split_flag(flags + ((int64_t)gridDim.y + blockIdx.x) * num_kb + kb, args.split.epoch, args.err,
-                               abort))
-            break;
-          // the blocks were written by other CTAs' ordinary stores: order
-          // them before this thread's TMA (async-proxy) reads
-          sm100::fence_proxy_async_global();
-        }
         sm100::mbar_arrive_expect_tx(&full_bar[s], Shape::kStage);
         const int kx = kb * Shape::BK;
         const int z = (int)blockIdx.z;
@@ -429,35 +343,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     constexpr int CPT = Shape::kColsPerThread;
-    if constexpr (FUSE) {
-      static_assert(BN == 32 * kEpilogueWarps && Shape::BK == 16, "one B row and half an A row per thread");
-      const InlineSplit &sp = args.split;
-      const int tid = threadIdx.x - 64;
-      const int nt = blockIdx.x, mt = blockIdx.y, n_tiles = gridDim.x, m_tiles = gridDim.y;
-      // A: row tid / 2 of the tile, 8 columns of the block; B: row tid, all 16
-      const int64_t a_row = m0 + (tid >> 1), b_row = n0 + tid;
-      const int a_col = (tid & 1) * 8;
-      const bool a_in = a_row < args.m, b_in = b_row < args.n;
-      for (int r = 0;; ++r) {
-        const int ka0 = nt + 2 * r * n_tiles, ka1 = ka0 + n_tiles, kbb = mt + r * m_tiles;
-        if (ka0 >= num_kb && kbb >= num_kb) break;
-        float va0[8], va1[8], vb[16];
-        if (a_in && ka0 < num_kb) load_row_chunk<8>(sp.a, sp.lda, a_row, ka0 * 16 + a_col, sp.k, sp.a_vec, va0);
-        if (a_in && ka1 < num_kb) load_row_chunk<8>(sp.a, sp.lda, a_row, ka1 * 16 + a_col, sp.k, sp.a_vec, va1);
-        if (b_in && kbb < num_kb) load_row_chunk<16>(sp.b, sp.ldb, b_row, kbb * 16, sp.k, sp.b_vec, vb);
-        if (a_in && ka0 < num_kb) store_row_chunk<8>(sp.a_hi, sp.a_lo, sp.kp, a_row, ka0 * 16 + a_col, va0);
-        if (a_in && ka1 < num_kb) store_row_chunk<8>(sp.a_hi, sp.a_lo, sp.kp, a_row, ka1 * 16 + a_col, va1);
-        if (b_in && kbb < num_kb) store_row_chunk<16>(sp.b_hi, sp.b_lo, sp.kp, b_row, kbb * 16, vb);
-        // every thread's stores of this round, then one release per block
-        sm100::named_barrier(11, 32 * kEpilogueWarps);
-        if (tid == 0) {
-          __threadfence();
-          if (ka0 < num_kb) sm100::st_release_gpu(sp.flags + (int64_t)mt * num_kb + ka0, sp.epoch);
-          if (ka1 < num_kb) sm100::st_release_gpu(sp.flags + (int64_t)mt * num_kb + ka1, sp.epoch);
-          if (kbb < num_kb) sm100::st_release_gpu(sp.flags + ((int64_t)m_tiles + nt) * num_kb + kbb, sp.epoch);
-        }
-      }
-    }
     float acc[CPT];
 #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0.0f;
@@ -586,30 +471,8 @@ int make_operand_map(b2k_ctx *ctx, CUtensorMap *map, const float *base, int64_t 
   return B2K_OK;
 }
 
-// The in-kernel split variant exists for the default 128 x 256 tile only.
-using FusedShape = GemmShape<256, 64, 4>;
-
-// Cooperative launch: the hardware starts every CTA of the grid at once or
-// refuses the launch, so CTAs may wait on one another's flags.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_cooperative(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                               Args &&...args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
 template <int BN, int SW, int STAGES>
-int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, GemmArgs args, cudaStream_t s,
-                bool fuse = false) {
+int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, GemmArgs args, cudaStream_t s) {
   using Shape = GemmShape<BN, SW, STAGES>;
   CUtensorMap maps[4];
   int status;
@@ -635,23 +498,10 @@ int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, Gemm
     if (res != CUDA_SUCCESS) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled (C) failed (%d)", (int)res);
   }
   static_assert((BN / 32) * kCBox <= STAGES * Shape::kStage, "C staging exceeds the ring");
-  dim3 grid((unsigned)((args.n + BN - 1) / BN), (unsigned)((args.m + BM - 1) / BM), (unsigned)batch);
-  if constexpr (std::is_same_v<Shape, FusedShape>) {
-    if (fuse) {
-      auto kernel = args.tma_c ? gemm_tf32x3_kernel<BN, SW, STAGES, true, true>
-                               : gemm_tf32x3_kernel<BN, SW, STAGES, false, true>;
-      cudaError_t err = b2k::set_max_smem(ctx, (const void *)kernel, Shape::kSmem);
-      if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (in-kernel split): set smem");
-      err = launch_cooperative(kernel, grid, dim3(kThreads), Shape::kSmem, s, maps[0], maps[1], maps[2], maps[3],
-                               map_c, args);
-      if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (in-kernel split) launch");
-      return b2k::check_launch(ctx, "gemm (in-kernel split) launch");
-    }
-  }
-  if (fuse) return b2k::fail(ctx, B2K_EINVAL, "gemm: in-kernel split needs the 128 x 256 tile");
   auto kernel = args.tma_c ? gemm_tf32x3_kernel<BN, SW, STAGES, true> : gemm_tf32x3_kernel<BN, SW, STAGES, false>;
   cudaError_t err = b2k::set_max_smem(ctx, (const void *)kernel, Shape::kSmem);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm: set smem");
+  dim3 grid((unsigned)((args.n + BN - 1) / BN), (unsigned)((args.m + BM - 1) / BM), (unsigned)batch);
   err = b2k::launch_kernel(b2k::pdl_enabled(), kernel, grid, dim3(kThreads), Shape::kSmem, s, maps[0], maps[1],
                            maps[2], maps[3], map_c, args);
   if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm launch");
@@ -664,63 +514,7 @@ int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, Gemm
 // tuning through b2k_gemm_set_variant.  Outputs at most 128 wide always use
 // the 128-wide tile.
 static int g_gemm_variant = 1;
-// b2k_gemm_set_inline_split: the pre-pass path splits inside the tensor-core
-// kernel where the whole grid fits on the GPU at once (default off).
-static bool g_inline_split = false;
-constexpr int64_t kSplitFlagWords = 1 << 16;
-
-extern "C" int b2k_gemm_set_inline_split(int on) {
-  g_inline_split = on != 0;
-  return B2K_OK;
-}
-
 namespace b2k {
-
-// Whether the pre-pass path may split inside the tensor-core kernel: the
-// default 128 x 256 tile, a context that may allocate its flag words, and a
-// grid every CTA of which is resident at once (one per SM).
-static bool inline_split_fits(b2k_ctx *ctx, int64_t m, int64_t n, int64_t kp) {
-  if (!g_inline_split || ctx->fixed_scratch || main_tile_width(n) != 256 || g_gemm_variant != 1) return false;
-  const int64_t m_tiles = (m + BM - 1) / BM, n_tiles = (n + 255) / 256, num_kb = kp / FusedShape::BK;
-  if ((m_tiles + n_tiles) * num_kb > kSplitFlagWords) return false;
-  static int per_sm = -1;  // resident CTAs per SM (both C paths have the same footprint)
-  if (per_sm < 0) {
-    auto kernel = gemm_tf32x3_kernel<256, 64, 4, true, true>;
-    int blocks = 0;
-    if (set_max_smem(ctx, (const void *)kernel, FusedShape::kSmem) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, FusedShape::kSmem) != cudaSuccess)
-      blocks = 0;
-    per_sm = blocks;
-  }
-  return m_tiles * n_tiles <= (int64_t)per_sm * ctx->sm_count;
-}
-
-// C = epilogue(A B^T) for row-major A [m][k] and B [n][k], the split done
-// inside the tensor-core kernel into the hi/lo copies of `ops`.
-static int gemm_inline_split(b2k_ctx *ctx, const float *a, int64_t lda, const float *b, int64_t ldb, int64_t k,
-                             const SplitOperands &ops, int64_t m, int64_t n, float *c, int64_t ldc, const float *bias,
-                             int relu, cudaStream_t s) {
-  if (!ctx->split_flags) {
-    cudaError_t err = cudaMalloc(&ctx->split_flags, kSplitFlagWords * sizeof(unsigned));
-    if (err != cudaSuccess) {
-      ctx->split_flags = nullptr;
-      return cuda_fail(ctx, err, "gemm: split flags");
-    }
-    ctx->split_epoch = 0;
-  }
-  // A flag is ready when it holds this call's epoch; when the counter wraps,
-  // clear the words so no old epoch can match.
-  if (ctx->split_epoch == 0 || ++ctx->split_epoch == 0) {
-    cudaError_t err = cudaMemsetAsync(ctx->split_flags, 0, kSplitFlagWords * sizeof(unsigned), s);
-    if (err != cudaSuccess) return cuda_fail(ctx, err, "gemm: clear split flags");
-    ctx->split_epoch = 1;
-  }
-  GemmArgs args{c, bias, nullptr, 1.0f, m, n, ldc, m * ldc, 0, relu, ctx->error_flag, 0};
-  args.split = InlineSplit{a, b, ops.a_hi, ops.a_lo, ops.b_hi, ops.b_lo, lda, ldb, k, ops.kp,
-                           ctx->split_flags, ctx->split_epoch, lda % 4 == 0 && aligned16(a), ldb % 4 == 0 && aligned16(b)};
-  PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
-  return launch_main<256, 64, 4>(ctx, ops, 1, args, s, true);
-}
 
 static void fill_job(RowSplitJob &o, const RowSplit &r) {
   // A batch stored back to back is one tall matrix: no per-row division.
@@ -834,10 +628,6 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
     return b2k::gemm_tmem_b(ctx, b, k, ldb, b_kmajor != 0, ops, c, m, n, ldc, bias, relu, s);
   }
   b2k::SplitOperands ops{ws, ws + m * kp, ws + 2 * m * kp, ws + 2 * m * kp + n * kp, kp};
-  // A row-major and B [n, K]: the split can run inside the kernel when the
-  // whole grid is resident at once (no pre-pass launch, no wait for it).
-  if (!divide && !a_t && b_kmajor && b2k::inline_split_fits(ctx, m, n, kp))
-    return b2k::gemm_inline_split(ctx, a, lda, b, ldb, k, ops, m, n, c, ldc, bias, relu, s);
   {
     b2k::PhaseTimer timer(ctx, B2K_PHASE_SPLIT, s);
     const b2k::RowSplit sa{a, m, k, lda, m * lda, 1, ops.a_hi, ops.a_lo};

@@ -96,7 +96,6 @@ extern "C" int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c,
   local.device = device;
   local.sm_count = symbols.sm_count;
   local.error_flag = symbols.status;
-  local.fixed_scratch = true;
   return b2k_gemm_tf32x3_impl(&local, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu,
                               symbols.scratch, (cudaStream_t)stream, nullptr, 1.0f);
 }

@@ -22,7 +22,6 @@ enum WaitSite : unsigned {
   kSiteDrain = 0x8,
   kSiteAttention = 0x10,
   kSiteConvert = 0x20,
-  kSiteSplitFlag = 0x40,  // a CTA's operand split block never became ready
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -206,23 +205,6 @@ __device__ __forceinline__ uint64_t desc_mn_sw128_32b(uint32_t saddr, uint32_t m
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool b_mn_major = false) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (b_mn_major ? (1u << 16) : 0u) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-// --- flags between CTAs of one (cooperative) launch ------------------------
-// GPU-scope release store / acquire load of a 32-bit flag in global memory.
-__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-// Order this thread's earlier (generic-proxy) global accesses -- including
-// what an acquire made visible -- before its later async-proxy accesses
-// (TMA loads of data another CTA wrote with ordinary stores).
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // 16-byte shared-memory load / store by 32-bit shared address.

@@ -116,7 +116,6 @@ SIGNATURES: dict[str, tuple] = {
                                  _P, _I32, _P], C.c_int),
     "b2k_gemm_set_variant": ([C.c_int], C.c_int),
     "b2k_gemm_set_fused_split": ([C.c_int], C.c_int),
-    "b2k_gemm_set_inline_split": ([C.c_int], C.c_int),
     "b2k_attention_set_fused": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
@@ -397,10 +396,6 @@ class Context:
         2 = B split in-kernel into TMEM, C^T = B^T A^T (transposed); 1 (default)
         = whichever of the three the estimate says is fastest."""
         self.check(self.lib.b2k_gemm_set_fused_split(int(mode)), "b2k_gemm_set_fused_split")
-
-    def set_gemm_inline_split(self, on: bool) -> None:
-        """Split inside the 128 x 256 pre-pass kernel when its grid fits on the GPU at once (process-wide, default off)."""
-        self.check(self.lib.b2k_gemm_set_inline_split(int(bool(on))), "b2k_gemm_set_inline_split")
 
     def set_pdl(self, on: bool) -> None:
         """Programmatic dependent launch between a call's kernels (process-wide, default on)."""

@@ -460,17 +460,6 @@ int b2k_gemm_set_variant(int variant);
  * the same 256-wide chunked FP32 accumulation.  Returns B2K_EINVAL for other
  * values.  No counterpart in the reference. */
 int b2k_gemm_set_fused_split(int mode);
-/* Process-wide switch (default off) for the pre-pass path (mode 0) with a
- * row-major A and an [N, K] B: when every CTA of the 128 x 256-tile kernel
- * fits on the GPU at once (at most one wave), the operand split runs inside
- * that kernel instead of a separate launch.  The grid is launched
- * cooperatively; each CTA's epilogue warps split their share of A and B K
- * block by K block before their first fold and publish each block with a
- * ready flag, which the TMA producers wait for (bounded).  Same bits as the
- * separate split.  Uses a context-owned array of 65536 flag words, allocated
- * on first use (never on the allocation-free entry point).  No counterpart in
- * the reference. */
-int b2k_gemm_set_inline_split(int on);
 
 /* --- pipelined host-array calls ----------------------------------------------
  * The runner's per-request host flow -- copy every input in, launch, copy

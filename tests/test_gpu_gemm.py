@@ -156,54 +156,6 @@ def test_gemm_split_modes_match_float64_and_each_other(ctx, torch_cuda, m, n, k,
             assert tf32.normwise_error(got[mode], model) <= 2e-6, mode
 
 
-INLINE_DEFAULT = False  # the library's default for b2k_gemm_set_inline_split
-INLINE_CASES = [
-    # (m, n, k, lda, ldb, c_shift)
-    (4097, 1000, 777, 777, 777, 0),  # the ragged configuration: 132 tiles, rows off 16-byte boundaries
-    (300, 520, 200, 200, 200, 0),    # aligned rows: float4 split loads
-    (1000, 257, 96, 99, 96, 1),      # padded A rows, C off 16 bytes (row stores)
-    (129, 300, 31, 31, 33, 0),       # one row past a tile, K under one 32-wide pad
-    (5000, 2000, 64, 64, 64, 0),     # 40 x 8 tiles, more than fit at once: the separate split
-]
-
-
-@pytest.mark.parametrize("m,n,k,lda,ldb,c_shift", INLINE_CASES)
-def test_gemm_inline_split_same_bits(ctx, torch_cuda, m, n, k, lda, ldb, c_shift):
-    """Row-major A and an [N, K] B on the pre-pass path: the operand split done
-    inside the cooperative tensor-core kernel (one launch, per-block ready
-    flags) gives exactly the bits of the separate split launch, and matches
-    float64.  Two calls in a row exercise the flag epochs."""
-    torch = torch_cuda
-    rng = np.random.default_rng(m + 3 * n + 7 * k + lda + ldb)
-    a = rng.standard_normal((m, lda)).astype(np.float32)
-    b = rng.standard_normal((n, ldb)).astype(np.float32)
-    bias = rng.uniform(-0.5, 0.5, n).astype(np.float32)
-    da, db, dbias = dev(torch, a), dev(torch, b), dev(torch, bias)
-    outs = {}
-    launches = {}
-    try:
-        ctx.set_gemm_fused_split(0)
-        for inline in (True, False, True):
-            ctx.set_gemm_inline_split(inline)
-            buf = torch.full((m * n + 4,), float("nan"), dtype=torch.float32, device="cuda")
-            c = buf[c_shift:c_shift + m * n]
-            before = ctx.kernel_launches()
-            ctx.gemm(da.data_ptr(), db.data_ptr(), c.data_ptr(), m, n, k, b_layout=1, lda=lda, ldb=ldb,
-                     bias=dbias.data_ptr(), relu=True)
-            ctx.sync()
-            launches[inline] = ctx.kernel_launches() - before
-            outs.setdefault(inline, []).append(c.cpu().numpy().reshape(m, n))
-    finally:
-        ctx.set_gemm_inline_split(INLINE_DEFAULT)
-        ctx.set_gemm_fused_split(1)
-    fits = ((m + 127) // 128) * ((n + 255) // 256) <= ctx.sm_count
-    assert launches[True] == (1 if fits else 2) and launches[False] == 2
-    for got in outs[True]:
-        assert np.array_equal(got, outs[False][0])
-    exact = np.maximum(a[:, :k].astype(np.float64) @ b[:, :k].astype(np.float64).T + bias, 0.0)
-    assert tf32.normwise_error(outs[True][1], exact) <= NORMWISE
-
-
 def test_gemm_fused_split_special_values(ctx, torch_cuda):
     """Max-finite times zero stays 0 and infinities propagate through the
     in-kernel split as through the pre-pass split."""
