@@ -160,6 +160,10 @@ int b2k_destroy(b2k_ctx *ctx) {
   if (ctx->copy_in) cudaStreamSynchronize(ctx->copy_in);
   if (ctx->copy_out) cudaStreamSynchronize(ctx->copy_out);
   for (cudaEvent_t e : ctx->sync_events) cudaEventDestroy(e);
+  for (cudaStream_t st : ctx->compute)
+    if (st) cudaStreamSynchronize(st);
+  for (cudaStream_t st : ctx->compute)
+    if (st) cudaStreamDestroy(st);
   if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
   if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
   if (ctx->staging) cudaFree(ctx->staging);

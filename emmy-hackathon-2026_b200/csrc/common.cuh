@@ -29,6 +29,10 @@ struct b2k_ctx {
   // Pipelined host-array calls (host.cu): copy streams, dependency events
   // (reused across calls) and the device staging arena.
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  // Compute streams of the pipelined GEMM: slab GEMMs run round-robin on
+  // these so that short slabs (a few tiles each) fill the GPU together.
+  static constexpr int kComputeStreams = 3;
+  cudaStream_t compute[kComputeStreams] = {};
   std::vector<cudaEvent_t> sync_events;
   void *staging = nullptr;
   size_t staging_bytes = 0;
