@@ -143,8 +143,10 @@ constexpr int kSplitDirect = 1;
 constexpr int kSplitTransposed = 2;
 int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
                     int layout, int sms);
-// Tile width (columns) of the pre-pass kernel gemm_main picks for n columns.
-int main_tile_width(int64_t n);
+// Tile width (columns) of the pre-pass kernel gemm_main picks for a [batch]
+// m x n output with kp K elements on `sms` SMs, and that kernel's estimated time.
+int main_tile_width(int64_t m, int64_t n, int64_t batch, int64_t kp, int sms);
+double prepass_cost_us(int64_t tiles, int bn, int64_t kp, int sms);
 // The tile variant selected with b2k_gemm_set_variant (2 = 128-wide tiles).
 int gemm_variant();
 int gemm_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const SplitOperands &ops, float *c, int64_t m,

@@ -561,12 +561,37 @@ int split_transpose(b2k_ctx *ctx, const float *src, int64_t k, int64_t n, int64_
   return check_launch(ctx, "split_transpose launch");
 }
 
-int main_tile_width(int64_t n) {
+// Estimated microseconds of one pre-pass kernel launch with 128 x bn tiles:
+// (waves of tiles over the SMs) x (one tile's time).  A tile is bound by the
+// tensor core's operand reads from shared memory, (128 + bn) words per K
+// element (A's 128 rows and B's bn), plus a fixed set-up and epilogue.
+// Calibrated on B200 on the 4097 x 1000 x 777 GEMM and its row shards (2049,
+// 1025 and 513 rows; one wave each, burst clock): 128 x 256 tiles
+// 30.8-32.9 us, 128 x 192 26.7-28.6 us, 128 x 128 22.6-22.8 us.  The
+// widths give identical bits (same products and chunk folds per element).
+double prepass_cost_us(int64_t tiles, int bn, int64_t kp, int sms) {
+  const int64_t waves = sms > 0 ? (tiles + sms - 1) / sms : tiles;
+  return (double)waves * ((double)(128 + bn) * (double)kp * 9.86e-5 + 2.5);
+}
+
+int main_tile_width(int64_t m, int64_t n, int64_t batch, int64_t kp, int sms) {
   if (n <= 128) return 128;
   switch (g_gemm_variant) {
+    case 0: return 256;
     case 2: return 128;
     case 3: return 192;
-    default: return 256;
+    default: {
+      // the width whose tiles cover the output in the least estimated time
+      // (ties to the wider tile)
+      const int64_t mt = (m + BM - 1) / BM * std::max<int64_t>(batch, 1);
+      int best = 256;
+      double best_us = prepass_cost_us(mt * ((n + 255) / 256), 256, kp, sms);
+      for (int bn : {192, 128}) {
+        const double us = prepass_cost_us(mt * ((n + bn - 1) / bn), bn, kp, sms);
+        if (us < best_us * 0.97) best = bn, best_us = us;
+      }
+      return best;
+    }
   }
 }
 
@@ -577,10 +602,10 @@ int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int6
   GemmArgs args{c, bias, div_ptr, div_value, m, n, ldc, batch_stride_c, 0, relu, ctx->error_flag, 0};
   PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
   if (n <= 128) return launch_main<128, 128, 3>(ctx, ops, batch, args, s);
-  switch (g_gemm_variant) {
-    case 0: return launch_main<256, 128, 2>(ctx, ops, batch, args, s);
-    case 2: return launch_main<128, 128, 3>(ctx, ops, batch, args, s);
-    case 3: return launch_main<192, 64, 5>(ctx, ops, batch, args, s);
+  if (g_gemm_variant == 0) return launch_main<256, 128, 2>(ctx, ops, batch, args, s);
+  switch (main_tile_width(m, n, batch, ops.kp, ctx->sm_count)) {
+    case 128: return launch_main<128, 128, 3>(ctx, ops, batch, args, s);
+    case 192: return launch_main<192, 64, 5>(ctx, ops, batch, args, s);
     default: return launch_main<256, 64, 4>(ctx, ops, batch, args, s);
   }
 }

@@ -615,9 +615,14 @@ int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_
   if (g_split_mode == 2) return transposed_ok ? kSplitTransposed : 0;
   if (sms <= 0) return direct_ok ? kSplitDirect : 0;
   const int64_t kp = gemm_kpad(k);
-  const int bn0 = main_tile_width(n), bn1 = tmem_tile_width(n), bn2 = gemm_transposed_tile_width(m, n, sms);
+  const int bn0 = main_tile_width(m, n, 1, kp, sms), bn1 = tmem_tile_width(n);
+  const int bn2 = gemm_transposed_tile_width(m, n, sms);
   const int64_t mt = (m + BM - 1) / BM, nt = (n + BM - 1) / BM;
-  const double c0 = path_cost_us(mt * ((n + bn0 - 1) / bn0), bn0, kp, kColUsPrepass, m + n, sms);
+  // the pre-pass kernel's cost per column grows as its tile narrows (A's
+  // operand reads are shared by fewer columns): (128 + bn) / bn, relative to
+  // the 256-wide tile the constant is calibrated on
+  const double c0 = path_cost_us(mt * ((n + bn0 - 1) / bn0), bn0, kp,
+                                 kColUsPrepass * ((128.0 + bn0) / bn0) / 1.5, m + n, sms);
   const double c1 = direct_ok ? path_cost_us(mt * ((n + bn1 - 1) / bn1), bn1, kp, col_us(bn1), n, sms) : 1e300;
   const double c2 = transposed_ok ? path_cost_us(nt * ((m + bn2 - 1) / bn2), bn2, kp, col_us(bn2), m, sms) : 1e300;
   if (c1 <= c0 && c1 <= c2) return kSplitDirect;

@@ -427,7 +427,10 @@ int b2k_mgpu_attention_tf32x3(b2k_mgpu *mg, const float *q, const float *k, cons
 
 /* Select the GEMM kernel variant for subsequent calls (process-wide; for
  * tuning and benchmarking): 0 = 128x256 tile, 128-byte swizzle, 2 stages;
- * 1 = 128x256, 64-byte swizzle, 4 stages (default); 2 = 128x128, 128-byte
+ * 1 (default) = 128x256, 64-byte swizzle, 4 stages, or the tile of variant 3
+ * or 2 when its tiles cover the output in clearly less estimated time (fewer
+ * waves over the SMs: a row shard of a multi-GPU GEMM); every width gives the
+ * same bits; 2 = 128x128, 128-byte
  * swizzle, 3 stages; 3 = 128x192, 64-byte swizzle, 5 stages.  Outputs at
  * most 128 columns wide always use 2.  For the in-kernel split kernels
  * (b2k_gemm_set_fused_split) variant 2 selects 128-wide tiles and every
