@@ -706,6 +706,7 @@ class Runner:
         self.ctx = pkg("runtime").Context(local)
         self.peaks, self.peak_basis = measured_peaks()
         self.group = None
+        self.use_graphs = True
 
     def native_group(self):
         """The library's own NCCL communicator (b2k_mgpu_*): rank 0 makes the
@@ -737,14 +738,46 @@ class Runner:
     def event_pair(self):
         return (self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True))
 
+    def capture(self, w: Workload, steps: int):
+        """The `steps` steps of a one-kernel workload as one CUDA graph: the same
+        bound library calls (same buffers, same operand-set rotation as the
+        loop), issued on a stream being captured.  A call made from Python costs
+        a few microseconds of host time, more than a whole step of a small
+        shard (the 2^21-element add of an 8-way partition); replayed from a
+        graph, the steps run back to back on the device.  Returns (graph,
+        launches captured, None) or (None, 0, the reason capture failed)."""
+        torch = self.torch
+        try:
+            side = torch.cuda.Stream()
+            calls = [call.with_stream(side.cuda_stream) for call in w.sets]
+            graph = torch.cuda.CUDAGraph()
+            self.ctx.sync()
+            before = self.ctx.kernel_launches()
+            # thread-local capture: other threads (the process group's NCCL
+            # watchdog) keep querying their events while this one captures
+            with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
+                for i in range(steps):
+                    calls[i % len(calls)]()
+            launches = self.ctx.kernel_launches() - before
+            graph.replay()  # untimed: uploads the graph, warms the kernels
+            torch.cuda.synchronize()
+            return graph, launches, None
+        except Exception as exc:  # the loop is used instead, and the line says why
+            torch.cuda.synchronize()
+            return None, 0, f"{type(exc).__name__}: {exc}"
+
     def timed(self, w: Workload, steps: int, warmup: int, sample_dominant: bool = True) -> dict:
         """Warm-up, then EXACTLY `steps` steps between barriers; device time with
         CUDA events (max over ranks), clocks sampled during the region, and the
-        dominant kernel's average launch time."""
+        dominant kernel's average launch time.  One-kernel workloads replay
+        their steps from a CUDA graph (see `capture`)."""
         ctx = self.ctx
         for _ in range(warmup):
             w.step()
         ctx.sync()
+        graph, graph_launches, graph_error = (None, 0, "the workload has several kernels per step")
+        if w.kernels_per_step == 1 and self.use_graphs:
+            graph, graph_launches, graph_error = self.capture(w, steps)
         sampler = ClockSampler(self.local)
         sampler.start()
         time.sleep(0.3)
@@ -753,15 +786,18 @@ class Runner:
         launches_before = ctx.kernel_launches()
         start, stop = self.event_pair()
         start.record()
-        for i in range(steps):
-            sampled = sample_dominant and w.kernels_per_step > 1 and i % self.TIMING_EVERY == 0
-            if sampled:
-                ctx.timing(True, phases=[w.phase])
-            w.step()
-            if sampled:
-                ctx.timing(False)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(steps):
+                sampled = sample_dominant and w.kernels_per_step > 1 and i % self.TIMING_EVERY == 0
+                if sampled:
+                    ctx.timing(True, phases=[w.phase])
+                w.step()
+                if sampled:
+                    ctx.timing(False)
         stop.record()
-        launches = ctx.kernel_launches() - launches_before
+        launches = graph_launches if graph is not None else ctx.kernel_launches() - launches_before
         self.barrier()
         clocks = sampler.stop()
         ctx.sync()  # surfaces a device-side error status
@@ -777,8 +813,10 @@ class Runner:
             dom_ms, dom_launches = ctx.timing_read(w.phase)
             dom_ms = self.max_over_ranks(dom_ms)
             basis = f"CUDA event pair around the kernel on 1 in {self.TIMING_EVERY} steps of the timed region"
+        issue = ("one CUDA graph of the timed steps' library calls, replayed once" if graph is not None
+                 else f"one library call per step from Python ({graph_error})")
         return {"ms": ms, "steps": steps, "launches": launches, "clocks": clocks,
-                "dom_ms": dom_ms / max(1, dom_launches), "dom_basis": basis}
+                "dom_ms": dom_ms / max(1, dom_launches), "dom_basis": basis, "issue": issue}
 
     def roofline(self, w: Workload, t: dict, sustained: bool = False) -> dict:
         peaks, basis = self.peaks, self.peak_basis
@@ -867,7 +905,7 @@ class Runner:
                "higher_is_better": True, "scaling": "strong" if self.world > 1 else "weak",
                "dtype": "f32 (3xtf32 tensor)" if w.bound == "tensor" else "f32",
                "config": w.config(), "roofline": self.roofline(w, t), "clocks": t["clocks"],
-               "gpu_launches": t["launches"]}
+               "gpu_launches": t["launches"], "step_issue": t["issue"]}
         if self.world > 1:
             rec["timing"] = ("kernels only, every rank's shard pre-placed in its HBM; time = max over ranks of each "
                              "rank's CUDA-event time")
@@ -923,6 +961,7 @@ def run_ours(args) -> dict | None:
             pkg("mgpu").init_from_env("nccl", timeout_s=120)
             dist.barrier()
     runner = Runner(torch, dist, rank, local, world)
+    runner.use_graphs = not args.no_graph
     try:
         rec = runner.record(args.workload, args, headline=True)
         if not args.only:
@@ -997,6 +1036,8 @@ def main():
     parser.add_argument("--sub-steps", type=int, default=None, help="timed steps of the other workloads' records")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline samples")
     parser.add_argument("--no-sustained", action="store_true", help="skip the >= 2 s sustained legs")
+    parser.add_argument("--no-graph", action="store_true",
+                        help="issue the one-kernel workloads' timed steps from Python instead of a CUDA graph")
     parser.add_argument("--shard-of", type=int, default=1,
                         help="on one GPU, time rank 0's shard of an N-way partition (profiling the multi-GPU shapes)")
     args = parser.parse_args()

@@ -205,6 +205,14 @@ class BoundCall:
         if status != B2K_OK:
             self._ctx.check(status, self._name)
 
+    def with_stream(self, stream: int) -> "BoundCall":
+        """The same call on another stream (every entry point takes its stream
+        as the last argument), e.g. a stream being captured into a CUDA graph."""
+        other = BoundCall.__new__(BoundCall)
+        other._fn, other._ctx, other._name, other._keep = self._fn, self._ctx, self._name, (self._keep, self)
+        other._args = self._args[:-1] + (_P(stream),)
+        return other
+
 
 class Context:
     """One ``b2k_ctx`` on one CUDA device (not thread-safe, like the C object)."""
