@@ -2,7 +2,7 @@
 """Benchmark of the B200 backend's hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|softmax|add|ragged|attention]
-                    [--impl ours|reference] [--only]
+                    [--impl ours|reference] [--only] [--no-graph]
 
 A step is one pass of the hot path over one batch of synthetic input, the
 BASELINE configurations:
@@ -14,6 +14,10 @@ BASELINE configurations:
 * ``ragged`` -- relu(A B^T + bias), 4097 x 1000 x 777, TFLOP/s;
 * ``attention`` -- softmax(Q K^T / sqrt(128)) V over 4 x 16 heads, S 2048,
   D 128, both contractions 3xTF32, TFLOP/s of useful 4*BH*S*S*D work.
+
+The one-kernel workloads (softmax, add) issue their K timed steps as one
+CUDA graph of the same library calls, replayed once (``step_issue`` in the
+line; ``--no-graph`` issues every step from Python instead).
 
 The line's top-level keys describe the selected workload (``--workload``,
 gemm by default); unless ``--only`` is given, a ``workloads`` object carries
