@@ -194,12 +194,12 @@ class Workload:
     # the partitioned step with its collectives (world > 1)
     def overlap_splits(self) -> int:
         """Pieces (row pieces, or B column panels for the GEMM) per rank in the
-        collective step, each gathered while the next computes.  Two at 2 and
-        4 GPUs: each piece still fills the GPU in as many waves as the whole
-        shard (2048 x 2048 GEMM panels and 1024 x 2048 ones in the transposed
-        orientation are 128 tiles; 16 and 8 attention heads are 256 and 128
-        query tiles).  One at 8, where a piece would leave SMs idle."""
-        return 2 if self.world in (2, 4) else 1
+        collective step, each gathered while the next computes.  One: measured
+        on two B200s, splitting made the step slower -- NCCL's collective
+        kernels take SMs from the single-wave kernels they overlap -- GEMM
+        560 -> 677 us with two panels, softmax 194 -> 248 us, add 116 -> 181 us
+        with two pieces."""
+        return 1
 
     def nccl_setup(self, ctx, torch, group):
         raise NotImplementedError
@@ -551,6 +551,11 @@ class Attention(Workload):
     kernels_per_step = 3
     steps_default = 100
     cpu_heads = 8           # heads per CPU sample (one head is ~0.3 s of float64 BLAS)
+
+    def overlap_splits(self) -> int:
+        """Two pieces of heads at 2 and 4 GPUs (each still several waves of
+        query tiles), one at 8: measured on two B200s, 494 -> 483 us."""
+        return 2 if self.world in (2, 4) else 1
 
     def __init__(self, rank, world, replica=False, bh=64, seq=2048, d=128):
         self.bh, self.seq, self.d = bh, seq, d

@@ -430,11 +430,16 @@ int b2k_mgpu_gemm_tf32x3(b2k_mgpu *mg, const float *a_rows, const float *b, floa
   // Broadcast every panel at once: they run in order on the communicator's
   // stream; panel p's GEMM waits only for panel p.  A [K, N] B is packed
   // panel by panel on rank 0 (its columns are strided); an [N, K] B's panels
-  // are contiguous rows.
+  // are contiguous rows.  One panel is the whole contiguous B: rank 0
+  // broadcasts it in place from the caller's buffer (NCCL's root only reads
+  // an in-place buffer) and multiplies from there, with no staging copy
+  // ahead of the broadcast.
+  const bool b_in_place = panels == 1 && mg->rank == 0;
+  const float *bsrc = b_in_place ? b : bstage;
   for (int p = 0; p < panels; ++p) {
     const int64_t w = cols[p].count;
-    float *dst = bstage + cols[p].start * k;  // panel p: [k][w] or [w][k]
-    if (mg->rank == 0) {
+    float *dst = b_in_place ? const_cast<float *>(b) : bstage + cols[p].start * k;  // panel p: [k][w] or [w][k]
+    if (mg->rank == 0 && !b_in_place) {
       cudaError_t err = b_layout == B2K_B_KN
                             ? cudaMemcpy2DAsync(dst, w * sizeof(float), b + cols[p].start, n * sizeof(float),
                                                 w * sizeof(float), k, cudaMemcpyDeviceToDevice, mg->comm_stream)
@@ -457,7 +462,7 @@ int b2k_mgpu_gemm_tf32x3(b2k_mgpu *mg, const float *a_rows, const float *b, floa
     if (rc) return rc;
     if (mine.count > 0) {
       float *dst = direct ? c + mine.start * n : cstage + cols[p].start * width;
-      rc = b2k_gemm_tf32x3(ctx, a_rows, bstage + cols[p].start * k, dst, mine.count, w, k, k,
+      rc = b2k_gemm_tf32x3(ctx, a_rows, bsrc + cols[p].start * k, dst, mine.count, w, k, k,
                            b_layout == B2K_B_KN ? w : k, direct ? n : w, b_layout,
                            bias ? bias + cols[p].start : nullptr, relu, s);
       if (rc) return rc;

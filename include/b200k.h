@@ -403,7 +403,8 @@ int b2k_mgpu_sync(b2k_mgpu *mg, void *stream, int64_t timeout_ms);
  * [k][n] (B2K_B_KN) or [n][k] (B2K_B_NK), contiguous.  bias: [n] on every
  * rank, or NULL.  B is broadcast in `panels` column panels (1..16): panel
  * p's GEMM waits only for panel p, and panel p's C is gathered while panel
- * p + 1 computes.  Replaces a launch of the reference's GEMM plan
+ * p + 1 computes; with one panel rank 0 broadcasts from `b` itself (read
+ * only, never written).  Replaces a launch of the reference's GEMM plan
  * (tensor_core.py:232-330) by its row-partitioned form. */
 int b2k_mgpu_gemm_tf32x3(b2k_mgpu *mg, const float *a_rows, const float *b, float *c, int64_t m, int64_t n,
                          int64_t k, int64_t align, int32_t b_layout, const float *bias, int32_t relu, int32_t panels,
