@@ -47,13 +47,15 @@ constexpr int kMaxSlabs = 32;
 // flat between 8 and 16 MB.
 constexpr size_t kSlabStream = size_t(8) << 20;
 constexpr size_t kSlabAttention = size_t(16) << 20;
-// GEMM slabs of A: 2 MB each, at most 16 of them. Measured end to end on
-// B200 with 1, 2 and 4 MB slabs: 4097 x 1000 x 777 (A 12.7 MB) took 0.545,
-// 0.495 and 0.546 ms (7 slabs of 2 MB best); 4096^3 (A 64 MB) took 3.08,
-// 3.07 and 2.98 ms (16 slabs of 4 MB best; more slabs add per-slab launch
-// and event overhead that the shorter last slab does not pay back).
-constexpr size_t kSlabGemm = size_t(2) << 20;
-constexpr int64_t kMaxSlabsGemm = 16;
+// GEMM slabs of A: a sixteenth of A, but no less than 2 MB and no more than
+// 4 MB (then at most kMaxSlabs of them). Measured end to end on B200 with 1,
+// 2 and 4 MB slabs: 4097 x 1000 x 777 (A 12.7 MB) took 0.545, 0.495 and
+// 0.546 ms (7 slabs of 2 MB best); 4096^3 (A 64 MB) took 3.08, 3.07 and
+// 2.98 ms (16 slabs of 4 MB best: more slabs add per-slab launch and event
+// overhead that the shorter last slab does not pay back).
+size_t gemm_slab_target(size_t a_bytes) {
+  return std::min(size_t(4) << 20, std::max(size_t(2) << 20, a_bytes / 16));
+}
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -321,8 +323,8 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
   float *dc = reinterpret_cast<float *>(base + oc);
   const float *dbias = bias ? reinterpret_cast<float *>(base + obias) : nullptr;
   // Slabs of rows of A (multiples of the 128-row tile).
-  const int64_t slabs =
-      std::min(b2k::kMaxSlabsGemm, b2k::slab_count((size_t)m * k * 4, (m + 127) / 128, b2k::kSlabGemm));
+  const size_t a_bytes = (size_t)m * k * 4;
+  const int64_t slabs = b2k::slab_count(a_bytes, (m + 127) / 128, b2k::gemm_slab_target(a_bytes));
   const int64_t per = ((m + slabs - 1) / slabs + 127) / 128 * 128;
   b2k::Pipe pipe(ctx, s);
   // The kernel is chosen for the whole call's m, as b2k_gemm_tf32x3 chooses
