@@ -99,3 +99,24 @@ extern "C" int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c,
   return b2k_gemm_tf32x3_impl(&local, a, b, c, m, n, k, lda, ldb, ldc, b_layout, bias, relu,
                               symbols.scratch, (cudaStream_t)stream, nullptr, 1.0f);
 }
+
+extern "C" int b2k_gemm_noalloc_status(int32_t device) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) return B2K_ECUDA;
+  if (device < 0 || device >= count || device >= kMaxDevices) return B2K_EINVAL;
+  int previous = 0;
+  if (cudaGetDevice(&previous) != cudaSuccess) return B2K_ECUDA;
+  if (cudaSetDevice(device) != cudaSuccess) return B2K_ECUDA;
+  DeviceSymbols symbols;
+  int status = device_symbols(device, &symbols);
+  unsigned int word = 0;
+  if (status == B2K_OK && cudaMemcpy(&word, symbols.status, sizeof word, cudaMemcpyDeviceToHost) != cudaSuccess)
+    status = B2K_ECUDA;
+  if (status == B2K_OK && word != 0) {
+    const unsigned int zero = 0;
+    status = cudaMemcpy(symbols.status, &zero, sizeof zero, cudaMemcpyHostToDevice) == cudaSuccess ? B2K_ETIMEOUT
+                                                                                                  : B2K_ECUDA;
+  }
+  if (cudaSetDevice(previous) != cudaSuccess && status == B2K_OK) status = B2K_ECUDA;
+  return status;
+}

@@ -119,6 +119,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_attention_set_fused": ([C.c_int], C.c_int),
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
+    "b2k_gemm_noalloc_status": ([_I32], C.c_int),
     "b2k_row_softmax_f32_host": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_pointwise_f32_host": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3_host": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),

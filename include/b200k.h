@@ -359,12 +359,23 @@ int b2k_launch(b2k_ctx *ctx, const b2k_kernel_desc *desc, void *const *args, int
  * array, so calls that overlap on the GPU (different streams, no ordering)
  * race and corrupt each other's results; calls on one stream are safe.  Each
  * call rewrites all the scratch it reads, so nothing needs clearing.  A
- * device-side bounded-wait expiry is not reported by this entry point.
+ * device-side bounded-wait expiry is not returned by this entry point (its
+ * kernels are still running when it returns): the kernels record it in a
+ * per-device word that b2k_gemm_noalloc_status reads.
  * Other return codes as b2k_gemm_tf32x3 (B2K_EINVAL, B2K_ECUDA). */
 #define B2K_NOALLOC_SCRATCH_BYTES (32u << 20)
 int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
                             int64_t lda, int64_t ldb, int64_t ldc, int32_t b_layout, const float *bias,
                             int32_t relu, void *stream);
+
+/* Read and clear the device error word of b2k_gemm_tf32x3_noalloc on
+ * `device`: B2K_ETIMEOUT when a bounded wait of one of its kernels expired
+ * since the last query (the word is then cleared), B2K_OK when none did,
+ * B2K_EINVAL for a device index out of range, B2K_ECUDA on a CUDA error.
+ * Synchronise the streams of the calls to be checked first; the calling
+ * thread's current device is left as it was.  No counterpart in the
+ * reference (its runner retires a worker on any CUDA error). */
+int b2k_gemm_noalloc_status(int32_t device);
 
 /* --- multi-GPU: one problem over the GPUs of a node -------------------------
  * One process per GPU, each with its own b2k_ctx and one NCCL communicator

@@ -85,3 +85,25 @@ def test_noalloc_rejects_problems_beyond_its_scratch(ctx, torch_cuda):
     status = call_noalloc(lib, p, p, p, 1, 1, 1 << 62, 1 << 62, 1, 1, 0, None, 0)
     assert status == runtime.B2K_EINVAL
     torch_cuda.cuda.synchronize()
+
+
+def test_noalloc_status_reads_and_clears_the_device_word(ctx, torch_cuda):
+    """b2k_gemm_noalloc_status: after completed calls with no expired wait it
+    returns B2K_OK (and again on a second query); device indices outside the
+    machine return B2K_EINVAL; the calling thread's current device is kept."""
+    torch = torch_cuda
+    runtime = pkg("runtime")
+    lib = runtime.library()
+    m, n, k = 256, 384, 96
+    rng = np.random.default_rng(7)
+    da = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda()
+    db = torch.from_numpy(rng.standard_normal((k, n)).astype(np.float32)).cuda()
+    dc = torch.empty((m, n), device="cuda")
+    assert call_noalloc(lib, da.data_ptr(), db.data_ptr(), dc.data_ptr(), m, n, k, k, n, n, 0, None, 0) == 0
+    torch.cuda.synchronize()
+    device = torch.cuda.current_device()
+    assert lib.b2k_gemm_noalloc_status(device) == runtime.B2K_OK
+    assert lib.b2k_gemm_noalloc_status(device) == runtime.B2K_OK
+    assert torch.cuda.current_device() == device
+    assert lib.b2k_gemm_noalloc_status(-1) == runtime.B2K_EINVAL
+    assert lib.b2k_gemm_noalloc_status(torch.cuda.device_count()) == runtime.B2K_EINVAL
