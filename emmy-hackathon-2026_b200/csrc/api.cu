@@ -5,26 +5,37 @@
 
 namespace b2k {
 
-int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream) {
-  if (bytes <= ctx->workspace_bytes) return B2K_OK;
-  // Scratch is reused by every call on this context's stream order; wait for
-  // in-flight users before releasing the old arena.
+// Grow one of the context's arenas to at least `bytes` (2 MiB granules).
+// An arena is reused by every call on this context's stream order; wait for
+// in-flight users before releasing the old one.
+static int grow_arena(b2k_ctx *ctx, void **arena, size_t *arena_bytes, size_t bytes, cudaStream_t stream,
+                      const char *name) {
+  if (bytes <= *arena_bytes) return B2K_OK;
+  if (ctx->fixed_scratch) return fail(ctx, B2K_ESCRATCH, "%s: this entry point allocates nothing", name);
   cudaError_t err = cudaStreamSynchronize(stream);
-  if (err != cudaSuccess) return cuda_fail(ctx, err, "workspace: stream sync");
-  if (ctx->workspace) {
-    err = cudaFree(ctx->workspace);
-    ctx->workspace = nullptr;
-    ctx->workspace_bytes = 0;
-    if (err != cudaSuccess) return cuda_fail(ctx, err, "workspace: cudaFree");
+  if (err != cudaSuccess) return fail(ctx, B2K_ECUDA, "%s: stream sync: %s", name, cudaGetErrorName(err));
+  if (*arena) {
+    err = cudaFree(*arena);
+    *arena = nullptr;
+    *arena_bytes = 0;
+    if (err != cudaSuccess) return fail(ctx, B2K_ECUDA, "%s: cudaFree: %s", name, cudaGetErrorName(err));
   }
   const size_t rounded = (bytes + (size_t(1) << 21) - 1) & ~((size_t(1) << 21) - 1);
-  err = cudaMalloc(&ctx->workspace, rounded);
+  err = cudaMalloc(arena, rounded);
   if (err != cudaSuccess) {
-    ctx->workspace = nullptr;
-    return cuda_fail(ctx, err, "workspace: cudaMalloc");
+    *arena = nullptr;
+    return fail(ctx, B2K_ECUDA, "%s: cudaMalloc: %s", name, cudaGetErrorName(err));
   }
-  ctx->workspace_bytes = rounded;
+  *arena_bytes = rounded;
   return B2K_OK;
+}
+
+int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream) {
+  return grow_arena(ctx, &ctx->workspace, &ctx->workspace_bytes, bytes, stream, "workspace");
+}
+
+int reserve_partials(b2k_ctx *ctx, size_t bytes, cudaStream_t stream) {
+  return grow_arena(ctx, &ctx->partials, &ctx->partials_bytes, bytes, stream, "partials");
 }
 
 static cudaEvent_t take_event(b2k_ctx *ctx) {
@@ -168,6 +179,7 @@ int b2k_destroy(b2k_ctx *ctx) {
   if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
   if (ctx->staging) cudaFree(ctx->staging);
   if (ctx->workspace) cudaFree(ctx->workspace);
+  if (ctx->partials) cudaFree(ctx->partials);
   if (ctx->error_flag) cudaFree(ctx->error_flag);
   delete ctx;
   return B2K_OK;

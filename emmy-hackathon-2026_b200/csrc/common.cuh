@@ -22,6 +22,12 @@ struct b2k_ctx {
   // Context-owned scratch arena (grown on demand, never shrunk).
   void *workspace = nullptr;
   size_t workspace_bytes = 0;
+  // Raw per-chunk accumulators of the chunk-split GEMM (grown on demand).
+  void *partials = nullptr;
+  size_t partials_bytes = 0;
+  // Set on the stack contexts of the allocation-free entry points: nothing
+  // may grow an arena, so paths that need one more (chunk split) are off.
+  bool fixed_scratch = false;
   // Device-side error word written by kernels whose bounded waits expire.
   unsigned int *error_flag = nullptr;
   // Kernels enqueued through this context (b2k_kernel_launches).
@@ -79,6 +85,8 @@ inline int make_current(b2k_ctx *ctx) {
 
 // Grow the context's scratch arena to at least `bytes`.
 int reserve_workspace(b2k_ctx *ctx, size_t bytes, cudaStream_t stream);
+// The same for the chunk-split GEMM's partial-accumulator arena.
+int reserve_partials(b2k_ctx *ctx, size_t bytes, cudaStream_t stream);
 
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device):
 // cudaFuncSetAttribute costs about a microsecond and a half of host time per
@@ -142,7 +150,12 @@ struct SplitOperands {
 constexpr int kSplitDirect = 1;
 constexpr int kSplitTransposed = 2;
 int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
-                    int layout, int sms);
+                    int layout, int sms, bool chunks_ok = true);
+// Estimated microseconds of the chunk-split pre-pass GEMM (one 256-wide K
+// chunk of one 128 x 128 tile per CTA, then an in-order fold of the chunks)
+// for an m x n output with kp K elements on `sms` SMs; a huge value where it
+// does not apply (fewer than two chunks, or b2k_gemm_set_chunk_split(0)).
+double chunked_cost_us(int64_t m, int64_t n, int64_t kp, int sms);
 // Tile width (columns) of the pre-pass kernel gemm_main picks for a [batch]
 // m x n output with kp K elements on `sms` SMs, and that kernel's estimated time.
 int main_tile_width(int64_t m, int64_t n, int64_t batch, int64_t kp, int sms);
@@ -192,7 +205,7 @@ int flash_attention(b2k_ctx *ctx, const float *q, const float *k, const float *v
 // epilogue divides by *div_ptr (or div_value), adds bias[n], applies ReLU.
 int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
-              cudaStream_t s);
+              cudaStream_t s, bool allow_chunks = false);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

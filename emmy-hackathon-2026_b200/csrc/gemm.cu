@@ -220,11 +220,18 @@ struct GemmShape {
 // TMA_C selects the C write path at compile time: one kernel holding both
 // paths needs more registers than the 168 a 320-thread CTA may use, and its
 // spills cost more than the whole epilogue.
-template <int BN, int SW, int STAGES, bool TMA_C>
+//
+// PARTIAL (chunk split, batch 1 only): blockIdx.z is a 256-wide K chunk
+// instead of a batch entry.  The CTA accumulates that one chunk and stores
+// the raw accumulator (no fold, divisor, bias or ReLU) through map_c, a map
+// over the partial arena [chunks][m][round_up(n, 4)]; chunk_fold_kernel then
+// folds the chunks in order exactly as the epilogue below does.
+template <int BN, int SW, int STAGES, bool TMA_C, bool PARTIAL = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                        const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                        const __grid_constant__ CUtensorMap map_c, const GemmArgs args) {
+  static_assert(!PARTIAL || TMA_C, "partial accumulators leave through TMA stores");
   using Shape = GemmShape<BN, SW, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
@@ -241,7 +248,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * BN;
   const int64_t m0 = (int64_t)blockIdx.y * BM;
-  const int num_kb = args.num_kb;
+  // PARTIAL: this CTA's K blocks are chunk blockIdx.z's; the operand maps'
+  // batch coordinate is 0.
+  const int kb_base = PARTIAL ? (int)blockIdx.z * Shape::kChunkBlocks : 0;
+  const int num_kb = PARTIAL ? min(Shape::kChunkBlocks, args.num_kb - kb_base) : args.num_kb;
+  const int zb = PARTIAL ? 0 : (int)blockIdx.z;
   const int num_chunks = (num_kb + Shape::kChunkBlocks - 1) / Shape::kChunkBlocks;
   volatile int *abort = &abort_word;
 
@@ -288,8 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             !sm100::mbar_wait(&empty_bar[s], (round & 1) ^ 1, args.err, sm100::kSiteProducerEmpty, abort))
           break;
         sm100::mbar_arrive_expect_tx(&full_bar[s], Shape::kStage);
-        const int kx = kb * Shape::BK;
-        const int z = (int)blockIdx.z;
+        const int kx = (kb_base + kb) * Shape::BK;
+        const int z = zb;
         sm100::tma_load_3d(a_hi(s), &map_ahi, &full_bar[s], kx, (int)m0, z);
         sm100::tma_load_3d(a_lo(s), &map_alo, &full_bar[s], kx, (int)m0, z);
         sm100::tma_load_3d(b_hi(s), &map_bhi, &full_bar[s], kx, (int)n0, z);
@@ -346,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float acc[CPT];
 #pragma unroll
     for (int j = 0; j < CPT; ++j) acc[j] = 0.0f;
-    if (TMA_C && args.bias) {
+    if (TMA_C && !PARTIAL && args.bias) {
       // The tile's bias columns, read once while the first chunk accumulates;
       // the staging loop then reads them as shared-memory broadcasts.
       for (int i = threadIdx.x - 64; i < BN; i += 32 * kEpilogueWarps)
@@ -369,7 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tmem_ld_32x32b_x16(taddr + j, r);
         sm100::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[j + i] = __fadd_rn(acc[j + i], __uint_as_float(r[i]));
+        for (int i = 0; i < 16; ++i)
+          acc[j + i] = PARTIAL ? __uint_as_float(r[i]) : __fadd_rn(acc[j + i], __uint_as_float(r[i]));
       }
       sm100::tc_fence_before();
       __syncwarp();
@@ -396,9 +408,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               float x = acc[j + q];
-              if (divide) x = __fdiv_rn(x, divisor);
-              if (has_bias) x = __fadd_rn(x, bias_tile[half * CPT + j + q]);
-              if (args.relu) x = x > 0.0f ? x : 0.0f;
+              if (!PARTIAL) {
+                if (divide) x = __fdiv_rn(x, divisor);
+                if (has_bias) x = __fadd_rn(x, bias_tile[half * CPT + j + q]);
+                if (args.relu) x = x > 0.0f ? x : 0.0f;
+              }
               v[q] = x;
             }
             const int col = half * CPT + j;
@@ -411,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::named_barrier(3 + half * 4 + b, 128);  // this half's four warps
         if (leader && ok) {
           const int box = half * (CPT / 32) + b;
-          sm100::tma_store_3d(&map_c, smem + box * kCBox, (int)n0 + 32 * box, (int)m0, (int)blockIdx.z);
+          sm100::tma_store_3d(&map_c, smem + box * kCBox, (int)n0 + 32 * box, (int)m0, (int)blockIdx.z);  // z: chunk when PARTIAL
         }
       }
       if (leader && ok) sm100::tma_store_flush();
@@ -449,6 +463,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_base, Shape::kTmemCols);
+  }
+}
+
+// Chunk split, second kernel: folds the raw chunk accumulators that the
+// PARTIAL kernel left in `part` ([chunks][m][ldp]) in chunk order -- acc = 0,
+// then acc = acc + chunk with round-to-nearest for each chunk in turn, the
+// fold of gemm_tf32x3_kernel's epilogue -- then applies the divisor, the
+// bias and ReLU in that epilogue's order and writes C.  So C is bit for bit
+// what the unsplit kernel writes.  Four columns of one row per thread.
+__global__ void __launch_bounds__(256)
+    chunk_fold_kernel(const float *__restrict__ part, int chunks, int64_t m, int64_t n, int64_t ldp,
+                      float *__restrict__ c, int64_t ldc, const float *__restrict__ bias, int relu,
+                      const float *__restrict__ div_ptr, float div_value, int vec_c) {
+  grid_dependency_wait();
+  const float divisor = div_ptr ? __ldg(div_ptr) : div_value;
+  const bool divide = div_ptr != nullptr || div_value != 1.0f;
+  const int64_t quads = ldp / 4, total = m * quads, plane = m * ldp;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / quads, col = (i - row * quads) * 4;
+    const float *p = part + row * ldp + col;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int g = 0; g < chunks; ++g) {
+      const float4 v = __ldcs(reinterpret_cast<const float4 *>(p + (int64_t)g * plane));
+      acc[0] = __fadd_rn(acc[0], v.x);
+      acc[1] = __fadd_rn(acc[1], v.y);
+      acc[2] = __fadd_rn(acc[2], v.z);
+      acc[3] = __fadd_rn(acc[3], v.w);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float x = acc[q];
+      if (divide) x = __fdiv_rn(x, divisor);
+      if (bias) x = __fadd_rn(x, col + q < n ? __ldg(bias + col + q) : 0.0f);
+      if (relu) x = x > 0.0f ? x : 0.0f;
+      acc[q] = x;
+    }
+    float *crow = c + row * ldc + col;
+    if (vec_c && col + 4 <= n) {
+      *reinterpret_cast<float4 *>(crow) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (col + q < n) crow[q] = acc[q];
+    }
   }
 }
 
@@ -508,12 +566,64 @@ int launch_main(b2k_ctx *ctx, const b2k::SplitOperands &ops, int64_t batch, Gemm
   return b2k::check_launch(ctx, "gemm launch");
 }
 
+// Chunk split: every (128 x 128 tile, 256-wide K chunk) pair is one CTA of
+// the PARTIAL kernel, then chunk_fold_kernel folds the chunks in order and
+// applies the epilogue.  Batch 1 only.
+int launch_chunked(b2k_ctx *ctx, const b2k::SplitOperands &ops, GemmArgs args, cudaStream_t s) {
+  using Shape = GemmShape<128, 128, 3>;
+  const int num_kb = (int)(ops.kp / Shape::BK);
+  const int64_t chunks = (num_kb + Shape::kChunkBlocks - 1) / Shape::kChunkBlocks;
+  const int64_t ldp = (args.n + 3) / 4 * 4;
+  int status = b2k::reserve_partials(ctx, (size_t)(chunks * args.m * ldp) * sizeof(float), s);
+  if (status != B2K_OK) return status;
+  float *part = static_cast<float *>(ctx->partials);
+  CUtensorMap maps[4];
+  if ((status = make_operand_map(ctx, &maps[0], ops.a_hi, args.m, ops.kp, 1, BM, 128)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[1], ops.a_lo, args.m, ops.kp, 1, BM, 128)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[2], ops.b_hi, args.n, ops.kp, 1, 128, 128)) != B2K_OK) return status;
+  if ((status = make_operand_map(ctx, &maps[3], ops.b_lo, args.n, ops.kp, 1, 128, 128)) != B2K_OK) return status;
+  // the partial arena as [chunks][m][ldp], written in the C map's 128 x 32 boxes
+  auto encode = b2k::tensor_map_encoder();
+  if (!encode) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap map_p{};
+  cuuint64_t dims[3] = {(cuuint64_t)args.n, (cuuint64_t)args.m, (cuuint64_t)chunks};
+  cuuint64_t strides[2] = {(cuuint64_t)ldp * 4, (cuuint64_t)(args.m * ldp) * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)BM, 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult res = encode(&map_p, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, part, dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) return b2k::fail(ctx, B2K_ECUDA, "cuTensorMapEncodeTiled (partials) failed (%d)", (int)res);
+  GemmArgs pargs = args;
+  pargs.num_kb = num_kb;
+  pargs.tma_c = 1;
+  auto kernel = gemm_tf32x3_kernel<128, 128, 3, true, true>;
+  cudaError_t err = b2k::set_max_smem(ctx, (const void *)kernel, Shape::kSmem);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (chunks): set smem");
+  const dim3 grid((unsigned)((args.n + 127) / 128), (unsigned)((args.m + BM - 1) / BM), (unsigned)chunks);
+  err = b2k::launch_kernel(b2k::pdl_enabled(), kernel, grid, dim3(kThreads), Shape::kSmem, s, maps[0], maps[1],
+                           maps[2], maps[3], map_p, pargs);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "gemm (chunks) launch");
+  if ((status = b2k::check_launch(ctx, "gemm (chunks) launch")) != B2K_OK) return status;
+  const int64_t quads = args.m * (ldp / 4);
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((quads + 255) / 256, (int64_t)ctx->sm_count * 8));
+  const int vec_c = b2k::aligned16(args.c) && args.ldc % 4 == 0;
+  err = b2k::launch_kernel(b2k::pdl_enabled(), chunk_fold_kernel, dim3((unsigned)blocks), dim3(256), 0, s,
+                           (const float *)part, (int)chunks, args.m, args.n, ldp, args.c, args.ldc, args.bias,
+                           args.relu, args.div_ptr, args.div_value, vec_c);
+  if (err != cudaSuccess) return b2k::cuda_fail(ctx, err, "chunk fold launch");
+  return b2k::check_launch(ctx, "chunk fold launch");
+}
+
 }  // namespace
 
 // Kernel variant selector (tile width, swizzle, stage count); settable for
 // tuning through b2k_gemm_set_variant.  Outputs at most 128 wide always use
 // the 128-wide tile.
 static int g_gemm_variant = 1;
+// Chunk split of the pre-pass kernel (b2k_gemm_set_chunk_split): 0 never,
+// 1 where the estimate says it is faster (default), 2 wherever it applies.
+static int g_chunk_split = 1;
 namespace b2k {
 
 static void fill_job(RowSplitJob &o, const RowSplit &r) {
@@ -595,12 +705,42 @@ int main_tile_width(int64_t m, int64_t n, int64_t batch, int64_t kp, int sms) {
   }
 }
 
+// The chunk split's estimate: its CTAs run chunk-major, so the short last
+// chunk's CTAs (K of kp - 256 (chunks - 1)) fill the last waves; each CTA is
+// a 128 x 128 tile of the pre-pass kernel over one chunk (the per-wave cost
+// of prepass_cost_us).  The fold streams the chunks' partials once more and
+// writes C: (2 chunks + 1) m n floats at ~5 TB/s, plus its launch.
+double chunked_cost_us(int64_t m, int64_t n, int64_t kp, int sms) {
+  if (g_chunk_split == 0 || sms <= 0) return 1e300;
+  const int64_t chunks = (kp + kChunkK - 1) / kChunkK;
+  if (chunks < 2 || chunks > 65535) return 1e300;
+  const int64_t ldp = (n + 3) / 4 * 4;
+  if ((double)chunks * (double)m * (double)ldp * 4.0 > double(size_t(1) << 31)) return 1e300;
+  const int64_t tiles = ((m + BM - 1) / BM) * ((n + 127) / 128);
+  const int64_t full = tiles * (chunks - 1), units = tiles * chunks;
+  const int64_t waves_full = (full + sms - 1) / sms, waves = (units + sms - 1) / sms;
+  const int64_t tail_k = kp - (chunks - 1) * kChunkK;
+  const double t_full = 256.0 * (double)kChunkK * 9.86e-5 + 2.5, t_tail = 256.0 * (double)tail_k * 9.86e-5 + 2.5;
+  return (double)waves_full * t_full + (double)(waves - waves_full) * t_tail + 2.0 +
+         (double)(2 * chunks + 1) * (double)m * (double)n * 4.0 / 5.0e6;
+}
+
 int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
-              cudaStream_t s) {
+              cudaStream_t s, bool allow_chunks) {
   if (batch > 65535) return fail(ctx, B2K_EINVAL, "gemm: batch exceeds 65535");
   GemmArgs args{c, bias, div_ptr, div_value, m, n, ldc, batch_stride_c, 0, relu, ctx->error_flag, 0};
   PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
+  if (allow_chunks && batch == 1 && !ctx->fixed_scratch && g_chunk_split != 0 &&
+      (g_gemm_variant == 1 || g_chunk_split == 2)) {
+    const double split_us = chunked_cost_us(m, n, ops.kp, ctx->sm_count);
+    bool take = split_us < 1e299 && g_chunk_split == 2;
+    if (!take && split_us < 1e299) {
+      const int bn = main_tile_width(m, n, 1, ops.kp, ctx->sm_count);
+      take = split_us < 0.85 * prepass_cost_us(((m + BM - 1) / BM) * ((n + bn - 1) / bn), bn, ops.kp, ctx->sm_count);
+    }
+    if (take) return launch_chunked(ctx, ops, args, s);
+  }
   if (n <= 128) return launch_main<128, 128, 3>(ctx, ops, batch, args, s);
   if (g_gemm_variant == 0) return launch_main<256, 128, 2>(ctx, ops, batch, args, s);
   switch (main_tile_width(m, n, batch, ops.kp, ctx->sm_count)) {
@@ -627,7 +767,7 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
   const bool a_t = (layout & B2K_A_KM) != 0;
   // A divided product runs on the pre-pass kernel, whose epilogue divides.
   const bool divide = div_ptr != nullptr || div_value != 1.0f;
-  const int mode = divide ? 0 : b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, layout, ctx->sm_count);
+  const int mode = divide ? 0 : b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, layout, ctx->sm_count, !ctx->fixed_scratch);
   const int64_t kp = b2k::gemm_kpad(k);
   int status;
   if (mode == b2k::kSplitDirect) {
@@ -672,10 +812,16 @@ int b2k_gemm_tf32x3_impl(b2k_ctx *ctx, const float *a, const float *b, float *c,
     }
   }
   if (status != B2K_OK) return status;
-  return b2k::gemm_main(ctx, ops, m, n, 1, c, ldc, m * ldc, bias, relu, div_ptr, div_value, s);
+  return b2k::gemm_main(ctx, ops, m, n, 1, c, ldc, m * ldc, bias, relu, div_ptr, div_value, s, !ctx->fixed_scratch);
 }
 
 int b2k::gemm_variant() { return g_gemm_variant; }
+
+extern "C" int b2k_gemm_set_chunk_split(int mode) {
+  if (mode < 0 || mode > 2) return B2K_EINVAL;
+  g_chunk_split = mode;
+  return B2K_OK;
+}
 
 extern "C" int b2k_gemm_set_variant(int variant) {
   if (variant < 0 || variant > 3) return B2K_EINVAL;

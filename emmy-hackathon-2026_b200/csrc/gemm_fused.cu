@@ -48,6 +48,8 @@
 // split is shared out by stage in four groups of four warps.  The kernel is
 // launched with programmatic dependent launch (its set-up overlaps the B
 // split's tail).  All waits are bounded.
+#include <algorithm>
+
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
@@ -604,7 +606,7 @@ int gemm_transposed_tile_width(int64_t m, int64_t n, int sms) {
 }
 
 int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
-                    int layout, int sms) {
+                    int layout, int sms, bool chunks_ok) {
   if (g_split_mode == 0 || k < kMinK || m > INT32_MAX - 256 || n > INT32_MAX - 256 || k > INT32_MAX - 64) return 0;
   const bool a_t = (layout & B2K_A_KM) != 0, b_nk = (layout & B2K_B_NK) != 0;
   // direct: A [m][k] read by TMA; transposed: B read by TMA, [n][k] K-major
@@ -621,8 +623,10 @@ int gemm_split_mode(const float *a, const float *b, int64_t m, int64_t n, int64_
   // the pre-pass kernel's cost per column grows as its tile narrows (A's
   // operand reads are shared by fewer columns): (128 + bn) / bn, relative to
   // the 256-wide tile the constant is calibrated on
-  const double c0 = path_cost_us(mt * ((n + bn0 - 1) / bn0), bn0, kp,
-                                 kColUsPrepass * ((128.0 + bn0) / bn0) / 1.5, m + n, sms);
+  double c0 = path_cost_us(mt * ((n + bn0 - 1) / bn0), bn0, kp, kColUsPrepass * ((128.0 + bn0) / bn0) / 1.5, m + n,
+                           sms);
+  // the pre-pass kernel split over K chunks (gemm_main takes it when faster)
+  if (chunks_ok) c0 = std::min(c0, chunked_cost_us(m, n, kp, sms) + (double)(m + n) * (double)kp * 2.4e-6);
   const double c1 = direct_ok ? path_cost_us(mt * ((n + bn1 - 1) / bn1), bn1, kp, col_us(bn1), n, sms) : 1e300;
   const double c2 = transposed_ok ? path_cost_us(nt * ((m + bn2 - 1) / bn2), bn2, kp, col_us(bn2), m, sms) : 1e300;
   if (c1 <= c0 && c1 <= c2) return kSplitDirect;

@@ -93,6 +93,7 @@ extern "C" int b2k_gemm_tf32x3_noalloc(const float *a, const float *b, float *c,
   // A context on the stack, pointing at the static scratch and status word;
   // it owns nothing and is never passed to b2k_destroy.
   b2k_ctx local;
+  local.fixed_scratch = true;
   local.device = device;
   local.sm_count = symbols.sm_count;
   local.error_flag = symbols.status;

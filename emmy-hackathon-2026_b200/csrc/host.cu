@@ -329,7 +329,9 @@ int b2k_gemm_tf32x3_host(b2k_ctx *ctx, const float *a, const float *b, float *c,
   b2k::Pipe pipe(ctx, s);
   // The kernel is chosen for the whole call's m, as b2k_gemm_tf32x3 chooses
   // it, so that the result equals the device entry point's bit for bit.
-  const int mode = k == 0 ? 0 : b2k::gemm_split_mode(da, db, m, n, k, k, b_cols, b_layout, ctx->sm_count);
+  // (slab calls run concurrently on three streams and share no partial
+  // arena, so the chunk split is not among the choices here)
+  const int mode = k == 0 ? 0 : b2k::gemm_split_mode(da, db, m, n, k, k, b_cols, b_layout, ctx->sm_count, false);
   if (k == 0) {
     // No split operands to share between slabs: each slab is a whole GEMM.
     B2K_TRY(pipe.begin());

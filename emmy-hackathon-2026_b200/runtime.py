@@ -120,6 +120,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_attention_tf32x3": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I32, _P], C.c_int),
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_noalloc_status": ([_I32], C.c_int),
+    "b2k_gemm_set_chunk_split": ([C.c_int], C.c_int),
     "b2k_row_softmax_f32_host": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_pointwise_f32_host": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3_host": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
@@ -399,6 +400,11 @@ class Context:
         count = _I64()
         self.check(self.lib.b2k_kernel_launches(self.handle, C.byref(count)), "b2k_kernel_launches")
         return int(count.value)
+
+    def set_gemm_chunk_split(self, mode: int) -> None:
+        """0 = never split the pre-pass GEMM over K chunks, 1 (default) = where
+        estimated faster, 2 = wherever it applies (same bits in every mode)."""
+        self.check(self.lib.b2k_gemm_set_chunk_split(int(mode)), "b2k_gemm_set_chunk_split")
 
     def set_gemm_fused_split(self, mode: int) -> None:
         """0 = pre-pass split of A and B; 3 = A split in-kernel into TMEM (direct);

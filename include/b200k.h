@@ -449,6 +449,20 @@ int b2k_mgpu_attention_tf32x3(b2k_mgpu *mg, const float *q, const float *k, cons
  * other variant 192-wide ones.  No counterpart in the reference, whose plan
  * geometry comes from the IR. */
 int b2k_gemm_set_variant(int variant);
+
+/* Chunk split of the pre-pass GEMM kernel (process-wide; for tuning and
+ * tests): 1 (default) = where the estimate says it is faster, 0 = never,
+ * 2 = wherever it applies.  It applies to single (not batched) calls with at
+ * least two 256-wide K chunks, made through a context: every 128 x 128 output
+ * tile is computed as one CTA per K chunk, each storing its chunk's raw
+ * accumulator in a context-owned arena, and a second kernel folds the chunks
+ * in order and applies the epilogue -- the fold the unsplit kernel makes --
+ * so the result is the same bits.  It fills the GPU when the output has few
+ * tiles and K is long (a row shard of the ragged GEMM on eight GPUs, a
+ * 256 x 512 x 4096 product).  The allocation-free entry point and the
+ * host-array calls never take it.  No counterpart in the reference (its
+ * split-K variant uses atomics, whose order is not fixed). */
+int b2k_gemm_set_chunk_split(int mode);
 /* Process-wide choice of where b2k_gemm_tf32x3 (and the no-alloc variant)
  * split operands into TF32 hi/lo halves:
  *   3            direct: A is staged raw by TMA and split inside the
