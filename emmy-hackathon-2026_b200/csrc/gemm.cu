@@ -484,12 +484,20 @@ __global__ void __launch_bounds__(256)
     const int64_t row = i / quads, col = (i - row * quads) * 4;
     const float *p = part + row * ldp + col;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int g = 0; g < chunks; ++g) {
-      const float4 v = __ldcs(reinterpret_cast<const float4 *>(p + (int64_t)g * plane));
-      acc[0] = __fadd_rn(acc[0], v.x);
-      acc[1] = __fadd_rn(acc[1], v.y);
-      acc[2] = __fadd_rn(acc[2], v.z);
-      acc[3] = __fadd_rn(acc[3], v.w);
+    // Four chunks' loads in flight at a time, added strictly in chunk order.
+    for (int g0 = 0; g0 < chunks; g0 += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (g0 + u < chunks) v[u] = __ldcs(reinterpret_cast<const float4 *>(p + (int64_t)(g0 + u) * plane));
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (g0 + u < chunks) {
+          acc[0] = __fadd_rn(acc[0], v[u].x);
+          acc[1] = __fadd_rn(acc[1], v[u].y);
+          acc[2] = __fadd_rn(acc[2], v[u].z);
+          acc[3] = __fadd_rn(acc[3], v[u].w);
+        }
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
