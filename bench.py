@@ -246,7 +246,7 @@ class Workload:
 
 class Gemm(Workload):
     name, unit, bound, phase = "gemm", "TFLOP/s", "tensor", "mma"
-    kernels_per_step = 2
+    kernels_per_step = 2  # operand split + tensor-core kernel (3 when K is chunk-split: + the fold)
     align = 128
     steps_default = 200
     cpu_seconds = 8.0
