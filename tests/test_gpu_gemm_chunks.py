@@ -33,6 +33,7 @@ CASES = [
     (1, 64, 2048, 0, False, True),       # one row
     (128, 128, 257, 0, False, False),    # two chunks: 256 and a tail of one K element (padded to 32)
     (384, 260, 520, 1, False, True),
+    (640, 384, 512, 0, True, False),     # two full chunks, no tail
 ]
 
 
