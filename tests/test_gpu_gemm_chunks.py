@@ -104,7 +104,7 @@ def test_chunk_split_divided_product_and_unaligned_c(ctx, torch_cuda):
 
 def test_chunk_split_default_takes_it_for_few_tiles_and_long_k(ctx, torch_cuda):
     """Under the default setting a 256 x 512 x 4096 product (8 output tiles on
-    148 SMs) runs split; a 4096 x 4096 x 256 one (one chunk) does not."""
+    148 SMs) runs split; a 1024 x 1024 x 256 one (one chunk) does not."""
     torch = torch_cuda
     rng = np.random.default_rng(5)
     for (m, n, k), want_split in (((256, 512, 4096), True), ((1024, 1024, 256), False)):
