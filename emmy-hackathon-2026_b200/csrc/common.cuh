@@ -171,6 +171,11 @@ int gemm_tmem_a(b2k_ctx *ctx, const float *a, int64_t k, int64_t lda, const Spli
 int gemm_tmem_b(b2k_ctx *ctx, const float *b, int64_t k, int64_t ldb, bool b_nk, const SplitOperands &ops, float *c,
                 int64_t m, int64_t n, int64_t ldc, const float *bias, int relu, cudaStream_t s, int bn = 0);
 int gemm_transposed_tile_width(int64_t m, int64_t n, int sms);
+// Tile width of the direct orientation's kernel (128 or 192).
+int gemm_direct_tile_width(int64_t n);
+// Whether gemm_main runs a batch-1 m x n pre-pass GEMM (kp K elements, `sms`
+// SMs) as the chunk split, under the current variant and chunk settings.
+bool gemm_takes_chunks(int64_t m, int64_t n, int64_t kp, int sms);
 
 // Row-major [batch][rows, k] -> hi/lo [batch][rows][kp].
 int split_rows(b2k_ctx *ctx, const float *src, int64_t rows, int64_t k, int64_t ld, int64_t bs, int64_t batch,

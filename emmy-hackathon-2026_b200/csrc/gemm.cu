@@ -733,22 +733,23 @@ double chunked_cost_us(int64_t m, int64_t n, int64_t kp, int sms) {
          (double)(2 * chunks + 1) * (double)m * (double)n * 4.0 / 5.0e6;
 }
 
+bool gemm_takes_chunks(int64_t m, int64_t n, int64_t kp, int sms) {
+  if (g_chunk_split == 0 || (g_gemm_variant != 1 && g_chunk_split != 2)) return false;
+  const double split_us = chunked_cost_us(m, n, kp, sms);
+  if (split_us >= 1e299) return false;
+  if (g_chunk_split == 2) return true;
+  const int bn = main_tile_width(m, n, 1, kp, sms);
+  return split_us < 0.85 * prepass_cost_us(((m + BM - 1) / BM) * ((n + bn - 1) / bn), bn, kp, sms);
+}
+
 int gemm_main(b2k_ctx *ctx, const SplitOperands &ops, int64_t m, int64_t n, int64_t batch, float *c, int64_t ldc,
               int64_t batch_stride_c, const float *bias, int relu, const float *div_ptr, float div_value,
               cudaStream_t s, bool allow_chunks) {
   if (batch > 65535) return fail(ctx, B2K_EINVAL, "gemm: batch exceeds 65535");
   GemmArgs args{c, bias, div_ptr, div_value, m, n, ldc, batch_stride_c, 0, relu, ctx->error_flag, 0};
   PhaseTimer timer(ctx, B2K_PHASE_MMA, s);
-  if (allow_chunks && batch == 1 && !ctx->fixed_scratch && g_chunk_split != 0 &&
-      (g_gemm_variant == 1 || g_chunk_split == 2)) {
-    const double split_us = chunked_cost_us(m, n, ops.kp, ctx->sm_count);
-    bool take = split_us < 1e299 && g_chunk_split == 2;
-    if (!take && split_us < 1e299) {
-      const int bn = main_tile_width(m, n, 1, ops.kp, ctx->sm_count);
-      take = split_us < 0.85 * prepass_cost_us(((m + BM - 1) / BM) * ((n + bn - 1) / bn), bn, ops.kp, ctx->sm_count);
-    }
-    if (take) return launch_chunked(ctx, ops, args, s);
-  }
+  if (allow_chunks && batch == 1 && !ctx->fixed_scratch && gemm_takes_chunks(m, n, ops.kp, ctx->sm_count))
+    return launch_chunked(ctx, ops, args, s);
   if (n <= 128) return launch_main<128, 128, 3>(ctx, ops, batch, args, s);
   if (g_gemm_variant == 0) return launch_main<256, 128, 2>(ctx, ops, batch, args, s);
   switch (main_tile_width(m, n, batch, ops.kp, ctx->sm_count)) {
@@ -828,6 +829,34 @@ int b2k::gemm_variant() { return g_gemm_variant; }
 extern "C" int b2k_gemm_set_chunk_split(int mode) {
   if (mode < 0 || mode > 2) return B2K_EINVAL;
   g_chunk_split = mode;
+  return B2K_OK;
+}
+
+// The path b2k_gemm_tf32x3 takes for a call, decided by the same functions
+// in the same order as the dispatch (b2k_gemm_tf32x3_impl, then gemm_main),
+// without touching the GPU.
+extern "C" int b2k_gemm_plan(int32_t sms, const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda,
+                             int64_t ldb, int32_t b_layout, b2k_gemm_plan_info *out) {
+  if (!out || sms <= 0 || m <= 0 || n <= 0 || k <= 0) return B2K_EINVAL;
+  if ((b_layout & ~(B2K_B_NK | B2K_A_KM)) != 0) return B2K_EINVAL;
+  if (m > INT32_MAX - 256 || n > INT32_MAX - 256 || k > INT32_MAX - 64) return B2K_EINVAL;
+  const bool a_t = (b_layout & B2K_A_KM) != 0, b_nk = (b_layout & B2K_B_NK) != 0;
+  if (lda < (a_t ? m : k) || ldb < (b_nk ? k : n)) return B2K_EINVAL;
+  const int64_t kp = b2k::gemm_kpad(k);
+  const int mode = b2k::gemm_split_mode(a, b, m, n, k, lda, ldb, b_layout, sms, true);
+  out->split_mode = mode;
+  out->chunks = (int32_t)((kp + kChunkK - 1) / kChunkK);
+  out->chunk_split = 0;
+  if (mode == b2k::kSplitDirect) {
+    out->tile_width = b2k::gemm_direct_tile_width(n);
+  } else if (mode == b2k::kSplitTransposed) {
+    out->tile_width = b2k::gemm_transposed_tile_width(m, n, sms);
+  } else if (b2k::gemm_takes_chunks(m, n, kp, sms)) {
+    out->chunk_split = 1;
+    out->tile_width = 128;
+  } else {
+    out->tile_width = n <= 128 ? 128 : g_gemm_variant == 0 ? 256 : b2k::main_tile_width(m, n, 1, kp, sms);
+  }
   return B2K_OK;
 }
 

@@ -595,6 +595,8 @@ static double path_cost_us(int64_t tiles, int bn, int64_t kp, double per_col_k, 
 
 static int tmem_tile_width(int64_t n) { return (n <= 128 || gemm_variant() == 2) ? 128 : 192; }
 
+int gemm_direct_tile_width(int64_t n) { return tmem_tile_width(n); }
+
 // Tile width of the transposed orientation's kernel B operand (the caller's
 // M): 128 or 192, whichever covers the output in less estimated time.
 int gemm_transposed_tile_width(int64_t m, int64_t n, int sms) {

@@ -87,6 +87,12 @@ class PwProgram(C.Structure):
                 ("insns", PwInsn * PW_MAX_INSNS)]
 
 
+class GemmPlan(C.Structure):
+    """b2k_gemm_plan_info: the kernel path of one b2k_gemm_tf32x3 call."""
+    _fields_ = [("split_mode", C.c_int32), ("tile_width", C.c_int32), ("chunk_split", C.c_int32),
+                ("chunks", C.c_int32)]
+
+
 _P, _I32, _I64, _SZ, _F = C.c_void_p, C.c_int32, C.c_int64, C.c_size_t, C.c_float
 
 # name -> (argtypes without the leading context pointer, or None for no ctx)
@@ -121,6 +127,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2k_gemm_tf32x3_noalloc": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
     "b2k_gemm_noalloc_status": ([_I32], C.c_int),
     "b2k_gemm_set_chunk_split": ([C.c_int], C.c_int),
+    "b2k_gemm_plan": ([_I32, _P, _P, _I64, _I64, _I64, _I64, _I64, _I32, C.POINTER(GemmPlan)], C.c_int),
     "b2k_row_softmax_f32_host": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P], C.c_int),
     "b2k_pointwise_f32_host": ([_P, C.POINTER(PwProgram), C.POINTER(_P), _P, _I64, _P], C.c_int),
     "b2k_gemm_tf32x3_host": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _I32, _P], C.c_int),
@@ -168,6 +175,21 @@ def library() -> C.CDLL:
 
 def exported_symbols() -> list[str]:
     return list(SIGNATURES)
+
+
+def gemm_plan(sms: int, m: int, n: int, k: int, *, a: int = 256, b: int = 256, lda: int | None = None,
+              ldb: int | None = None, b_layout: int = B_KN) -> dict:
+    """The kernel path b2k_gemm_tf32x3 takes for these operands on a GPU of
+    `sms` SMs (b2k_gemm_plan): host arithmetic, no GPU; `a` and `b` are
+    addresses read only for their alignment."""
+    lda = (m if b_layout & A_KM else k) if lda is None else lda
+    ldb = (k if b_layout & B_NK else n) if ldb is None else ldb
+    out = GemmPlan()
+    status = library().b2k_gemm_plan(sms, a or None, b or None, m, n, k, lda, ldb, b_layout, C.byref(out))
+    if status != B2K_OK:
+        raise B2KError(status, "arguments b2k_gemm_tf32x3 refuses", "b2k_gemm_plan")
+    return {"split_mode": out.split_mode, "tile_width": out.tile_width, "chunk_split": bool(out.chunk_split),
+            "chunks": out.chunks}
 
 
 def make_program(n_inputs: int, insns: list[tuple], result: int, broadcast=(), offsets=()) -> PwProgram:

@@ -463,6 +463,25 @@ int b2k_gemm_set_variant(int variant);
  * host-array calls never take it.  No counterpart in the reference (its
  * split-K variant uses atomics, whose order is not fixed). */
 int b2k_gemm_set_chunk_split(int mode);
+
+/* Which kernel path b2k_gemm_tf32x3 takes for a call with these operands on
+ * a GPU of `sms` SMs, under the current settings (variant, split modes,
+ * chunk split), decided by the dispatch's own functions.  Host arithmetic
+ * only: it touches no GPU and dereferences no pointer (a and b are read for
+ * their alignment).  A divided product (b2k_gemm_tf32x3_scaled) always takes
+ * split mode 0.  B2K_EINVAL for the arguments b2k_gemm_tf32x3 refuses, and
+ * for m, n or k of 0 (nothing is launched then). */
+typedef struct {
+  int32_t split_mode;  /* 0 both operands pre-split, 1 A split in the kernel,
+                          2 B split in the kernel (C^T = B^T A^T) */
+  int32_t tile_width;  /* the kernel's tile width: output columns, or output
+                          rows in mode 2 */
+  int32_t chunk_split; /* 1: one CTA per (128 x 128 tile, 256-wide K chunk),
+                          then the in-order fold */
+  int32_t chunks;      /* 256-wide K chunks of the call */
+} b2k_gemm_plan_info;
+int b2k_gemm_plan(int32_t sms, const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda,
+                  int64_t ldb, int32_t b_layout, b2k_gemm_plan_info *out);
 /* Process-wide choice of where b2k_gemm_tf32x3 (and the no-alloc variant)
  * split operands into TF32 hi/lo halves:
  *   3            direct: A is staged raw by TMA and split inside the
