@@ -243,7 +243,12 @@ int b2k_selective_exp_f32(b2k_ctx *ctx, const float *x, float *y, int64_t n, voi
  * transposed, row-major [k, m] (lda >= m; the pre-pass split transposes it;
  * not accepted by the host-array and batched calls).  bias may be NULL; relu
  * is 0 or 1.  C is row-major (ldc >= n).  Uses 2 * (m + n) * round_up(k, 32)
- * * 4 bytes of context scratch for the split operands. */
+ * * 4 bytes of context scratch for the split operands, and, when the call
+ * takes the K-chunk split (b2k_gemm_set_chunk_split, b2k_gemm_plan), a
+ * second context arena of chunks * m * round_up(n, 4) * 4 bytes (chunks =
+ * round_up(k, 32) / 256 rounded up) for the chunks' raw accumulators.  Both
+ * arenas grow on first need (a synchronising cudaMalloc) and are then
+ * reused. */
 #define B2K_B_KN 0
 #define B2K_B_NK 1
 #define B2K_A_KM 2
