@@ -244,6 +244,11 @@ class Workload:
         return f"{self.world} GPUs, one problem partitioned by {axis} (rank {self.rank}: {self.shard.count} of {self.units()})"
 
 
+PLAN_SPLITS = {0: "pre-pass (A and B split before the tensor-core kernel)",
+               1: "direct (A split inside the tensor-core kernel)",
+               2: "transposed (B split inside the tensor-core kernel, C^T = B^T A^T)"}
+
+
 class Gemm(Workload):
     name, unit, bound, phase = "gemm", "TFLOP/s", "tensor", "mma"
     kernels_per_step = 2  # operand split + tensor-core kernel (3 when K is chunk-split: + the fold)
@@ -292,6 +297,12 @@ class Gemm(Workload):
                              b_layout=1 if self.ragged else 0,
                              bias=dbias.data_ptr() if dbias is not None else 0, relu=self.ragged)
         call.keep = (da, db, dbias, dc)
+        if getattr(self, "plan", None) is None:
+            # the library's own path decision for this rank's call (b2k_gemm_plan)
+            p = pkg("runtime").gemm_plan(ctx.sm_count, a.shape[0], self.n, self.k, a=da.data_ptr(), b=db.data_ptr(),
+                                         b_layout=1 if self.ragged else 0)
+            self.plan = {"split": PLAN_SPLITS[p["split_mode"]], "tile_width": p["tile_width"],
+                         "k_chunk_split": p["chunk_split"], "k_chunks": p["chunks"]}
         return call
 
     def e2e_setup(self, session):
@@ -915,6 +926,8 @@ class Runner:
                "dtype": "f32 (3xtf32 tensor)" if w.bound == "tensor" else "f32",
                "config": w.config(), "roofline": self.roofline(w, t), "clocks": t["clocks"],
                "gpu_launches": t["launches"], "step_issue": t["issue"]}
+        if getattr(w, "plan", None):
+            rec["kernel_path"] = dict(w.plan, of="the device-resident calls of `value` (rank 0's shard)")
         if self.world > 1:
             rec["timing"] = ("kernels only, every rank's shard pre-placed in its HBM; time = max over ranks of each "
                              "rank's CUDA-event time")
